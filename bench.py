@@ -1,0 +1,443 @@
+#!/usr/bin/env python
+"""Benchmark of the streaming-attention hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the multi-head GQA decode sweep at its
+largest single-GPU point): one decode step of attention for batch 1, 16 query
+heads sharing 8 KV heads, head_dim 128, KV length T = 262144 per GPU, fp32
+(the reference's element type), block 64, scale 1/sqrt(128); Q/K/V i.i.d.
+N(0,1) from a fixed seed.  K+V = 512 MiB per GPU > L2 (126 MB), so every timed
+step streams from HBM with no flush needed.
+
+A step = one pass of the hot path over that KV: at N = 1 one sa_attn_decode
+launch; at N > 1 (torchrun, one rank per GPU) each rank owns its own T-row KV
+shard (weak scaling, total KV = N*T), reduces it to per-head partial
+(m, l, O) states (sa_attn_decode_partial), the partials are all-gathered with
+NCCL and merged on every rank (sa_attn_merge) -- the sequence-parallel
+decomposition of streaming_attention_mpi_simple.
+
+Metric: attention GB/s = algorithmic bytes (K + V + q + out, each read or
+written once) / time, whole job.  `e2e` is the same metric through the C ABI
+with pinned HOST buffers (the attention.h drop-in: H2D of q, K, V and D2H of
+the output inside the timed region).  `roofline` compares the decode kernel's
+own time with the measured HBM copy bandwidth.  `cpu_baseline` and
+`--impl reference` time the reference's own CPU implementation
+(streaming_attention_omp per query head, compiled from the reference's
+sources into oracle/_ref/libsa_ref.so) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HQ, HKV, D, T_PER_GPU, BLOCK = 16, 8, 128, 262144, 64
+SCALE = 1.0 / math.sqrt(D)
+SEED = 20261201
+METRIC = "attn GB/s"
+WORKLOAD = ("configs[1] GQA decode: B=1, hq=16, hkv=8, d=128, T=262144 per GPU, block 64, "
+            "scale 1/sqrt(128), fp32, N(0,1) seeded")
+FALLBACK_HBM_GBS = 6650.0
+
+
+def algo_bytes(T: int, elt: int = 4) -> int:
+    return (2 * HKV * T * D + 2 * HQ * D) * elt
+
+
+def env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clock / throttle reasons while work runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            f = [x.strip() for x in r.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- helpers
+def load_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def load_traffic(key: str):
+    """DRAM bytes per launch from a committed ncu summary (profiles/ncu_traffic.txt)."""
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
+    try:
+        for line in open(p):
+            f = line.split()
+            if len(f) >= 2 and f[0] == key:
+                return float(f[1])
+    except OSError:
+        pass
+    return None
+
+
+def make_inputs(T: int, dtype, device, seed: int):
+    import torch
+    g = torch.Generator(device=device).manual_seed(seed)
+    q = torch.randn(HQ, D, generator=g, device=device, dtype=torch.float32).to(dtype)
+    k = torch.randn(HKV, T, D, generator=g, device=device, dtype=torch.float32).to(dtype)
+    v = torch.randn(HKV, T, D, generator=g, device=device, dtype=torch.float32).to(dtype)
+    return q, k, v
+
+
+def cpu_reference_time(q, k, v, T_sample: int, budget_s: float, min_reps: int = 3):
+    """Time the reference CPU path (per-head streaming_attention_omp) on a
+    T_sample-row slice of the workload; returns (s per step-of-sample, reps)."""
+    from oracle.oracle import Reference
+    import numpy as np
+    R = Reference()
+    ks = np.ascontiguousarray(k[:, :T_sample])
+    vs = np.ascontiguousarray(v[:, :T_sample])
+    out = np.empty((HQ, D), np.float32)
+    R.gqa_decode_omp(q, ks, vs, BLOCK, 0, SCALE, out)       # warm-up (page-in, threads)
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < min_reps or time.perf_counter() < t_end:
+        t0 = time.perf_counter()
+        R.gqa_decode_omp(q, ks, vs, BLOCK, 0, SCALE, out)
+        times.append(time.perf_counter() - t0)
+        if len(times) >= 1000:
+            break
+    return statistics.median(times), len(times)
+
+
+# ---------------------------------------------------------------- reference arm
+def run_reference(args):
+    rank = env_int("RANK", 0)
+    if rank != 0:
+        return 0
+    import numpy as np
+    import torch
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    q, k, v = make_inputs(T_PER_GPU, torch.float32, dev, SEED)
+    q, k, v = q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy()
+    from oracle.oracle import Reference
+    R = Reference()
+    cores = os.cpu_count() or 1
+    out = np.empty((HQ, D), np.float32)
+    # size each step's sample so that warm-up + timed steps end within ~2 min
+    t0 = time.perf_counter()
+    R.gqa_decode_omp(q, k[:, :8192], v[:, :8192], BLOCK, 0, SCALE, out)
+    R.gqa_decode_omp(q, k[:, :8192], v[:, :8192], BLOCK, 0, SCALE, out)
+    t_small = (time.perf_counter() - t0) / 2
+    est_full = t_small * T_PER_GPU / 8192
+    n = args.steps + args.warmup
+    T_s = T_PER_GPU
+    if est_full * n > 120:
+        T_s = max(8192, int(T_PER_GPU * 120 / (est_full * n)) // 64 * 64)
+    ks, vs = np.ascontiguousarray(k[:, :T_s]), np.ascontiguousarray(v[:, :T_s])
+    for _ in range(args.warmup):
+        R.gqa_decode_omp(q, ks, vs, BLOCK, 0, SCALE, out)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        R.gqa_decode_omp(q, ks, vs, BLOCK, 0, SCALE, out)
+    el = time.perf_counter() - t0
+    gbs = algo_bytes(T_s) * args.steps / el / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el / args.steps * 1e3 * T_PER_GPU / T_s, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": WORKLOAD, "parallelism": "cpu"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores,
+                         "kind": "reference",
+                         "sample": f"streaming_attention_omp per query head (16), T={T_s} of "
+                                   f"{T_PER_GPU} rows per step, {cores} OpenMP threads"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- our arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local = env_int("LOCAL_RANK", 0)
+    if world != args.gpus:
+        print(f"bench.py: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
+        return 2
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    import streaming_attention_b200 as sa
+    from streaming_attention_b200 import _capi
+    ctx = sa.Context(local)
+    stream = torch.cuda.Stream(dev)
+    ctx.set_stream(stream.cuda_stream)
+    L = _capi.lib()
+
+    T = T_PER_GPU
+    q, k, v = make_inputs(T, torch.float32, dev, SEED + rank)
+    out = torch.empty(HQ, D, device=dev)
+    m = torch.empty(HQ, device=dev)
+    l = torch.empty(HQ, device=dev)
+    packed = torch.empty(HQ * (D + 2), device=dev)
+    gathered = torch.empty(world, HQ * (D + 2), device=dev)
+    P = lambda t: _capi.C.c_void_p(t.data_ptr())
+
+    def step():
+        if world == 1:
+            _capi.check(L.sa_attn_decode(ctx.h, 0, P(q), P(k), P(v), T * D, T, D, HQ, HKV, BLOCK,
+                                         SCALE, P(out), 0))
+        else:
+            _capi.check(L.sa_attn_decode_partial(ctx.h, 0, P(q), P(k), P(v), T * D, T, D, HQ, HKV,
+                                                 BLOCK, SCALE, P(packed[:HQ]), P(packed[HQ:2 * HQ]),
+                                                 P(packed[2 * HQ:]), 0))
+            with torch.cuda.stream(stream):
+                dist.all_gather_into_tensor(gathered, packed)
+                gm = gathered[:, :HQ].contiguous()
+                gl = gathered[:, HQ:2 * HQ].contiguous()
+                go = gathered[:, 2 * HQ:].contiguous()
+            _capi.check(L.sa_attn_merge(ctx.h, world, HQ, D, P(gm), P(gl), P(go), P(out), None,
+                                        None, 0))
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    # warm-up, then a ~1 s soak under clock sampling that runs into the timed region
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    if args.profile:
+        # short device-only sequence for ncu: W warm-up launches + K launches
+        for _ in range(args.steps):
+            step()
+        barrier()
+        if rank == 0:
+            print(json.dumps({"profile": True, "launches": args.warmup + args.steps}), flush=True)
+        ctx.close()
+        if world > 1:
+            dist.destroy_process_group()
+        return 0
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    smi_id = vis.split(",")[local].strip() if vis else str(local)
+    clocks = ClockSampler(smi_id)
+    clocks.start()
+    t_soak = time.perf_counter() + 1.0
+    while time.perf_counter() < t_soak:
+        for _ in range(50):
+            step()
+        torch.cuda.synchronize(dev)
+    barrier()
+
+    # timed region: K steps, CUDA events on the launching stream
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    barrier()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    value = algo_bytes(T) * world * args.steps / (ms / 1e3) / 1e9
+    launches = args.steps * (1 if world == 1 else 2)
+
+    # kernel-only timing for the roofline: decode launches back to back
+    kt0 = torch.cuda.Event(enable_timing=True)
+    kt1 = torch.cuda.Event(enable_timing=True)
+    nk = max(20, args.steps)
+    kt0.record(stream)
+    for _ in range(nk):
+        _capi.check(L.sa_attn_decode_partial(ctx.h, 0, P(q), P(k), P(v), T * D, T, D, HQ, HKV,
+                                             BLOCK, SCALE, P(m), P(l), P(out), 0))
+    kt1.record(stream)
+    torch.cuda.synchronize(dev)
+    k_ms = kt0.elapsed_time(kt1) / nk
+
+    result = None
+    if rank == 0:
+        peak, peak_kind = load_peak()
+        achieved = algo_bytes(T) / (k_ms / 1e3) / 1e9
+        traffic = load_traffic("decode_f32_T262144")
+        result = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_kv_len": T * world, "T_per_gpu": T,
+                       "parallelism": f"sp{world}" if world > 1 else "single",
+                       "l2": "inputs (512 MiB K+V per GPU) exceed L2; no flush"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_kind": f"{peak_kind} hbm_gbs (copy bandwidth)",
+                         "kernel": "sa::dec::decode_kernel<float,128,2>",
+                         "kernel_ms": round(k_ms, 5), "traffic": traffic},
+            "clocks": clk,
+            "gpu_launches": launches,
+        }
+
+    # ---- e2e through the C ABI with pinned host buffers (rank-local, N=1 style)
+    hq_ = q.cpu().pin_memory()
+    hk = k.cpu().pin_memory()
+    hv = v.cpu().pin_memory()
+    hout = torch.empty(HQ, D).pin_memory()
+    HP = lambda t: _capi.C.c_void_p(t.data_ptr())
+    ne = max(3, min(args.steps, 20))
+
+    def e2e_step():
+        if world == 1:
+            # the attention.h drop-in: host buffers through the C ABI
+            _capi.check(L.sa_attn_decode(ctx.h, 0, HP(hq_), HP(hk), HP(hv), T * D, T, D, HQ, HKV,
+                                         BLOCK, SCALE, HP(hout), _capi.SA_HOST_PTRS))
+        else:
+            with torch.cuda.stream(stream):
+                q.copy_(hq_, non_blocking=True)
+                k.copy_(hk, non_blocking=True)
+                v.copy_(hv, non_blocking=True)
+            step()
+            with torch.cuda.stream(stream):
+                hout.copy_(out, non_blocking=True)
+            stream.synchronize()
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    w0 = time.perf_counter()
+    for _ in range(ne):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    wall = time.perf_counter() - w0
+    e_ms = max(e0.elapsed_time(e1), wall * 1e3)
+    if world > 1:
+        t = torch.tensor([e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_ms = float(t.item())
+    e2e = algo_bytes(T) * world * ne / (e_ms / 1e3) / 1e9
+
+    if rank == 0:
+        result["e2e"] = {"value": round(e2e, 2), "unit": "GB/s",
+                         "h2d_bytes_per_step": (HQ * D + 2 * HKV * T * D) * 4,
+                         "d2h_bytes_per_step": HQ * D * 4, "steps": ne,
+                         "path": "sa_attn_decode(SA_HOST_PTRS) from pinned host memory"}
+        # ---- CPU baseline: the reference's CPU path on a bounded sample (rank 0, N=1)
+        if world == 1 and not args.no_cpu:
+            try:
+                import numpy as np
+                qn, kn, vn = q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy()
+                T_s = 65536
+                t_s, reps = cpu_reference_time(qn, kn, vn, T_s, budget_s=args.cpu_budget)
+                result["cpu_baseline"] = {
+                    "value": round(algo_bytes(T_s) / t_s / 1e9, 3), "unit": "GB/s",
+                    "cores": os.cpu_count(), "kind": "reference",
+                    "sample": f"streaming_attention_omp per query head (16 heads) over the first "
+                              f"{T_s} of {T} KV rows, {reps} reps, median"}
+            except Exception as e:  # the baseline is reported, never required
+                result["cpu_baseline"] = {"value": None, "unit": "GB/s", "cores": os.cpu_count(),
+                                          "kind": "reference", "sample": f"unavailable: {e}"}
+        print(json.dumps(result), flush=True)
+
+    ctx.close()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--profile", action="store_true",
+                    help="only W warm-up + K device steps (a short launch sequence for ncu)")
+    ap.add_argument("--cpu-budget", type=float, default=10.0,
+                    help="seconds of CPU work for the cpu_baseline sample")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

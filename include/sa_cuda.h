@@ -1,0 +1,138 @@
+/*
+ * sa_cuda.h -- C ABI of libsa_cuda.so, the B200 (sm_100a) implementation of
+ * streaming-attention's hot path: online-softmax block attention and the
+ * Qwen3 forward it drives.
+ *
+ * Plain C: opaque handles, raw pointers, sizes and int status codes.  No C++
+ * or torch types cross this boundary.  Each entry point names the reference
+ * interface it replaces (path:line inside the reference project).
+ *
+ * Conventions
+ *  - Every call returns SA_OK (0) or a negative SA_ERR_* code; the message of
+ *    the last failure on the calling thread is returned by sa_last_error().
+ *  - Pointers are device pointers unless SA_HOST_PTRS is set in `flags`; then
+ *    inputs are read from and outputs written to host memory (pinned memory
+ *    gives full PCIe bandwidth) and the call returns after the result is on
+ *    the host.
+ *  - Device-pointer calls are asynchronous on the context's stream
+ *    (sa_ctx_stream); sa_ctx_synchronize() waits for them and reports any
+ *    asynchronous CUDA error.
+ *  - A context is bound to one GPU and is not thread-safe; distinct contexts
+ *    may be used concurrently from different threads.
+ *  - Results are deterministic run to run: split counts depend only on the
+ *    shape and the GPU's SM count.
+ */
+#ifndef SA_CUDA_H
+#define SA_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define SA_OK            0
+#define SA_ERR_ARG      -1   /* bad shape, null pointer, misalignment      */
+#define SA_ERR_CUDA     -2   /* a CUDA runtime call failed                 */
+#define SA_ERR_OOM      -3   /* device or pinned allocation failed         */
+#define SA_ERR_TIMEOUT  -4   /* a bounded device-side wait expired         */
+#define SA_ERR_NCCL     -5   /* a collective failed                        */
+#define SA_ERR_RANGE    -6   /* index out of range (token id, cache slot)  */
+#define SA_ERR_FULL     -7   /* KV cache full (kv_cache.h:109-111)         */
+
+/* ---- element types ------------------------------------------------------ */
+#define SA_F32   0
+#define SA_BF16  1
+
+/* ---- flags -------------------------------------------------------------- */
+#define SA_HOST_PTRS   1u    /* pointers are host memory; call is blocking */
+
+typedef struct sa_ctx sa_ctx;
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* sa_last_error(void);
+
+/* Library version string. */
+const char* sa_version(void);
+
+/* Create a context on `device` with its own non-blocking stream. */
+int sa_ctx_create(int device, sa_ctx** out);
+/* Destroy a context (synchronises its stream first). */
+int sa_ctx_destroy(sa_ctx* ctx);
+/* Use a caller-owned stream (a cudaStream_t) instead of the context's own;
+ * NULL restores the context's own stream. */
+int sa_ctx_set_stream(sa_ctx* ctx, void* stream);
+/* The stream device-pointer calls are issued on (a cudaStream_t). */
+void* sa_ctx_stream(sa_ctx* ctx);
+/* Wait for all work on the context's stream; returns SA_ERR_CUDA with the
+ * CUDA error text on an asynchronous failure. */
+int sa_ctx_synchronize(sa_ctx* ctx);
+/* Number of SMs of the context's GPU (148 on B200). */
+int sa_ctx_num_sms(sa_ctx* ctx);
+
+/* ======================================================================== */
+/* Decode (single-query) streaming attention                                 */
+/* ======================================================================== */
+
+/*
+ * Multi-head GQA decode attention for one query token.
+ *
+ *   q    [hq, d]                     element type `dtype`
+ *   k, v head h at k + h*kv_head_stride (elements), rows of d elements,
+ *        T rows: [hkv, T(+pad), d]   element type `dtype`
+ *   out  [hq, d] fp32
+ *
+ * out[h] = softmax(scale * q[h] . K[h/(hq/hkv)]^T) V[h/(hq/hkv)]
+ *
+ * With hq = hkv = 1 and scale = 1 this is streaming_attention_serial /
+ * streaming_attention_omp / naive_attention_serial of
+ * attention/src/attention.h:27-208 (which apply no 1/sqrt(d) scale).  With
+ * hq = 16, hkv = 8 and scale = 1/sqrt(d) it is the decode attention of
+ * qwen3_decoder_layer_with_cache (tensor_cpp/src/qwen3_ops.cpp:860-900:
+ * repeat_kv + ops::self_attention over the cache).
+ *
+ * `block` is the reference's online-softmax block size (64 or 128); it must be
+ * > 0 but does not change the result beyond fp32 rounding -- the GPU tiles the
+ * sequence its own way.  T = 0 yields zeros (as the reference's serial path).
+ * Requirements: d in {64, 128, 256}; hq % hkv == 0 and hq/hkv in {1,2,4,8};
+ * k, v and kv_head_stride*elt 16-byte aligned.
+ * The call keeps its (m, l, O) split partials in context scratch memory, so
+ * two calls on one context must not overlap on different streams.
+ */
+int sa_attn_decode(sa_ctx* ctx, int dtype, const void* q, const void* k, const void* v,
+                   long long kv_head_stride, int T, int d, int hq, int hkv, int block,
+                   float scale, float* out, unsigned flags);
+
+/*
+ * Same attention, returning the un-finalised online-softmax state so that
+ * several KV shards (e.g. one per GPU) can be merged with sa_attn_merge.
+ *   m_out, l_out [hq]   running max and normaliser (reference: PartialResult,
+ *                       attention/src/streaming_omp.cpp:12-16; m=-inf, l=1
+ *                       for an empty shard)
+ *   o_out [hq, d]       output normalised by l (process_blocks_serial,
+ *                       streaming_omp.cpp:53-89)
+ * Replaces the rank-local part of streaming_attention_mpi_simple
+ * (attention/src/streaming_mpi.cpp:252-292).
+ */
+int sa_attn_decode_partial(sa_ctx* ctx, int dtype, const void* q, const void* k,
+                           const void* v, long long kv_head_stride, int T, int d, int hq,
+                           int hkv, int block, float scale, float* m_out, float* l_out,
+                           float* o_out, unsigned flags);
+
+/*
+ * Merge n_parts partial states, part-major:
+ *   m, l [n_parts, hq];  o [n_parts, hq, d];  out [hq, d] fp32.
+ * Optional m_out/l_out [hq] (may be NULL) receive the merged state.
+ * The associative merge of merge_partial_results
+ * (attention/src/streaming_omp.cpp:27-48) used by rank 0 at
+ * streaming_mpi.cpp:295-305.  All pointers device unless SA_HOST_PTRS.
+ */
+int sa_attn_merge(sa_ctx* ctx, int n_parts, int hq, int d, const float* m, const float* l,
+                  const float* o, float* out, float* m_out, float* l_out, unsigned flags);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SA_CUDA_H */

@@ -1,0 +1,173 @@
+"""Attention entry points, mirroring the reference's operator interface.
+
+``streaming_attention_cuda`` / ``naive_attention_cuda`` take the arguments of
+``streaming_attention_serial`` / ``naive_attention_serial``
+(attention/src/attention.h:27-44, 118-125): a query row, row-major K and V of
+T x d, unscaled scores, and return the d-vector.  ``streaming_attention_mpi_cuda``
+is ``streaming_attention_mpi_simple`` (attention.h:191-208) over
+torch.distributed ranks, one GPU per rank.
+
+Arrays may be numpy (host memory: the library copies them in and the result
+out) or CUDA torch tensors (device memory: the call runs on torch's current
+stream, asynchronously).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from ._capi import SA_BF16, SA_F32, SA_HOST_PTRS, Context, check, default_context, lib
+
+
+def _is_torch(x) -> bool:
+    return type(x).__module__.startswith("torch")
+
+
+def _dtype_code(x) -> int:
+    if _is_torch(x):
+        import torch
+        if x.dtype == torch.float32:
+            return SA_F32
+        if x.dtype == torch.bfloat16:
+            return SA_BF16
+        raise TypeError(f"unsupported dtype {x.dtype}")
+    if x.dtype == np.float32:
+        return SA_F32
+    raise TypeError(f"host arrays must be float32 (got {x.dtype}); pass bf16 as torch tensors")
+
+
+def _ctx_for(x, ctx: Context | None) -> Context:
+    if ctx is not None:
+        return ctx
+    if _is_torch(x):
+        return default_context(x.device.index or 0)
+    return default_context(0)
+
+
+def _bind_stream(ctx: Context, x) -> None:
+    if _is_torch(x):
+        import torch
+        ctx.set_stream(torch.cuda.current_stream(x.device).cuda_stream)
+
+
+def _ptr(x):
+    if _is_torch(x):
+        return C.c_void_p(x.data_ptr())
+    return x.ctypes.data_as(C.c_void_p)
+
+
+def _prep(x):
+    if _is_torch(x):
+        return x.contiguous()
+    return np.ascontiguousarray(x)
+
+
+def _out_like(x, shape):
+    if _is_torch(x):
+        import torch
+        return torch.empty(shape, dtype=torch.float32, device=x.device)
+    return np.empty(shape, np.float32)
+
+
+def attn_decode(q, k, v, scale: float = 1.0, block: int = 64, ctx: Context | None = None,
+                out=None):
+    """GQA decode attention (sa_attn_decode).
+
+    q [hq, d]; k, v [hkv, T, d] (same dtype: fp32, or bf16 torch tensors);
+    returns out [hq, d] fp32.  ``scale`` multiplies the scores (1.0 reproduces
+    the unscaled attention.h kernels; 1/sqrt(d) the Qwen3 attention).
+    """
+    q, k, v = _prep(q), _prep(k), _prep(v)
+    hq, d = q.shape
+    hkv, T, d2 = k.shape
+    assert d2 == d and tuple(v.shape) == tuple(k.shape)
+    ctx = _ctx_for(q, ctx)
+    dt = _dtype_code(q)
+    flags = 0 if _is_torch(q) else SA_HOST_PTRS
+    if out is None:
+        out = _out_like(q, (hq, d))
+    _bind_stream(ctx, q)
+    check(lib().sa_attn_decode(ctx.h, dt, _ptr(q), _ptr(k), _ptr(v), T * d, T, d, hq, hkv, block,
+                               scale, _ptr(out), flags))
+    return out
+
+
+def attn_decode_partial(q, k, v, scale: float = 1.0, block: int = 64, ctx: Context | None = None):
+    """Un-finalised state (m [hq], l [hq], o [hq, d]) of attn_decode (sa_attn_decode_partial)."""
+    q, k, v = _prep(q), _prep(k), _prep(v)
+    hq, d = q.shape
+    hkv, T, _ = k.shape
+    ctx = _ctx_for(q, ctx)
+    flags = 0 if _is_torch(q) else SA_HOST_PTRS
+    m, l, o = _out_like(q, (hq,)), _out_like(q, (hq,)), _out_like(q, (hq, d))
+    _bind_stream(ctx, q)
+    check(lib().sa_attn_decode_partial(ctx.h, _dtype_code(q), _ptr(q), _ptr(k), _ptr(v), T * d, T,
+                                       d, hq, hkv, block, scale, _ptr(m), _ptr(l), _ptr(o), flags))
+    return m, l, o
+
+
+def attn_merge(m, l, o, ctx: Context | None = None, with_state: bool = False):
+    """Merge part-major partials m, l [n, hq], o [n, hq, d] (sa_attn_merge)."""
+    m, l, o = _prep(m), _prep(l), _prep(o)
+    n, hq, d = o.shape
+    ctx = _ctx_for(o, ctx)
+    flags = 0 if _is_torch(o) else SA_HOST_PTRS
+    out = _out_like(o, (hq, d))
+    mo = _out_like(o, (hq,)) if with_state else None
+    lo = _out_like(o, (hq,)) if with_state else None
+    _bind_stream(ctx, o)
+    check(lib().sa_attn_merge(ctx.h, n, hq, d, _ptr(m), _ptr(l), _ptr(o), _ptr(out),
+                              _ptr(mo) if with_state else None, _ptr(lo) if with_state else None,
+                              flags))
+    return (out, mo, lo) if with_state else out
+
+
+# ---- attention.h mirror ---------------------------------------------------
+
+def streaming_attention_cuda(Q, K, V, T: int, d: int, block_size: int, ctx: Context | None = None):
+    """streaming_attention_serial/_omp (attention.h:118-125, 159-167) on the GPU."""
+    q = _prep(Q).reshape(1, d)
+    k = _prep(K).reshape(1, T, d)
+    v = _prep(V).reshape(1, T, d)
+    return attn_decode(q, k, v, 1.0, block_size, ctx).reshape(d)
+
+
+def naive_attention_cuda(Q, K, V, T: int, d: int, ctx: Context | None = None):
+    """naive_attention_serial (attention.h:27-33): the same softmax(qK^T)V."""
+    return streaming_attention_cuda(Q, K, V, T, d, 64, ctx)
+
+
+def streaming_attention_mpi_cuda(Q_local, K_local, V_local, T_local: int, T_global: int, d: int,
+                                 block_size: int, group=None, ctx: Context | None = None):
+    """streaming_attention_mpi_simple (attention/src/streaming_mpi.cpp:252-309).
+
+    One rank per GPU under torch.distributed: rank 0's query is broadcast,
+    every rank reduces its local KV slice to a partial (m, l, O) on its GPU,
+    the partials are all-gathered (one collective of hq*(d+2) floats), and
+    merged on the device.  As in the reference, rank 0 returns the result and
+    the other ranks return zeros.  Q/K/V are CUDA torch tensors on this
+    rank's device.
+    """
+    import torch
+    import torch.distributed as dist
+
+    rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
+    q = Q_local.reshape(1, d).contiguous()
+    if q.dtype != K_local.dtype:
+        q = q.to(K_local.dtype)
+    dist.broadcast(q, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+    k = K_local.reshape(1, T_local, d)
+    v = V_local.reshape(1, T_local, d)
+    m, l, o = attn_decode_partial(q, k, v, 1.0, block_size, ctx)
+    packed = torch.cat([m, l, o.reshape(-1)])
+    gathered = torch.empty(world, packed.numel(), dtype=torch.float32, device=packed.device)
+    dist.all_gather_into_tensor(gathered, packed, group=group)
+    gm = gathered[:, 0:1].contiguous()
+    gl = gathered[:, 1:2].contiguous()
+    go = gathered[:, 2:].reshape(world, 1, d).contiguous()
+    out = attn_merge(gm, gl, go, ctx).reshape(d)
+    if rank != 0:
+        out.zero_()
+    return out

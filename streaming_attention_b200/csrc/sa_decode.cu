@@ -1,0 +1,591 @@
+// sa_decode.cu -- single-query (decode) streaming attention on B200.
+//
+// Replaces the reference's online-softmax block attention
+// (attention/src/streaming_serial.cpp:20-71, streaming_omp.cpp:99-154,
+// streaming_mpi.cpp:252-309; softmax update utils/softmax_online.h:40-87) and
+// the decode attention of qwen3_decoder_layer_with_cache
+// (tensor_cpp/src/qwen3_ops.cpp:860-900).
+//
+// Design (HBM-bound: every K/V byte is read exactly once).
+//  * Grid = (KV splits, KV heads).  Each CTA owns one contiguous slice of the
+//    sequence of one KV head and serves all G = hq/hkv query heads that share
+//    it, so GQA never re-reads K/V.  Split counts fill 2 CTAs per SM.
+//  * One producer warp streams the slice through shared memory with 1-D bulk
+//    copies (cp.async.bulk, TMA engine) into a 3-stage mbarrier ring of 32 KB
+//    (K+V) stages, with an L2 evict-first hint (the data is used once).
+//  * Four consumer warps split each stage's rows.  Inside a warp, 8-lane groups
+//    each own one row at a time; a lane holds D/8 columns of q (pre-scaled by
+//    scale*log2 e) and of the output accumulator.  Scores are reduced with
+//    three xor-shuffles; the (m, l, O) online-softmax recurrence runs per group
+//    in the exp2 domain with an unnormalised O (normalised once at the end).
+//  * States are combined across groups (shuffles) and warps (shared memory);
+//    each CTA writes its (m, l, O/l) split partial, and the last CTA of a KV
+//    head to finish (atomic arrival counter) merges all splits -- the
+//    associative merge of streaming_omp.cpp:27-48 -- so a call is one launch.
+#include <cuda_bf16.h>
+#include <cmath>
+
+#include "sa_internal.h"
+#include "sa_ptx.cuh"
+
+namespace sa {
+namespace dec {
+
+constexpr int NW = 4;                      // consumer warps
+constexpr int THREADS = (NW + 1) * 32;     // + one producer warp
+constexpr int STAGE_BYTES = 32768;         // K + V bytes per stage
+constexpr int STAGES = 3;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 2 * STAGES * 8 + 16;
+constexpr int MAX_SPLITS = 1024;
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float LN2 = 0.6931471805599453f;
+
+struct Args {
+    const void* q;
+    const void* k;
+    const void* v;
+    long long kv_head_stride;   // elements between KV heads
+    int T, hq, hkv;
+    int rows_per_split, n_splits;
+    float qscale;               // scale * log2(e)
+    float* part_m;              // [hq][n_splits]  (log2 domain)
+    float* part_l;              // [hq][n_splits]
+    float* part_o;              // [hq][n_splits][D] normalised by l
+    unsigned* counters;         // [hkv] arrival counters, zero between launches
+    float* out;                 // [hq][D]
+    float* out_m;               // optional [hq], natural-log domain
+    float* out_l;               // optional [hq]
+    int* status;
+};
+
+// Unpack one 16-byte chunk into VEC floats.
+template <typename KT> struct Chunk;
+template <> struct Chunk<float> {
+    static constexpr int VEC = 4;
+    static __device__ __forceinline__ void load(const void* p, float* f) {
+        float4 r = *reinterpret_cast<const float4*>(p);
+        f[0] = r.x; f[1] = r.y; f[2] = r.z; f[3] = r.w;
+    }
+};
+template <> struct Chunk<__nv_bfloat16> {
+    static constexpr int VEC = 8;
+    static __device__ __forceinline__ void load(const void* p, float* f) {
+        uint4 r = *reinterpret_cast<const uint4*>(p);
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            f[2 * i] = __uint_as_float(w[i] << 16);
+            f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+        }
+    }
+};
+
+template <typename KT, int D>
+struct Shape {
+    static constexpr int ELT = sizeof(KT);
+    static constexpr int ROW_BYTES = D * ELT;
+    static constexpr int STAGE_ROWS = STAGE_BYTES / (2 * ROW_BYTES);
+    static constexpr int RW = STAGE_ROWS / NW;   // rows per warp per stage
+    static constexpr int NR = RW / 4;            // rows per 8-lane group per stage
+    static constexpr int VEC = Chunk<KT>::VEC;
+    static constexpr int CPL = D / 8;            // columns per lane
+    static constexpr int CH = CPL / VEC;         // 16-byte chunks per lane per row
+    static_assert(NR >= 1 && CH >= 1, "tile shape");
+};
+
+// Fold state (m2, l2, o2) into (m, l, o); exp2 domain, unnormalised o.
+__device__ __forceinline__ void combine_weights(float m, float m2, float& a, float& b, float& M) {
+    M = fmaxf(m, m2);
+    a = (m == -INFINITY) ? 0.f : ex2(m - M);
+    b = (m2 == -INFINITY) ? 0.f : ex2(m2 - M);
+}
+
+template <typename KT, int D, int G>
+__global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
+    using S = Shape<KT, D>;
+    constexpr int SR = S::STAGE_ROWS, RB = S::ROW_BYTES, CPL = S::CPL, CH = S::CH, VEC = S::VEC;
+
+    extern __shared__ __align__(128) unsigned char smem[];
+    unsigned char* kbuf = smem;
+    unsigned char* vbuf = smem + STAGES * SR * RB;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    __shared__ float red_m[NW][G], red_l[NW][G];
+    __shared__ int s_issued, s_consumed, s_last;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int kvh = blockIdx.y, split = blockIdx.x;
+    const int t0 = split * a.rows_per_split;
+    const int nrows = max(0, min(a.T - t0, a.rows_per_split));
+    const int nst = (nrows + SR - 1) / SR;
+    const KT* kg = static_cast<const KT*>(a.k) + (size_t)kvh * a.kv_head_stride + (size_t)t0 * D;
+    const KT* vg = static_cast<const KT*>(a.v) + (size_t)kvh * a.kv_head_stride + (size_t)t0 * D;
+
+    if (tid == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, NW);
+        }
+        fence_barrier_init();
+        s_issued = 0;
+        s_consumed = nst;
+    }
+    __syncthreads();
+
+    float m[G], l[G], o[G][CPL];
+    const int grp = lane >> 3, sub = lane & 7;
+
+    if (warp == NW) {
+        // ---------------- producer: one elected lane issues the bulk copies
+        if (lane == 0) {
+            const uint64_t pol = policy_evict_first();
+            int it = 0;
+            for (; it < nst; ++it) {
+                const int s = it % STAGES;
+                if (it >= STAGES && !mbar_wait(empty + s, ((it / STAGES) & 1) ^ 1, a.status)) break;
+                const int rows = min(SR, nrows - it * SR);
+                const uint32_t bytes = (uint32_t)(rows * RB);
+                mbar_arrive_expect_tx(full + s, 2 * bytes);
+                bulk_g2s_hint(kbuf + s * SR * RB, kg + (size_t)it * SR * D, bytes, full + s, pol);
+                bulk_g2s_hint(vbuf + s * SR * RB, vg + (size_t)it * SR * D, bytes, full + s, pol);
+            }
+            s_issued = it;
+        }
+    } else {
+        // ---------------- consumers
+        float qr[G][CPL];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const KT* qh = static_cast<const KT*>(a.q) + (size_t)(kvh * G + g) * D;
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+                Chunk<KT>::load(qh + (sub + 8 * c) * VEC, &qr[g][c * VEC]);
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) qr[g][c * VEC + e] *= a.qscale;
+            }
+            m[g] = -INFINITY;
+            l[g] = 0.f;
+#pragma unroll
+            for (int i = 0; i < CPL; ++i) o[g][i] = 0.f;
+        }
+
+        int it = 0;
+        for (; it < nst; ++it) {
+            const int s = it % STAGES;
+            if (!mbar_wait(full + s, (it / STAGES) & 1, a.status)) break;
+            const int valid_rows = min(SR, nrows - it * SR);
+            const unsigned char* ks = kbuf + s * SR * RB;
+            const unsigned char* vs = vbuf + s * SR * RB;
+
+            float sc[G][S::NR];
+#pragma unroll
+            for (int j = 0; j < S::NR; ++j) {
+                const int r = warp * S::RW + grp + 4 * j;
+                float kf[CPL];
+#pragma unroll
+                for (int c = 0; c < CH; ++c)
+                    Chunk<KT>::load(ks + (size_t)r * RB + (sub + 8 * c) * 16, &kf[c * VEC]);
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int i = 0; i < CPL; ++i) acc = fmaf(qr[g][i], kf[i], acc);
+                    sc[g][j] = acc;
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+#pragma unroll
+                for (int j = 0; j < S::NR; ++j) {
+                    float x = sc[g][j];
+                    x += __shfl_xor_sync(0xffffffffu, x, 1);
+                    x += __shfl_xor_sync(0xffffffffu, x, 2);
+                    x += __shfl_xor_sync(0xffffffffu, x, 4);
+                    sc[g][j] = x;
+                }
+
+            float p[G][S::NR];
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                float mx = m[g];
+#pragma unroll
+                for (int j = 0; j < S::NR; ++j)
+                    if (warp * S::RW + grp + 4 * j < valid_rows) mx = fmaxf(mx, sc[g][j]);
+                const float corr = (m[g] == -INFINITY) ? 0.f : ex2(m[g] - mx);
+                float ps = 0.f;
+#pragma unroll
+                for (int j = 0; j < S::NR; ++j) {
+                    const bool ok = warp * S::RW + grp + 4 * j < valid_rows;
+                    p[g][j] = ok ? ex2(sc[g][j] - mx) : 0.f;
+                    ps += p[g][j];
+                }
+                l[g] = l[g] * corr + ps;
+#pragma unroll
+                for (int i = 0; i < CPL; ++i) o[g][i] *= corr;
+                m[g] = mx;
+            }
+#pragma unroll
+            for (int j = 0; j < S::NR; ++j) {
+                const int r = warp * S::RW + grp + 4 * j;
+                if (r < valid_rows) {
+                    float vf[CPL];
+#pragma unroll
+                    for (int c = 0; c < CH; ++c)
+                        Chunk<KT>::load(vs + (size_t)r * RB + (sub + 8 * c) * 16, &vf[c * VEC]);
+#pragma unroll
+                    for (int g = 0; g < G; ++g)
+#pragma unroll
+                        for (int i = 0; i < CPL; ++i) o[g][i] = fmaf(p[g][j], vf[i], o[g][i]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty + s);
+        }
+        if (lane == 0 && it < nst) atomicMin(&s_consumed, it);
+
+        // combine the 4 row groups of this warp (lanes with equal `sub` hold
+        // the same columns)
+#pragma unroll
+        for (int off = 8; off <= 16; off <<= 1) {
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float m2 = __shfl_xor_sync(0xffffffffu, m[g], off);
+                const float l2 = __shfl_xor_sync(0xffffffffu, l[g], off);
+                float wa, wb, M;
+                combine_weights(m[g], m2, wa, wb, M);
+                l[g] = l[g] * wa + l2 * wb;
+#pragma unroll
+                for (int i = 0; i < CPL; ++i) {
+                    const float o2 = __shfl_xor_sync(0xffffffffu, o[g][i], off);
+                    o[g][i] = o[g][i] * wa + o2 * wb;
+                }
+                m[g] = M;
+            }
+        }
+    }
+    __syncthreads();
+
+    // On an aborted pipeline, let copies still in flight land (bounded) before
+    // the stage buffers are reused or the CTA exits.
+    if (tid == 0 && s_consumed < s_issued) {
+        for (int it = s_consumed; it < s_issued; ++it)
+            mbar_wait(full + it % STAGES, (it / STAGES) & 1, nullptr);
+    }
+    __syncthreads();
+
+    // cross-warp reduction through the (now idle) stage buffers
+    float* red_o = reinterpret_cast<float*>(smem);   // [NW][G][D]
+    if (warp < NW && grp == 0) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+#pragma unroll
+            for (int c = 0; c < CH; ++c)
+#pragma unroll
+                for (int e = 0; e < VEC; ++e)
+                    red_o[(warp * G + g) * D + (sub + 8 * c) * VEC + e] = o[g][c * VEC + e];
+            if (sub == 0) {
+                red_m[warp][g] = m[g];
+                red_l[warp][g] = l[g];
+            }
+        }
+    }
+    __syncthreads();
+
+    for (int idx = tid; idx < G * D; idx += THREADS) {
+        const int g = idx / D, col = idx % D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, red_m[w][g]);
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            const float wt = (red_m[w][g] == -INFINITY) ? 0.f : ex2(red_m[w][g] - M);
+            L += red_l[w][g] * wt;
+            O += red_o[(w * G + g) * D + col] * wt;
+        }
+        const int h = kvh * G + g;
+        const size_t pi = (size_t)h * a.n_splits + split;
+        a.part_o[pi * D + col] = L > 0.f ? O / L : 0.f;
+        if (col == 0) {
+            a.part_m[pi] = M;
+            a.part_l[pi] = L;
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = (atomicAdd(&a.counters[kvh], 1u) == (unsigned)(a.n_splits - 1));
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+
+    // ---------------- last CTA of this KV head: merge the split partials
+    float* wts = reinterpret_cast<float*>(smem);                 // [G][n_splits]
+    float* hdr = wts + G * a.n_splits;                           // [G]: M, L
+    const int ns = a.n_splits;
+    for (int g = warp; g < G; g += THREADS / 32) {
+        const int h = kvh * G + g;
+        float M = -INFINITY;
+        for (int i = lane; i < ns; i += 32) M = fmaxf(M, __ldcg(a.part_m + (size_t)h * ns + i));
+#pragma unroll
+        for (int off = 16; off; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+        float L = 0.f;
+        for (int i = lane; i < ns; i += 32) {
+            const float mi = __ldcg(a.part_m + (size_t)h * ns + i);
+            const float wi = (mi == -INFINITY) ? 0.f : __ldcg(a.part_l + (size_t)h * ns + i) * ex2(mi - M);
+            wts[g * ns + i] = wi;
+            L += wi;
+        }
+#pragma unroll
+        for (int off = 16; off; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+        if (lane == 0) {
+            hdr[2 * g] = M;
+            hdr[2 * g + 1] = L;
+        }
+    }
+    __syncthreads();
+    for (int idx = tid; idx < G * D; idx += THREADS) {
+        const int g = idx / D, col = idx % D;
+        const int h = kvh * G + g;
+        const float L = hdr[2 * g + 1];
+        float O = 0.f;
+        for (int i = 0; i < ns; ++i) O += wts[g * ns + i] * __ldcg(a.part_o + ((size_t)h * ns + i) * D + col);
+        a.out[(size_t)h * D + col] = L > 0.f ? O / L : 0.f;
+        if (col == 0 && a.out_m) {
+            a.out_m[h] = L > 0.f ? hdr[2 * g] * LN2 : -INFINITY;
+            a.out_l[h] = L > 0.f ? L : 1.f;
+        }
+    }
+    if (tid == 0) a.counters[kvh] = 0u;
+}
+
+// Merge n partial states given in the natural-log domain (API layout
+// part-major: m, l [n][hq]; o [n][hq][d]).
+__global__ void merge_kernel(int n, int hq, int d, const float* __restrict__ m,
+                             const float* __restrict__ l, const float* __restrict__ o,
+                             float* __restrict__ out, float* __restrict__ out_m,
+                             float* __restrict__ out_l) {
+    const int h = blockIdx.x;
+    float M = -INFINITY;
+    for (int i = 0; i < n; ++i) M = fmaxf(M, m[(size_t)i * hq + h]);
+    float L = 0.f;
+    for (int i = 0; i < n; ++i) {
+        const float mi = m[(size_t)i * hq + h];
+        L += (mi == -INFINITY) ? 0.f : l[(size_t)i * hq + h] * ex2((mi - M) * LOG2E);
+    }
+    for (int c = threadIdx.x; c < d; c += blockDim.x) {
+        float O = 0.f;
+        for (int i = 0; i < n; ++i) {
+            const float mi = m[(size_t)i * hq + h];
+            const float wi = (mi == -INFINITY) ? 0.f : l[(size_t)i * hq + h] * ex2((mi - M) * LOG2E);
+            O += wi * o[((size_t)i * hq + h) * d + c];
+        }
+        out[(size_t)h * d + c] = L > 0.f ? O / L : 0.f;
+    }
+    if (threadIdx.x == 0 && out_m) {
+        out_m[h] = L > 0.f ? M : -INFINITY;
+        out_l[h] = L > 0.f ? L : 1.f;
+    }
+}
+
+using KernelFn = void (*)(const Args);
+
+template <typename KT, int D>
+static KernelFn pick_g(int G) {
+    switch (G) {
+        case 1: return decode_kernel<KT, D, 1>;
+        case 2: return decode_kernel<KT, D, 2>;
+        case 4: if constexpr (D <= 128) return decode_kernel<KT, D, 4>; else return nullptr;
+        case 8: if constexpr (D <= 64) return decode_kernel<KT, D, 8>; else return nullptr;
+        default: return nullptr;
+    }
+}
+
+template <typename KT>
+static KernelFn pick(int d, int G) {
+    switch (d) {
+        case 64: return pick_g<KT, 64>(G);
+        case 128: return pick_g<KT, 128>(G);
+        case 256: return pick_g<KT, 256>(G);
+        default: return nullptr;
+    }
+}
+
+static int stage_rows(int dtype, int d) { return STAGE_BYTES / (2 * d * (dtype == SA_F32 ? 4 : 2)); }
+
+}  // namespace dec
+
+// Plan the split of T rows over CTAs: about 2 CTAs per SM overall.
+static void plan_splits(int num_sms, int T, int hkv, int stage_rows, int* n_splits, int* rows_per_split) {
+    if (T <= 0) {
+        *n_splits = 1;
+        *rows_per_split = stage_rows;
+        return;
+    }
+    const int slots = 2 * num_sms;
+    int ns = slots / hkv;
+    const int max_by_rows = (T + stage_rows - 1) / stage_rows;
+    if (ns > max_by_rows) ns = max_by_rows;
+    if (ns > dec::MAX_SPLITS) ns = dec::MAX_SPLITS;
+    if (ns < 1) ns = 1;
+    int rps = (T + ns - 1) / ns;
+    rps = (rps + stage_rows - 1) / stage_rows * stage_rows;
+    *rows_per_split = rps;
+    *n_splits = (T + rps - 1) / rps;
+}
+
+// Validate a decode call's arguments (shared by the host- and device-pointer
+// paths and by the entry point that takes caller-provided scratch).
+static int check_decode_args(const char* fn, int dtype, const void* q, const void* k, const void* v,
+                             long long stride, int T, int d, int hq, int hkv, int block) {
+    SA_CHECK_ARG(dtype == SA_F32 || dtype == SA_BF16, "%s: dtype %d (want SA_F32 or SA_BF16)", fn, dtype);
+    SA_CHECK_ARG(q && (T == 0 || (k && v)), "%s: null q/k/v", fn);
+    SA_CHECK_ARG(T >= 0, "%s: T = %d", fn, T);
+    SA_CHECK_ARG(block > 0, "%s: block = %d", fn, block);
+    SA_CHECK_ARG(hkv > 0 && hq > 0 && hq % hkv == 0, "%s: hq = %d, hkv = %d", fn, hq, hkv);
+    SA_CHECK_ARG(hkv <= SA_MAX_KV_HEADS, "%s: hkv = %d > %d", fn, hkv, SA_MAX_KV_HEADS);
+    SA_CHECK_ARG(d == 64 || d == 128 || d == 256, "%s: d = %d (supported: 64, 128, 256)", fn, d);
+    const int elt = dtype == SA_F32 ? 4 : 2;
+    SA_CHECK_ARG(stride >= (long long)T * d || hkv == 1, "%s: kv_head_stride %lld < T*d", fn, stride);
+    SA_CHECK_ARG(((stride * elt) % 16) == 0, "%s: kv_head_stride*%d bytes not 16-byte aligned", fn, elt);
+    SA_CHECK_ARG(dec::pick<float>(d, hq / hkv) != nullptr,
+                 "%s: hq/hkv = %d unsupported at d = %d", fn, hq / hkv, d);
+    return SA_OK;
+}
+
+// Launch the decode kernel on device pointers.  `part` must hold
+// hq*n_splits*(d+2) floats for the plan the call computes.
+static int launch_decode(sa_ctx* ctx, int dtype, const void* q, const void* k, const void* v,
+                         long long stride, int T, int d, int hq, int hkv, float scale, float* out,
+                         float* out_m, float* out_l) {
+    SA_CHECK_ARG((((uintptr_t)k | (uintptr_t)v) & 15) == 0, "decode: k/v not 16-byte aligned");
+    SA_CHECK_ARG((((uintptr_t)q) & 15) == 0, "decode: q not 16-byte aligned");
+    int ns, rps;
+    const int sr = dec::stage_rows(dtype, d);
+    plan_splits(ctx->num_sms, T, hkv, sr, &ns, &rps);
+    const size_t npart = (size_t)hq * ns;
+    int rc = ensure_ws(ctx, npart * (d + 2) * sizeof(float));
+    if (rc) return rc;
+    dec::Args a;
+    a.q = q; a.k = k; a.v = v;
+    a.kv_head_stride = hkv == 1 ? 0 : stride;
+    a.T = T; a.hq = hq; a.hkv = hkv;
+    a.rows_per_split = rps; a.n_splits = ns;
+    a.qscale = scale * dec::LOG2E;
+    float* ws = static_cast<float*>(ctx->ws);
+    a.part_m = ws;
+    a.part_l = ws + npart;
+    a.part_o = ws + 2 * npart;
+    a.counters = ctx->counters;
+    a.out = out; a.out_m = out_m; a.out_l = out_l;
+    a.status = ctx->status;
+    dec::KernelFn fn = dtype == SA_F32 ? dec::pick<float>(d, hq / hkv) : dec::pick<__nv_bfloat16>(d, hq / hkv);
+    SA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::SMEM_BYTES));
+    fn<<<dim3(ns, hkv), dec::THREADS, dec::SMEM_BYTES, ctx->stream>>>(a);
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
+
+static int decode_common(const char* fn_name, sa_ctx* ctx, int dtype, const void* q, const void* k,
+                         const void* v, long long stride, int T, int d, int hq, int hkv, int block,
+                         float scale, float* out, float* m_out, float* l_out, unsigned flags) {
+    clear_error();
+    SA_CHECK_ARG(ctx != nullptr, "%s: ctx is NULL", fn_name);
+    SA_CHECK_ARG(out != nullptr, "%s: out is NULL", fn_name);
+    int rc = check_decode_args(fn_name, dtype, q, k, v, stride, T, d, hq, hkv, block);
+    if (rc) return rc;
+    DeviceGuard guard(ctx->device);
+    if (!(flags & SA_HOST_PTRS))
+        return launch_decode(ctx, dtype, q, k, v, stride, T, d, hq, hkv, scale, out, m_out, l_out);
+
+    // Host buffers: stage through device memory on the context's stream.
+    const int elt = dtype == SA_F32 ? 4 : 2;
+    const size_t qb = align_up((size_t)hq * d * elt, 256);
+    const size_t kvb = align_up((size_t)hkv * T * d * elt, 256);
+    const size_t ob = align_up((size_t)hq * d * 4, 256);
+    const size_t sb = align_up((size_t)hq * 4, 256);
+    rc = ensure_stage(ctx, qb + 2 * kvb + ob + 2 * sb);
+    if (rc) return rc;
+    char* base = static_cast<char*>(ctx->stage);
+    void* dq = base;
+    void* dk = base + qb;
+    void* dv = base + qb + kvb;
+    float* dout = reinterpret_cast<float*>(base + qb + 2 * kvb);
+    float* dm = reinterpret_cast<float*>(base + qb + 2 * kvb + ob);
+    float* dl = reinterpret_cast<float*>(base + qb + 2 * kvb + ob + sb);
+    cudaStream_t st = ctx->stream;
+    const size_t row = (size_t)T * d * elt;
+    SA_CUDA_TRY(cudaMemcpyAsync(dq, q, (size_t)hq * d * elt, cudaMemcpyHostToDevice, st));
+    if (T > 0) {
+        const size_t pitch = hkv == 1 ? row : (size_t)stride * elt;
+        SA_CUDA_TRY(cudaMemcpy2DAsync(dk, row, k, pitch, row, hkv, cudaMemcpyHostToDevice, st));
+        SA_CUDA_TRY(cudaMemcpy2DAsync(dv, row, v, pitch, row, hkv, cudaMemcpyHostToDevice, st));
+    }
+    rc = launch_decode(ctx, dtype, dq, dk, dv, (long long)T * d, T, d, hq, hkv, scale, dout,
+                       m_out ? dm : nullptr, m_out ? dl : nullptr);
+    if (rc) return rc;
+    SA_CUDA_TRY(cudaMemcpyAsync(out, dout, (size_t)hq * d * 4, cudaMemcpyDeviceToHost, st));
+    if (m_out) {
+        SA_CUDA_TRY(cudaMemcpyAsync(m_out, dm, (size_t)hq * 4, cudaMemcpyDeviceToHost, st));
+        SA_CUDA_TRY(cudaMemcpyAsync(l_out, dl, (size_t)hq * 4, cudaMemcpyDeviceToHost, st));
+    }
+    return sync_and_check(ctx);
+}
+
+}  // namespace sa
+
+SA_API int sa_attn_decode(sa_ctx* ctx, int dtype, const void* q, const void* k, const void* v,
+                          long long kv_head_stride, int T, int d, int hq, int hkv, int block,
+                          float scale, float* out, unsigned flags) {
+    return sa::decode_common("sa_attn_decode", ctx, dtype, q, k, v, kv_head_stride, T, d, hq, hkv,
+                             block, scale, out, nullptr, nullptr, flags);
+}
+
+SA_API int sa_attn_decode_partial(sa_ctx* ctx, int dtype, const void* q, const void* k,
+                                  const void* v, long long kv_head_stride, int T, int d, int hq,
+                                  int hkv, int block, float scale, float* m_out, float* l_out,
+                                  float* o_out, unsigned flags) {
+    SA_CHECK_ARG(m_out && l_out, "sa_attn_decode_partial: null m_out/l_out");
+    return sa::decode_common("sa_attn_decode_partial", ctx, dtype, q, k, v, kv_head_stride, T, d, hq,
+                             hkv, block, scale, o_out, m_out, l_out, flags);
+}
+
+SA_API int sa_attn_merge(sa_ctx* ctx, int n_parts, int hq, int d, const float* m, const float* l,
+                         const float* o, float* out, float* m_out, float* l_out, unsigned flags) {
+    sa::clear_error();
+    SA_CHECK_ARG(ctx != nullptr, "sa_attn_merge: ctx is NULL");
+    SA_CHECK_ARG(n_parts >= 1 && hq >= 1 && d >= 1, "sa_attn_merge: n_parts=%d hq=%d d=%d", n_parts, hq, d);
+    SA_CHECK_ARG(m && l && o && out, "sa_attn_merge: null pointer");
+    SA_CHECK_ARG((m_out == nullptr) == (l_out == nullptr), "sa_attn_merge: m_out/l_out must both be set or NULL");
+    sa::DeviceGuard guard(ctx->device);
+    cudaStream_t st = ctx->stream;
+    if (!(flags & SA_HOST_PTRS)) {
+        sa::dec::merge_kernel<<<hq, 128, 0, st>>>(n_parts, hq, d, m, l, o, out, m_out, l_out);
+        SA_CUDA_TRY(cudaGetLastError());
+        return SA_OK;
+    }
+    const size_t ml = sa::align_up((size_t)n_parts * hq * 4, 256);
+    const size_t ob = sa::align_up((size_t)n_parts * hq * d * 4, 256);
+    const size_t outb = sa::align_up((size_t)hq * d * 4, 256);
+    const size_t sb = sa::align_up((size_t)hq * 4, 256);
+    int rc = sa::ensure_stage(ctx, 2 * ml + ob + outb + 2 * sb);
+    if (rc) return rc;
+    char* b = static_cast<char*>(ctx->stage);
+    float* dm = (float*)b;
+    float* dl = (float*)(b + ml);
+    float* dO = (float*)(b + 2 * ml);
+    float* dout = (float*)(b + 2 * ml + ob);
+    float* dmo = (float*)(b + 2 * ml + ob + outb);
+    float* dlo = (float*)(b + 2 * ml + ob + outb + sb);
+    SA_CUDA_TRY(cudaMemcpyAsync(dm, m, (size_t)n_parts * hq * 4, cudaMemcpyHostToDevice, st));
+    SA_CUDA_TRY(cudaMemcpyAsync(dl, l, (size_t)n_parts * hq * 4, cudaMemcpyHostToDevice, st));
+    SA_CUDA_TRY(cudaMemcpyAsync(dO, o, (size_t)n_parts * hq * d * 4, cudaMemcpyHostToDevice, st));
+    sa::dec::merge_kernel<<<hq, 128, 0, st>>>(n_parts, hq, d, dm, dl, dO, dout, m_out ? dmo : nullptr,
+                                              m_out ? dlo : nullptr);
+    SA_CUDA_TRY(cudaGetLastError());
+    SA_CUDA_TRY(cudaMemcpyAsync(out, dout, (size_t)hq * d * 4, cudaMemcpyDeviceToHost, st));
+    if (m_out) {
+        SA_CUDA_TRY(cudaMemcpyAsync(m_out, dmo, (size_t)hq * 4, cudaMemcpyDeviceToHost, st));
+        SA_CUDA_TRY(cudaMemcpyAsync(l_out, dlo, (size_t)hq * 4, cudaMemcpyDeviceToHost, st));
+    }
+    return sa::sync_and_check(ctx);
+}

@@ -1,0 +1,77 @@
+// sa_internal.h -- context object and error plumbing shared by the C-ABI
+// translation units of libsa_cuda.so.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdarg>
+#include <cstddef>
+#include <cstdio>
+#include <string>
+
+#include "../../include/sa_cuda.h"
+
+#define SA_API extern "C" __attribute__((visibility("default")))
+
+// Largest number of KV heads a decode call may use (size of the per-head
+// completion counters the last-CTA merge uses).
+#define SA_MAX_KV_HEADS 1024
+
+struct sa_ctx {
+    int device = 0;
+    int num_sms = 0;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    // grow-only device scratch (split partials etc.)
+    void* ws = nullptr;
+    size_t ws_bytes = 0;
+    // per-KV-head arrival counters for the decode kernel's last-CTA merge;
+    // zero between launches (the last CTA resets its counter)
+    unsigned* counters = nullptr;
+    // device status word: 0 ok, else a SA_STATUS_* code set by a kernel
+    int* status = nullptr;
+    // grow-only device staging for SA_HOST_PTRS calls
+    void* stage = nullptr;
+    size_t stage_bytes = 0;
+};
+
+namespace sa {
+
+int set_error(int code, const char* fmt, ...);
+void clear_error();
+
+// Switch to the context's device for the duration of a call.
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+// Ensure ctx->ws holds at least `bytes` (grow-only; synchronises on growth).
+int ensure_ws(sa_ctx* ctx, size_t bytes);
+// Ensure ctx->stage holds at least `bytes`.
+int ensure_stage(sa_ctx* ctx, size_t bytes);
+// Synchronise the stream and translate CUDA / device-status errors.
+int sync_and_check(sa_ctx* ctx);
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+}  // namespace sa
+
+#define SA_CUDA_TRY(expr)                                                          \
+    do {                                                                           \
+        cudaError_t e_ = (expr);                                                   \
+        if (e_ != cudaSuccess)                                                     \
+            return sa::set_error(SA_ERR_CUDA, "%s failed: %s (%s:%d)", #expr,      \
+                                 cudaGetErrorString(e_), __FILE__, __LINE__);      \
+    } while (0)
+
+#define SA_CHECK_ARG(cond, ...)                                                    \
+    do {                                                                           \
+        if (!(cond)) return sa::set_error(SA_ERR_ARG, __VA_ARGS__);                \
+    } while (0)
