@@ -61,8 +61,10 @@ const char* sa_version(void);
 int sa_ctx_create(int device, sa_ctx** out);
 /* Destroy a context (synchronises its stream first). */
 int sa_ctx_destroy(sa_ctx* ctx);
-/* Use a caller-owned stream (a cudaStream_t) instead of the context's own;
- * NULL restores the context's own stream. */
+/* Issue device-pointer calls on a caller-owned stream (a cudaStream_t)
+ * instead of the context's own.  NULL selects CUDA's legacy default stream
+ * (stream 0); to go back to the context's own stream pass the handle that
+ * sa_ctx_stream returned before the first sa_ctx_set_stream call. */
 int sa_ctx_set_stream(sa_ctx* ctx, void* stream);
 /* The stream device-pointer calls are issued on (a cudaStream_t). */
 void* sa_ctx_stream(sa_ctx* ctx);

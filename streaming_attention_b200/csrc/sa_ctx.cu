@@ -123,7 +123,10 @@ SA_API int sa_ctx_destroy(sa_ctx* ctx) {
 SA_API int sa_ctx_set_stream(sa_ctx* ctx, void* stream) {
     sa::clear_error();
     SA_CHECK_ARG(ctx != nullptr, "sa_ctx_set_stream: ctx is NULL");
-    ctx->stream = stream ? static_cast<cudaStream_t>(stream) : ctx->own_stream;
+    // NULL is CUDA's legacy default stream (the one torch's default stream
+    // handle 0 denotes), never the context's own non-blocking stream: work
+    // issued by the caller on stream 0 must stay ordered with this library's.
+    ctx->stream = stream ? static_cast<cudaStream_t>(stream) : cudaStreamLegacy;
     return SA_OK;
 }
 
