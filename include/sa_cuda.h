@@ -134,6 +134,39 @@ int sa_attn_decode_partial(sa_ctx* ctx, int dtype, const void* q, const void* k,
 int sa_attn_merge(sa_ctx* ctx, int n_parts, int hq, int d, const float* m, const float* l,
                   const float* o, float* out, float* m_out, float* l_out, unsigned flags);
 
+/*
+ * Allocation-free variant of sa_attn_decode.  It has no counterpart in the
+ * reference; it exists for callers that cannot call cudaMalloc -- serving
+ * runtimes that reserve nearly all device memory for their own pools at
+ * start-up, and latency-critical loops that cannot afford cudaMalloc's
+ * implicit device synchronisation.  Such callers cannot create an sa_ctx
+ * either (its constructor allocates), so this call takes a plain stream.
+ *
+ * Same arguments and result as sa_attn_decode with device pointers (q, k, v
+ * and out are the caller's device memory; `stream` is a cudaStream_t, NULL =
+ * the legacy default stream; the GPU is the one holding `out`).  The call
+ * never calls cudaMalloc, cudaFree or any allocating routine: its scratch
+ * (per-split partial states and per-KV-head counters) lives in a file-scope
+ * device array of SA_NOALLOC_SCRATCH_BYTES that every GPU which loads the
+ * library holds until the process exits.
+ *  - Shapes whose scratch (about hq * splits * (d + 2) * 4 bytes, splits
+ *    ~ 2 * SMs / hkv) exceeds SA_NOALLOC_SCRATCH_BYTES are rejected with
+ *    SA_ERR_ARG and a message naming the sizes.
+ *  - The first call on a GPU looks up the array's device address
+ *    (cudaGetSymbolAddress) with that GPU current and caches it; make that
+ *    first call before any stream capture.
+ *  - All calls on a GPU share the array, which keeps the last call's
+ *    contents; each call clears the counters it needs.  Calls whose
+ *    executions overlap on the GPU (different streams, or host threads
+ *    without ordering) race on the array and give wrong results.
+ *  - Asynchronous: errors of the kernel itself (a device-side wait that
+ *    expired) are not reported back; argument errors are.
+ */
+#define SA_NOALLOC_SCRATCH_BYTES (2u << 20)
+int sa_attn_decode_noalloc(void* stream, int dtype, const void* q, const void* k, const void* v,
+                           long long kv_head_stride, int T, int d, int hq, int hkv, int block,
+                           float scale, float* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -589,3 +589,109 @@ SA_API int sa_attn_merge(sa_ctx* ctx, int n_parts, int hq, int d, const float* m
     }
     return sa::sync_and_check(ctx);
 }
+
+// ===========================================================================
+// Allocation-free decode entry point.
+//
+// Some callers cannot call cudaMalloc: serving runtimes that reserve nearly
+// all device memory for their own pools at start-up (a later cudaMalloc can
+// fail or fragment their budget), and latency-critical loops that must not
+// pay for cudaMalloc's implicit device synchronisation.  They also cannot
+// create an sa_ctx, whose constructor allocates.  For them this entry point
+// keeps the decode kernel's scratch -- the per-split (m, l, O) partials, the
+// per-KV-head arrival counters and the status word -- in one file-scope
+// device array of fixed size instead.  Every GPU that loads the library holds
+// the array until the process exits; every call on a GPU shares it.
+// ===========================================================================
+#include <mutex>
+
+#define SA_NOALLOC_MAX_DEVICES 64
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[SA_NOALLOC_SCRATCH_BYTES];
+
+namespace sa {
+
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_addr[SA_NOALLOC_MAX_DEVICES] = {};
+
+// Device address of g_noalloc_scratch on `device` (which must be current).
+// In host code the array's name is only a host-side stand-in, so the address
+// is looked up once per device and cached.
+static int noalloc_scratch(int device, void** out) {
+    SA_CHECK_ARG(device >= 0 && device < SA_NOALLOC_MAX_DEVICES, "noalloc: device %d", device);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[device]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr)
+            return set_error(SA_ERR_CUDA, "cudaGetSymbolAddress(static scratch) on device %d: %s",
+                             device, cudaGetErrorString(e));
+        g_noalloc_addr[device] = p;
+    }
+    *out = g_noalloc_addr[device];
+    return SA_OK;
+}
+
+}  // namespace sa
+
+SA_API int sa_attn_decode_noalloc(void* stream, int dtype, const void* q, const void* k,
+                                  const void* v, long long kv_head_stride, int T, int d, int hq,
+                                  int hkv, int block, float scale, float* out) {
+    using namespace sa;
+    clear_error();
+    SA_CHECK_ARG(out != nullptr, "sa_attn_decode_noalloc: out is NULL");
+    int rc = check_decode_args("sa_attn_decode_noalloc", dtype, q, k, v, kv_head_stride, T, d, hq,
+                               hkv, block);
+    if (rc) return rc;
+    SA_CHECK_ARG((((uintptr_t)k | (uintptr_t)v | (uintptr_t)q) & 15) == 0,
+                 "sa_attn_decode_noalloc: q/k/v not 16-byte aligned");
+    // the GPU is the one that holds `out`
+    cudaPointerAttributes attr;
+    SA_CUDA_TRY(cudaPointerGetAttributes(&attr, out));
+    SA_CHECK_ARG(attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged,
+                 "sa_attn_decode_noalloc: out must be device memory");
+    DeviceGuard guard(attr.device);
+    int num_sms = 0;
+    SA_CUDA_TRY(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, attr.device));
+
+    int ns, rps;
+    plan_splits(num_sms, T, hkv, dec::stage_rows(dtype, d), &ns, &rps);
+    const size_t cnt_bytes = align_up((size_t)hkv * sizeof(unsigned), 256);
+    const size_t st_bytes = 256;
+    const size_t npart = (size_t)hq * ns;
+    const size_t need = cnt_bytes + st_bytes + npart * (d + 2) * sizeof(float);
+    if (need > SA_NOALLOC_SCRATCH_BYTES)
+        return set_error(SA_ERR_ARG,
+                         "sa_attn_decode_noalloc: hq=%d hkv=%d d=%d needs %zu scratch bytes, more than "
+                         "the static maximum of %u (SA_NOALLOC_SCRATCH_BYTES); use sa_attn_decode",
+                         hq, hkv, d, need, (unsigned)SA_NOALLOC_SCRATCH_BYTES);
+    void* base = nullptr;
+    rc = noalloc_scratch(attr.device, &base);
+    if (rc) return rc;
+    char* b = static_cast<char*>(base);
+    unsigned* counters = reinterpret_cast<unsigned*>(b);
+    int* status = reinterpret_cast<int*>(b + cnt_bytes);
+    float* part = reinterpret_cast<float*>(b + cnt_bytes + st_bytes);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // The kernel's last CTA leaves the counters at zero, but a call that ended
+    // early could not; start every call from zero.
+    SA_CUDA_TRY(cudaMemsetAsync(counters, 0, (size_t)hkv * sizeof(unsigned), st));
+
+    dec::Args a;
+    a.q = q; a.k = k; a.v = v;
+    a.kv_head_stride = hkv == 1 ? 0 : kv_head_stride;
+    a.T = T; a.hq = hq; a.hkv = hkv;
+    a.rows_per_split = rps; a.n_splits = ns;
+    a.qscale = scale * dec::LOG2E;
+    a.part_m = part;
+    a.part_l = part + npart;
+    a.part_o = part + 2 * npart;
+    a.counters = counters;
+    a.out = out; a.out_m = nullptr; a.out_l = nullptr;
+    a.status = status;
+    dec::KernelFn fn = dtype == SA_F32 ? dec::pick<float>(d, hq / hkv) : dec::pick<__nv_bfloat16>(d, hq / hkv);
+    SA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::SMEM_BYTES));
+    fn<<<dim3(ns, hkv), dec::THREADS, dec::SMEM_BYTES, st>>>(a);
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
