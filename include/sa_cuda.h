@@ -134,6 +134,50 @@ int sa_attn_decode_partial(sa_ctx* ctx, int dtype, const void* q, const void* k,
 int sa_attn_merge(sa_ctx* ctx, int n_parts, int hq, int d, const float* m, const float* l,
                   const float* o, float* out, float* m_out, float* l_out, unsigned flags);
 
+/* ======================================================================== */
+/* Causal prefill attention (tensor cores)                                   */
+/* ======================================================================== */
+
+/*
+ * Causal multi-head GQA attention for Sq query tokens against Skv keys.
+ *   q   [Sq,  hq  heads, d]  bf16, token stride q_tok_stride (elements)
+ *   k,v [Skv, hkv heads, d]  bf16, token stride kv_tok_stride
+ *   out [Sq,  hq  heads, d]  fp32 (SA_F32) or bf16 (SA_BF16), token stride
+ *                            o_tok_stride
+ * Query i (global position q_pos0 + i) sees keys 0 .. q_pos0 + i; the usual
+ * prefill is q_pos0 = 0, Skv = Sq; a chunk of a longer prompt (sequence
+ * parallelism, chunked prefill) passes its offset and the keys before it.
+ * out = softmax(scale * q k^T + causal mask) v, computed with bf16 operands
+ * and fp32 accumulation on tcgen05 tensor cores.
+ * Replaces ops::self_attention with create_causal_mask
+ * (tensor_cpp/src/ops.cpp:514-641, qwen3_ops.cpp:240-259) and
+ * self_attention_streaming_blockwise (ops.cpp:1027-1112,1383-1450) after
+ * repeat_kv (qwen3_ops.cpp:194-234).  Requirements: d = 128; hq/hkv = 1 or
+ * even; q_pos0 + Sq <= Skv; device pointers (16-byte aligned, token strides
+ * multiples of 8 elements).
+ */
+int sa_attn_prefill(sa_ctx* ctx, const void* q, const void* k, const void* v, int Sq, int Skv,
+                    int q_pos0, int d, int hq, int hkv, long long q_tok_stride,
+                    long long kv_tok_stride, float scale, void* out, int out_dtype,
+                    long long o_tok_stride, unsigned flags);
+
+/*
+ * One decode step over a device-resident KV cache (batch 1):
+ *   k_cache, v_cache [hkv, max_seq, d]  device memory, element type `dtype`
+ *   k_new, v_new     [hkv, d]           the new token's key / value
+ *   q [hq, d] -> out [hq, d] fp32
+ * Writes k_new / v_new at row `pos` of every head, then attends over rows
+ * [0, pos] (pos + 1 rows).  Replaces, per layer, kv_cache->update() +
+ * attention over the cache in qwen3_decoder_layer_with_cache
+ * (tensor_cpp/src/qwen3_ops.cpp:849,876-885; kv_cache.h:94-130).
+ * SA_ERR_FULL when pos >= max_seq (kv_cache.h:109-111).  With SA_HOST_PTRS,
+ * q, k_new, v_new and out are host memory (the cache stays on the device).
+ */
+int sa_attn_decode_step(sa_ctx* ctx, int dtype, const void* q, const void* k_new,
+                        const void* v_new, void* k_cache, void* v_cache, int max_seq, int pos,
+                        int d, int hq, int hkv, int block, float scale, float* out,
+                        unsigned flags);
+
 /*
  * Allocation-free variant of sa_attn_decode.  It has no counterpart in the
  * reference; it exists for callers that cannot call cudaMalloc -- serving

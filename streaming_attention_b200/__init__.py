@@ -19,7 +19,9 @@ from ._capi import (  # noqa: F401
 from .attention import (  # noqa: F401
     attn_decode,
     attn_decode_partial,
+    attn_decode_step,
     attn_merge,
+    attn_prefill,
     naive_attention_cuda,
     streaming_attention_cuda,
     streaming_attention_mpi_cuda,
@@ -27,6 +29,6 @@ from .attention import (  # noqa: F401
 
 __all__ = [
     "Context", "SAError", "lib", "LIB_PATH", "SA_F32", "SA_BF16", "SA_HOST_PTRS",
-    "attn_decode", "attn_decode_partial", "attn_merge", "streaming_attention_cuda",
+    "attn_decode", "attn_decode_partial", "attn_decode_step", "attn_merge", "attn_prefill", "streaming_attention_cuda",
     "naive_attention_cuda", "streaming_attention_mpi_cuda",
 ]

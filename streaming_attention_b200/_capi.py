@@ -41,6 +41,11 @@ SIGNATURES = {
                                          _vp, C.c_uint]),
     "sa_attn_merge": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp, _vp, _vp, _vp,
                                 C.c_uint]),
+    "sa_attn_decode_step": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int,
+                                      C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, _vp, C.c_uint]),
+    "sa_attn_prefill": (C.c_int, [_vp, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                  C.c_int, C.c_longlong, C.c_longlong, C.c_float, _vp, C.c_int,
+                                  C.c_longlong, C.c_uint]),
     "sa_attn_decode_noalloc": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, C.c_longlong, C.c_int,
                                          C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, _vp]),
 }

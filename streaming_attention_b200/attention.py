@@ -123,6 +123,54 @@ def attn_merge(m, l, o, ctx: Context | None = None, with_state: bool = False):
     return (out, mo, lo) if with_state else out
 
 
+def attn_decode_step(q, k_new, v_new, k_cache, v_cache, pos: int, scale: float = 1.0,
+                     block: int = 64, ctx: Context | None = None, out=None):
+    """One decode step over a device KV cache (sa_attn_decode_step).
+
+    k_cache, v_cache: CUDA torch tensors [hkv, max_seq, d]; the new token's
+    k_new, v_new [hkv, d] are written at row ``pos`` and q [hq, d] attends over
+    rows [0, pos].  q / k_new / v_new may be numpy (host; the call then copies
+    them in, and returns the output on the host) or CUDA tensors.
+    """
+    hkv, max_seq, d = k_cache.shape
+    hq = q.shape[0]
+    host = not _is_torch(q)
+    q, k_new, v_new = _prep(q), _prep(k_new), _prep(v_new)
+    ctx = _ctx_for(k_cache, ctx)
+    if out is None:
+        out = np.empty((hq, d), np.float32) if host else _out_like(q, (hq, d))
+    _bind_stream(ctx, k_cache)
+    dt = _dtype_code(k_cache)
+    check(lib().sa_attn_decode_step(ctx.h, dt, _ptr(q), _ptr(k_new), _ptr(v_new), _ptr(k_cache),
+                                    _ptr(v_cache), max_seq, pos, d, hq, hkv, block, scale, _ptr(out),
+                                    SA_HOST_PTRS if host else 0))
+    return out
+
+
+def attn_prefill(q, k, v, scale: float, q_pos0: int = 0, out_dtype: str = "float32",
+                 ctx: Context | None = None, out=None):
+    """Causal GQA prefill attention on tensor cores (sa_attn_prefill).
+
+    q [Sq, hq, 128], k, v [Skv, hkv, 128]: bf16 CUDA tensors (token-major; any
+    token stride).  Query i sits at position q_pos0 + i and sees keys
+    0 .. q_pos0 + i.  Returns out [Sq, hq, 128] in ``out_dtype``.
+    """
+    import torch
+    Sq, hq, d = q.shape
+    Skv, hkv, _ = k.shape
+    for t in (q, k, v):
+        assert t.dtype == torch.bfloat16 and t.is_cuda and t.stride(2) == 1 and t.stride(1) == d
+    odt = torch.float32 if out_dtype == "float32" else torch.bfloat16
+    if out is None:
+        out = torch.empty(Sq, hq, d, dtype=odt, device=q.device)
+    ctx = _ctx_for(q, ctx)
+    _bind_stream(ctx, q)
+    check(lib().sa_attn_prefill(ctx.h, _ptr(q), _ptr(k), _ptr(v), Sq, Skv, q_pos0, d, hq, hkv,
+                                q.stride(0), k.stride(0), scale, _ptr(out),
+                                SA_F32 if odt == torch.float32 else SA_BF16, out.stride(0), 0))
+    return out
+
+
 # ---- attention.h mirror ---------------------------------------------------
 
 def streaming_attention_cuda(Q, K, V, T: int, d: int, block_size: int, ctx: Context | None = None):

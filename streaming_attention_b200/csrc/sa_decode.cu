@@ -695,3 +695,53 @@ SA_API int sa_attn_decode_noalloc(void* stream, int dtype, const void* q, const 
     SA_CUDA_TRY(cudaGetLastError());
     return SA_OK;
 }
+
+// ===========================================================================
+// One decode step over a device-resident KV cache: append the new token's
+// K/V row at `pos`, then attend over rows [0, pos].  The reference does the
+// same per layer in qwen3_decoder_layer_with_cache: kv_cache->update(...)
+// (tensor_cpp/src/qwen3_ops.cpp:849, kv_cache.h:94-130) followed by attention
+// over the cached prefix (:876-885).  The cache is [hkv][max_seq][d], the
+// KVCache layout (kv_cache.h:24-25) with batch 1.
+// ===========================================================================
+SA_API int sa_attn_decode_step(sa_ctx* ctx, int dtype, const void* q, const void* k_new,
+                               const void* v_new, void* k_cache, void* v_cache, int max_seq,
+                               int pos, int d, int hq, int hkv, int block, float scale, float* out,
+                               unsigned flags) {
+    using namespace sa;
+    clear_error();
+    SA_CHECK_ARG(ctx != nullptr, "sa_attn_decode_step: ctx is NULL");
+    SA_CHECK_ARG(out && k_new && v_new && k_cache && v_cache, "sa_attn_decode_step: null pointer");
+    SA_CHECK_ARG(pos >= 0 && max_seq > 0, "sa_attn_decode_step: pos = %d, max_seq = %d", pos, max_seq);
+    if (pos >= max_seq)
+        return set_error(SA_ERR_FULL, "sa_attn_decode_step: KV cache full, cannot append at %d (max_seq %d)",
+                         pos, max_seq);
+    const long long stride = (long long)max_seq * d;
+    int rc = check_decode_args("sa_attn_decode_step", dtype, q, k_cache, v_cache, stride, pos + 1, d, hq,
+                               hkv, block);
+    if (rc) return rc;
+    DeviceGuard guard(ctx->device);
+    const int elt = dtype == SA_F32 ? 4 : 2;
+    const size_t row = (size_t)d * elt, pitch = (size_t)stride * elt;
+    cudaStream_t st = ctx->stream;
+    char* kc = static_cast<char*>(k_cache) + (size_t)pos * row;
+    char* vc = static_cast<char*>(v_cache) + (size_t)pos * row;
+    const bool host = flags & SA_HOST_PTRS;
+    const cudaMemcpyKind kind = host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+    SA_CUDA_TRY(cudaMemcpy2DAsync(kc, pitch, k_new, row, row, hkv, kind, st));
+    SA_CUDA_TRY(cudaMemcpy2DAsync(vc, pitch, v_new, row, row, hkv, kind, st));
+    if (!host)
+        return launch_decode(ctx, dtype, q, k_cache, v_cache, stride, pos + 1, d, hq, hkv, scale, out,
+                             nullptr, nullptr);
+    const size_t qb = align_up((size_t)hq * d * elt, 256);
+    rc = ensure_stage(ctx, qb + (size_t)hq * d * 4);
+    if (rc) return rc;
+    char* dq = static_cast<char*>(ctx->stage);
+    float* dout = reinterpret_cast<float*>(dq + qb);
+    SA_CUDA_TRY(cudaMemcpyAsync(dq, q, (size_t)hq * d * elt, cudaMemcpyHostToDevice, st));
+    rc = launch_decode(ctx, dtype, dq, k_cache, v_cache, stride, pos + 1, d, hq, hkv, scale, dout,
+                       nullptr, nullptr);
+    if (rc) return rc;
+    SA_CUDA_TRY(cudaMemcpyAsync(out, dout, (size_t)hq * d * 4, cudaMemcpyDeviceToHost, st));
+    return sync_and_check(ctx);
+}

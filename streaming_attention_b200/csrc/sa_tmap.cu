@@ -1,0 +1,47 @@
+// sa_tmap.cu -- host-side TMA tensor-map encoding.  cuTensorMapEncodeTiled is
+// a driver API; it is fetched through the runtime's driver entry point so the
+// library does not link libcuda directly.
+#include <cudaTypedefs.h>
+#include <mutex>
+
+#include "sa_internal.h"
+#include "sa_tc.cuh"
+
+namespace sa {
+
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+static std::once_flag g_encode_once;
+
+static int get_encode() {
+    std::call_once(g_encode_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess && q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    if (!g_encode) return set_error(SA_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    return SA_OK;
+}
+
+int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                      uint64_t row_stride_elems, uint32_t box_rows, uint32_t box_cols) {
+    int rc = get_encode();
+    if (rc) return rc;
+    SA_CHECK_ARG(((uintptr_t)base & 15) == 0, "tensor map base not 16-byte aligned");
+    SA_CHECK_ARG((row_stride_elems * 2) % 16 == 0, "tensor map row stride not a multiple of 16 bytes");
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {row_stride_elems * 2};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                          box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(SA_ERR_ARG, "cuTensorMapEncodeTiled failed (%d): rows=%llu cols=%llu stride=%llu box=%ux%u",
+                         (int)r, (unsigned long long)rows, (unsigned long long)cols,
+                         (unsigned long long)row_stride_elems, box_rows, box_cols);
+    return SA_OK;
+}
+
+}  // namespace sa

@@ -15,7 +15,7 @@ SINGLE_CASES = [(512, 64), (1000, 128), (4096, 256), (8192, 128), (1, 128), (63,
 GQA_CASES = [  # (hq, hkv, T, d)
     (16, 8, 2048, 128), (16, 8, 777, 128), (4, 4, 300, 64), (8, 2, 1500, 64), (4, 2, 513, 256)]
 PREFILL_CASES = [  # (S, hq, hkv, d)
-    (200, 4, 2, 64), (130, 2, 1, 128)]
+    (200, 4, 2, 128), (130, 2, 1, 128), (70, 2, 2, 128)]
 
 
 def rng(seed: int) -> np.random.Generator:

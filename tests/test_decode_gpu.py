@@ -202,3 +202,39 @@ def test_argument_errors(ctx):
                               C.c_void_p(out.data_ptr()), 0)
     assert rc == -1 and b"aligned" in lib().sa_last_error()
     ctx.synchronize()
+
+
+def test_decode_step_appends_and_attends(ctx, oracle):
+    """KV-cache decode step: the new row lands at `pos` and attention covers
+    rows [0, pos] (kv_cache.h:94-130 + qwen3_ops.cpp:876-885)."""
+    import torch
+    from streaming_attention_b200 import attn_decode_step
+    hq, hkv, d, max_seq, pos = 16, 8, 128, 5000, 4000
+    q, k, v = I.gqa(hq, hkv, max_seq, d, 77)
+    kc, vc = _t(k), _t(v)
+    kn, vn = k[:, pos].copy() + 1.0, v[:, pos].copy() - 1.0
+    s = 1 / np.sqrt(d)
+    out = attn_decode_step(q, kn, vn, kc, vc, pos, s, 64, ctx)       # host q/k/v/out
+    k2, v2 = k.copy(), v.copy()
+    k2[:, pos], v2[:, pos] = kn, vn
+    ref = oracle.gqa_decode(q, np.ascontiguousarray(k2[:, :pos + 1]), np.ascontiguousarray(v2[:, :pos + 1]), 64, s)
+    np.testing.assert_allclose(out, ref, atol=TOL, rtol=0)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(kc[:, pos].cpu().numpy(), kn)
+    # device-pointer variant on the next position
+    out2 = attn_decode_step(_t(q), _t(kn), _t(vn), kc, vc, pos + 1, s, 64, ctx)
+    torch.cuda.synchronize()
+    k2[:, pos + 1], v2[:, pos + 1] = kn, vn
+    ref2 = oracle.gqa_decode(q, np.ascontiguousarray(k2[:, :pos + 2]), np.ascontiguousarray(v2[:, :pos + 2]), 64, s)
+    np.testing.assert_allclose(out2.cpu().numpy(), ref2, atol=TOL, rtol=0)
+
+
+def test_decode_step_cache_full(ctx):
+    import torch
+    from streaming_attention_b200 import SAError, attn_decode_step
+    kc = torch.zeros(2, 8, 64, device="cuda")
+    q = np.zeros((2, 64), np.float32)
+    kn = np.zeros((2, 64), np.float32)
+    with pytest.raises(SAError) as e:
+        attn_decode_step(q, kn, kn, kc, kc.clone(), 8, 1.0, 64, ctx)
+    assert e.value.code == -7 and "full" in str(e.value)
