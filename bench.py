@@ -449,12 +449,108 @@ def run_ours(args):
             except Exception as e:  # the baseline is reported, never required
                 result["cpu_baseline"] = {"value": None, "unit": "GB/s", "cores": os.cpu_count(),
                                           "kind": "reference", "sample": f"unavailable: {e}"}
+        if world == 1 and not args.no_extra:
+            pms, ptf = measure_prefill(ctx, dev, stream, 10, 3)
+            bpk, bkind = load_bf16_peak()
+            result["extra"] = {"prefill_configs2": {
+                "metric": "attn TFLOP/s (causal prefill)", "value": round(ptf, 2),
+                "ms": round(pms, 4), "frac_of_bf16_peak": round(ptf / bpk, 4),
+                "peak": f"{bpk} ({bkind} bf16_tflops)", "workload": PF_WORKLOAD}}
         print(json.dumps(result), flush=True)
 
     ctx.close()
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+    return 0
+
+
+# ---------------------------------------------------------------- prefill
+PF_S, PF_HQ, PF_HKV = 8192, 16, 8
+PF_WORKLOAD = ("configs[2] causal prefill: Q [8192, 16, 128], K/V [8192, 8, 128] bf16 N(0,1), "
+               "scale 1/sqrt(128), fp32 accumulation")
+
+
+def prefill_flops(S=PF_S, hq=PF_HQ, d=D):
+    """Causal FLOPs: 2 GEMMs x 2 FLOP x hq x d x S(S+1)/2 (the non-causal 2x is not counted)."""
+    return 4.0 * hq * d * S * (S + 1) / 2
+
+
+def measure_prefill(ctx, dev, stream, steps, warmup, out_dtype="bfloat16"):
+    import torch
+    import streaming_attention_b200 as sa
+    g = torch.Generator(device=dev).manual_seed(SEED)
+    q = torch.randn(PF_S, PF_HQ, D, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(PF_S, PF_HKV, D, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(PF_S, PF_HKV, D, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty(PF_S, PF_HQ, D, device=dev, dtype=getattr(torch, out_dtype))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)    # 256 MB > L2
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            sa.attn_prefill(q, k, v, SCALE, 0, out_dtype, ctx, out)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        tot = 0.0
+        for _ in range(steps):
+            flush.zero_()                       # L2 flush between timed launches
+            e0.record(stream)
+            sa.attn_prefill(q, k, v, SCALE, 0, out_dtype, ctx, out)
+            e1.record(stream)
+            e1.synchronize()
+            tot += e0.elapsed_time(e1)
+    ms = tot / steps
+    return ms, prefill_flops() / (ms / 1e3) / 1e12
+
+
+def load_bf16_peak(sustained=False):
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["bf16_tflops_sustained" if sustained else "bf16_tflops"]), "measured"
+    except Exception:
+        return (1400.0 if sustained else 1590.0), "fallback"
+
+
+def run_prefill(args):
+    import torch
+    import streaming_attention_b200 as sa
+    local = env_int("LOCAL_RANK", 0)
+    if env_int("RANK", 0) != 0:
+        return 0
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    ctx = sa.Context(local)
+    stream = torch.cuda.Stream(dev)
+    if args.profile:
+        g = torch.Generator(device=dev).manual_seed(SEED)
+        q = torch.randn(PF_S, PF_HQ, D, device=dev, generator=g).to(torch.bfloat16)
+        k = torch.randn(PF_S, PF_HKV, D, device=dev, generator=g).to(torch.bfloat16)
+        v = torch.randn(PF_S, PF_HKV, D, device=dev, generator=g).to(torch.bfloat16)
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup + args.steps):
+                sa.attn_prefill(q, k, v, SCALE, 0, "bfloat16", ctx)
+        torch.cuda.synchronize(dev)
+        print(json.dumps({"profile": True, "workload": "prefill",
+                          "launches": args.warmup + args.steps}), flush=True)
+        return 0
+    clocks = ClockSampler(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local].strip()
+                          if os.environ.get("CUDA_VISIBLE_DEVICES") else str(local))
+    clocks.start()
+    ms, tf = measure_prefill(ctx, dev, stream, args.steps, args.warmup)
+    clk = clocks.stop()
+    peak, kind = load_bf16_peak()
+    print(json.dumps({
+        "metric": "attn TFLOP/s (causal prefill)", "value": round(tf, 2), "unit": "TFLOP/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": PF_WORKLOAD, "l2": "256 MB buffer written between timed launches"},
+        "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(tf / peak, 4), "peak_kind": f"{kind} bf16_tflops (burst)",
+                     "kernel": "sa::pf::prefill_kernel", "kernel_ms": round(ms, 4),
+                     "traffic": load_traffic("prefill_S8192")},
+        "clocks": clk, "gpu_launches": args.steps}), flush=True)
+    ctx.close()
     return 0
 
 
@@ -465,6 +561,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the extra (non-headline) measurements in the decode line")
+    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+                    help="decode: the headline configs[1] line; prefill: configs[2] causal "
+                         "prefill on tensor cores (TFLOP/s)")
     ap.add_argument("--profile", action="store_true",
                     help="only W warm-up + K device steps (a short launch sequence for ncu)")
     ap.add_argument("--cpu-budget", type=float, default=10.0,
@@ -472,6 +573,8 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.workload == "prefill":
+        return run_prefill(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -211,6 +211,72 @@ int sa_attn_decode_noalloc(void* stream, int dtype, const void* q, const void* k
                            long long kv_head_stride, int T, int d, int hq, int hkv, int block,
                            float scale, float* out);
 
+/* ======================================================================== */
+/* Qwen3 forward                                                             */
+/* ======================================================================== */
+
+typedef struct sa_qwen3 sa_qwen3;
+
+/* Model shape (Qwen3-0.6B: vocab 151936, hidden 1024, 28 layers, 16/8 heads,
+ * head_dim 128, intermediate 3072, eps 1e-6, theta 1e6) and KV-cache
+ * capacity in tokens (the reference's KVCache max_seq_len, kv_cache.h:47-52). */
+typedef struct {
+    int vocab, hidden, n_layers, hq, hkv, head_dim, inter;
+    float eps, theta;
+    int max_seq;
+} sa_qwen3_config;
+
+/* Allocate a model (weights, fp32 KV cache of n_layers x hkv x max_seq x
+ * head_dim, activation buffers) on the context's GPU.  Weights are uploaded
+ * with sa_qwen3_set_embed / sa_qwen3_set_layer.  Requirements: head_dim 128,
+ * hidden and inter multiples of 64, hq/hkv in {1, 2, 4}. */
+int sa_qwen3_create(sa_ctx* ctx, const sa_qwen3_config* cfg, sa_qwen3** out);
+int sa_qwen3_destroy(sa_qwen3* m);
+
+/* Token embedding [vocab, hidden], final norm [hidden], lm_head [vocab,
+ * hidden] (NULL or equal to the embedding = tied), host fp32, stored as bf16
+ * (exact for bf16 checkpoints; qwen3_loader.cpp reads bf16). */
+int sa_qwen3_set_embed(sa_qwen3* m, const float* embed, const float* final_norm, const float* lm_head);
+
+/* One decoder layer's weights, host fp32, in the reference's shapes
+ * (Qwen3LayerWeights, tensor_cpp/include/tensor_cpp/qwen3_ops.h:37-57):
+ * norms [hidden]; q [hq*128, hidden]; k, v [hkv*128, hidden]; q_norm, k_norm
+ * [128]; o [hidden, hq*128]; gate, up [inter, hidden]; down [hidden, inter]. */
+int sa_qwen3_set_layer(sa_qwen3* m, int layer, const float* in_norm, const float* wq, const float* wk,
+                       const float* wv, const float* q_norm, const float* k_norm, const float* wo,
+                       const float* post_norm, const float* w_gate, const float* w_up,
+                       const float* w_down);
+
+/* KVCache::reset (kv_cache.h:142-153): the cache length returns to 0. */
+int sa_qwen3_reset(sa_qwen3* m);
+/* KVCache::current_seq_len. */
+int sa_qwen3_cache_len(sa_qwen3* m);
+
+/*
+ * Forward S tokens.  use_cache = 0: qwen3_forward (qwen3_ops.cpp:537-614),
+ * positions 0..S-1, the cache length is left unchanged.  use_cache = 1:
+ * qwen3_forward_with_cache (:936-1014, STANDARD attention): positions start
+ * at the cache length, K/V are appended and the length advances by S.
+ * logits_mode 0: logits [S, vocab]; 1: last token only [vocab]; 2: none.
+ * ids are checked against the vocabulary (SA_ERR_RANGE, ops.cpp:296);
+ * SA_ERR_FULL when the cache cannot hold S more tokens (kv_cache.h:109-111).
+ * With SA_HOST_PTRS ids/logits are host memory and the call is blocking.
+ */
+int sa_qwen3_forward(sa_qwen3* m, const int64_t* ids, int S, int use_cache, float* logits,
+                     int logits_mode, unsigned flags);
+
+/*
+ * Greedy decode: forward the S-token prompt with the cache, then n_new times
+ * take the argmax of the last logits (ops::argmax, ops.cpp:213-272; first
+ * index of the maximum) as the next token and forward it.  Writes the n_new
+ * generated tokens.  Token selection stays on the GPU; with SA_HOST_PTRS the
+ * prompt/tokens are host memory.  The driver loop of benchmark_qwen3's decode
+ * phase (benchmark_qwen3.cpp:406-520) with the argmax taken over the returned
+ * logits.
+ */
+int sa_qwen3_generate(sa_qwen3* m, const int64_t* prompt, int S, int n_new, int64_t* out_tokens,
+                      unsigned flags);
+
 #ifdef __cplusplus
 }
 #endif

@@ -27,8 +27,10 @@ from .attention import (  # noqa: F401
     streaming_attention_mpi_cuda,
 )
 
+from .qwen3 import QWEN3_0_6B, Qwen3, Qwen3Config  # noqa: F401
+
 __all__ = [
     "Context", "SAError", "lib", "LIB_PATH", "SA_F32", "SA_BF16", "SA_HOST_PTRS",
     "attn_decode", "attn_decode_partial", "attn_decode_step", "attn_merge", "attn_prefill", "streaming_attention_cuda",
-    "naive_attention_cuda", "streaming_attention_mpi_cuda",
+    "naive_attention_cuda", "streaming_attention_mpi_cuda", "Qwen3", "Qwen3Config", "QWEN3_0_6B",
 ]

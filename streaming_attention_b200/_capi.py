@@ -46,6 +46,16 @@ SIGNATURES = {
     "sa_attn_prefill": (C.c_int, [_vp, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                   C.c_int, C.c_longlong, C.c_longlong, C.c_float, _vp, C.c_int,
                                   C.c_longlong, C.c_uint]),
+    "sa_qwen3_create": (C.c_int, [_vp, _vp, C.POINTER(_vp)]),
+    "sa_qwen3_destroy": (C.c_int, [_vp]),
+    "sa_qwen3_set_embed": (C.c_int, [_vp, _fp, _fp, _fp]),
+    "sa_qwen3_set_layer": (C.c_int, [_vp, C.c_int] + [_fp] * 11),
+    "sa_qwen3_reset": (C.c_int, [_vp]),
+    "sa_qwen3_cache_len": (C.c_int, [_vp]),
+    "sa_qwen3_forward": (C.c_int, [_vp, C.POINTER(C.c_int64), C.c_int, C.c_int, _fp, C.c_int,
+                                   C.c_uint]),
+    "sa_qwen3_generate": (C.c_int, [_vp, C.POINTER(C.c_int64), C.c_int, C.c_int,
+                                    C.POINTER(C.c_int64), C.c_uint]),
     "sa_attn_decode_noalloc": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, C.c_longlong, C.c_int,
                                          C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, _vp]),
 }

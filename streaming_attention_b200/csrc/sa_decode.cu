@@ -27,6 +27,7 @@
 
 #include "sa_internal.h"
 #include "sa_ptx.cuh"
+#include "sa_qwen3.h"
 
 namespace sa {
 namespace dec {
@@ -56,6 +57,9 @@ struct Args {
     float* out_m;               // optional [hq], natural-log domain
     float* out_l;               // optional [hq]
     int* status;
+    // multi-query launches (gridDim.z > 1): query z reads q + z*q_stride,
+    // attends rows [0, T + z) and writes out + z*o_stride (n_splits == 1)
+    long long q_stride, o_stride;
 };
 
 // Unpack one 16-byte chunk into VEC floats.
@@ -114,9 +118,9 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
     __shared__ int s_issued, s_consumed, s_last;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int kvh = blockIdx.y, split = blockIdx.x;
+    const int kvh = blockIdx.y, split = blockIdx.x, qz = blockIdx.z;
     const int t0 = split * a.rows_per_split;
-    const int nrows = max(0, min(a.T - t0, a.rows_per_split));
+    const int nrows = max(0, min(a.T + qz - t0, a.rows_per_split));
     const int nst = (nrows + SR - 1) / SR;
     const KT* kg = static_cast<const KT*>(a.k) + (size_t)kvh * a.kv_head_stride + (size_t)t0 * D;
     const KT* vg = static_cast<const KT*>(a.v) + (size_t)kvh * a.kv_head_stride + (size_t)t0 * D;
@@ -156,7 +160,7 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
         float qr[G][CPL];
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            const KT* qh = static_cast<const KT*>(a.q) + (size_t)(kvh * G + g) * D;
+            const KT* qh = static_cast<const KT*>(a.q) + (size_t)qz * a.q_stride + (size_t)(kvh * G + g) * D;
 #pragma unroll
             for (int c = 0; c < CH; ++c) {
                 Chunk<KT>::load(qh + (sub + 8 * c) * VEC, &qr[g][c * VEC]);
@@ -304,6 +308,15 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
             O += red_o[(w * G + g) * D + col] * wt;
         }
         const int h = kvh * G + g;
+        if (a.n_splits == 1) {
+            // one split: this CTA holds the whole state; finalise in place
+            a.out[(size_t)qz * a.o_stride + (size_t)h * D + col] = L > 0.f ? O / L : 0.f;
+            if (col == 0 && a.out_m) {
+                a.out_m[h] = L > 0.f ? M * LN2 : -INFINITY;
+                a.out_l[h] = L > 0.f ? L : 1.f;
+            }
+            continue;
+        }
         const size_t pi = (size_t)h * a.n_splits + split;
         a.part_o[pi * D + col] = L > 0.f ? O / L : 0.f;
         if (col == 0) {
@@ -311,6 +324,7 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
             a.part_l[pi] = L;
         }
     }
+    if (a.n_splits == 1) return;
     __threadfence();
     __syncthreads();
     if (tid == 0) s_last = (atomicAdd(&a.counters[kvh], 1u) == (unsigned)(a.n_splits - 1));
@@ -478,6 +492,7 @@ static int launch_decode(sa_ctx* ctx, int dtype, const void* q, const void* k, c
     a.counters = ctx->counters;
     a.out = out; a.out_m = out_m; a.out_l = out_l;
     a.status = ctx->status;
+    a.q_stride = 0; a.o_stride = 0;
     dec::KernelFn fn = dtype == SA_F32 ? dec::pick<float>(d, hq / hkv) : dec::pick<__nv_bfloat16>(d, hq / hkv);
     SA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::SMEM_BYTES));
     fn<<<dim3(ns, hkv), dec::THREADS, dec::SMEM_BYTES, ctx->stream>>>(a);
@@ -590,6 +605,35 @@ SA_API int sa_attn_merge(sa_ctx* ctx, int n_parts, int hq, int d, const float* m
     return sa::sync_and_check(ctx);
 }
 
+namespace sa {
+// Multi-query causal attention (prompt processing of the Qwen3 forward): one
+// CTA per (query, KV head), each a single split, so no scratch or counters.
+int decode_multi_launch(cudaStream_t st, int* status, const float* q, long long q_stride, const float* k,
+                        const float* v, long long kv_head_stride, int T0, int n_q, int d, int hq, int hkv,
+                        float scale, float* out, long long o_stride) {
+    SA_CHECK_ARG(n_q >= 1 && n_q <= 65535 && T0 >= 1, "decode_multi: n_q=%d T0=%d", n_q, T0);
+    dec::Args a;
+    a.q = q; a.k = k; a.v = v;
+    a.kv_head_stride = kv_head_stride;
+    a.T = T0; a.hq = hq; a.hkv = hkv;
+    const int sr = dec::stage_rows(SA_F32, d);
+    a.rows_per_split = (T0 + n_q - 1 + sr - 1) / sr * sr;
+    a.n_splits = 1;
+    a.qscale = scale * dec::LOG2E;
+    a.part_m = a.part_l = a.part_o = nullptr;
+    a.counters = nullptr;
+    a.out = out; a.out_m = nullptr; a.out_l = nullptr;
+    a.status = status;
+    a.q_stride = q_stride; a.o_stride = o_stride;
+    dec::KernelFn fn = dec::pick<float>(d, hq / hkv);
+    SA_CHECK_ARG(fn != nullptr, "decode_multi: hq/hkv=%d d=%d unsupported", hq / hkv, d);
+    SA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::SMEM_BYTES));
+    fn<<<dim3(1, hkv, n_q), dec::THREADS, dec::SMEM_BYTES, st>>>(a);
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
+}  // namespace sa
+
 // ===========================================================================
 // Allocation-free decode entry point.
 //
@@ -689,6 +733,7 @@ SA_API int sa_attn_decode_noalloc(void* stream, int dtype, const void* q, const 
     a.counters = counters;
     a.out = out; a.out_m = nullptr; a.out_l = nullptr;
     a.status = status;
+    a.q_stride = 0; a.o_stride = 0;
     dec::KernelFn fn = dtype == SA_F32 ? dec::pick<float>(d, hq / hkv) : dec::pick<__nv_bfloat16>(d, hq / hkv);
     SA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::SMEM_BYTES));
     fn<<<dim3(ns, hkv), dec::THREADS, dec::SMEM_BYTES, st>>>(a);

@@ -1,0 +1,460 @@
+// sa_qwen3.cu -- Qwen3 forward on B200: weights, KV cache and the layer
+// schedule behind the C ABI (sa_qwen3_*).
+//
+// Replaces tensor_cpp's qwen3_forward (qwen3_ops.cpp:537-614),
+// qwen3_forward_with_cache (:936-1014) with the STANDARD attention type, and
+// the KVCache it advances (kv_cache.h:27-238).
+//
+// Numerics: weights are held in bf16 (the reference loads bf16 checkpoints,
+// qwen3_loader.cpp:157-164, so bf16 weights are exact); activations, the
+// residual stream and the KV cache are fp32 like the reference.  Prompt
+// projections run on tcgen05 tensor cores with each fp32 activation split
+// into two bf16 terms (sa_gemm.cu); single-token decode runs GEMVs that
+// stream the bf16 weights against fp32 activations.  Greedy decode therefore
+// follows the fp32 reference token for token.
+#include <cuda_bf16.h>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "sa_internal.h"
+#include "sa_qwen3.h"
+
+struct sa_qwen3 {
+    sa_ctx* ctx = nullptr;
+    sa_qwen3_config c{};
+    int QD = 0, KD = 0, NQKV = 0;
+    // weights (device)
+    __nv_bfloat16* embed = nullptr;      // [V, H]
+    __nv_bfloat16* lm_head = nullptr;    // [V, H] (== embed when tied)
+    float* final_norm = nullptr;         // [H]
+    struct Layer {
+        float* in_norm = nullptr;        // [H]
+        float* post_norm = nullptr;      // [H]
+        float* q_norm = nullptr;         // [D]
+        float* k_norm = nullptr;         // [D]
+        __nv_bfloat16* wqkv = nullptr;   // [QD + 2 KD, H]  rows: q | k | v
+        __nv_bfloat16* wo = nullptr;     // [H, QD]
+        __nv_bfloat16* wgu = nullptr;    // [2 I, H]  blocks of [gate 32; up 32]
+        __nv_bfloat16* wd = nullptr;     // [H, I]
+    };
+    std::vector<Layer> layers;
+    bool loaded_embed = false;
+    std::vector<bool> loaded_layer;
+    // KV cache (fp32) [L][hkv][max_seq][D] and its current length
+    float* kc = nullptr;
+    float* vc = nullptr;
+    int cache_len = 0;
+    float* cos_t = nullptr;              // [max_seq, D/2]
+    float* sin_t = nullptr;
+    // activations for up to cap_m tokens
+    int cap_m = 0;
+    float* x = nullptr;                  // [M, H]
+    float* qkv = nullptr;                // [M, NQKV]
+    float* q = nullptr;                  // [M, QD]
+    float* attn = nullptr;               // [M, QD]
+    float* act = nullptr;                // [M, I]  (decode path)
+    float* xn = nullptr;                 // [M, H]  (final norm, decode path)
+    __nv_bfloat16 *a_hi = nullptr, *a_lo = nullptr, *b_hi = nullptr, *b_lo = nullptr;   // [M, max(QD, I, H)]
+    float* logits = nullptr;             // [logits_rows, V]
+    int logits_rows = 0;
+    int64_t* ids = nullptr;              // [M]
+    float* gemm_ws = nullptr;            // split-K partials
+    size_t gemm_ws_floats = 0;
+    unsigned* gemm_cnt = nullptr;
+    size_t gemm_cnt_n = 0;
+};
+
+namespace sa {
+
+static int dmalloc(void** p, size_t bytes) {
+    if (cudaMalloc(p, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(SA_ERR_OOM, "cudaMalloc of %zu bytes failed", bytes);
+    }
+    return SA_OK;
+}
+
+template <typename T>
+static int dalloc(T** p, size_t n) { return dmalloc(reinterpret_cast<void**>(p), n * sizeof(T)); }
+
+static uint16_t f2bf(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+// Upload `rows` x `cols` fp32 host values as bf16 into dst at row offset.
+static int upload_bf16(__nv_bfloat16* dst, const float* src, size_t n, cudaStream_t st) {
+    std::vector<uint16_t> tmp(n);
+    for (size_t i = 0; i < n; ++i) tmp[i] = f2bf(src[i]);
+    SA_CUDA_TRY(cudaMemcpyAsync(dst, tmp.data(), n * 2, cudaMemcpyHostToDevice, st));
+    SA_CUDA_TRY(cudaStreamSynchronize(st));
+    return SA_OK;
+}
+static int upload_f32(float* dst, const float* src, size_t n, cudaStream_t st) {
+    SA_CUDA_TRY(cudaMemcpyAsync(dst, src, n * 4, cudaMemcpyHostToDevice, st));
+    SA_CUDA_TRY(cudaStreamSynchronize(st));
+    return SA_OK;
+}
+
+static void free_model(sa_qwen3* m) {
+    cudaFree(m->embed);
+    if (m->lm_head != m->embed) cudaFree(m->lm_head);
+    cudaFree(m->final_norm);
+    for (auto& L : m->layers) {
+        cudaFree(L.in_norm); cudaFree(L.post_norm); cudaFree(L.q_norm); cudaFree(L.k_norm);
+        cudaFree(L.wqkv); cudaFree(L.wo); cudaFree(L.wgu); cudaFree(L.wd);
+    }
+    cudaFree(m->kc); cudaFree(m->vc); cudaFree(m->cos_t); cudaFree(m->sin_t);
+    cudaFree(m->x); cudaFree(m->qkv); cudaFree(m->q); cudaFree(m->attn); cudaFree(m->act); cudaFree(m->xn);
+    cudaFree(m->a_hi); cudaFree(m->a_lo); cudaFree(m->b_hi); cudaFree(m->b_lo);
+    cudaFree(m->logits); cudaFree(m->ids); cudaFree(m->gemm_ws); cudaFree(m->gemm_cnt);
+}
+
+// Activation buffers for up to M tokens (grow-only).
+static int ensure_acts(sa_qwen3* m, int M) {
+    if (M <= m->cap_m) return SA_OK;
+    SA_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    cudaFree(m->x); cudaFree(m->qkv); cudaFree(m->q); cudaFree(m->attn); cudaFree(m->act); cudaFree(m->xn);
+    cudaFree(m->a_hi); cudaFree(m->a_lo); cudaFree(m->b_hi); cudaFree(m->b_lo); cudaFree(m->ids);
+    const sa_qwen3_config& c = m->c;
+    const size_t wmax = (size_t)std::max(std::max(m->QD, c.inter), c.hidden);
+    int rc = SA_OK;
+    if (!rc) rc = dalloc(&m->x, (size_t)M * c.hidden);
+    if (!rc) rc = dalloc(&m->qkv, (size_t)M * m->NQKV);
+    if (!rc) rc = dalloc(&m->q, (size_t)M * m->QD);
+    if (!rc) rc = dalloc(&m->attn, (size_t)M * m->QD);
+    if (!rc) rc = dalloc(&m->act, (size_t)M * c.inter);
+    if (!rc) rc = dalloc(&m->xn, (size_t)M * c.hidden);
+    if (!rc) rc = dalloc(&m->a_hi, (size_t)M * wmax);
+    if (!rc) rc = dalloc(&m->a_lo, (size_t)M * wmax);
+    if (!rc) rc = dalloc(&m->b_hi, (size_t)M * wmax);
+    if (!rc) rc = dalloc(&m->b_lo, (size_t)M * wmax);
+    if (!rc) rc = dalloc(&m->ids, (size_t)M);
+    if (rc) { m->cap_m = 0; return rc; }
+    m->cap_m = M;
+    return SA_OK;
+}
+
+static int ensure_logits(sa_qwen3* m, int rows) {
+    if (rows <= m->logits_rows) return SA_OK;
+    SA_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    cudaFree(m->logits);
+    m->logits = nullptr;
+    int rc = dalloc(&m->logits, (size_t)rows * m->c.vocab);
+    m->logits_rows = rc ? 0 : rows;
+    return rc;
+}
+
+// Split-K so that a GEMM of this shape fills the GPU with >= ~1 CTA per SM.
+static int pick_splits(const sa_qwen3* m, int M, int N, int K) {
+    const int tiles = ((N + 63) / 64) * ((M + 127) / 128);
+    int s = 1;
+    while (tiles * s < m->ctx->num_sms && s * 2 <= K / 64 / 2) s *= 2;
+    return s;
+}
+
+static int gemm(sa_qwen3* m, const __nv_bfloat16* hi, const __nv_bfloat16* lo, long long lda,
+                const __nv_bfloat16* w, int M, int N, int K, int mode, float* C, long long ldc,
+                __nv_bfloat16* ohi, __nv_bfloat16* olo, long long ldo) {
+    const int splits = mode == QW_EPI_SWIGLU ? 1 : pick_splits(m, M, N, K);
+    const size_t tiles = (size_t)((N + 63) / 64) * ((M + 127) / 128);
+    if (splits > 1) {
+        const size_t need = tiles * splits * 128 * 64;
+        if (need > m->gemm_ws_floats) {
+            SA_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+            cudaFree(m->gemm_ws);
+            m->gemm_ws = nullptr;
+            m->gemm_ws_floats = 0;
+            int rc = dalloc(&m->gemm_ws, need);
+            if (rc) return rc;
+            m->gemm_ws_floats = need;
+        }
+        if (tiles > m->gemm_cnt_n) {
+            SA_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+            cudaFree(m->gemm_cnt);
+            m->gemm_cnt = nullptr;
+            m->gemm_cnt_n = 0;
+            int rc = dalloc(&m->gemm_cnt, tiles);
+            if (rc) return rc;
+            SA_CUDA_TRY(cudaMemset(m->gemm_cnt, 0, tiles * sizeof(unsigned)));
+            m->gemm_cnt_n = tiles;
+        }
+    }
+    return gemm_launch(m->ctx->stream, m->ctx->status, hi, lo, lda, w, M, N, K, mode, C, ldc, ohi, olo, ldo,
+                       splits, m->gemm_ws, m->gemm_ws_floats, m->gemm_cnt, m->gemm_cnt_n);
+}
+
+#define SA_RC(expr) do { int rc_ = (expr); if (rc_) return rc_; } while (0)
+
+// Tokens ids (device) at positions pos0 .. pos0+M-1 through every layer,
+// appending K/V to the cache.  M == 1 uses the GEMV path.
+static int run_layers(sa_qwen3* m, int M, int pos0) {
+    const sa_qwen3_config& c = m->c;
+    cudaStream_t st = m->ctx->stream;
+    const int H = c.hidden, I = c.inter, D = c.head_dim;
+    const float scale = 1.0f / sqrtf((float)D);
+    const size_t layer_kv = (size_t)c.hkv * c.max_seq * D;
+    SA_RC(launch_embedding(st, m->ids, M, m->embed, c.vocab, H, m->x, m->ctx->status));
+    for (int l = 0; l < c.n_layers; ++l) {
+        const sa_qwen3::Layer& L = m->layers[l];
+        float* kc = m->kc + l * layer_kv;
+        float* vc = m->vc + l * layer_kv;
+        if (M == 1) {
+            SA_RC(launch_gemv(st, QW_EPI_STORE, true, L.wqkv, m->NQKV, H, m->x, L.in_norm, c.eps, m->qkv, m->ctx->num_sms));
+            SA_RC(launch_qknorm_rope_append(st, m->qkv, 1, c.hq, c.hkv, L.q_norm, L.k_norm, m->cos_t, m->sin_t, pos0,
+                                            m->q, kc, vc, c.max_seq));
+            SA_RC(sa_attn_decode(m->ctx, SA_F32, m->q, kc, vc, (long long)c.max_seq * D, pos0 + 1, D, c.hq, c.hkv,
+                                 64, scale, m->attn, 0));
+            SA_RC(launch_gemv(st, QW_EPI_RESID, false, L.wo, H, m->QD, m->attn, nullptr, 0.f, m->x, m->ctx->num_sms));
+            SA_RC(launch_gemv(st, QW_EPI_SWIGLU, true, L.wgu, I, H, m->x, L.post_norm, c.eps, m->act, m->ctx->num_sms));
+            SA_RC(launch_gemv(st, QW_EPI_RESID, false, L.wd, H, I, m->act, nullptr, 0.f, m->x, m->ctx->num_sms));
+        } else {
+            SA_RC(launch_rmsnorm_hilo(st, m->x, L.in_norm, M, H, c.eps, m->a_hi, m->a_lo));
+            SA_RC(gemm(m, m->a_hi, m->a_lo, H, L.wqkv, M, m->NQKV, H, QW_EPI_STORE, m->qkv, m->NQKV, nullptr, nullptr, 0));
+            SA_RC(launch_qknorm_rope_append(st, m->qkv, M, c.hq, c.hkv, L.q_norm, L.k_norm, m->cos_t, m->sin_t, pos0,
+                                            m->q, kc, vc, c.max_seq));
+            SA_RC(decode_multi_launch(st, m->ctx->status, m->q, m->QD, kc, vc, (long long)c.max_seq * D, pos0 + 1, M, D,
+                                      c.hq, c.hkv, scale, m->attn, m->QD));
+            SA_RC(launch_split_hilo(st, m->attn, (size_t)M * m->QD, m->a_hi, m->a_lo));
+            SA_RC(gemm(m, m->a_hi, m->a_lo, m->QD, L.wo, M, H, m->QD, QW_EPI_RESID, m->x, H, nullptr, nullptr, 0));
+            SA_RC(launch_rmsnorm_hilo(st, m->x, L.post_norm, M, H, c.eps, m->a_hi, m->a_lo));
+            SA_RC(gemm(m, m->a_hi, m->a_lo, H, L.wgu, M, 2 * I, H, QW_EPI_SWIGLU, nullptr, 0, m->b_hi, m->b_lo, I));
+            SA_RC(gemm(m, m->b_hi, m->b_lo, I, L.wd, M, H, I, QW_EPI_RESID, m->x, H, nullptr, nullptr, 0));
+        }
+    }
+    return SA_OK;
+}
+
+// Final norm + lm_head for rows [r0, r0 + n) of the residual stream.
+static int run_head(sa_qwen3* m, int r0, int n) {
+    const sa_qwen3_config& c = m->c;
+    cudaStream_t st = m->ctx->stream;
+    SA_RC(ensure_logits(m, n));
+    if (n == 1) {
+        SA_RC(launch_gemv(st, QW_EPI_STORE, true, m->lm_head, c.vocab, c.hidden, m->x + (size_t)r0 * c.hidden,
+                          m->final_norm, c.eps, m->logits, m->ctx->num_sms));
+    } else {
+        SA_RC(launch_rmsnorm_hilo(st, m->x + (size_t)r0 * c.hidden, m->final_norm, n, c.hidden, c.eps, m->a_hi, m->a_lo));
+        SA_RC(gemm(m, m->a_hi, m->a_lo, c.hidden, m->lm_head, n, c.vocab, c.hidden, QW_EPI_STORE, m->logits, c.vocab,
+                   nullptr, nullptr, 0));
+    }
+    return SA_OK;
+}
+
+}  // namespace sa
+
+using namespace sa;
+
+SA_API int sa_qwen3_create(sa_ctx* ctx, const sa_qwen3_config* cfg, sa_qwen3** out) {
+    clear_error();
+    SA_CHECK_ARG(ctx && cfg && out, "sa_qwen3_create: null argument");
+    *out = nullptr;
+    const sa_qwen3_config& c = *cfg;
+    SA_CHECK_ARG(c.head_dim == 128, "sa_qwen3_create: head_dim %d (128 supported)", c.head_dim);
+    SA_CHECK_ARG(c.hidden > 0 && c.hidden % 64 == 0 && c.inter % 64 == 0 && c.vocab > 0 && c.n_layers > 0,
+                 "sa_qwen3_create: hidden=%d inter=%d vocab=%d layers=%d", c.hidden, c.inter, c.vocab, c.n_layers);
+    SA_CHECK_ARG(c.hkv > 0 && c.hq % c.hkv == 0 && (c.hq / c.hkv == 1 || c.hq / c.hkv == 2 || c.hq / c.hkv == 4),
+                 "sa_qwen3_create: hq=%d hkv=%d", c.hq, c.hkv);
+    SA_CHECK_ARG(c.max_seq > 0, "sa_qwen3_create: max_seq=%d", c.max_seq);
+    DeviceGuard guard(ctx->device);
+    sa_qwen3* m = new sa_qwen3();
+    m->ctx = ctx;
+    m->c = c;
+    m->QD = c.hq * c.head_dim;
+    m->KD = c.hkv * c.head_dim;
+    m->NQKV = m->QD + 2 * m->KD;
+    m->layers.resize(c.n_layers);
+    m->loaded_layer.assign(c.n_layers, false);
+    const size_t H = c.hidden, I = c.inter, D = c.head_dim;
+    int rc = SA_OK;
+    if (!rc) rc = dalloc(&m->embed, (size_t)c.vocab * H);
+    if (!rc) rc = dalloc(&m->final_norm, H);
+    for (int l = 0; l < c.n_layers && !rc; ++l) {
+        auto& L = m->layers[l];
+        rc = dalloc(&L.in_norm, H);
+        if (!rc) rc = dalloc(&L.post_norm, H);
+        if (!rc) rc = dalloc(&L.q_norm, D);
+        if (!rc) rc = dalloc(&L.k_norm, D);
+        if (!rc) rc = dalloc(&L.wqkv, (size_t)m->NQKV * H);
+        if (!rc) rc = dalloc(&L.wo, H * m->QD);
+        if (!rc) rc = dalloc(&L.wgu, 2 * I * H);
+        if (!rc) rc = dalloc(&L.wd, H * I);
+    }
+    const size_t kv = (size_t)c.n_layers * c.hkv * c.max_seq * D;
+    if (!rc) rc = dalloc(&m->kc, kv);
+    if (!rc) rc = dalloc(&m->vc, kv);
+    if (!rc) rc = dalloc(&m->cos_t, (size_t)c.max_seq * D / 2);
+    if (!rc) rc = dalloc(&m->sin_t, (size_t)c.max_seq * D / 2);
+    if (!rc) rc = launch_rope_table(ctx->stream, c.max_seq, (int)D, c.theta, m->cos_t, m->sin_t);
+    if (!rc && cudaMemsetAsync(m->kc, 0, kv * 4, ctx->stream) != cudaSuccess) rc = set_error(SA_ERR_CUDA, "memset");
+    if (!rc && cudaMemsetAsync(m->vc, 0, kv * 4, ctx->stream) != cudaSuccess) rc = set_error(SA_ERR_CUDA, "memset");
+    if (!rc && cudaStreamSynchronize(ctx->stream) != cudaSuccess) rc = set_error(SA_ERR_CUDA, "sync");
+    if (rc) {
+        free_model(m);
+        delete m;
+        return rc;
+    }
+    m->lm_head = m->embed;
+    *out = m;
+    return SA_OK;
+}
+
+SA_API int sa_qwen3_destroy(sa_qwen3* m) {
+    clear_error();
+    if (!m) return SA_OK;
+    DeviceGuard guard(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    free_model(m);
+    delete m;
+    return SA_OK;
+}
+
+SA_API int sa_qwen3_set_embed(sa_qwen3* m, const float* embed, const float* final_norm, const float* lm_head) {
+    clear_error();
+    SA_CHECK_ARG(m && embed && final_norm, "sa_qwen3_set_embed: null argument");
+    DeviceGuard guard(m->ctx->device);
+    const size_t VH = (size_t)m->c.vocab * m->c.hidden;
+    cudaStream_t st = m->ctx->stream;
+    SA_RC(upload_bf16(m->embed, embed, VH, st));
+    SA_RC(upload_f32(m->final_norm, final_norm, m->c.hidden, st));
+    const bool tied = lm_head == nullptr || lm_head == embed ||
+                      std::memcmp(lm_head, embed, VH * sizeof(float)) == 0;
+    if (tied) {
+        if (m->lm_head != m->embed) cudaFree(m->lm_head);
+        m->lm_head = m->embed;
+    } else {
+        if (m->lm_head == m->embed) SA_RC(dalloc(&m->lm_head, VH));
+        SA_RC(upload_bf16(m->lm_head, lm_head, VH, st));
+    }
+    m->loaded_embed = true;
+    return SA_OK;
+}
+
+SA_API int sa_qwen3_set_layer(sa_qwen3* m, int layer, const float* in_norm, const float* wq, const float* wk,
+                              const float* wv, const float* q_norm, const float* k_norm, const float* wo,
+                              const float* post_norm, const float* w_gate, const float* w_up, const float* w_down) {
+    clear_error();
+    SA_CHECK_ARG(m && layer >= 0 && layer < m->c.n_layers, "sa_qwen3_set_layer: layer %d", layer);
+    SA_CHECK_ARG(in_norm && wq && wk && wv && q_norm && k_norm && wo && post_norm && w_gate && w_up && w_down,
+                 "sa_qwen3_set_layer: null weight");
+    DeviceGuard guard(m->ctx->device);
+    const sa_qwen3_config& c = m->c;
+    const size_t H = c.hidden, I = c.inter, D = c.head_dim;
+    auto& L = m->layers[layer];
+    cudaStream_t st = m->ctx->stream;
+    SA_RC(upload_f32(L.in_norm, in_norm, H, st));
+    SA_RC(upload_f32(L.post_norm, post_norm, H, st));
+    SA_RC(upload_f32(L.q_norm, q_norm, D, st));
+    SA_RC(upload_f32(L.k_norm, k_norm, D, st));
+    // [q; k; v] rows, as qwen3_loader.cpp builds qkv_projs
+    std::vector<float> qkv((size_t)m->NQKV * H);
+    std::memcpy(qkv.data(), wq, (size_t)m->QD * H * 4);
+    std::memcpy(qkv.data() + (size_t)m->QD * H, wk, (size_t)m->KD * H * 4);
+    std::memcpy(qkv.data() + (size_t)(m->QD + m->KD) * H, wv, (size_t)m->KD * H * 4);
+    SA_RC(upload_bf16(L.wqkv, qkv.data(), qkv.size(), st));
+    SA_RC(upload_bf16(L.wo, wo, H * m->QD, st));
+    // gate/up interleaved in blocks of 32 rows: [gate 32b..32b+31 ; up 32b..32b+31]
+    std::vector<float> gu(2 * I * H);
+    for (size_t b = 0; b < I / 32; ++b) {
+        std::memcpy(gu.data() + (2 * b) * 32 * H, w_gate + b * 32 * H, 32 * H * 4);
+        std::memcpy(gu.data() + (2 * b + 1) * 32 * H, w_up + b * 32 * H, 32 * H * 4);
+    }
+    SA_RC(upload_bf16(L.wgu, gu.data(), gu.size(), st));
+    SA_RC(upload_bf16(L.wd, w_down, H * I, st));
+    m->loaded_layer[layer] = true;
+    return SA_OK;
+}
+
+SA_API int sa_qwen3_reset(sa_qwen3* m) {
+    clear_error();
+    SA_CHECK_ARG(m, "sa_qwen3_reset: null model");
+    m->cache_len = 0;   // rows past cache_len are never read; no zeroing needed
+    return SA_OK;
+}
+
+SA_API int sa_qwen3_cache_len(sa_qwen3* m) { return m ? m->cache_len : -1; }
+
+SA_API int sa_qwen3_forward(sa_qwen3* m, const int64_t* ids, int S, int use_cache, float* logits, int logits_mode,
+                            unsigned flags) {
+    clear_error();
+    SA_CHECK_ARG(m && ids, "sa_qwen3_forward: null argument");
+    SA_CHECK_ARG(S >= 1, "sa_qwen3_forward: S = %d", S);
+    SA_CHECK_ARG(logits_mode >= 0 && logits_mode <= 2, "sa_qwen3_forward: logits_mode %d", logits_mode);
+    SA_CHECK_ARG(logits_mode == 2 || logits, "sa_qwen3_forward: logits is NULL");
+    SA_CHECK_ARG(m->loaded_embed, "sa_qwen3_forward: embedding not loaded");
+    for (int l = 0; l < m->c.n_layers; ++l)
+        SA_CHECK_ARG(m->loaded_layer[l], "sa_qwen3_forward: layer %d not loaded", l);
+    DeviceGuard guard(m->ctx->device);
+    const int pos0 = use_cache ? m->cache_len : 0;
+    if (pos0 + S > m->c.max_seq)
+        return set_error(SA_ERR_FULL, "KV cache full, cannot append %d tokens at %d (max_seq %d)", S, pos0,
+                         m->c.max_seq);
+    const bool host = flags & SA_HOST_PTRS;
+    if (host)
+        for (int s = 0; s < S; ++s)
+            if (ids[s] < 0 || ids[s] >= m->c.vocab)
+                return set_error(SA_ERR_RANGE, "Embedding index out of range: ids[%d] = %lld", s, (long long)ids[s]);
+    SA_RC(ensure_acts(m, S));
+    cudaStream_t st = m->ctx->stream;
+    SA_CUDA_TRY(cudaMemcpyAsync(m->ids, ids, (size_t)S * 8, host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, st));
+    SA_RC(run_layers(m, S, pos0));
+    if (use_cache) m->cache_len = pos0 + S;
+    if (logits_mode != 2) {
+        const int r0 = logits_mode == 1 ? S - 1 : 0, n = logits_mode == 1 ? 1 : S;
+        SA_RC(run_head(m, r0, n));
+        SA_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, (size_t)n * m->c.vocab * 4,
+                                    host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, st));
+    }
+    if (host) return sync_and_check(m->ctx);
+    return SA_OK;
+}
+
+SA_API int sa_qwen3_generate(sa_qwen3* m, const int64_t* prompt, int S, int n_new, int64_t* out_tokens,
+                             unsigned flags) {
+    clear_error();
+    SA_CHECK_ARG(m && prompt && out_tokens && S >= 1 && n_new >= 0, "sa_qwen3_generate: bad argument");
+    DeviceGuard guard(m->ctx->device);
+    if (m->cache_len + S + n_new > m->c.max_seq + 1)
+        return set_error(SA_ERR_FULL, "KV cache full: %d + %d prompt + %d new > max_seq %d", m->cache_len, S, n_new,
+                         m->c.max_seq);
+    const bool host = flags & SA_HOST_PTRS;
+    if (host)
+        for (int s = 0; s < S; ++s)
+            if (prompt[s] < 0 || prompt[s] >= m->c.vocab)
+                return set_error(SA_ERR_RANGE, "Embedding index out of range: prompt[%d]", s);
+    SA_RC(ensure_acts(m, S));
+    cudaStream_t st = m->ctx->stream;
+    int64_t* toks = nullptr;
+    SA_RC(dalloc(&toks, (size_t)std::max(n_new, 1)));
+    int rc = SA_OK;
+    do {
+        if (cudaMemcpyAsync(m->ids, prompt, (size_t)S * 8, host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice,
+                            st) != cudaSuccess) { rc = set_error(SA_ERR_CUDA, "copy prompt"); break; }
+        const int pos0 = m->cache_len;
+        if ((rc = run_layers(m, S, pos0))) break;
+        m->cache_len = pos0 + S;
+        if ((rc = run_head(m, S - 1, 1))) break;
+        for (int t = 0; t < n_new; ++t) {
+            if ((rc = launch_argmax(st, m->logits, m->c.vocab, toks + t))) break;
+            if (t + 1 == n_new) break;
+            if (cudaMemcpyAsync(m->ids, toks + t, 8, cudaMemcpyDeviceToDevice, st) != cudaSuccess) {
+                rc = set_error(SA_ERR_CUDA, "copy token");
+                break;
+            }
+            if ((rc = run_layers(m, 1, m->cache_len))) break;
+            m->cache_len += 1;
+            if ((rc = run_head(m, 0, 1))) break;
+        }
+        if (rc) break;
+        if (n_new > 0 && cudaMemcpyAsync(out_tokens, toks, (size_t)n_new * 8,
+                                         host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+            rc = set_error(SA_ERR_CUDA, "copy tokens");
+    } while (0);
+    if (!rc) rc = sync_and_check(m->ctx);
+    cudaFree(toks);
+    return rc;
+}

@@ -1,0 +1,43 @@
+// sa_qwen3.h -- internal declarations shared by the Qwen3 translation units.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+// GEMM / GEMV epilogues
+#define QW_EPI_STORE  0   // y = W x
+#define QW_EPI_RESID  1   // y += W x          (residual stream)
+#define QW_EPI_SWIGLU 2   // y_i = silu(g_i) * u_i over [gate(32); up(32)] row blocks
+
+namespace sa {
+
+int gemm_launch(cudaStream_t st, int* status, const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo,
+                long long lda, const __nv_bfloat16* w, int M, int N, int K, int mode, float* C,
+                long long ldc, __nv_bfloat16* out_hi, __nv_bfloat16* out_lo, long long ldo, int splits,
+                float* ws, size_t ws_floats, unsigned* counters, size_t n_counters);
+
+// Multi-query causal attention over a head-major fp32 KV cache: query m of
+// n_q (q at q + m*q_stride, [hq, d]) attends rows [0, T0 + m] of each KV head;
+// out at out + m*o_stride.  One CTA per (query, KV head); defined in
+// sa_decode.cu.
+int decode_multi_launch(cudaStream_t st, int* status, const float* q, long long q_stride, const float* k,
+                        const float* v, long long kv_head_stride, int T0, int n_q, int d, int hq, int hkv,
+                        float scale, float* out, long long o_stride);
+
+// element-wise / GEMV launchers (sa_qwen3_kernels.cu)
+int launch_embedding(cudaStream_t st, const int64_t* ids, int M, const __nv_bfloat16* E, int V, int H, float* x,
+                     int* status);
+int launch_rmsnorm_hilo(cudaStream_t st, const float* x, const float* w, int M, int H, float eps,
+                        __nv_bfloat16* hi, __nv_bfloat16* lo);
+int launch_rmsnorm_f32(cudaStream_t st, const float* x, const float* w, int M, int H, float eps, float* y);
+int launch_split_hilo(cudaStream_t st, const float* x, size_t n, __nv_bfloat16* hi, __nv_bfloat16* lo);
+int launch_rope_table(cudaStream_t st, int n_pos, int D, float theta, float* cos_t, float* sin_t);
+int launch_qknorm_rope_append(cudaStream_t st, const float* qkv, int M, int hq, int hkv, const float* qn,
+                              const float* kn, const float* cos_t, const float* sin_t, int pos0, float* q_out,
+                              float* kc, float* vc, int max_seq);
+int launch_gemv(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, int N_out, int K, const float* x,
+                const float* nw, float eps, float* y, int num_sms);
+int launch_argmax(cudaStream_t st, const float* v, int n, int64_t* out);
+
+}  // namespace sa

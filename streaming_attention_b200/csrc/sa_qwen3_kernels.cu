@@ -1,0 +1,317 @@
+// sa_qwen3_kernels.cu -- the Qwen3 layer kernels other than the tensor-core
+// GEMM and the attention: embedding, RMSNorm, QK-norm + RoPE + KV-cache
+// append, the decode GEMVs with fused prologue/epilogues, and argmax.
+//
+// Numerics follow the reference's fp32 arithmetic (tensor_cpp/src/ops.cpp,
+// qwen3_ops.cpp): fp32 activations and residual stream, weights in bf16
+// (exact for bf16-representable weights), RMSNorm eps inside the sqrt,
+// rotate-half RoPE with the reference's fp32 inverse-frequency table.
+#include <cuda_bf16.h>
+#include <cmath>
+
+#include "sa_internal.h"
+#include "sa_ptx.cuh"
+#include "sa_qwen3.h"
+#include <algorithm>
+
+namespace sa {
+namespace qk {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Block-wide sum for blockDim.x <= 1024; `red` holds 32 floats.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[w] = v;
+    __syncthreads();
+    float t = (threadIdx.x < (blockDim.x + 31) / 32) ? red[threadIdx.x] : 0.f;
+    if (w == 0) t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = t;
+    __syncthreads();
+    return red[0];
+}
+
+// ---- embedding (ops.cpp:278-309): x[m, :] = E[id_m, :] ---------------------
+__global__ void embedding_kernel(const int64_t* ids, int M, const __nv_bfloat16* E, int V, int H, float* x,
+                                 int* status) {
+    const int m = blockIdx.x;
+    const int64_t id = ids[m];
+    const bool ok = id >= 0 && id < V;
+    if (!ok && threadIdx.x == 0) atomicExch(status, SA_STATUS_BAD_INDEX);
+    for (int i = threadIdx.x; i < H; i += blockDim.x)
+        x[(size_t)m * H + i] = ok ? __bfloat162float(E[(size_t)id * H + i]) : 0.f;
+}
+
+// ---- RMSNorm (ops.cpp:375-418) to the two bf16 GEMM operand terms ---------
+__global__ void rmsnorm_hilo_kernel(const float* x, const float* w, int H, float eps, __nv_bfloat16* hi,
+                                    __nv_bfloat16* lo) {
+    __shared__ float red[32];
+    const int m = blockIdx.x;
+    const float* xr = x + (size_t)m * H;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) ss += xr[i] * xr[i];
+    ss = block_sum(ss, red);
+    const float rms = sqrtf(ss / (float)H + eps);
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+        const float y = (xr[i] / rms) * w[i];
+        const __nv_bfloat16 h = __float2bfloat16_rn(y);
+        hi[(size_t)m * H + i] = h;
+        lo[(size_t)m * H + i] = __float2bfloat16_rn(y - __bfloat162float(h));
+    }
+}
+
+// RMSNorm to fp32 (the final norm before the lm_head GEMV).
+__global__ void rmsnorm_f32_kernel(const float* x, const float* w, int H, float eps, float* y) {
+    __shared__ float red[32];
+    const int m = blockIdx.x;
+    const float* xr = x + (size_t)m * H;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) ss += xr[i] * xr[i];
+    ss = block_sum(ss, red);
+    const float rms = sqrtf(ss / (float)H + eps);
+    for (int i = threadIdx.x; i < H; i += blockDim.x) y[(size_t)m * H + i] = (xr[i] / rms) * w[i];
+}
+
+// fp32 -> (hi, lo) bf16 split of an activation for the tensor-core GEMM.
+__global__ void split_hilo_kernel(const float* x, size_t n, __nv_bfloat16* hi, __nv_bfloat16* lo) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const float y = x[i];
+        const __nv_bfloat16 h = __float2bfloat16_rn(y);
+        hi[i] = h;
+        lo[i] = __float2bfloat16_rn(y - __bfloat162float(h));
+    }
+}
+
+// ---- RoPE tables (qwen3_ops.cpp:70-104): cos/sin[pos, i], i < D/2 ----------
+__global__ void rope_table_kernel(int n_pos, int D, float theta, float* cos_t, float* sin_t) {
+    const int half = D / 2;
+    const size_t n = (size_t)n_pos * half;
+    for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < n; idx += (size_t)gridDim.x * blockDim.x) {
+        const int p = (int)(idx / half), i = (int)(idx % half);
+        const float inv = 1.0f / powf(theta, (float)i / (float)D);
+        const float ang = (float)p * inv;
+        cos_t[idx] = cosf(ang);
+        sin_t[idx] = sinf(ang);
+    }
+}
+
+// ---- QK-norm + RoPE + cache append ----------------------------------------
+// qkv [M, (hq + 2 hkv) * 128] fp32 from the QKV projection (rows = tokens).
+// One warp per (token, head); lane l holds elements 4l..4l+3 of the head.
+// Q heads: RMS over the head (eps 1e-6 inside the sqrt, qwen3_ops.cpp:355-369)
+// times q_norm, then rotate-half RoPE at position pos0 + m
+// (qwen3_ops.cpp:110-188) -> q_out [M, hq, 128].  K heads: the same with
+// k_norm -> K cache row pos0 + m.  V heads: copied to the V cache.
+__global__ void qknorm_rope_append_kernel(const float* qkv, int M, int hq, int hkv, const float* qn,
+                                          const float* kn, const float* cos_t, const float* sin_t, int pos0,
+                                          float* q_out, float* kc, float* vc, int max_seq) {
+    constexpr int D = 128;
+    const int lane = threadIdx.x & 31;
+    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int nh = hq + 2 * hkv;
+    if (gw >= M * nh) return;
+    const int m = gw / nh, h = gw % nh;
+    const int pos = pos0 + m;
+    const float* src = qkv + (size_t)m * nh * D + (size_t)h * D;
+    float4 v4 = *reinterpret_cast<const float4*>(src + 4 * lane);
+    float e[4] = {v4.x, v4.y, v4.z, v4.w};
+    if (h >= hq + hkv) {  // V head
+        float* dst = vc + ((size_t)(h - hq - hkv) * max_seq + pos) * D;
+        *reinterpret_cast<float4*>(dst + 4 * lane) = v4;
+        return;
+    }
+    const float* nw = h < hq ? qn : kn;
+    float ss = e[0] * e[0] + e[1] * e[1] + e[2] * e[2] + e[3] * e[3];
+    ss = warp_sum(ss);
+    const float rms = sqrtf(ss / (float)D + 1e-6f);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) e[j] = (e[j] / rms) * nw[4 * lane + j];
+    // rotate-half: element i pairs with i + 64 (lanes l and l ^ 16)
+    float p[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) p[j] = __shfl_xor_sync(0xffffffffu, e[j], 16);
+    const bool first = lane < 16;
+    const float* cr = cos_t + (size_t)pos * (D / 2);
+    const float* sr = sin_t + (size_t)pos * (D / 2);
+    float o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int i = (4 * lane + j) & (D / 2 - 1);
+        const float c = cr[i], s = sr[i];
+        // first half: x1*c + (-x2)*s ; second half: x2*c + x1*s
+        o[j] = first ? e[j] * c + (-p[j]) * s : e[j] * c + p[j] * s;
+    }
+    const float4 r4 = make_float4(o[0], o[1], o[2], o[3]);
+    if (h < hq) {
+        *reinterpret_cast<float4*>(q_out + ((size_t)m * hq + h) * D + 4 * lane) = r4;
+    } else {
+        float* dst = kc + ((size_t)(h - hq) * max_seq + pos) * D;
+        *reinterpret_cast<float4*>(dst + 4 * lane) = r4;
+    }
+}
+
+// ---- decode GEMV: y = W x with optional RMSNorm prologue --------------------
+// W [N, K] bf16 row-major, x [K] fp32.  8 warps per CTA; a warp produces one
+// output at a time, each lane streaming 16-byte chunks of the row(s).
+template <int MODE, bool NORM>
+__global__ void __launch_bounds__(256) gemv_kernel(const __nv_bfloat16* __restrict__ W, int N_out, int K,
+                                                   const float* __restrict__ x, const float* __restrict__ nw,
+                                                   float eps, float* __restrict__ y) {
+    extern __shared__ float xs[];          // [K]
+    __shared__ float red[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (NORM) {
+        float ss = 0.f;
+        for (int i = threadIdx.x; i < K; i += blockDim.x) ss += x[i] * x[i];
+        ss = block_sum(ss, red);
+        const float rms = sqrtf(ss / (float)K + eps);
+        for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = (x[i] / rms) * nw[i];
+    } else {
+        for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = x[i];
+    }
+    __syncthreads();
+    const int nchunk = K / 8;                      // 16-byte chunks per row
+    for (int n = blockIdx.x * 8 + warp; n < N_out; n += gridDim.x * 8) {
+        int r0 = n, r1 = -1;
+        if (MODE == QW_EPI_SWIGLU) {
+            r0 = (n / 32) * 64 + (n % 32);
+            r1 = r0 + 32;
+        }
+        float acc0 = 0.f, acc1 = 0.f;
+        const uint4* w0 = reinterpret_cast<const uint4*>(W + (size_t)r0 * K);
+        const uint4* w1 = reinterpret_cast<const uint4*>(W + (size_t)(MODE == QW_EPI_SWIGLU ? r1 : r0) * K);
+#pragma unroll 4
+        for (int c = lane; c < nchunk; c += 32) {
+            const uint4 a = __ldg(w0 + c);
+            uint4 b;
+            if (MODE == QW_EPI_SWIGLU) b = __ldg(w1 + c);
+            const float4 xa = *reinterpret_cast<const float4*>(xs + c * 8);
+            const float4 xb = *reinterpret_cast<const float4*>(xs + c * 8 + 4);
+            const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+            const uint32_t wa[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                acc0 = fmaf(__uint_as_float(wa[j] << 16), xv[2 * j], acc0);
+                acc0 = fmaf(__uint_as_float(wa[j] & 0xffff0000u), xv[2 * j + 1], acc0);
+            }
+            if (MODE == QW_EPI_SWIGLU) {
+                const uint32_t wb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    acc1 = fmaf(__uint_as_float(wb[j] << 16), xv[2 * j], acc1);
+                    acc1 = fmaf(__uint_as_float(wb[j] & 0xffff0000u), xv[2 * j + 1], acc1);
+                }
+            }
+        }
+        acc0 = warp_sum(acc0);
+        if (MODE == QW_EPI_SWIGLU) acc1 = warp_sum(acc1);
+        if (lane == 0) {
+            if (MODE == QW_EPI_SWIGLU) y[n] = (acc0 / (1.f + expf(-acc0))) * acc1;
+            else if (MODE == QW_EPI_RESID) y[n] += acc0;
+            else y[n] = acc0;
+        }
+    }
+}
+
+// ---- argmax (ops.cpp:213-272): first index of the maximum ------------------
+__global__ void argmax_kernel(const float* __restrict__ v, int n, int64_t* out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float x = v[i];
+        if (x > best) { best = x; bi = i; }   // ascending i: keeps the first maximum
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+    }
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    if (lane == 0) { sv[w] = best; si[w] = bi; }
+    __syncthreads();
+    if (w == 0) {
+        best = lane < (int)(blockDim.x / 32) ? sv[lane] : -INFINITY;
+        bi = lane < (int)(blockDim.x / 32) ? si[lane] : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+        }
+        if (lane == 0) *out = bi == 0x7fffffff ? 0 : bi;
+    }
+}
+
+}  // namespace qk
+
+// ---- launchers --------------------------------------------------------------
+int launch_embedding(cudaStream_t st, const int64_t* ids, int M, const __nv_bfloat16* E, int V, int H, float* x,
+                     int* status) {
+    qk::embedding_kernel<<<M, 256, 0, st>>>(ids, M, E, V, H, x, status);
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
+int launch_rmsnorm_hilo(cudaStream_t st, const float* x, const float* w, int M, int H, float eps,
+                        __nv_bfloat16* hi, __nv_bfloat16* lo) {
+    qk::rmsnorm_hilo_kernel<<<M, 256, 0, st>>>(x, w, H, eps, hi, lo);
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
+int launch_rmsnorm_f32(cudaStream_t st, const float* x, const float* w, int M, int H, float eps, float* y) {
+    qk::rmsnorm_f32_kernel<<<M, 256, 0, st>>>(x, w, H, eps, y);
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
+int launch_split_hilo(cudaStream_t st, const float* x, size_t n, __nv_bfloat16* hi, __nv_bfloat16* lo) {
+    const int grid = (int)std::min<size_t>((n + 255) / 256, 4096);
+    qk::split_hilo_kernel<<<grid, 256, 0, st>>>(x, n, hi, lo);
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
+int launch_rope_table(cudaStream_t st, int n_pos, int D, float theta, float* cos_t, float* sin_t) {
+    const size_t n = (size_t)n_pos * (D / 2);
+    const int grid = (int)std::min<size_t>((n + 255) / 256, 4096);
+    qk::rope_table_kernel<<<grid, 256, 0, st>>>(n_pos, D, theta, cos_t, sin_t);
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
+int launch_qknorm_rope_append(cudaStream_t st, const float* qkv, int M, int hq, int hkv, const float* qn,
+                              const float* kn, const float* cos_t, const float* sin_t, int pos0, float* q_out,
+                              float* kc, float* vc, int max_seq) {
+    const int warps = M * (hq + 2 * hkv);
+    qk::qknorm_rope_append_kernel<<<(warps + 7) / 8, 256, 0, st>>>(qkv, M, hq, hkv, qn, kn, cos_t, sin_t, pos0,
+                                                                   q_out, kc, vc, max_seq);
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
+int launch_gemv(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, int N_out, int K, const float* x,
+                const float* nw, float eps, float* y, int num_sms) {
+    SA_CHECK_ARG(K % 8 == 0, "gemv: K=%d", K);
+    const size_t smem = (size_t)K * sizeof(float);
+    int grid = (N_out + 7) / 8;
+    const int cap = num_sms * 8;
+    if (grid > cap) grid = cap;
+#define SA_GEMV(MODE, NORM) qk::gemv_kernel<MODE, NORM><<<grid, 256, smem, st>>>(W, N_out, K, x, nw, eps, y)
+    if (mode == QW_EPI_STORE) { if (norm) SA_GEMV(QW_EPI_STORE, true); else SA_GEMV(QW_EPI_STORE, false); }
+    else if (mode == QW_EPI_RESID) { if (norm) SA_GEMV(QW_EPI_RESID, true); else SA_GEMV(QW_EPI_RESID, false); }
+    else { if (norm) SA_GEMV(QW_EPI_SWIGLU, true); else SA_GEMV(QW_EPI_SWIGLU, false); }
+#undef SA_GEMV
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
+int launch_argmax(cudaStream_t st, const float* v, int n, int64_t* out) {
+    qk::argmax_kernel<<<1, 1024, 0, st>>>(v, n, out);
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
+
+}  // namespace sa

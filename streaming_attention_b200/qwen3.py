@@ -1,0 +1,120 @@
+"""Qwen3 forward on the GPU (sa_qwen3_* of include/sa_cuda.h).
+
+Mirrors the reference's model API: ``forward`` is ``qwen3_forward`` /
+``qwen3_forward_with_cache`` (tensor_cpp/include/tensor_cpp/qwen3_ops.h:242-333),
+``reset`` / ``cache_len`` are the ``KVCache`` calls (kv_cache.h), ``generate``
+is the greedy decode loop of benchmark_qwen3 with the argmax on the device.
+Weights come as fp32 host arrays in the reference's shapes.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from ._capi import SA_HOST_PTRS, Context, check, default_context, lib
+
+
+class Qwen3Config(C.Structure):
+    """sa_qwen3_config."""
+    _fields_ = [("vocab", C.c_int), ("hidden", C.c_int), ("n_layers", C.c_int), ("hq", C.c_int),
+                ("hkv", C.c_int), ("head_dim", C.c_int), ("inter", C.c_int), ("eps", C.c_float),
+                ("theta", C.c_float), ("max_seq", C.c_int)]
+
+
+# Qwen3-0.6B (SURVEY/BASELINE configs[3], configs[4])
+QWEN3_0_6B = dict(vocab=151936, hidden=1024, n_layers=28, hq=16, hkv=8, head_dim=128, inter=3072,
+                  eps=1e-6, theta=1e6)
+
+# order of one layer's tensors in a packed per-layer fp32 block
+LAYER_FIELDS = ("in_norm", "q", "k", "v", "q_norm", "k_norm", "o", "post_norm", "gate", "up", "down")
+
+
+def layer_shapes(cfg: dict) -> list:
+    H, D, I = cfg["hidden"], cfg["head_dim"], cfg["inter"]
+    QD, KD = cfg["hq"] * D, cfg["hkv"] * D
+    return [(H,), (QD, H), (KD, H), (KD, H), (D,), (D,), (H, QD), (H,), (I, H), (I, H), (H, I)]
+
+
+def unpack_layer(cfg: dict, flat: np.ndarray) -> dict:
+    """Split one packed layer block into named arrays (views)."""
+    out, off = {}, 0
+    for name, shp in zip(LAYER_FIELDS, layer_shapes(cfg)):
+        n = int(np.prod(shp))
+        out[name] = flat[off:off + n].reshape(shp)
+        off += n
+    assert off == flat.size, (off, flat.size)
+    return out
+
+
+def _fp(a: np.ndarray):
+    return a.ctypes.data_as(C.POINTER(C.c_float))
+
+
+class Qwen3:
+    def __init__(self, cfg: dict, max_seq: int = 4096, ctx: Context | None = None):
+        self.cfg = dict(cfg)
+        self.ctx = ctx or default_context(0)
+        c = Qwen3Config(vocab=cfg["vocab"], hidden=cfg["hidden"], n_layers=cfg["n_layers"],
+                        hq=cfg["hq"], hkv=cfg["hkv"], head_dim=cfg["head_dim"], inter=cfg["inter"],
+                        eps=cfg.get("eps", 1e-6), theta=cfg.get("theta", 1e6), max_seq=max_seq)
+        h = C.c_void_p()
+        check(lib().sa_qwen3_create(self.ctx.h, C.byref(c), C.byref(h)))
+        self.h = h
+        self.max_seq = max_seq
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().sa_qwen3_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- weights ------------------------------------------------------------
+    def set_embed(self, embed, final_norm, lm_head=None):
+        e = np.ascontiguousarray(embed, np.float32)
+        n = np.ascontiguousarray(final_norm, np.float32)
+        lm = None if lm_head is None or lm_head is embed else np.ascontiguousarray(lm_head, np.float32)
+        check(lib().sa_qwen3_set_embed(self.h, _fp(e), _fp(n), _fp(lm) if lm is not None else None))
+
+    def set_layer(self, i: int, w: dict):
+        a = [np.ascontiguousarray(w[k], np.float32) for k in LAYER_FIELDS]
+        check(lib().sa_qwen3_set_layer(self.h, i, *[_fp(x) for x in a]))
+
+    def load(self, weights: dict):
+        """weights: {"embed", "final_norm", "lm_head", "layers"} with "layers" the
+        packed per-layer fp32 blocks (LAYER_FIELDS order) concatenated."""
+        self.set_embed(weights["embed"], weights["final_norm"], weights.get("lm_head"))
+        flat = np.ascontiguousarray(weights["layers"], np.float32)
+        per = flat.size // self.cfg["n_layers"]
+        for i in range(self.cfg["n_layers"]):
+            self.set_layer(i, unpack_layer(self.cfg, flat[i * per:(i + 1) * per]))
+
+    # -- forward ------------------------------------------------------------
+    def reset(self):
+        check(lib().sa_qwen3_reset(self.h))
+
+    @property
+    def cache_len(self) -> int:
+        return lib().sa_qwen3_cache_len(self.h)
+
+    def forward(self, ids, use_cache: bool = False, logits: str = "all"):
+        ids = np.ascontiguousarray(ids, np.int64).ravel()
+        S = ids.size
+        mode = {"all": 0, "last": 1, "none": 2}[logits]
+        out = None if mode == 2 else np.empty((S if mode == 0 else 1, self.cfg["vocab"]), np.float32)
+        check(lib().sa_qwen3_forward(self.h, ids.ctypes.data_as(C.POINTER(C.c_int64)), S,
+                                     1 if use_cache else 0,
+                                     _fp(out) if out is not None else None, mode, SA_HOST_PTRS))
+        return out
+
+    def generate(self, prompt, n_new: int) -> np.ndarray:
+        prompt = np.ascontiguousarray(prompt, np.int64).ravel()
+        out = np.empty(max(n_new, 1), np.int64)
+        check(lib().sa_qwen3_generate(self.h, prompt.ctypes.data_as(C.POINTER(C.c_int64)), prompt.size,
+                                      n_new, out.ctypes.data_as(C.POINTER(C.c_int64)), SA_HOST_PTRS))
+        return out[:n_new]
