@@ -554,6 +554,151 @@ def run_prefill(args):
     return 0
 
 
+# ---------------------------------------------------------------- Qwen3
+Q3_PROMPT, Q3_GEN = 128, 100
+Q3_WORKLOAD = ("configs[3]/[4] Qwen3-0.6B random-init (bf16-exact N(0,0.02) weights, tied lm_head), "
+               "batch 1: prefill of a 128-token prompt (logits for all positions, as qwen3_forward); "
+               "decode of 100 greedy tokens after a 128-token prompt with the KV cache")
+
+
+def measure_qwen3(ctx, dev, stream, steps, warmup, weights=None, long_prompt=False):
+    """Returns dict with prefill / decode tok/s (device-resident and e2e)."""
+    import ctypes as C
+    import torch
+    import streaming_attention_b200 as sa
+    from streaming_attention_b200 import _capi
+    cfg = sa.QWEN3_0_6B
+    if weights is None:
+        weights = sa.qwen3.random_weights(cfg, SEED)
+    max_seq = 4096 + Q3_GEN + 8 if long_prompt else 512
+    m = sa.Qwen3(cfg, max_seq=max_seq, ctx=ctx)
+    m.load(weights)
+    L = _capi.lib()
+    rng = __import__("numpy").random.default_rng(SEED)
+    ids = rng.integers(0, cfg["vocab"], Q3_PROMPT).astype("int64")
+    ids_d = torch.from_numpy(ids).to(dev)
+    logits_d = torch.empty(Q3_PROMPT, cfg["vocab"], device=dev)
+    P = lambda t: C.c_void_p(t.data_ptr())
+    out = {}
+    with torch.cuda.stream(stream):
+        ctx.set_stream(stream.cuda_stream)
+        # ---- prefill, inputs resident (device ids -> device logits)
+        def pf():
+            _capi.check(L.sa_qwen3_forward(m.h, C.cast(P(ids_d), C.POINTER(C.c_int64)), Q3_PROMPT, 0,
+                                           C.cast(P(logits_d), C.POINTER(C.c_float)), 0, 0))
+        for _ in range(warmup):
+            pf()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            pf()
+        e1.record(stream)
+        e1.synchronize()
+        pms = e0.elapsed_time(e1) / steps
+        out["prefill_tok_s"] = Q3_PROMPT / (pms / 1e3)
+        out["prefill_ms"] = pms
+        # ---- prefill e2e: pinned host ids in, pinned host logits [128, V] out,
+        # through the C ABI with SA_HOST_PTRS (blocking call)
+        ids_h = torch.from_numpy(ids).pin_memory()
+        logits_h = torch.empty(Q3_PROMPT, cfg["vocab"]).pin_memory()
+        def pf_host():
+            _capi.check(L.sa_qwen3_forward(m.h, C.cast(P(ids_h), C.POINTER(C.c_int64)), Q3_PROMPT, 0,
+                                           C.cast(P(logits_h), C.POINTER(C.c_float)), 0,
+                                           _capi.SA_HOST_PTRS))
+        pf_host()
+        t0 = time.perf_counter()
+        ne = max(2, min(steps, 5))
+        for _ in range(ne):
+            pf_host()
+        out["prefill_e2e_tok_s"] = Q3_PROMPT * ne / (time.perf_counter() - t0)
+        # ---- decode: generate(101) - generate(1) = 100 decode steps (same prefill)
+        def gen(n, prompt):
+            m.reset()
+            t0 = time.perf_counter()
+            toks = m.generate(prompt, n)
+            return time.perf_counter() - t0, toks
+        for p_len, key in ([(Q3_PROMPT, "decode")] + ([(4096, "decode_4096")] if long_prompt else [])):
+            prompt = rng.integers(0, cfg["vocab"], p_len).astype("int64")
+            gen(Q3_GEN + 1, prompt)                       # warm-up
+            reps = 3
+            t_long = min(gen(Q3_GEN + 1, prompt)[0] for _ in range(reps))
+            t_short = min(gen(1, prompt)[0] for _ in range(reps))
+            dt = max(t_long - t_short, 1e-9)
+            out[f"{key}_tok_s"] = Q3_GEN / dt
+            out[f"{key}_ms_per_token"] = dt / Q3_GEN * 1e3
+    m.close()
+    return out, weights
+
+
+def cpu_qwen3_baseline(weights, budget_tokens=16):
+    """The reference's AVX2 Qwen3 forward (qwen3_ops_avx.cpp:383) on the host:
+    prefill of a bounded prompt, and a few cached decode steps."""
+    import numpy as np
+    from oracle.oracle import Qwen3Cfg, Reference
+    import streaming_attention_b200 as sa
+    c = sa.QWEN3_0_6B
+    cfg = Qwen3Cfg(**{k: c[k] for k in ("vocab", "hidden", "n_layers", "hq", "hkv", "head_dim", "inter",
+                                        "eps", "theta")})
+    R = Reference()
+    m = R.qwen3(cfg, weights)
+    ids = np.random.default_rng(SEED).integers(0, cfg.vocab, budget_tokens).astype(np.int64)
+    t0 = time.perf_counter()
+    m.forward(ids, method=1)
+    t_pf = time.perf_counter() - t0
+    kv = m.new_cache(budget_tokens + 8)
+    m.forward_cached(kv, ids, method=1)
+    steps = 3
+    t0 = time.perf_counter()
+    nxt = 0
+    for _ in range(steps):
+        lg = m.forward_cached(kv, np.array([nxt], np.int64), method=1)
+        nxt = int(np.argmax(lg[-1]))
+    t_dec = time.perf_counter() - t0
+    m.free_cache(kv)
+    m.close()
+    return {"prefill_tok_s": budget_tokens / t_pf, "decode_tok_s": steps / t_dec,
+            "cores": os.cpu_count(), "kind": "reference",
+            "sample": f"avx2::qwen3_forward_avx on a {budget_tokens}-token prompt; "
+                      f"{steps} cached decode steps (qwen3_forward_avx_with_cache) after it; "
+                      f"{os.cpu_count()} OpenMP threads"}
+
+
+def run_qwen3(args):
+    import torch
+    import streaming_attention_b200 as sa
+    local = env_int("LOCAL_RANK", 0)
+    if env_int("RANK", 0) != 0:
+        return 0
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    ctx = sa.Context(local)
+    stream = torch.cuda.Stream(dev)
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    clocks = ClockSampler(vis.split(",")[local].strip() if vis else str(local))
+    clocks.start()
+    res, weights = measure_qwen3(ctx, dev, stream, args.steps, args.warmup, long_prompt=args.long_prompt)
+    clk = clocks.stop()
+    line = {
+        "metric": "Qwen3-0.6B tok/s (prefill)", "value": round(res["prefill_tok_s"], 1), "unit": "tok/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(res["prefill_ms"], 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 weights, fp32 activations", "data": "synthetic",
+        "config": {"workload": Q3_WORKLOAD},
+        "decode": {k: round(v, 3) for k, v in res.items() if k.startswith("decode")},
+        "e2e": {"value": round(res["prefill_e2e_tok_s"], 1), "unit": "tok/s",
+                "h2d_bytes_per_step": Q3_PROMPT * 8, "d2h_bytes_per_step": Q3_PROMPT * 151936 * 4},
+        "clocks": clk,
+    }
+    if not args.no_cpu:
+        try:
+            line["cpu_baseline"] = cpu_qwen3_baseline(weights)
+        except Exception as e:
+            line["cpu_baseline"] = {"value": None, "sample": f"unavailable: {e}"}
+    print(json.dumps(line), flush=True)
+    ctx.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -561,9 +706,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--long-prompt", action="store_true",
+                    help="qwen3 workload: also decode after a 4096-token prompt (configs[4] second run)")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the extra (non-headline) measurements in the decode line")
-    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "qwen3"], default="decode",
                     help="decode: the headline configs[1] line; prefill: configs[2] causal "
                          "prefill on tensor cores (TFLOP/s)")
     ap.add_argument("--profile", action="store_true",
@@ -575,6 +722,8 @@ def main():
         args.warmup = 3
     if args.workload == "prefill":
         return run_prefill(args)
+    if args.workload == "qwen3":
+        return run_qwen3(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -118,3 +118,31 @@ class Qwen3:
         check(lib().sa_qwen3_generate(self.h, prompt.ctypes.data_as(C.POINTER(C.c_int64)), prompt.size,
                                       n_new, out.ctypes.data_as(C.POINTER(C.c_int64)), SA_HOST_PTRS))
         return out[:n_new]
+
+
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    """Round fp32 values to the nearest bf16 (ties to even), kept as fp32."""
+    x = np.ascontiguousarray(x, np.float32)
+    u = x.view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
+    return r.view(np.float32).reshape(x.shape)
+
+
+def random_weights(cfg: dict, seed: int, std: float = 0.02) -> dict:
+    """Synthetic random-init weights for benchmarking (no checkpoint is
+    available): matrices N(0, std) rounded to bf16, norm gains 1, lm_head tied
+    to the embedding -- the initialisation BASELINE.json's Qwen3 configs name.
+    Returns the packed layout ``Qwen3.load`` takes."""
+    rng = np.random.default_rng(seed)
+    shapes = layer_shapes(cfg)
+    parts = []
+    for _ in range(cfg["n_layers"]):
+        for name, shp in zip(LAYER_FIELDS, shapes):
+            if len(shp) == 1:
+                parts.append(np.ones(shp, np.float32))
+            else:
+                parts.append(bf16_round(rng.standard_normal(shp, dtype=np.float32) * std).ravel())
+    layers = np.concatenate([p.ravel() for p in parts])
+    embed = bf16_round(rng.standard_normal((cfg["vocab"], cfg["hidden"]), dtype=np.float32) * std)
+    return {"embed": embed, "layers": layers, "final_norm": np.ones(cfg["hidden"], np.float32),
+            "lm_head": embed}
