@@ -190,32 +190,16 @@ def streaming_attention_mpi_cuda(Q_local, K_local, V_local, T_local: int, T_glob
                                  block_size: int, group=None, ctx: Context | None = None):
     """streaming_attention_mpi_simple (attention/src/streaming_mpi.cpp:252-309).
 
-    One rank per GPU under torch.distributed: rank 0's query is broadcast,
-    every rank reduces its local KV slice to a partial (m, l, O) on its GPU,
-    the partials are all-gathered (one collective of hq*(d+2) floats), and
-    merged on the device.  As in the reference, rank 0 returns the result and
-    the other ranks return zeros.  Q/K/V are CUDA torch tensors on this
-    rank's device.
+    One rank per GPU under torch.distributed; Q (meaningful on rank 0) and the
+    rank's K/V slice are CUDA torch tensors.  Unscaled scores, as attention.h.
+    Rank 0 returns the d-vector, the other ranks zeros.
     """
-    import torch
-    import torch.distributed as dist
-
-    rank = dist.get_rank(group)
-    world = dist.get_world_size(group)
-    q = Q_local.reshape(1, d).contiguous()
+    from .sequence_parallel import sp_decode
+    q = Q_local.reshape(1, d)
     if q.dtype != K_local.dtype:
         q = q.to(K_local.dtype)
-    dist.broadcast(q, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
     k = K_local.reshape(1, T_local, d)
     v = V_local.reshape(1, T_local, d)
-    m, l, o = attn_decode_partial(q, k, v, 1.0, block_size, ctx)
-    packed = torch.cat([m, l, o.reshape(-1)])
-    gathered = torch.empty(world, packed.numel(), dtype=torch.float32, device=packed.device)
-    dist.all_gather_into_tensor(gathered, packed, group=group)
-    gm = gathered[:, 0:1].contiguous()
-    gl = gathered[:, 1:2].contiguous()
-    go = gathered[:, 2:].reshape(world, 1, d).contiguous()
-    out = attn_merge(gm, gl, go, ctx).reshape(d)
-    if rank != 0:
-        out.zero_()
-    return out
+    pf = lambda q_, k_, v_, s_, b_: attn_decode_partial(q_, k_, v_, s_, b_, ctx)
+    mf = lambda m_, l_, o_: attn_merge(m_, l_, o_, ctx)
+    return sp_decode(q, k, v, 1.0, block_size, group, pf, mf).reshape(d)

@@ -1,0 +1,59 @@
+"""Sequence-parallel decode across 2 GPUs (NCCL), through the C ABI on each
+rank: the KV sequence is split over the ranks, partials are all-gathered and
+merged on the device; rank 0's result must equal the unsharded attention.
+Skipped on boxes with fewer than 2 GPUs."""
+import os
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+pytestmark = pytest.mark.gpu
+
+
+def _worker(rank, world, port, res):
+    import sys
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from datetime import timedelta
+    import torch
+    import torch.distributed as dist
+    import _inputs as I
+    import streaming_attention_b200 as sa
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    hq, hkv, d, T = 16, 8, 128, 20001
+    q, k, v = I.gqa(hq, hkv, T, d, 9)
+    cuts = np.linspace(0, T, world + 1).astype(int)
+    a, b = cuts[rank], cuts[rank + 1]
+    dev = torch.device("cuda", rank)
+    kt = torch.from_numpy(np.ascontiguousarray(k[:, a:b])).to(dev)
+    vt = torch.from_numpy(np.ascontiguousarray(v[:, a:b])).to(dev)
+    qt = torch.from_numpy(q).to(dev) if rank == 0 else torch.zeros(hq, d, device=dev)
+    ctx = sa.Context(rank)
+    from streaming_attention_b200.sequence_parallel import sp_decode
+    pf = lambda q_, k_, v_, s_, b_: sa.attn_decode_partial(q_, k_, v_, s_, b_, ctx)
+    mf = lambda m_, l_, o_: sa.attn_merge(m_, l_, o_, ctx)
+    out = sp_decode(qt, kt, vt, 1 / np.sqrt(d), 64, None, pf, mf)
+    torch.cuda.synchronize(dev)
+    if rank == 0:
+        np.save(res, out.cpu().numpy())
+    dist.barrier(device_ids=[rank])
+    ctx.close()
+    dist.destroy_process_group()
+
+
+def test_sp_decode_two_gpus(tmp_path, oracle):
+    import torch
+    import torch.multiprocessing as mp
+    import _inputs as I
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    res = str(tmp_path / "out.npy")
+    mp.spawn(_worker, args=(2, 29600 + os.getpid() % 200, res), nprocs=2, join=True)
+    q, k, v = I.gqa(16, 8, 20001, 128, 9)
+    ref = oracle.gqa_decode(q, k, v, 64, 1 / np.sqrt(128))
+    np.testing.assert_allclose(np.load(res), ref, atol=1e-4, rtol=0)
