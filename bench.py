@@ -679,6 +679,19 @@ def run_qwen3(args):
     torch.cuda.set_device(dev)
     ctx = sa.Context(local)
     stream = torch.cuda.Stream(dev)
+    if args.profile:
+        # short sequence for ncu: one cache-free 128-token forward, then a
+        # generate of 4 tokens (prefill + 3 captured decode steps)
+        import numpy as np
+        cfg = sa.QWEN3_0_6B
+        m = sa.Qwen3(cfg, max_seq=512, ctx=ctx)
+        m.load(sa.qwen3.random_weights(cfg, SEED))
+        ids = np.random.default_rng(SEED).integers(0, cfg["vocab"], Q3_PROMPT)
+        m.forward(ids, logits="all")
+        m.generate(ids, 4)
+        torch.cuda.synchronize(dev)
+        print(json.dumps({"profile": True, "workload": "qwen3"}), flush=True)
+        return 0
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     clocks = ClockSampler(vis.split(",")[local].strip() if vis else str(local))
     clocks.start()

@@ -28,6 +28,7 @@
 #include "sa_internal.h"
 #include "sa_ptx.cuh"
 #include "sa_qwen3.h"
+#include "sa_tc.cuh"
 
 namespace sa {
 namespace dec {
@@ -60,6 +61,10 @@ struct Args {
     // multi-query launches (gridDim.z > 1): query z reads q + z*q_stride,
     // attends rows [0, T + z) and writes out + z*o_stride (n_splits == 1)
     long long q_stride, o_stride;
+    // when set, the row count is read on the device: T = *len_dev + 1 (the
+    // KV-cache length before the token being decoded, plus that token), so a
+    // captured launch stays valid as the cache grows
+    const int* len_dev;
 };
 
 // Unpack one 16-byte chunk into VEC floats.
@@ -120,7 +125,8 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int kvh = blockIdx.y, split = blockIdx.x, qz = blockIdx.z;
     const int t0 = split * a.rows_per_split;
-    const int nrows = max(0, min(a.T + qz - t0, a.rows_per_split));
+    const int T = a.len_dev ? (*a.len_dev + 1) : a.T;
+    const int nrows = max(0, min(T + qz - t0, a.rows_per_split));
     const int nst = (nrows + SR - 1) / SR;
     const KT* kg = static_cast<const KT*>(a.k) + (size_t)kvh * a.kv_head_stride + (size_t)t0 * D;
     const KT* vg = static_cast<const KT*>(a.v) + (size_t)kvh * a.kv_head_stride + (size_t)t0 * D;
@@ -493,6 +499,7 @@ static int launch_decode(sa_ctx* ctx, int dtype, const void* q, const void* k, c
     a.out = out; a.out_m = out_m; a.out_l = out_l;
     a.status = ctx->status;
     a.q_stride = 0; a.o_stride = 0;
+    a.len_dev = nullptr;
     dec::KernelFn fn = dtype == SA_F32 ? dec::pick<float>(d, hq / hkv) : dec::pick<__nv_bfloat16>(d, hq / hkv);
     SA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::SMEM_BYTES));
     fn<<<dim3(ns, hkv), dec::THREADS, dec::SMEM_BYTES, ctx->stream>>>(a);
@@ -625,10 +632,53 @@ int decode_multi_launch(cudaStream_t st, int* status, const float* q, long long 
     a.out = out; a.out_m = nullptr; a.out_l = nullptr;
     a.status = status;
     a.q_stride = q_stride; a.o_stride = o_stride;
+    a.len_dev = nullptr;
     dec::KernelFn fn = dec::pick<float>(d, hq / hkv);
     SA_CHECK_ARG(fn != nullptr, "decode_multi: hq/hkv=%d d=%d unsupported", hq / hkv, d);
-    SA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::SMEM_BYTES));
+    SA_RC_TRY(set_smem_attr_once((const void*)fn, dec::SMEM_BYTES));
     fn<<<dim3(1, hkv, n_q), dec::THREADS, dec::SMEM_BYTES, st>>>(a);
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
+}  // namespace sa
+
+namespace sa {
+// Split-KV decode whose row count comes from device memory (T = *len_dev + 1)
+// with a split plan fixed for max_T rows: splits past the current length are
+// empty and drop out of the merge.  Scratch (partials, counters) is the
+// caller's, sized by decode_dev_scratch_floats.  Used by the Qwen3 decode
+// step, which is captured once in a CUDA graph and replayed per token.
+size_t decode_dev_scratch_floats(int num_sms, int max_T, int d, int hq, int hkv, int* n_splits) {
+    int ns, rps;
+    plan_splits(num_sms, max_T, hkv, dec::stage_rows(SA_F32, d), &ns, &rps);
+    if (n_splits) *n_splits = ns;
+    return (size_t)hq * ns * (d + 2);
+}
+
+int decode_dev_launch(cudaStream_t st, int* status, int num_sms, const float* q, const float* k, const float* v,
+                      long long kv_head_stride, const int* len_dev, int T_host, int max_T, int d, int hq, int hkv,
+                      float scale, float* out, float* scratch, unsigned* counters) {
+    int ns, rps;
+    plan_splits(num_sms, max_T, hkv, dec::stage_rows(SA_F32, d), &ns, &rps);
+    const size_t npart = (size_t)hq * ns;
+    dec::Args a;
+    a.q = q; a.k = k; a.v = v;
+    a.kv_head_stride = kv_head_stride;
+    a.T = len_dev ? max_T : T_host; a.hq = hq; a.hkv = hkv;
+    a.rows_per_split = rps; a.n_splits = ns;
+    a.qscale = scale * dec::LOG2E;
+    a.part_m = scratch;
+    a.part_l = scratch + npart;
+    a.part_o = scratch + 2 * npart;
+    a.counters = counters;
+    a.out = out; a.out_m = nullptr; a.out_l = nullptr;
+    a.status = status;
+    a.q_stride = 0; a.o_stride = 0;
+    a.len_dev = len_dev;
+    dec::KernelFn fn = dec::pick<float>(d, hq / hkv);
+    SA_CHECK_ARG(fn != nullptr, "decode_dev: hq/hkv=%d d=%d unsupported", hq / hkv, d);
+    SA_RC_TRY(set_smem_attr_once((const void*)fn, dec::SMEM_BYTES));
+    fn<<<dim3(ns, hkv), dec::THREADS, dec::SMEM_BYTES, st>>>(a);
     SA_CUDA_TRY(cudaGetLastError());
     return SA_OK;
 }
@@ -734,6 +784,7 @@ SA_API int sa_attn_decode_noalloc(void* stream, int dtype, const void* q, const 
     a.out = out; a.out_m = nullptr; a.out_l = nullptr;
     a.status = status;
     a.q_stride = 0; a.o_stride = 0;
+    a.len_dev = nullptr;
     dec::KernelFn fn = dtype == SA_F32 ? dec::pick<float>(d, hq / hkv) : dec::pick<__nv_bfloat16>(d, hq / hkv);
     SA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::SMEM_BYTES));
     fn<<<dim3(ns, hkv), dec::THREADS, dec::SMEM_BYTES, st>>>(a);

@@ -243,15 +243,15 @@ int gemm_launch(cudaStream_t st, int* status, const __nv_bfloat16* a_hi, const _
         SA_CHECK_ARG((size_t)nt * mt <= n_counters, "gemm: counters too small");
     }
     CUtensorMap mh, ml, mw;
-    int rc = make_tmap_2d_bf16(&mh, a_hi, (uint64_t)M, (uint64_t)K, (uint64_t)lda, gm::BM, gm::BK);
-    if (!rc) rc = make_tmap_2d_bf16(&ml, a_lo, (uint64_t)M, (uint64_t)K, (uint64_t)lda, gm::BM, gm::BK);
-    if (!rc) rc = make_tmap_2d_bf16(&mw, w, (uint64_t)N, (uint64_t)K, (uint64_t)K, gm::BN, gm::BK);
+    int rc = cached_tmap_2d_bf16(&mh, a_hi, (uint64_t)M, (uint64_t)K, (uint64_t)lda, gm::BM, gm::BK);
+    if (!rc) rc = cached_tmap_2d_bf16(&ml, a_lo, (uint64_t)M, (uint64_t)K, (uint64_t)lda, gm::BM, gm::BK);
+    if (!rc) rc = cached_tmap_2d_bf16(&mw, w, (uint64_t)N, (uint64_t)K, (uint64_t)K, gm::BN, gm::BK);
     if (rc) return rc;
     gm::Args a;
     a.M = M; a.N = N; a.K = K; a.splits = splits; a.k_blocks_per_split = kbps; a.mode = mode;
     a.C = C; a.ldc = ldc; a.out_hi = out_hi; a.out_lo = out_lo; a.ldo = ldo;
     a.part = ws; a.counters = counters; a.status = status;
-    SA_CUDA_TRY(cudaFuncSetAttribute(gm::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gm::SMEM_BYTES));
+    SA_RC_TRY(set_smem_attr_once((const void*)gm::gemm_kernel, gm::SMEM_BYTES));
     gm::gemm_kernel<<<dim3(nt, mt, splits), gm::THREADS, gm::SMEM_BYTES, st>>>(mh, ml, mw, a);
     SA_CUDA_TRY(cudaGetLastError());
     return SA_OK;

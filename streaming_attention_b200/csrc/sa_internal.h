@@ -71,6 +71,12 @@ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
                                  cudaGetErrorString(e_), __FILE__, __LINE__);      \
     } while (0)
 
+#define SA_RC_TRY(expr)                                                            \
+    do {                                                                           \
+        int rc_ = (expr);                                                          \
+        if (rc_) return rc_;                                                       \
+    } while (0)
+
 #define SA_CHECK_ARG(cond, ...)                                                    \
     do {                                                                           \
         if (!(cond)) return sa::set_error(SA_ERR_ARG, __VA_ARGS__);                \

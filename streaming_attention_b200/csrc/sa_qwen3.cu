@@ -15,6 +15,9 @@
 #include <cuda_bf16.h>
 #include <cmath>
 #include <cstring>
+#include <map>
+#include <set>
+#include <utility>
 #include <vector>
 
 #include "sa_internal.h"
@@ -63,6 +66,21 @@ struct sa_qwen3 {
     size_t gemm_ws_floats = 0;
     unsigned* gemm_cnt = nullptr;
     size_t gemm_cnt_n = 0;
+    // streams: `cur` is where launches go (the context's stream, or the
+    // model's own capturable stream inside graph-using calls)
+    cudaStream_t own = nullptr;
+    cudaStream_t cur = nullptr;
+    cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+    // device-side decode state: [0] cache length, [1] tokens recorded
+    int* d_state = nullptr;
+    int64_t* d_toks = nullptr;           // [toks_cap]
+    int toks_cap = 0;
+    float* dec_scratch = nullptr;        // split partials for the decode step (max plan)
+    unsigned* dec_cnt = nullptr;         // [hkv]
+    // CUDA graphs: the single-token decode step; cache-free prefill per (S, logits mode)
+    cudaGraphExec_t dec_graph = nullptr;
+    std::map<std::pair<int, int>, cudaGraphExec_t> pf_graphs;
+    std::set<std::pair<int, int>> pf_seen;
 };
 
 namespace sa {
@@ -112,12 +130,29 @@ static void free_model(sa_qwen3* m) {
     cudaFree(m->x); cudaFree(m->qkv); cudaFree(m->q); cudaFree(m->attn); cudaFree(m->act); cudaFree(m->xn);
     cudaFree(m->a_hi); cudaFree(m->a_lo); cudaFree(m->b_hi); cudaFree(m->b_lo);
     cudaFree(m->logits); cudaFree(m->ids); cudaFree(m->gemm_ws); cudaFree(m->gemm_cnt);
+    cudaFree(m->d_state); cudaFree(m->d_toks); cudaFree(m->dec_scratch); cudaFree(m->dec_cnt);
+    if (m->dec_graph) cudaGraphExecDestroy(m->dec_graph);
+    for (auto& kv : m->pf_graphs) cudaGraphExecDestroy(kv.second);
+    if (m->ev_in) cudaEventDestroy(m->ev_in);
+    if (m->ev_out) cudaEventDestroy(m->ev_out);
+    if (m->own) cudaStreamDestroy(m->own);
+}
+
+// Graphs hold buffer addresses; drop them whenever a buffer is reallocated.
+static void invalidate_graphs(sa_qwen3* m) {
+    if (m->dec_graph) cudaGraphExecDestroy(m->dec_graph);
+    m->dec_graph = nullptr;
+    for (auto& kv : m->pf_graphs) cudaGraphExecDestroy(kv.second);
+    m->pf_graphs.clear();
+    m->pf_seen.clear();
 }
 
 // Activation buffers for up to M tokens (grow-only).
 static int ensure_acts(sa_qwen3* m, int M) {
     if (M <= m->cap_m) return SA_OK;
+    SA_CUDA_TRY(cudaStreamSynchronize(m->cur));
     SA_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    invalidate_graphs(m);
     cudaFree(m->x); cudaFree(m->qkv); cudaFree(m->q); cudaFree(m->attn); cudaFree(m->act); cudaFree(m->xn);
     cudaFree(m->a_hi); cudaFree(m->a_lo); cudaFree(m->b_hi); cudaFree(m->b_lo); cudaFree(m->ids);
     const sa_qwen3_config& c = m->c;
@@ -141,7 +176,9 @@ static int ensure_acts(sa_qwen3* m, int M) {
 
 static int ensure_logits(sa_qwen3* m, int rows) {
     if (rows <= m->logits_rows) return SA_OK;
+    SA_CUDA_TRY(cudaStreamSynchronize(m->cur));
     SA_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    invalidate_graphs(m);
     cudaFree(m->logits);
     m->logits = nullptr;
     int rc = dalloc(&m->logits, (size_t)rows * m->c.vocab);
@@ -165,7 +202,8 @@ static int gemm(sa_qwen3* m, const __nv_bfloat16* hi, const __nv_bfloat16* lo, l
     if (splits > 1) {
         const size_t need = tiles * splits * 128 * 64;
         if (need > m->gemm_ws_floats) {
-            SA_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+            SA_CUDA_TRY(cudaStreamSynchronize(m->cur));
+            invalidate_graphs(m);
             cudaFree(m->gemm_ws);
             m->gemm_ws = nullptr;
             m->gemm_ws_floats = 0;
@@ -174,27 +212,33 @@ static int gemm(sa_qwen3* m, const __nv_bfloat16* hi, const __nv_bfloat16* lo, l
             m->gemm_ws_floats = need;
         }
         if (tiles > m->gemm_cnt_n) {
-            SA_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+            SA_CUDA_TRY(cudaStreamSynchronize(m->cur));
+            invalidate_graphs(m);
             cudaFree(m->gemm_cnt);
             m->gemm_cnt = nullptr;
             m->gemm_cnt_n = 0;
             int rc = dalloc(&m->gemm_cnt, tiles);
             if (rc) return rc;
-            SA_CUDA_TRY(cudaMemset(m->gemm_cnt, 0, tiles * sizeof(unsigned)));
+            SA_CUDA_TRY(cudaMemsetAsync(m->gemm_cnt, 0, tiles * sizeof(unsigned), m->cur));
             m->gemm_cnt_n = tiles;
         }
     }
-    return gemm_launch(m->ctx->stream, m->ctx->status, hi, lo, lda, w, M, N, K, mode, C, ldc, ohi, olo, ldo,
+    return gemm_launch(m->cur, m->ctx->status, hi, lo, lda, w, M, N, K, mode, C, ldc, ohi, olo, ldo,
                        splits, m->gemm_ws, m->gemm_ws_floats, m->gemm_cnt, m->gemm_cnt_n);
 }
 
 #define SA_RC(expr) do { int rc_ = (expr); if (rc_) return rc_; } while (0)
 
-// Tokens ids (device) at positions pos0 .. pos0+M-1 through every layer,
-// appending K/V to the cache.  M == 1 uses the GEMV path.
-static int run_layers(sa_qwen3* m, int M, int pos0) {
+// Tokens ids (device) at positions pos0 .. pos0+M-1 through every layer.
+// Their K/V go to cache rows kv_row0 + (0 .. M-1) and attention reads rows
+// from kv_row0 - pos0: with the cache, kv_row0 = pos0 = cache length; a
+// cache-free forward (positions from 0) uses the rows after the live prefix
+// as scratch, kv_row0 = cache length, so the cache is left as it was.
+// M == 1 uses the GEMV path; pos_dev makes the position a device value.
+static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr, int kv_row0 = -1) {
+    if (kv_row0 < 0) kv_row0 = pos0;
     const sa_qwen3_config& c = m->c;
-    cudaStream_t st = m->ctx->stream;
+    cudaStream_t st = m->cur;
     const int H = c.hidden, I = c.inter, D = c.head_dim;
     const float scale = 1.0f / sqrtf((float)D);
     const size_t layer_kv = (size_t)c.hkv * c.max_seq * D;
@@ -203,12 +247,16 @@ static int run_layers(sa_qwen3* m, int M, int pos0) {
         const sa_qwen3::Layer& L = m->layers[l];
         float* kc = m->kc + l * layer_kv;
         float* vc = m->vc + l * layer_kv;
+        const int shift = kv_row0 - pos0;                     // cache row - RoPE position
+        const float* ka = kc + (size_t)shift * D;             // attention view of this sequence
+        const float* va = vc + (size_t)shift * D;
         if (M == 1) {
             SA_RC(launch_gemv(st, QW_EPI_STORE, true, L.wqkv, m->NQKV, H, m->x, L.in_norm, c.eps, m->qkv, m->ctx->num_sms));
             SA_RC(launch_qknorm_rope_append(st, m->qkv, 1, c.hq, c.hkv, L.q_norm, L.k_norm, m->cos_t, m->sin_t, pos0,
-                                            m->q, kc, vc, c.max_seq));
-            SA_RC(sa_attn_decode(m->ctx, SA_F32, m->q, kc, vc, (long long)c.max_seq * D, pos0 + 1, D, c.hq, c.hkv,
-                                 64, scale, m->attn, 0));
+                                            pos_dev, shift, m->q, kc, vc, c.max_seq));
+            SA_RC(decode_dev_launch(st, m->ctx->status, m->ctx->num_sms, m->q, ka, va, (long long)c.max_seq * D,
+                                    pos_dev, pos0 + 1, c.max_seq - shift, D, c.hq, c.hkv, scale, m->attn,
+                                    m->dec_scratch, m->dec_cnt));
             SA_RC(launch_gemv(st, QW_EPI_RESID, false, L.wo, H, m->QD, m->attn, nullptr, 0.f, m->x, m->ctx->num_sms));
             SA_RC(launch_gemv(st, QW_EPI_SWIGLU, true, L.wgu, I, H, m->x, L.post_norm, c.eps, m->act, m->ctx->num_sms));
             SA_RC(launch_gemv(st, QW_EPI_RESID, false, L.wd, H, I, m->act, nullptr, 0.f, m->x, m->ctx->num_sms));
@@ -216,8 +264,8 @@ static int run_layers(sa_qwen3* m, int M, int pos0) {
             SA_RC(launch_rmsnorm_hilo(st, m->x, L.in_norm, M, H, c.eps, m->a_hi, m->a_lo));
             SA_RC(gemm(m, m->a_hi, m->a_lo, H, L.wqkv, M, m->NQKV, H, QW_EPI_STORE, m->qkv, m->NQKV, nullptr, nullptr, 0));
             SA_RC(launch_qknorm_rope_append(st, m->qkv, M, c.hq, c.hkv, L.q_norm, L.k_norm, m->cos_t, m->sin_t, pos0,
-                                            m->q, kc, vc, c.max_seq));
-            SA_RC(decode_multi_launch(st, m->ctx->status, m->q, m->QD, kc, vc, (long long)c.max_seq * D, pos0 + 1, M, D,
+                                            nullptr, shift, m->q, kc, vc, c.max_seq));
+            SA_RC(decode_multi_launch(st, m->ctx->status, m->q, m->QD, ka, va, (long long)c.max_seq * D, pos0 + 1, M, D,
                                       c.hq, c.hkv, scale, m->attn, m->QD));
             SA_RC(launch_split_hilo(st, m->attn, (size_t)M * m->QD, m->a_hi, m->a_lo));
             SA_RC(gemm(m, m->a_hi, m->a_lo, m->QD, L.wo, M, H, m->QD, QW_EPI_RESID, m->x, H, nullptr, nullptr, 0));
@@ -232,7 +280,7 @@ static int run_layers(sa_qwen3* m, int M, int pos0) {
 // Final norm + lm_head for rows [r0, r0 + n) of the residual stream.
 static int run_head(sa_qwen3* m, int r0, int n) {
     const sa_qwen3_config& c = m->c;
-    cudaStream_t st = m->ctx->stream;
+    cudaStream_t st = m->cur;
     SA_RC(ensure_logits(m, n));
     if (n == 1) {
         SA_RC(launch_gemv(st, QW_EPI_STORE, true, m->lm_head, c.vocab, c.hidden, m->x + (size_t)r0 * c.hidden,
@@ -289,6 +337,20 @@ SA_API int sa_qwen3_create(sa_ctx* ctx, const sa_qwen3_config* cfg, sa_qwen3** o
     if (!rc) rc = dalloc(&m->vc, kv);
     if (!rc) rc = dalloc(&m->cos_t, (size_t)c.max_seq * D / 2);
     if (!rc) rc = dalloc(&m->sin_t, (size_t)c.max_seq * D / 2);
+    if (!rc && cudaStreamCreateWithFlags(&m->own, cudaStreamNonBlocking) != cudaSuccess)
+        rc = set_error(SA_ERR_CUDA, "stream create");
+    if (!rc && (cudaEventCreateWithFlags(&m->ev_in, cudaEventDisableTiming) != cudaSuccess ||
+                cudaEventCreateWithFlags(&m->ev_out, cudaEventDisableTiming) != cudaSuccess))
+        rc = set_error(SA_ERR_CUDA, "event create");
+    m->toks_cap = c.max_seq + 1;
+    if (!rc) rc = dalloc(&m->d_state, 2);
+    if (!rc) rc = dalloc(&m->d_toks, (size_t)m->toks_cap);
+    if (!rc) rc = dalloc(&m->dec_scratch,
+                         decode_dev_scratch_floats(ctx->num_sms, c.max_seq, (int)D, c.hq, c.hkv, nullptr));
+    if (!rc) rc = dalloc(&m->dec_cnt, (size_t)c.hkv);
+    if (!rc && cudaMemsetAsync(m->dec_cnt, 0, c.hkv * sizeof(unsigned), ctx->stream) != cudaSuccess)
+        rc = set_error(SA_ERR_CUDA, "memset");
+    m->cur = ctx->stream;
     if (!rc) rc = launch_rope_table(ctx->stream, c.max_seq, (int)D, c.theta, m->cos_t, m->sin_t);
     if (!rc && cudaMemsetAsync(m->kc, 0, kv * 4, ctx->stream) != cudaSuccess) rc = set_error(SA_ERR_CUDA, "memset");
     if (!rc && cudaMemsetAsync(m->vc, 0, kv * 4, ctx->stream) != cudaSuccess) rc = set_error(SA_ERR_CUDA, "memset");
@@ -378,6 +440,42 @@ SA_API int sa_qwen3_reset(sa_qwen3* m) {
 
 SA_API int sa_qwen3_cache_len(sa_qwen3* m) { return m ? m->cache_len : -1; }
 
+// Run `body` on the model's own (capturable) stream, ordered after the
+// context's stream and before anything the caller issues on it afterwards.
+template <typename F>
+static int on_own_stream(sa_qwen3* m, F body) {
+    SA_CUDA_TRY(cudaEventRecord(m->ev_in, m->ctx->stream));
+    SA_CUDA_TRY(cudaStreamWaitEvent(m->own, m->ev_in, 0));
+    m->cur = m->own;
+    int rc = body();
+    m->cur = m->ctx->stream;
+    if (cudaEventRecord(m->ev_out, m->own) != cudaSuccess ||
+        cudaStreamWaitEvent(m->ctx->stream, m->ev_out, 0) != cudaSuccess)
+        return rc ? rc : set_error(SA_ERR_CUDA, "stream join failed");
+    return rc;
+}
+
+// Capture `body` (launches on m->own) into a graph; *exec receives it.
+template <typename F>
+static int capture(sa_qwen3* m, cudaGraphExec_t* exec, F body) {
+    cudaGraph_t g = nullptr;
+    SA_CUDA_TRY(cudaStreamBeginCapture(m->own, cudaStreamCaptureModeThreadLocal));
+    const int rc = body();
+    const cudaError_t e = cudaStreamEndCapture(m->own, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return set_error(SA_ERR_CUDA, "graph capture failed: %s", cudaGetErrorString(e));
+    const cudaError_t e2 = cudaGraphInstantiate(exec, g, 0);
+    cudaGraphDestroy(g);
+    if (e2 != cudaSuccess) {
+        *exec = nullptr;
+        return set_error(SA_ERR_CUDA, "graph instantiate failed: %s", cudaGetErrorString(e2));
+    }
+    return SA_OK;
+}
+
 SA_API int sa_qwen3_forward(sa_qwen3* m, const int64_t* ids, int S, int use_cache, float* logits, int logits_mode,
                             unsigned flags) {
     clear_error();
@@ -389,27 +487,63 @@ SA_API int sa_qwen3_forward(sa_qwen3* m, const int64_t* ids, int S, int use_cach
     for (int l = 0; l < m->c.n_layers; ++l)
         SA_CHECK_ARG(m->loaded_layer[l], "sa_qwen3_forward: layer %d not loaded", l);
     DeviceGuard guard(m->ctx->device);
+    m->cur = m->ctx->stream;
     const int pos0 = use_cache ? m->cache_len : 0;
-    if (pos0 + S > m->c.max_seq)
-        return set_error(SA_ERR_FULL, "KV cache full, cannot append %d tokens at %d (max_seq %d)", S, pos0,
-                         m->c.max_seq);
+    const int kv_row0 = m->cache_len;      // cache-free forwards use the rows after the live prefix
+    if (kv_row0 + S > m->c.max_seq)
+        return set_error(SA_ERR_FULL, "KV cache full, cannot place %d tokens after %d cached (max_seq %d)", S,
+                         m->cache_len, m->c.max_seq);
     const bool host = flags & SA_HOST_PTRS;
     if (host)
         for (int s = 0; s < S; ++s)
             if (ids[s] < 0 || ids[s] >= m->c.vocab)
                 return set_error(SA_ERR_RANGE, "Embedding index out of range: ids[%d] = %lld", s, (long long)ids[s]);
     SA_RC(ensure_acts(m, S));
-    cudaStream_t st = m->ctx->stream;
-    SA_CUDA_TRY(cudaMemcpyAsync(m->ids, ids, (size_t)S * 8, host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, st));
-    SA_RC(run_layers(m, S, pos0));
+    const int r0 = logits_mode == 1 ? S - 1 : 0, n = logits_mode == 1 ? 1 : S;
+    if (logits_mode != 2) SA_RC(ensure_logits(m, n));
+    const cudaMemcpyKind in_kind = host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+    int rc = on_own_stream(m, [&]() -> int {
+        SA_CUDA_TRY(cudaMemcpyAsync(m->ids, ids, (size_t)S * 8, in_kind, m->own));
+        auto body = [&]() -> int {
+            SA_RC(run_layers(m, S, pos0, nullptr, kv_row0));
+            if (logits_mode != 2) SA_RC(run_head(m, r0, n));
+            return SA_OK;
+        };
+        if (use_cache) return body();
+        // qwen3_forward without a cache has a fixed schedule per (S, logits
+        // mode): the second call of a shape captures it, later ones replay
+        const std::pair<int, int> key{S, logits_mode * 1048576 + kv_row0};
+        auto it = m->pf_graphs.find(key);
+        if (it == m->pf_graphs.end() && m->pf_seen.count(key)) {
+            cudaGraphExec_t ex = nullptr;
+            SA_RC(capture(m, &ex, body));
+            it = m->pf_graphs.emplace(key, ex).first;
+        }
+        if (it != m->pf_graphs.end()) {
+            SA_CUDA_TRY(cudaGraphLaunch(it->second, m->own));
+            return SA_OK;
+        }
+        m->pf_seen.insert(key);
+        return body();
+    });
+    if (rc) return rc;
     if (use_cache) m->cache_len = pos0 + S;
-    if (logits_mode != 2) {
-        const int r0 = logits_mode == 1 ? S - 1 : 0, n = logits_mode == 1 ? 1 : S;
-        SA_RC(run_head(m, r0, n));
+    if (logits_mode != 2)
         SA_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, (size_t)n * m->c.vocab * 4,
-                                    host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, st));
-    }
+                                    host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, m->ctx->stream));
     if (host) return sync_and_check(m->ctx);
+    return SA_OK;
+}
+
+// One decode step driven entirely by device state: the token in ids[0] at
+// cache position d_state[0] goes through every layer (K/V appended), the
+// lm_head GEMV and argmax write the next token back to ids[0], which is
+// recorded at d_toks[d_state[1]]; then both counters advance.
+static int decode_step_dev(sa_qwen3* m) {
+    SA_RC(run_layers(m, 1, 0, m->d_state));
+    SA_RC(run_head(m, 0, 1));
+    SA_RC(launch_argmax(m->cur, m->logits, m->c.vocab, m->ids));
+    SA_RC(launch_advance(m->cur, m->d_state, m->ids, m->d_toks, m->toks_cap, 1));
     return SA_OK;
 }
 
@@ -417,7 +551,11 @@ SA_API int sa_qwen3_generate(sa_qwen3* m, const int64_t* prompt, int S, int n_ne
                              unsigned flags) {
     clear_error();
     SA_CHECK_ARG(m && prompt && out_tokens && S >= 1 && n_new >= 0, "sa_qwen3_generate: bad argument");
+    SA_CHECK_ARG(m->loaded_embed, "sa_qwen3_generate: embedding not loaded");
+    for (int l = 0; l < m->c.n_layers; ++l)
+        SA_CHECK_ARG(m->loaded_layer[l], "sa_qwen3_generate: layer %d not loaded", l);
     DeviceGuard guard(m->ctx->device);
+    m->cur = m->ctx->stream;
     if (m->cache_len + S + n_new > m->c.max_seq + 1)
         return set_error(SA_ERR_FULL, "KV cache full: %d + %d prompt + %d new > max_seq %d", m->cache_len, S, n_new,
                          m->c.max_seq);
@@ -427,34 +565,27 @@ SA_API int sa_qwen3_generate(sa_qwen3* m, const int64_t* prompt, int S, int n_ne
             if (prompt[s] < 0 || prompt[s] >= m->c.vocab)
                 return set_error(SA_ERR_RANGE, "Embedding index out of range: prompt[%d]", s);
     SA_RC(ensure_acts(m, S));
-    cudaStream_t st = m->ctx->stream;
-    int64_t* toks = nullptr;
-    SA_RC(dalloc(&toks, (size_t)std::max(n_new, 1)));
-    int rc = SA_OK;
-    do {
-        if (cudaMemcpyAsync(m->ids, prompt, (size_t)S * 8, host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice,
-                            st) != cudaSuccess) { rc = set_error(SA_ERR_CUDA, "copy prompt"); break; }
-        const int pos0 = m->cache_len;
-        if ((rc = run_layers(m, S, pos0))) break;
-        m->cache_len = pos0 + S;
-        if ((rc = run_head(m, S - 1, 1))) break;
-        for (int t = 0; t < n_new; ++t) {
-            if ((rc = launch_argmax(st, m->logits, m->c.vocab, toks + t))) break;
-            if (t + 1 == n_new) break;
-            if (cudaMemcpyAsync(m->ids, toks + t, 8, cudaMemcpyDeviceToDevice, st) != cudaSuccess) {
-                rc = set_error(SA_ERR_CUDA, "copy token");
-                break;
-            }
-            if ((rc = run_layers(m, 1, m->cache_len))) break;
-            m->cache_len += 1;
-            if ((rc = run_head(m, 0, 1))) break;
-        }
-        if (rc) break;
-        if (n_new > 0 && cudaMemcpyAsync(out_tokens, toks, (size_t)n_new * 8,
-                                         host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, st) != cudaSuccess)
-            rc = set_error(SA_ERR_CUDA, "copy tokens");
-    } while (0);
-    if (!rc) rc = sync_and_check(m->ctx);
-    cudaFree(toks);
-    return rc;
+    SA_RC(ensure_logits(m, 1));
+    const int pos0 = m->cache_len;
+    int rc = on_own_stream(m, [&]() -> int {
+        cudaStream_t st = m->own;
+        SA_CUDA_TRY(cudaMemcpyAsync(m->ids, prompt, (size_t)S * 8,
+                                    host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, st));
+        SA_RC(run_layers(m, S, pos0));
+        SA_RC(run_head(m, S - 1, 1));
+        if (n_new == 0) return SA_OK;
+        SA_RC(launch_argmax(st, m->logits, m->c.vocab, m->ids));
+        const int state[2] = {pos0 + S, 0};
+        SA_CUDA_TRY(cudaMemcpyAsync(m->d_state, state, sizeof(state), cudaMemcpyHostToDevice, st));
+        SA_RC(launch_advance(st, m->d_state, m->ids, m->d_toks, m->toks_cap, 0));   // first new token
+        if (n_new > 1 && !m->dec_graph) SA_RC(capture(m, &m->dec_graph, [&]() { return decode_step_dev(m); }));
+        for (int t = 1; t < n_new; ++t) SA_CUDA_TRY(cudaGraphLaunch(m->dec_graph, st));
+        SA_CUDA_TRY(cudaMemcpyAsync(out_tokens, m->d_toks, (size_t)n_new * 8,
+                                    host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, st));
+        return SA_OK;
+    });
+    if (rc) return rc;
+    m->cache_len = pos0 + S + (n_new > 0 ? n_new - 1 : 0);
+    if (host) return sync_and_check(m->ctx);
+    return SA_OK;
 }

@@ -110,19 +110,22 @@ __global__ void rope_table_kernel(int n_pos, int D, float theta, float* cos_t, f
 // k_norm -> K cache row pos0 + m.  V heads: copied to the V cache.
 __global__ void qknorm_rope_append_kernel(const float* qkv, int M, int hq, int hkv, const float* qn,
                                           const float* kn, const float* cos_t, const float* sin_t, int pos0,
-                                          float* q_out, float* kc, float* vc, int max_seq) {
+                                          const int* pos_dev, int row_shift, float* q_out, float* kc, float* vc,
+                                          int max_seq) {
     constexpr int D = 128;
     const int lane = threadIdx.x & 31;
     const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nh = hq + 2 * hkv;
     if (gw >= M * nh) return;
     const int m = gw / nh, h = gw % nh;
-    const int pos = pos0 + m;
+    const int pos = (pos_dev ? *pos_dev : pos0) + m;      // RoPE position
+    const int row = pos + row_shift;                       // cache row written
+    if (row >= max_seq) return;       // the host checks capacity; never write past the cache
     const float* src = qkv + (size_t)m * nh * D + (size_t)h * D;
     float4 v4 = *reinterpret_cast<const float4*>(src + 4 * lane);
     float e[4] = {v4.x, v4.y, v4.z, v4.w};
     if (h >= hq + hkv) {  // V head
-        float* dst = vc + ((size_t)(h - hq - hkv) * max_seq + pos) * D;
+        float* dst = vc + ((size_t)(h - hq - hkv) * max_seq + row) * D;
         *reinterpret_cast<float4*>(dst + 4 * lane) = v4;
         return;
     }
@@ -151,7 +154,7 @@ __global__ void qknorm_rope_append_kernel(const float* qkv, int M, int hq, int h
     if (h < hq) {
         *reinterpret_cast<float4*>(q_out + ((size_t)m * hq + h) * D + 4 * lane) = r4;
     } else {
-        float* dst = kc + ((size_t)(h - hq) * max_seq + pos) * D;
+        float* dst = kc + ((size_t)(h - hq) * max_seq + row) * D;
         *reinterpret_cast<float4*>(dst + 4 * lane) = r4;
     }
 }
@@ -251,9 +254,24 @@ __global__ void argmax_kernel(const float* __restrict__ v, int n, int64_t* out) 
     }
 }
 
+// Decode-loop bookkeeping after a token was chosen: record it and advance the
+// step counter; with inc_len the token just processed is now in the cache.
+// state[0] = cache length, state[1] = tokens recorded.
+__global__ void advance_kernel(int* state, const int64_t* tok, int64_t* toks, int cap, int inc_len) {
+    const int s = state[1];
+    if (s < cap) toks[s] = *tok;
+    state[1] = s + 1;
+    if (inc_len) state[0] += 1;
+}
+
 }  // namespace qk
 
 // ---- launchers --------------------------------------------------------------
+int launch_advance(cudaStream_t st, int* state, const int64_t* tok, int64_t* toks, int cap, int inc_len) {
+    qk::advance_kernel<<<1, 1, 0, st>>>(state, tok, toks, cap, inc_len);
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
 int launch_embedding(cudaStream_t st, const int64_t* ids, int M, const __nv_bfloat16* E, int V, int H, float* x,
                      int* status) {
     qk::embedding_kernel<<<M, 256, 0, st>>>(ids, M, E, V, H, x, status);
@@ -285,11 +303,11 @@ int launch_rope_table(cudaStream_t st, int n_pos, int D, float theta, float* cos
     return SA_OK;
 }
 int launch_qknorm_rope_append(cudaStream_t st, const float* qkv, int M, int hq, int hkv, const float* qn,
-                              const float* kn, const float* cos_t, const float* sin_t, int pos0, float* q_out,
-                              float* kc, float* vc, int max_seq) {
+                              const float* kn, const float* cos_t, const float* sin_t, int pos0, const int* pos_dev,
+                              int row_shift, float* q_out, float* kc, float* vc, int max_seq) {
     const int warps = M * (hq + 2 * hkv);
     qk::qknorm_rope_append_kernel<<<(warps + 7) / 8, 256, 0, st>>>(qkv, M, hq, hkv, qn, kn, cos_t, sin_t, pos0,
-                                                                   q_out, kc, vc, max_seq);
+                                                                   pos_dev, row_shift, q_out, kc, vc, max_seq);
     SA_CUDA_TRY(cudaGetLastError());
     return SA_OK;
 }

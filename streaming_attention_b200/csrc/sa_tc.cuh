@@ -119,5 +119,9 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
 // Defined in sa_tmap.cu.
 int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
                       uint64_t row_stride_elems, uint32_t box_rows, uint32_t box_cols);
+int cached_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                        uint64_t row_stride_elems, uint32_t box_rows, uint32_t box_cols);
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (function, device).
+int set_smem_attr_once(const void* fn, int bytes);
 
 }  // namespace sa

@@ -2,7 +2,10 @@
 // a driver API; it is fetched through the runtime's driver entry point so the
 // library does not link libcuda directly.
 #include <cudaTypedefs.h>
+#include <map>
 #include <mutex>
+#include <set>
+#include <tuple>
 
 #include "sa_internal.h"
 #include "sa_tc.cuh"
@@ -41,6 +44,43 @@ int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_
         return set_error(SA_ERR_ARG, "cuTensorMapEncodeTiled failed (%d): rows=%llu cols=%llu stride=%llu box=%ux%u",
                          (int)r, (unsigned long long)rows, (unsigned long long)cols,
                          (unsigned long long)row_stride_elems, box_rows, box_cols);
+    return SA_OK;
+}
+
+// Tensor maps depend only on (address, shape, stride, box); the Qwen3 forward
+// reuses the same few hundred for its fixed buffers, so encode each once.
+int cached_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                        uint64_t row_stride_elems, uint32_t box_rows, uint32_t box_cols) {
+    using Key = std::tuple<const void*, uint64_t, uint64_t, uint64_t, uint32_t, uint32_t>;
+    static std::mutex mu;
+    static std::map<Key, CUtensorMap> cache;
+    const Key key{base, rows, cols, row_stride_elems, box_rows, box_cols};
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) {
+            *map = it->second;
+            return SA_OK;
+        }
+    }
+    int rc = make_tmap_2d_bf16(map, base, rows, cols, row_stride_elems, box_rows, box_cols);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lk(mu);
+    if (cache.size() > 8192) cache.clear();
+    cache.emplace(key, *map);
+    return SA_OK;
+}
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (function, device).
+int set_smem_attr_once(const void* fn, int bytes) {
+    static std::mutex mu;
+    static std::set<std::pair<int, const void*>> done;
+    int dev = 0;
+    SA_CUDA_TRY(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(mu);
+    if (done.count({dev, fn})) return SA_OK;
+    SA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done.insert({dev, fn});
     return SA_OK;
 }
 

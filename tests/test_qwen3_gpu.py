@@ -144,3 +144,31 @@ def test_qwen3_0_6b_full_size(ctx, oracle):
         pos += 1
         nxt = int(np.argmax(lg[0]))
     assert [int(t) for t in toks] == ref_toks
+
+
+def test_qwen3_graph_replay_and_cache_isolation(ctx):
+    """Cache-free forwards of one shape run eagerly, then captured, then
+    replayed (CUDA graph): identical logits each time; a cache-free forward
+    leaves a live KV cache untouched (qwen3_forward never touches KVCache);
+    a second generate() reuses the captured decode step."""
+    from streaming_attention_b200 import Qwen3
+    cfg = Qwen3Cfg(vocab=700, hidden=256, n_layers=2, hq=4, hkv=2, head_dim=128, inter=512,
+                   eps=1e-6, theta=1e6)
+    w = make_qwen3_weights(cfg, 8)
+    m = Qwen3(_cfgdict(cfg), max_seq=256, ctx=ctx)
+    m.load(w)
+    ids = I.rng(1).integers(0, cfg.vocab, 40)
+    outs = [m.forward(ids) for _ in range(3)]
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[1], outs[2])
+    # live cache + an interleaved cache-free forward
+    prompt = I.rng(2).integers(0, cfg.vocab, 30)
+    a = m.generate(prompt, 5)
+    m.reset()
+    m.forward(prompt, use_cache=True, logits="none")
+    m.forward(ids, logits="last")                       # must not disturb the cache
+    assert m.cache_len == 30
+    lg = m.forward(np.array([a[0]]), use_cache=True, logits="last")
+    assert int(np.argmax(lg[0])) == int(a[1])
+    m.reset()
+    b = m.generate(prompt, 5)
+    assert [int(x) for x in a] == [int(x) for x in b]
