@@ -77,6 +77,7 @@ struct sa_qwen3 {
     int toks_cap = 0;
     float* dec_scratch = nullptr;        // split partials for the decode step (max plan)
     unsigned* dec_cnt = nullptr;         // [hkv]
+    unsigned long long* d_amax = nullptr;  // argmax key of the last lm_head GEMV (0 between uses)
     // CUDA graphs: the single-token decode step; cache-free prefill per (S, logits mode)
     cudaGraphExec_t dec_graph = nullptr;
     std::map<std::pair<int, int>, cudaGraphExec_t> pf_graphs;
@@ -130,7 +131,7 @@ static void free_model(sa_qwen3* m) {
     cudaFree(m->x); cudaFree(m->qkv); cudaFree(m->q); cudaFree(m->attn); cudaFree(m->act); cudaFree(m->xn);
     cudaFree(m->a_hi); cudaFree(m->a_lo); cudaFree(m->b_hi); cudaFree(m->b_lo);
     cudaFree(m->logits); cudaFree(m->ids); cudaFree(m->gemm_ws); cudaFree(m->gemm_cnt);
-    cudaFree(m->d_state); cudaFree(m->d_toks); cudaFree(m->dec_scratch); cudaFree(m->dec_cnt);
+    cudaFree(m->d_state); cudaFree(m->d_toks); cudaFree(m->dec_scratch); cudaFree(m->dec_cnt); cudaFree(m->d_amax);
     if (m->dec_graph) cudaGraphExecDestroy(m->dec_graph);
     for (auto& kv : m->pf_graphs) cudaGraphExecDestroy(kv.second);
     if (m->ev_in) cudaEventDestroy(m->ev_in);
@@ -189,8 +190,9 @@ static int ensure_logits(sa_qwen3* m, int rows) {
 // Split-K so that a GEMM of this shape fills the GPU with >= ~1 CTA per SM.
 static int pick_splits(const sa_qwen3* m, int M, int N, int K) {
     const int tiles = ((N + 63) / 64) * ((M + 127) / 128);
+    // at most 4 splits: the last CTA of a tile sums every split's partial
     int s = 1;
-    while (tiles * s < m->ctx->num_sms && s * 2 <= K / 64 / 2) s *= 2;
+    while (tiles * s < m->ctx->num_sms && s * 2 <= K / 64 / 2 && s < 4) s *= 2;
     return s;
 }
 
@@ -251,15 +253,15 @@ static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr
         const float* ka = kc + (size_t)shift * D;             // attention view of this sequence
         const float* va = vc + (size_t)shift * D;
         if (M == 1) {
-            SA_RC(launch_gemv(st, QW_EPI_STORE, true, L.wqkv, m->NQKV, H, m->x, L.in_norm, c.eps, m->qkv, m->ctx->num_sms));
+            SA_RC(launch_gemv2(st, QW_EPI_STORE, true, L.wqkv, m->NQKV, H, m->x, L.in_norm, c.eps, m->qkv, nullptr));
             SA_RC(launch_qknorm_rope_append(st, m->qkv, 1, c.hq, c.hkv, L.q_norm, L.k_norm, m->cos_t, m->sin_t, pos0,
                                             pos_dev, shift, m->q, kc, vc, c.max_seq));
             SA_RC(decode_dev_launch(st, m->ctx->status, m->ctx->num_sms, m->q, ka, va, (long long)c.max_seq * D,
                                     pos_dev, pos0 + 1, c.max_seq - shift, D, c.hq, c.hkv, scale, m->attn,
                                     m->dec_scratch, m->dec_cnt));
-            SA_RC(launch_gemv(st, QW_EPI_RESID, false, L.wo, H, m->QD, m->attn, nullptr, 0.f, m->x, m->ctx->num_sms));
-            SA_RC(launch_gemv(st, QW_EPI_SWIGLU, true, L.wgu, I, H, m->x, L.post_norm, c.eps, m->act, m->ctx->num_sms));
-            SA_RC(launch_gemv(st, QW_EPI_RESID, false, L.wd, H, I, m->act, nullptr, 0.f, m->x, m->ctx->num_sms));
+            SA_RC(launch_gemv2(st, QW_EPI_RESID, false, L.wo, H, m->QD, m->attn, nullptr, 0.f, m->x, nullptr));
+            SA_RC(launch_gemv2(st, QW_EPI_SWIGLU, true, L.wgu, I, H, m->x, L.post_norm, c.eps, m->act, nullptr));
+            SA_RC(launch_gemv2(st, QW_EPI_RESID, false, L.wd, H, I, m->act, nullptr, 0.f, m->x, nullptr));
         } else {
             SA_RC(launch_rmsnorm_hilo(st, m->x, L.in_norm, M, H, c.eps, m->a_hi, m->a_lo));
             SA_RC(gemm(m, m->a_hi, m->a_lo, H, L.wqkv, M, m->NQKV, H, QW_EPI_STORE, m->qkv, m->NQKV, nullptr, nullptr, 0));
@@ -277,14 +279,17 @@ static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr
     return SA_OK;
 }
 
-// Final norm + lm_head for rows [r0, r0 + n) of the residual stream.
-static int run_head(sa_qwen3* m, int r0, int n) {
+// Final norm + lm_head for rows [r0, r0 + n) of the residual stream.  With
+// `token` (n == 1 only) the argmax of the logits is also written there
+// (first index of the maximum, as ops::argmax).
+static int run_head(sa_qwen3* m, int r0, int n, int64_t* token = nullptr) {
     const sa_qwen3_config& c = m->c;
     cudaStream_t st = m->cur;
     SA_RC(ensure_logits(m, n));
     if (n == 1) {
-        SA_RC(launch_gemv(st, QW_EPI_STORE, true, m->lm_head, c.vocab, c.hidden, m->x + (size_t)r0 * c.hidden,
-                          m->final_norm, c.eps, m->logits, m->ctx->num_sms));
+        SA_RC(launch_gemv2(st, QW_EPI_STORE, true, m->lm_head, c.vocab, c.hidden, m->x + (size_t)r0 * c.hidden,
+                           m->final_norm, c.eps, m->logits, token ? m->d_amax : nullptr));
+        if (token) SA_RC(launch_amax_to_token(st, m->d_amax, token));
     } else {
         SA_RC(launch_rmsnorm_hilo(st, m->x + (size_t)r0 * c.hidden, m->final_norm, n, c.hidden, c.eps, m->a_hi, m->a_lo));
         SA_RC(gemm(m, m->a_hi, m->a_lo, c.hidden, m->lm_head, n, c.vocab, c.hidden, QW_EPI_STORE, m->logits, c.vocab,
@@ -348,6 +353,9 @@ SA_API int sa_qwen3_create(sa_ctx* ctx, const sa_qwen3_config* cfg, sa_qwen3** o
     if (!rc) rc = dalloc(&m->dec_scratch,
                          decode_dev_scratch_floats(ctx->num_sms, c.max_seq, (int)D, c.hq, c.hkv, nullptr));
     if (!rc) rc = dalloc(&m->dec_cnt, (size_t)c.hkv);
+    if (!rc) rc = dalloc(&m->d_amax, 1);
+    if (!rc && cudaMemsetAsync(m->d_amax, 0, sizeof(unsigned long long), ctx->stream) != cudaSuccess)
+        rc = set_error(SA_ERR_CUDA, "memset");
     if (!rc && cudaMemsetAsync(m->dec_cnt, 0, c.hkv * sizeof(unsigned), ctx->stream) != cudaSuccess)
         rc = set_error(SA_ERR_CUDA, "memset");
     m->cur = ctx->stream;
@@ -541,8 +549,7 @@ SA_API int sa_qwen3_forward(sa_qwen3* m, const int64_t* ids, int S, int use_cach
 // recorded at d_toks[d_state[1]]; then both counters advance.
 static int decode_step_dev(sa_qwen3* m) {
     SA_RC(run_layers(m, 1, 0, m->d_state));
-    SA_RC(run_head(m, 0, 1));
-    SA_RC(launch_argmax(m->cur, m->logits, m->c.vocab, m->ids));
+    SA_RC(run_head(m, 0, 1, m->ids));
     SA_RC(launch_advance(m->cur, m->d_state, m->ids, m->d_toks, m->toks_cap, 1));
     return SA_OK;
 }
@@ -572,9 +579,8 @@ SA_API int sa_qwen3_generate(sa_qwen3* m, const int64_t* prompt, int S, int n_ne
         SA_CUDA_TRY(cudaMemcpyAsync(m->ids, prompt, (size_t)S * 8,
                                     host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, st));
         SA_RC(run_layers(m, S, pos0));
-        SA_RC(run_head(m, S - 1, 1));
-        if (n_new == 0) return SA_OK;
-        SA_RC(launch_argmax(st, m->logits, m->c.vocab, m->ids));
+        if (n_new == 0) return run_head(m, S - 1, 1);
+        SA_RC(run_head(m, S - 1, 1, m->ids));
         const int state[2] = {pos0 + S, 0};
         SA_CUDA_TRY(cudaMemcpyAsync(m->d_state, state, sizeof(state), cudaMemcpyHostToDevice, st));
         SA_RC(launch_advance(st, m->d_state, m->ids, m->d_toks, m->toks_cap, 0));   // first new token

@@ -44,5 +44,8 @@ int decode_dev_launch(cudaStream_t st, int* status, int num_sms, const float* q,
 int launch_gemv(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, int N_out, int K, const float* x,
                 const float* nw, float eps, float* y, int num_sms);
 int launch_argmax(cudaStream_t st, const float* v, int n, int64_t* out);
+int launch_gemv2(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, int N_out, int K, const float* x,
+                 const float* nw, float eps, float* y, unsigned long long* amax);
+int launch_amax_to_token(cudaStream_t st, unsigned long long* amax, int64_t* tok);
 
 }  // namespace sa

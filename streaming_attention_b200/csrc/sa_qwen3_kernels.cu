@@ -222,6 +222,124 @@ __global__ void __launch_bounds__(256) gemv_kernel(const __nv_bfloat16* __restri
     }
 }
 
+// ---- decode GEMV v2: one 16-byte chunk column per thread, R rows per CTA ----
+// blockDim = K/8: thread t owns K-chunk t (8 bf16) of each of the CTA's R
+// rows and the matching 8 activations, so all R weight loads of a thread are
+// in flight at once and every weight byte is read exactly once.  NORM folds
+// RMSNorm in as a scalar: dot(W, (x / rms) * g) = (1/rms) * dot(W, x * g),
+// with sum(x^2) reduced from the same activation loads.  SWIGLU: the CTA's
+// rows are (gate, up) pairs of R/2 outputs ([gate 32; up 32] row blocks).
+// ARGMAX additionally folds the CTA's maxima into *amax as a 64-bit key
+// (ordered value << 32 | ~index): the largest value, first index on ties.
+__device__ __forceinline__ uint32_t ordered_f32(float f) {
+    const uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+template <int MODE, bool NORM, int R, bool ARGMAX>
+__global__ void gemv2_kernel(const __nv_bfloat16* __restrict__ W, int N_out, int K,
+                             const float* __restrict__ x, const float* __restrict__ nw, float eps,
+                             float* __restrict__ y, unsigned long long* amax) {
+    constexpr int NV = R + 1;                      // R dot products + sum of squares
+    __shared__ float red[32][NV];
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5, nwarp = blockDim.x >> 5;
+    const int OUT_PER_CTA = MODE == QW_EPI_SWIGLU ? R / 2 : R;
+    const int o0 = blockIdx.x * OUT_PER_CTA;
+    // rows of this CTA
+    int rows[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        if (MODE == QW_EPI_SWIGLU) {
+            const int n = min(o0 + r / 2, N_out - 1);
+            const int g = (n / 32) * 64 + (n % 32);
+            rows[r] = (r & 1) ? g + 32 : g;
+        } else {
+            rows[r] = min(o0 + r, N_out - 1);
+        }
+    }
+    uint4 w[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) w[r] = __ldg(reinterpret_cast<const uint4*>(W + (size_t)rows[r] * K) + t);
+    const float4 xa = __ldg(reinterpret_cast<const float4*>(x) + 2 * t);
+    const float4 xb = __ldg(reinterpret_cast<const float4*>(x) + 2 * t + 1);
+    float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+    float v[NV];
+    v[R] = 0.f;
+    if (NORM) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[R] = fmaf(xv[e], xv[e], v[R]);
+        const float4 ga = __ldg(reinterpret_cast<const float4*>(nw) + 2 * t);
+        const float4 gb = __ldg(reinterpret_cast<const float4*>(nw) + 2 * t + 1);
+        const float gv[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xv[e] *= gv[e];
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const uint32_t wr[4] = {w[r].x, w[r].y, w[r].z, w[r].w};
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            acc = fmaf(__uint_as_float(wr[j] << 16), xv[2 * j], acc);
+            acc = fmaf(__uint_as_float(wr[j] & 0xffff0000u), xv[2 * j + 1], acc);
+        }
+        v[r] = acc;
+    }
+#pragma unroll
+    for (int i = 0; i < NV; ++i) v[i] = warp_sum(v[i]);
+    if (lane == 0)
+#pragma unroll
+        for (int i = 0; i < NV; ++i) red[warp][i] = v[i];
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            float a = lane < nwarp ? red[lane][i] : 0.f;
+            a = warp_sum(a);
+            v[i] = a;
+        }
+        float scale = 1.f;
+        if (NORM) scale = 1.f / sqrtf(v[R] / (float)K + eps);
+        unsigned long long best = 0ull;
+        if (lane < OUT_PER_CTA) {
+            const int n = o0 + lane;
+            float out = 0.f;
+#pragma unroll
+            for (int r = 0; r < OUT_PER_CTA; ++r) {
+                if (r == lane) {
+                    if (MODE == QW_EPI_SWIGLU) {
+                        const float g = v[2 * r] * scale, u = v[2 * r + 1] * scale;
+                        out = (g / (1.f + expf(-g))) * u;
+                    } else {
+                        out = v[r] * scale;
+                    }
+                }
+            }
+            if (n < N_out) {
+                if (MODE == QW_EPI_RESID) y[n] += out;
+                else y[n] = out;
+                if (ARGMAX)
+                    best = ((unsigned long long)ordered_f32(out) << 32) | (unsigned long long)(0xffffffffu - (uint32_t)n);
+            }
+        }
+        if (ARGMAX) {
+#pragma unroll
+            for (int off = 16; off; off >>= 1) {
+                const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
+                best = o > best ? o : best;
+            }
+            if (lane == 0) atomicMax(amax, best);
+        }
+    }
+}
+
+// Decode the argmax key into a token id and clear the key for the next step.
+__global__ void amax_to_token_kernel(unsigned long long* amax, int64_t* tok) {
+    const unsigned long long k = *amax;
+    *tok = (int64_t)(0xffffffffu - (uint32_t)(k & 0xffffffffull));
+    *amax = 0ull;
+}
+
 // ---- argmax (ops.cpp:213-272): first index of the maximum ------------------
 __global__ void argmax_kernel(const float* __restrict__ v, int n, int64_t* out) {
     __shared__ float sv[32];
@@ -323,6 +441,37 @@ int launch_gemv(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, in
     else if (mode == QW_EPI_RESID) { if (norm) SA_GEMV(QW_EPI_RESID, true); else SA_GEMV(QW_EPI_RESID, false); }
     else { if (norm) SA_GEMV(QW_EPI_SWIGLU, true); else SA_GEMV(QW_EPI_SWIGLU, false); }
 #undef SA_GEMV
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
+int launch_gemv2(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, int N_out, int K, const float* x,
+                 const float* nw, float eps, float* y, unsigned long long* amax) {
+    SA_CHECK_ARG(K % 256 == 0 && K / 8 <= 1024, "gemv2: K=%d (multiple of 256, <= 8192)", K);
+    const int threads = K / 8;
+    // rows per CTA: enough CTAs to cover the SMs several times over
+    const int rows = mode == QW_EPI_SWIGLU ? 2 * N_out : N_out;
+    const int R = rows >= 8 * 1024 ? 8 : (rows >= 4 * 512 ? 4 : 2);
+    const int outs = mode == QW_EPI_SWIGLU ? R / 2 : R;
+    const int grid = (N_out + outs - 1) / outs;
+#define SA_G2(M, N, RR, A) qk::gemv2_kernel<M, N, RR, A><<<grid, threads, 0, st>>>(W, N_out, K, x, nw, eps, y, amax)
+#define SA_G2R(M, N, A) do { if (R == 8) SA_G2(M, N, 8, A); else if (R == 4) SA_G2(M, N, 4, A); else SA_G2(M, N, 2, A); } while (0)
+    if (amax) {
+        SA_CHECK_ARG(mode == QW_EPI_STORE && norm, "gemv2: argmax only with the normed STORE head");
+        SA_G2R(QW_EPI_STORE, true, true);
+    } else if (mode == QW_EPI_STORE) {
+        if (norm) SA_G2R(QW_EPI_STORE, true, false); else SA_G2R(QW_EPI_STORE, false, false);
+    } else if (mode == QW_EPI_RESID) {
+        if (norm) SA_G2R(QW_EPI_RESID, true, false); else SA_G2R(QW_EPI_RESID, false, false);
+    } else {
+        if (norm) SA_G2R(QW_EPI_SWIGLU, true, false); else SA_G2R(QW_EPI_SWIGLU, false, false);
+    }
+#undef SA_G2R
+#undef SA_G2
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
+int launch_amax_to_token(cudaStream_t st, unsigned long long* amax, int64_t* tok) {
+    qk::amax_to_token_kernel<<<1, 1, 0, st>>>(amax, tok);
     SA_CUDA_TRY(cudaGetLastError());
     return SA_OK;
 }
