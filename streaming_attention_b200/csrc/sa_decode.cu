@@ -75,17 +75,27 @@ template <> struct Chunk<float> {
         float4 r = *reinterpret_cast<const float4*>(p);
         f[0] = r.x; f[1] = r.y; f[2] = r.z; f[3] = r.w;
     }
+    // global memory written by a kernel that may still be draining (programmatic launch)
+    static __device__ __forceinline__ void load_cg(const void* p, float* f) {
+        float4 r = __ldcg(reinterpret_cast<const float4*>(p));
+        f[0] = r.x; f[1] = r.y; f[2] = r.z; f[3] = r.w;
+    }
 };
 template <> struct Chunk<__nv_bfloat16> {
     static constexpr int VEC = 8;
-    static __device__ __forceinline__ void load(const void* p, float* f) {
-        uint4 r = *reinterpret_cast<const uint4*>(p);
+    static __device__ __forceinline__ void unpack(uint4 r, float* f) {
         const uint32_t w[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             f[2 * i] = __uint_as_float(w[i] << 16);
             f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
         }
+    }
+    static __device__ __forceinline__ void load(const void* p, float* f) {
+        unpack(*reinterpret_cast<const uint4*>(p), f);
+    }
+    static __device__ __forceinline__ void load_cg(const void* p, float* f) {
+        unpack(__ldcg(reinterpret_cast<const uint4*>(p)), f);
     }
 };
 
@@ -114,6 +124,8 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
     using S = Shape<KT, D>;
     constexpr int SR = S::STAGE_ROWS, RB = S::ROW_BYTES, CPL = S::CPL, CH = S::CH, VEC = S::VEC;
 
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ __align__(128) unsigned char smem[];
     unsigned char* kbuf = smem;
     unsigned char* vbuf = smem + STAGES * SR * RB;
@@ -169,7 +181,7 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
             const KT* qh = static_cast<const KT*>(a.q) + (size_t)qz * a.q_stride + (size_t)(kvh * G + g) * D;
 #pragma unroll
             for (int c = 0; c < CH; ++c) {
-                Chunk<KT>::load(qh + (sub + 8 * c) * VEC, &qr[g][c * VEC]);
+                Chunk<KT>::load_cg(qh + (sub + 8 * c) * VEC, &qr[g][c * VEC]);
 #pragma unroll
                 for (int e = 0; e < VEC; ++e) qr[g][c * VEC + e] *= a.qscale;
             }
@@ -678,8 +690,7 @@ int decode_dev_launch(cudaStream_t st, int* status, int num_sms, const float* q,
     dec::KernelFn fn = dec::pick<float>(d, hq / hkv);
     SA_CHECK_ARG(fn != nullptr, "decode_dev: hq/hkv=%d d=%d unsupported", hq / hkv, d);
     SA_RC_TRY(set_smem_attr_once((const void*)fn, dec::SMEM_BYTES));
-    fn<<<dim3(ns, hkv), dec::THREADS, dec::SMEM_BYTES, st>>>(a);
-    SA_CUDA_TRY(cudaGetLastError());
+    SA_CUDA_TRY(launch_pdl_k(2, fn, dim3(ns, hkv), dim3(dec::THREADS), dec::SMEM_BYTES, st, a));
     return SA_OK;
 }
 }  // namespace sa

@@ -5,6 +5,7 @@
 #include <cstdarg>
 #include <cstddef>
 #include <cstdio>
+#include <cstdlib>
 #include <string>
 
 #include "../../include/sa_cuda.h"
@@ -61,6 +62,41 @@ int sync_and_check(sa_ctx* ctx);
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+}  // namespace sa
+
+namespace sa {
+// Launch `k` with programmatic stream serialization (PDL): the kernel may start
+// while the previous kernel in the stream drains; it must call pdl_wait()
+// before reading that kernel's outputs.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args);
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl_k(int kind, void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                Args... args) {
+    static const int mask = std::getenv("SA_PDL_MASK") ? std::atoi(std::getenv("SA_PDL_MASK")) : -1;
+    if (!(mask & (1 << kind))) {
+        k<<<grid, block, smem, st>>>(static_cast<KArgs>(args)...);
+        return cudaGetLastError();
+    }
+    return launch_pdl(k, grid, block, smem, st, args...);
+}
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    static const bool disabled = std::getenv("SA_NO_PDL") != nullptr;   // ordinary launches if set
+    cfg.numAttrs = disabled ? 0 : 1;
+    return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
 }  // namespace sa
 
 #define SA_CUDA_TRY(expr)                                                          \

@@ -92,6 +92,13 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
     return p;
 }
 
+// Programmatic dependent launch: let the next kernel in the stream start its
+// launch now, and (in a kernel launched with programmatic serialization) wait
+// until the previous kernel has completed and its writes are visible.  Both
+// are no-ops for kernels launched the ordinary way.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // 2^x on the SFU (MUFU.EX2), flush-to-zero; 2^-inf = 0.
 __device__ __forceinline__ float ex2(float x) {
     float y;

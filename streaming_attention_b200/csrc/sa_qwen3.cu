@@ -25,6 +25,7 @@
 
 struct sa_qwen3 {
     sa_ctx* ctx = nullptr;
+    int device = 0;                      // the context's GPU (the model may outlive the context object)
     sa_qwen3_config c{};
     int QD = 0, KD = 0, NQKV = 0;
     // weights (device)
@@ -316,6 +317,7 @@ SA_API int sa_qwen3_create(sa_ctx* ctx, const sa_qwen3_config* cfg, sa_qwen3** o
     DeviceGuard guard(ctx->device);
     sa_qwen3* m = new sa_qwen3();
     m->ctx = ctx;
+    m->device = ctx->device;
     m->c = c;
     m->QD = c.hq * c.head_dim;
     m->KD = c.hkv * c.head_dim;
@@ -376,8 +378,9 @@ SA_API int sa_qwen3_create(sa_ctx* ctx, const sa_qwen3_config* cfg, sa_qwen3** o
 SA_API int sa_qwen3_destroy(sa_qwen3* m) {
     clear_error();
     if (!m) return SA_OK;
-    DeviceGuard guard(m->ctx->device);
-    cudaStreamSynchronize(m->ctx->stream);
+    // the context may already be destroyed: use only the model's own state
+    DeviceGuard guard(m->device);
+    cudaDeviceSynchronize();
     free_model(m);
     delete m;
     return SA_OK;
@@ -550,7 +553,7 @@ SA_API int sa_qwen3_forward(sa_qwen3* m, const int64_t* ids, int S, int use_cach
 static int decode_step_dev(sa_qwen3* m) {
     SA_RC(run_layers(m, 1, 0, m->d_state));
     SA_RC(run_head(m, 0, 1, m->ids));
-    SA_RC(launch_advance(m->cur, m->d_state, m->ids, m->d_toks, m->toks_cap, 1));
+    SA_RC(launch_advance(m->cur, m->d_state, m->ids, m->d_toks, m->toks_cap, 1, true));
     return SA_OK;
 }
 
@@ -583,7 +586,7 @@ SA_API int sa_qwen3_generate(sa_qwen3* m, const int64_t* prompt, int S, int n_ne
         SA_RC(run_head(m, S - 1, 1, m->ids));
         const int state[2] = {pos0 + S, 0};
         SA_CUDA_TRY(cudaMemcpyAsync(m->d_state, state, sizeof(state), cudaMemcpyHostToDevice, st));
-        SA_RC(launch_advance(st, m->d_state, m->ids, m->d_toks, m->toks_cap, 0));   // first new token
+        SA_RC(launch_advance(st, m->d_state, m->ids, m->d_toks, m->toks_cap, 0, false));   // first new token
         if (n_new > 1 && !m->dec_graph) SA_RC(capture(m, &m->dec_graph, [&]() { return decode_step_dev(m); }));
         for (int t = 1; t < n_new; ++t) SA_CUDA_TRY(cudaGraphLaunch(m->dec_graph, st));
         SA_CUDA_TRY(cudaMemcpyAsync(out_tokens, m->d_toks, (size_t)n_new * 8,

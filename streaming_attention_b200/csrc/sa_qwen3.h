@@ -36,7 +36,8 @@ int launch_rope_table(cudaStream_t st, int n_pos, int D, float theta, float* cos
 int launch_qknorm_rope_append(cudaStream_t st, const float* qkv, int M, int hq, int hkv, const float* qn,
                               const float* kn, const float* cos_t, const float* sin_t, int pos0, const int* pos_dev,
                               int row_shift, float* q_out, float* kc, float* vc, int max_seq);
-int launch_advance(cudaStream_t st, int* state, const int64_t* tok, int64_t* toks, int cap, int inc_len);
+int launch_advance(cudaStream_t st, int* state, const int64_t* tok, int64_t* toks, int cap, int inc_len,
+                   bool after_kernel);
 size_t decode_dev_scratch_floats(int num_sms, int max_T, int d, int hq, int hkv, int* n_splits);
 int decode_dev_launch(cudaStream_t st, int* status, int num_sms, const float* q, const float* k, const float* v,
                       long long kv_head_stride, const int* len_dev, int T_host, int max_T, int d, int hq, int hkv,

@@ -40,6 +40,8 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 // ---- embedding (ops.cpp:278-309): x[m, :] = E[id_m, :] ---------------------
 __global__ void embedding_kernel(const int64_t* ids, int M, const __nv_bfloat16* E, int V, int H, float* x,
                                  int* status) {
+    pdl_trigger();
+    pdl_wait();
     const int m = blockIdx.x;
     const int64_t id = ids[m];
     const bool ok = id >= 0 && id < V;
@@ -113,6 +115,8 @@ __global__ void qknorm_rope_append_kernel(const float* qkv, int M, int hq, int h
                                           const int* pos_dev, int row_shift, float* q_out, float* kc, float* vc,
                                           int max_seq) {
     constexpr int D = 128;
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nh = hq + 2 * hkv;
@@ -122,7 +126,7 @@ __global__ void qknorm_rope_append_kernel(const float* qkv, int M, int hq, int h
     const int row = pos + row_shift;                       // cache row written
     if (row >= max_seq) return;       // the host checks capacity; never write past the cache
     const float* src = qkv + (size_t)m * nh * D + (size_t)h * D;
-    float4 v4 = *reinterpret_cast<const float4*>(src + 4 * lane);
+    float4 v4 = __ldcg(reinterpret_cast<const float4*>(src + 4 * lane));   // produced by the previous kernel
     float e[4] = {v4.x, v4.y, v4.z, v4.w};
     if (h >= hq + hkv) {  // V head
         float* dst = vc + ((size_t)(h - hq - hkv) * max_seq + row) * D;
@@ -236,10 +240,13 @@ __device__ __forceinline__ uint32_t ordered_f32(float f) {
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// Activations (x, and y in RESID mode) come from the previous kernel, which may
+// still be draining when this one starts (programmatic launch): they are read
+// through L2 (ld.global.cg) after pdl_wait, never through the read-only path.
 template <int MODE, bool NORM, int R, bool ARGMAX>
 __global__ void gemv2_kernel(const __nv_bfloat16* __restrict__ W, int N_out, int K,
-                             const float* __restrict__ x, const float* __restrict__ nw, float eps,
-                             float* __restrict__ y, unsigned long long* amax) {
+                             const float* x, const float* __restrict__ nw, float eps,
+                             float* y, unsigned long long* amax) {
     constexpr int NV = R + 1;                      // R dot products + sum of squares
     __shared__ float red[32][NV];
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5, nwarp = blockDim.x >> 5;
@@ -257,11 +264,14 @@ __global__ void gemv2_kernel(const __nv_bfloat16* __restrict__ W, int N_out, int
             rows[r] = min(o0 + r, N_out - 1);
         }
     }
+    pdl_trigger();
     uint4 w[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) w[r] = __ldg(reinterpret_cast<const uint4*>(W + (size_t)rows[r] * K) + t);
-    const float4 xa = __ldg(reinterpret_cast<const float4*>(x) + 2 * t);
-    const float4 xb = __ldg(reinterpret_cast<const float4*>(x) + 2 * t + 1);
+    // weights do not depend on the previous kernel; the activations do
+    pdl_wait();
+    const float4 xa = __ldcg(reinterpret_cast<const float4*>(x) + 2 * t);
+    const float4 xb = __ldcg(reinterpret_cast<const float4*>(x) + 2 * t + 1);
     float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
     float v[NV];
     v[R] = 0.f;
@@ -316,7 +326,7 @@ __global__ void gemv2_kernel(const __nv_bfloat16* __restrict__ W, int N_out, int
                 }
             }
             if (n < N_out) {
-                if (MODE == QW_EPI_RESID) y[n] += out;
+                if (MODE == QW_EPI_RESID) y[n] = __ldcg(y + n) + out;
                 else y[n] = out;
                 if (ARGMAX)
                     best = ((unsigned long long)ordered_f32(out) << 32) | (unsigned long long)(0xffffffffu - (uint32_t)n);
@@ -335,7 +345,9 @@ __global__ void gemv2_kernel(const __nv_bfloat16* __restrict__ W, int N_out, int
 
 // Decode the argmax key into a token id and clear the key for the next step.
 __global__ void amax_to_token_kernel(unsigned long long* amax, int64_t* tok) {
-    const unsigned long long k = *amax;
+    pdl_trigger();
+    pdl_wait();
+    const unsigned long long k = __ldcg(amax);      // folded in by the previous kernel's atomics
     *tok = (int64_t)(0xffffffffu - (uint32_t)(k & 0xffffffffull));
     *amax = 0ull;
 }
@@ -376,23 +388,35 @@ __global__ void argmax_kernel(const float* __restrict__ v, int n, int64_t* out) 
 // step counter; with inc_len the token just processed is now in the cache.
 // state[0] = cache length, state[1] = tokens recorded.
 __global__ void advance_kernel(int* state, const int64_t* tok, int64_t* toks, int cap, int inc_len) {
-    const int s = state[1];
-    if (s < cap) toks[s] = *tok;
-    state[1] = s + 1;
-    if (inc_len) state[0] += 1;
+    pdl_trigger();
+    pdl_wait();
+    volatile int* vs = state;                       // written by earlier steps
+    const int s = vs[1];
+    if (s < cap) toks[s] = __ldcg(reinterpret_cast<const long long*>(tok));
+    vs[1] = s + 1;
+    if (inc_len) vs[0] = vs[0] + 1;
 }
 
 }  // namespace qk
 
 // ---- launchers --------------------------------------------------------------
-int launch_advance(cudaStream_t st, int* state, const int64_t* tok, int64_t* toks, int cap, int inc_len) {
-    qk::advance_kernel<<<1, 1, 0, st>>>(state, tok, toks, cap, inc_len);
+int launch_advance(cudaStream_t st, int* state, const int64_t* tok, int64_t* toks, int cap, int inc_len,
+                   bool after_kernel) {
+    // programmatic launch only directly after another kernel: after a copy
+    // (the decode state) the ordinary stream order is needed
+    if (after_kernel)
+        SA_CUDA_TRY(launch_pdl_k(3, qk::advance_kernel, dim3(1), dim3(1), 0, st, state, tok, toks, cap, inc_len));
+    else
+        qk::advance_kernel<<<1, 1, 0, st>>>(state, tok, toks, cap, inc_len);
     SA_CUDA_TRY(cudaGetLastError());
     return SA_OK;
 }
 int launch_embedding(cudaStream_t st, const int64_t* ids, int M, const __nv_bfloat16* E, int V, int H, float* x,
                      int* status) {
+    // the first kernel of a forward follows the copy of the token ids, a
+    // non-kernel stream operation, so it is launched the ordinary way
     qk::embedding_kernel<<<M, 256, 0, st>>>(ids, M, E, V, H, x, status);
+    SA_CUDA_TRY(cudaGetLastError());
     SA_CUDA_TRY(cudaGetLastError());
     return SA_OK;
 }
@@ -424,8 +448,8 @@ int launch_qknorm_rope_append(cudaStream_t st, const float* qkv, int M, int hq, 
                               const float* kn, const float* cos_t, const float* sin_t, int pos0, const int* pos_dev,
                               int row_shift, float* q_out, float* kc, float* vc, int max_seq) {
     const int warps = M * (hq + 2 * hkv);
-    qk::qknorm_rope_append_kernel<<<(warps + 7) / 8, 256, 0, st>>>(qkv, M, hq, hkv, qn, kn, cos_t, sin_t, pos0,
-                                                                   pos_dev, row_shift, q_out, kc, vc, max_seq);
+    SA_CUDA_TRY(launch_pdl_k(1, qk::qknorm_rope_append_kernel, dim3((warps + 7) / 8), dim3(256), 0, st, qkv, M, hq, hkv,
+                           qn, kn, cos_t, sin_t, pos0, pos_dev, row_shift, q_out, kc, vc, max_seq));
     SA_CUDA_TRY(cudaGetLastError());
     return SA_OK;
 }
@@ -453,7 +477,8 @@ int launch_gemv2(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, i
     const int R = rows >= 8 * 1024 ? 8 : (rows >= 4 * 512 ? 4 : 2);
     const int outs = mode == QW_EPI_SWIGLU ? R / 2 : R;
     const int grid = (N_out + outs - 1) / outs;
-#define SA_G2(M, N, RR, A) qk::gemv2_kernel<M, N, RR, A><<<grid, threads, 0, st>>>(W, N_out, K, x, nw, eps, y, amax)
+#define SA_G2(M, N, RR, A) SA_CUDA_TRY(launch_pdl_k(0, qk::gemv2_kernel<M, N, RR, A>, dim3(grid), dim3(threads), 0, st, \
+                                                  W, N_out, K, x, nw, eps, y, amax))
 #define SA_G2R(M, N, A) do { if (R == 8) SA_G2(M, N, 8, A); else if (R == 4) SA_G2(M, N, 4, A); else SA_G2(M, N, 2, A); } while (0)
     if (amax) {
         SA_CHECK_ARG(mode == QW_EPI_STORE && norm, "gemv2: argmax only with the normed STORE head");
@@ -471,7 +496,7 @@ int launch_gemv2(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, i
     return SA_OK;
 }
 int launch_amax_to_token(cudaStream_t st, unsigned long long* amax, int64_t* tok) {
-    qk::amax_to_token_kernel<<<1, 1, 0, st>>>(amax, tok);
+    SA_CUDA_TRY(launch_pdl_k(3, qk::amax_to_token_kernel, dim3(1), dim3(1), 0, st, amax, tok));
     SA_CUDA_TRY(cudaGetLastError());
     return SA_OK;
 }
