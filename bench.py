@@ -462,6 +462,18 @@ def run_ours(args):
                 "metric": "attn TFLOP/s (causal prefill)", "value": round(ptf, 2),
                 "ms": round(pms, 4), "frac_of_bf16_peak": round(ptf / bpk, 4),
                 "peak": f"{bpk} ({bkind} bf16_tflops)", "workload": PF_WORKLOAD}}
+            try:
+                q3, weights = measure_qwen3(ctx, dev, stream, 5, 2)
+                q3line = {"metric": "Qwen3-0.6B tok/s", "workload": Q3_WORKLOAD,
+                          **{k: round(v, 3) for k, v in q3.items()}}
+                if not args.no_cpu:
+                    try:
+                        q3line["cpu_baseline"] = cpu_qwen3_baseline(weights)
+                    except Exception as e:
+                        q3line["cpu_baseline"] = {"value": None, "sample": f"unavailable: {e}"}
+                result["extra"]["qwen3_configs3_4"] = q3line
+            except Exception as e:
+                result["extra"]["qwen3_configs3_4"] = {"error": str(e)}
         print(json.dumps(result), flush=True)
 
     ctx.close()
