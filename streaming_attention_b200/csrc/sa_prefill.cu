@@ -8,25 +8,35 @@
 //   both after repeat_kv (qwen3_ops.cpp:194-234).
 //
 // Design (tensor-core bound: 4*hq*d*S(S+1)/2 FLOPs causal).
-//  * One CTA per (128-row query tile, pair of query heads sharing a KV head).
-//    The two heads' Q tiles share every K/V tile in shared memory, so GQA
-//    costs one K/V load per pair, and the two softmax warpgroups alternate
-//    with the tensor core (while one head's softmax runs, the MMA warp
-//    computes the other head's P.V and next S).
-//  * Warp roles (12 warps): warp 0 issues TMA loads (Q once; K and V tiles of
-//    64 keys into a 3-stage ring, 128-byte swizzle); warp 1 owns TMEM (512
-//    columns: S_A, S_B 64 columns each, O_A, O_B 128 each) and one lane issues
-//    every tcgen05.mma; warps 4-7 and 8-11 are the softmax warpgroups of the
-//    two heads (one thread per query row = TMEM lane).
-//  * S = Q K^T: M=128, N=64, K=128 (8 MMAs of K=16), A and B K-major.
-//    O += P V: M=128, N=128, K=64 (4 MMAs), A = P (bf16, written by the softmax
-//    threads to shared memory in the K-major 128-byte-swizzled layout), B = V
-//    MN-major (the V tile as loaded: keys x d).
+//  * One CTA per unit of two 128-row query "slots" that read the same K/V
+//    tiles: two query heads of one KV group at the same query tile (hq/hkv
+//    even), or one head at two neighbouring query tiles (hq/hkv odd).  The two
+//    slots' softmaxes alternate with the tensor core: while one slot's
+//    softmax runs, the tensor core computes the other slot's P.V and next S.
+//  * Warp roles (12 warps): warp 0 issues TMA loads (Q of both slots once; K
+//    and V tiles of 128 keys into separate 2-deep rings, 128-byte swizzle);
+//    warp 1 owns TMEM and one lane issues every tcgen05.mma; warps 4-7 and
+//    8-11 are the softmax warpgroups of slots 0 and 1 (one thread per query
+//    row = TMEM lane; warp w reads lanes 32*(w%4)..).  The launch grants 168
+//    registers a thread; the first warpgroup gives back down to 72 and the
+//    softmax warpgroups take 216 (128*72 + 256*216 = 384*168).
+//  * TMEM (512 columns): S of slot x at 128x (128 fp32 columns); P, the bf16
+//    probabilities, written back over the upper half of S (64 columns of bf16
+//    pairs); O of slot x at 256 + 128x.
+//  * S = Q K^T: M=128, N=128, K=128 (8 MMAs of K=16, A and B K-major from
+//    shared memory).  O += P V: M=128, N=128, K=128 (8 MMAs), A = P read from
+//    TMEM, B = V MN-major from shared memory (the V tile as loaded: keys x d).
+//    MMAs into different accumulators are not ordered by the hardware, so S
+//    of the next tile (which overwrites P) is issued only once the P.V that
+//    reads P has completed.
 //  * Online softmax in the exp2 domain (scale*log2 e folded into the scores)
 //    with a lazy rescale: the running max used for the exponent only moves
 //    when a row's max grows by more than 8 (2^8 headroom in P), and only then
-//    is the row's O accumulator in TMEM loaded, scaled and stored back.
-//  * Causal: a tile's KV range stops at the last key its last row may see;
+//    is the row's O accumulator in TMEM loaded, scaled and stored back.  The
+//    kernel can evaluate a fraction of the exponentials on the FMA pipe
+//    (exp2_poly, template parameter POLY); the shipped instance keeps them all
+//    on the SFU, which measured fastest.
+//  * Causal: a slot's KV range stops at the last key its last row may see;
 //    only tiles crossing the diagonal are masked.  Heavy (late) query tiles
 //    are scheduled first.
 //  * Every mbarrier wait is bounded; a timeout sets the status word, stops all
@@ -40,30 +50,29 @@
 namespace sa {
 namespace pf {
 
-constexpr int BM = 128, BN = 64, D = 128;
-constexpr int STAGES = 3;
+constexpr int BM = 128, BN = 128, D = 128;
+constexpr int KST = 2, VST = 2;                // K and V ring depths
 constexpr int THREADS = 384;
-constexpr int Q_BYTES = BM * D * 2;            // 32 KB per head
-constexpr int KV_BYTES = BN * D * 2;           // 16 KB per K (or V) tile
-constexpr int P_BYTES = BM * BN * 2;           // 16 KB per head
-constexpr int OFF_QA = 0;
-constexpr int OFF_QB = OFF_QA + Q_BYTES;
-constexpr int OFF_K = OFF_QB + Q_BYTES;
-constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
-constexpr int OFF_PA = OFF_V + STAGES * KV_BYTES;
-constexpr int OFF_PB = OFF_PA + P_BYTES;
-constexpr int OFF_BAR = OFF_PB + P_BYTES;      // 196608
+constexpr int REG_CTRL = 72, REG_SOFTMAX = 216;   // 128*72 + 256*216 == THREADS*168
+constexpr int BOX_BYTES = 128 * 128;           // one [128 rows x 64 bf16] box (16 KB)
+constexpr int TILE_BYTES = 2 * BOX_BYTES;      // a [128 x 128] bf16 tile as two boxes
+constexpr int OFF_Q = 0;                       // slot x at OFF_Q + x * TILE_BYTES
+constexpr int OFF_K = 2 * TILE_BYTES;
+constexpr int OFF_V = OFF_K + KST * TILE_BYTES;
+constexpr int OFF_BAR = OFF_V + VST * TILE_BYTES;  // 196608
 constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;   // + barriers + alignment slack
 constexpr uint32_t TMEM_COLS = 512;
-// TMEM columns: S of head x at x*64 (64 columns), O of head x at 128 + x*128
-__device__ __forceinline__ uint32_t col_s(int x) { return (uint32_t)x * 64u; }
-__device__ __forceinline__ uint32_t col_o(int x) { return 128u + (uint32_t)x * 128u; }
+__device__ __forceinline__ uint32_t col_s(int x) { return (uint32_t)x * 128u; }
+__device__ __forceinline__ uint32_t col_p(int x) { return (uint32_t)x * 128u + 64u; }
+__device__ __forceinline__ uint32_t col_o(int x) { return 256u + (uint32_t)x * 128u; }
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float RESCALE_THRESHOLD = 8.0f;      // log2 units
 
 struct Args {
     int Sq, Skv, q_pos0, hq, hkv, G;
-    int n_qtiles, upk;          // units (head pairs or singles) per KV head
+    int n_qtiles;
+    int pair_heads;             // 1: slots are heads (h, h+1) of one q tile; 0: q tiles (2p, 2p+1) of one head
+    int units_per_row;          // units per heavy-first row of the schedule
     float sl2;                  // scale * log2(e)
     void* out;
     long long o_tok, o_head;    // element strides of out
@@ -73,8 +82,8 @@ struct Args {
 
 struct Bars {
     uint64_t q_full;
-    uint64_t k_full[STAGES], v_full[STAGES], kv_empty[STAGES];
-    uint64_t s_full[2], p_full[2], o_full[2];
+    uint64_t k_full[KST], k_empty[KST], v_full[VST], v_empty[VST];
+    uint64_t s_full[2], p_full[2], pv_done[2], o_full[2];
     uint64_t drain;
     uint32_t tmem_base;
     int abort;
@@ -99,6 +108,32 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// 2^x on the FMA pipe, for x <= 8 (clamped below at -126): x = n + f with n
+// the nearest integer (taken from the low mantissa bits of x + 1.5*2^23) and
+// f in [-0.5, 0.5]; 2^f by a degree-3 polynomial fitted here to 2^f on that
+// interval (max relative error 7.5e-5, far below the bf16 rounding of P);
+// 2^n added to the exponent field with an integer add.  No transcendental-
+// unit instruction is used.
+__device__ __forceinline__ float exp2_poly(float x) {
+    x = fmaxf(x, -126.f);
+    const float t = x + 12582912.f;
+    const float f = x - (t - 12582912.f);
+    float p = fmaf(0.0551716685295105f, f, 0.2426111251115799f);
+    p = fmaf(p, f, 0.6932609677314758f);
+    p = fmaf(p, f, 0.9999280571937561f);
+    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+// Every POLY-th exponential (by column) on the FMA pipe; 0: all on the SFU.
+template <int POLY>
+__device__ __forceinline__ float exp2_mix(float x, int c) {
+    if constexpr (POLY > 0) {
+        if ((c % POLY) == POLY - 1) return exp2_poly(x);
+    }
+    return ex2(x);
+}
+
+template <int POLY>
 __global__ void __launch_bounds__(THREADS, 1)
 prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                const __grid_constant__ CUtensorMap tv, const Args a) {
@@ -110,27 +145,51 @@ prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     volatile int* abort = &B->abort;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const bool paired = a.G >= 2;
-    const int per_tile = a.hkv * a.upk;
-    const int qt = a.n_qtiles - 1 - (int)blockIdx.x / per_tile;     // heavy tiles first
-    const int r = (int)blockIdx.x % per_tile;
-    const int kvh = r / a.upk, pair = r % a.upk;
-    const int hA = paired ? kvh * a.G + 2 * pair : kvh;
-    const int q0 = qt * BM;
-    const int last_row = min(q0 + BM - 1, a.Sq - 1);
-    const int last_key = min(a.Skv - 1, a.q_pos0 + last_row);
-    const int n_kv = last_key / BN + 1;
+    // ---- this CTA's unit: heads, first query rows and KV extent of its two slots
+    const int rowi = (int)blockIdx.x / a.units_per_row;
+    const int u = (int)blockIdx.x % a.units_per_row;
+    int head[2], q0[2], nkv[2];
+    bool on[2];
+    int kvh;
+    if (a.pair_heads) {
+        const int qt = a.n_qtiles - 1 - rowi;                       // heavy tiles first
+        const int upk = a.G / 2;
+        kvh = u / upk;
+        head[0] = kvh * a.G + 2 * (u % upk);
+        head[1] = head[0] + 1;
+        q0[0] = q0[1] = qt * BM;
+        on[0] = on[1] = true;
+    } else {
+        const int n_pairs = (a.n_qtiles + 1) / 2;
+        const int qp = n_pairs - 1 - rowi;
+        head[0] = head[1] = u;
+        kvh = u / a.G;
+        q0[0] = 2 * qp * BM;
+        q0[1] = q0[0] + BM;
+        on[0] = true;
+        on[1] = q0[1] < a.Sq;
+    }
+    for (int x = 0; x < 2; ++x) {
+        const int last_row = min(q0[x] + BM - 1, a.Sq - 1);
+        const int last_key = min(a.Skv - 1, a.q_pos0 + last_row);
+        nkv[x] = on[x] ? last_key / BN + 1 : 0;
+    }
+    const int n_kv = max(nkv[0], nkv[1]);
 
     if (tid == 0) {
         mbar_init(&B->q_full, 1);
-        for (int s = 0; s < STAGES; ++s) {
+        for (int s = 0; s < KST; ++s) {
             mbar_init(&B->k_full[s], 1);
+            mbar_init(&B->k_empty[s], 1);
+        }
+        for (int s = 0; s < VST; ++s) {
             mbar_init(&B->v_full[s], 1);
-            mbar_init(&B->kv_empty[s], 1);
+            mbar_init(&B->v_empty[s], 1);
         }
         for (int x = 0; x < 2; ++x) {
             mbar_init(&B->s_full[x], 1);
-            mbar_init(&B->p_full[x], 128);
+            mbar_init(&B->p_full[x], 4);      // one arrival per softmax warp
+            mbar_init(&B->pv_done[x], 1);
             mbar_init(&B->o_full[x], 1);
         }
         mbar_init(&B->drain, 1);
@@ -143,164 +202,162 @@ prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     tc::fence_after_sync();
     const uint32_t tbase = B->tmem_base;
 
-    if (warp == 0) {
+    if (warp < 4) {
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
+      if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
             tc::prefetch_tmap(&tq);
             tc::prefetch_tmap(&tk);
             tc::prefetch_tmap(&tv);
-            mbar_arrive_expect_tx(&B->q_full, (paired ? 2 : 1) * Q_BYTES);
-            for (int kb = 0; kb < 2; ++kb) {
-                tc::tma_load_2d(sm + OFF_QA + kb * (Q_BYTES / 2), &tq, hA * D + kb * 64, q0, &B->q_full);
-                if (paired)
-                    tc::tma_load_2d(sm + OFF_QB + kb * (Q_BYTES / 2), &tq, (hA + 1) * D + kb * 64, q0,
+            mbar_arrive_expect_tx(&B->q_full, (on[1] ? 2 : 1) * TILE_BYTES);
+            for (int x = 0; x < 2; ++x) {
+                if (!on[x]) continue;
+                for (int kb = 0; kb < 2; ++kb)
+                    tc::tma_load_2d(sm + OFF_Q + x * TILE_BYTES + kb * BOX_BYTES, &tq, head[x] * D + kb * 64, q0[x],
                                     &B->q_full);
             }
-            int issued = 0;
+            int k_issued = 0, v_issued = 0;
             for (int j = 0; j < n_kv; ++j) {
-                const int s = j % STAGES;
-                if (j >= STAGES && !wait_ab(&B->kv_empty[s], ((j / STAGES) & 1) ^ 1, abort, a.status)) break;
-                mbar_arrive_expect_tx(&B->k_full[s], KV_BYTES);
+                const int ks = j % KST, vs = j % VST;
+                if (j >= KST && !wait_ab(&B->k_empty[ks], ((j / KST) & 1) ^ 1, abort, a.status)) break;
+                mbar_arrive_expect_tx(&B->k_full[ks], TILE_BYTES);
                 for (int kb = 0; kb < 2; ++kb)
-                    tc::tma_load_2d(sm + OFF_K + s * KV_BYTES + kb * (KV_BYTES / 2), &tk, kvh * D + kb * 64,
-                                    j * BN, &B->k_full[s]);
-                mbar_arrive_expect_tx(&B->v_full[s], KV_BYTES);
+                    tc::tma_load_2d(sm + OFF_K + ks * TILE_BYTES + kb * BOX_BYTES, &tk, kvh * D + kb * 64, j * BN,
+                                    &B->k_full[ks]);
+                k_issued = j + 1;
+                if (j >= VST && !wait_ab(&B->v_empty[vs], ((j / VST) & 1) ^ 1, abort, a.status)) break;
+                mbar_arrive_expect_tx(&B->v_full[vs], TILE_BYTES);
                 for (int kb = 0; kb < 2; ++kb)
-                    tc::tma_load_2d(sm + OFF_V + s * KV_BYTES + kb * (KV_BYTES / 2), &tv, kvh * D + kb * 64,
-                                    j * BN, &B->v_full[s]);
-                issued = j + 1;
+                    tc::tma_load_2d(sm + OFF_V + vs * TILE_BYTES + kb * BOX_BYTES, &tv, kvh * D + kb * 64, j * BN,
+                                    &B->v_full[vs]);
+                v_issued = j + 1;
             }
             if (*abort) {
                 // let the loads still in flight land before the CTA exits
                 mbar_wait(&B->q_full, 0, nullptr);
-                for (int j = max(0, issued - STAGES); j < issued; ++j) {
-                    mbar_wait(&B->k_full[j % STAGES], (j / STAGES) & 1, nullptr);
-                    mbar_wait(&B->v_full[j % STAGES], (j / STAGES) & 1, nullptr);
-                }
+                for (int j = max(0, k_issued - KST); j < k_issued; ++j)
+                    mbar_wait(&B->k_full[j % KST], (j / KST) & 1, nullptr);
+                for (int j = max(0, v_issued - VST); j < v_issued; ++j)
+                    mbar_wait(&B->v_full[j % VST], (j / VST) & 1, nullptr);
             }
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
+        // Per KV tile j and slot x: P.V(j) once the slot's P is in TMEM, then,
+        // after that P.V has completed, S(j+1) over the same TMEM columns.
+        // The other slot's softmax runs meanwhile.
         if (lane == 0) {
             constexpr uint32_t idS = tc::idesc_bf16_f32(BM, BN, false, false);
             constexpr uint32_t idO = tc::idesc_bf16_f32(BM, D, false, true);
-            const uint32_t sQ[2] = {smem_u32(sm + OFF_QA), smem_u32(sm + OFF_QB)};
-            const uint32_t sP[2] = {smem_u32(sm + OFF_PA), smem_u32(sm + OFF_PB)};
-            const uint32_t sK = smem_u32(sm + OFF_K), sV = smem_u32(sm + OFF_V);
-            auto issue_S = [&](int x, int s) {
+            const uint32_t sQ = smem_u32(sm + OFF_Q), sK = smem_u32(sm + OFF_K), sV = smem_u32(sm + OFF_V);
+            auto act = [&](int x, int j) { return j < nkv[x]; };
+            auto issue_S = [&](int x, int j) {
+                const uint32_t q = sQ + x * TILE_BYTES, k = sK + (j % KST) * TILE_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint64_t ad = tc::sdesc_sw128(sQ[x] + (kk >> 2) * (Q_BYTES / 2) + (kk & 3) * 32, 16, 1024);
-                    const uint64_t bd = tc::sdesc_sw128(sK + s * KV_BYTES + (kk >> 2) * (KV_BYTES / 2) + (kk & 3) * 32,
-                                                        16, 1024);
-                    tc::mma_bf16(tbase + col_s(x), ad, bd, idS, kk > 0);
+                    const uint32_t off = (kk >> 2) * BOX_BYTES + (kk & 3) * 32;
+                    tc::mma_bf16(tbase + col_s(x), tc::sdesc_sw128(q + off, 16, 1024),
+                                 tc::sdesc_sw128(k + off, 16, 1024), idS, kk > 0);
                 }
             };
-            auto issue_PV = [&](int x, int s, bool acc) {
+            auto issue_PV = [&](int x, int j) {
+                const uint32_t v = sV + (j % VST) * TILE_BYTES;
 #pragma unroll
-                for (int kk = 0; kk < BN / 16; ++kk) {
-                    const uint64_t ad = tc::sdesc_sw128(sP[x] + kk * 32, 16, 1024);
-                    const uint64_t bd = tc::sdesc_sw128(sV + s * KV_BYTES + kk * 2048, KV_BYTES / 2, 1024);
-                    tc::mma_bf16(tbase + col_o(x), ad, bd, idO, (acc || kk > 0) ? 1u : 0u);
-                }
+                for (int kk = 0; kk < BN / 16; ++kk)
+                    tc::mma_bf16_ts(tbase + col_o(x), tbase + col_p(x) + kk * 8,
+                                    tc::sdesc_sw128(v + kk * 2048, BOX_BYTES, 1024), idO,
+                                    (j > 0 || kk > 0) ? 1u : 0u);
             };
-            bool ok = wait_ab(&B->q_full, 0, abort, a.status);
+            bool ok = wait_ab(&B->q_full, 0, abort, a.status) && wait_ab(&B->k_full[0], 0, abort, a.status);
             tc::fence_after_sync();
+            if (ok) {
+                for (int x = 0; x < 2; ++x)
+                    if (act(x, 0)) {
+                        issue_S(x, 0);
+                        tc::mma_commit(&B->s_full[x]);
+                    }
+                tc::mma_commit(&B->k_empty[0]);
+            }
             for (int j = 0; ok && j < n_kv; ++j) {
-                const int s = j % STAGES;
-                const uint32_t ph = (j / STAGES) & 1;
-                if (j == 0) {
-                    if (!(ok = wait_ab(&B->k_full[s], ph, abort, a.status))) break;
+                if (!(ok = wait_ab(&B->v_full[j % VST], (j / VST) & 1, abort, a.status))) break;
+                bool k_next = false;
+                for (int x = 0; ok && x < 2; ++x) {
+                    if (!act(x, j)) continue;
+                    if (!(ok = wait_ab(&B->p_full[x], j & 1, abort, a.status))) break;
                     tc::fence_after_sync();
-                    issue_S(0, s);
-                    tc::mma_commit(&B->s_full[0]);
-                    if (paired) {
-                        issue_S(1, s);
-                        tc::mma_commit(&B->s_full[1]);
+                    issue_PV(x, j);
+                    tc::mma_commit(&B->pv_done[x]);
+                    if (j + 1 == nkv[x]) {
+                        tc::mma_commit(&B->o_full[x]);
+                        continue;
                     }
-                }
-                if (!(ok = wait_ab(&B->v_full[s], ph, abort, a.status))) break;
-                if (!(ok = wait_ab(&B->p_full[0], j & 1, abort, a.status))) break;
-                tc::fence_after_sync();
-                issue_PV(0, s, j > 0);
-                const int s2 = (j + 1) % STAGES;
-                if (j + 1 < n_kv) {
-                    if (!(ok = wait_ab(&B->k_full[s2], ((j + 1) / STAGES) & 1, abort, a.status))) break;
-                    tc::fence_after_sync();
-                    issue_S(0, s2);
-                    tc::mma_commit(&B->s_full[0]);
-                } else {
-                    tc::mma_commit(&B->o_full[0]);
-                }
-                if (paired) {
-                    if (!(ok = wait_ab(&B->p_full[1], j & 1, abort, a.status))) break;
-                    tc::fence_after_sync();
-                    issue_PV(1, s, j > 0);
-                }
-                tc::mma_commit(&B->kv_empty[s]);
-                if (paired) {
-                    if (j + 1 < n_kv) {
-                        issue_S(1, s2);
-                        tc::mma_commit(&B->s_full[1]);
-                    } else {
-                        tc::mma_commit(&B->o_full[1]);
+                    if (!k_next) {
+                        const int j1 = j + 1;
+                        if (!(ok = wait_ab(&B->k_full[j1 % KST], (j1 / KST) & 1, abort, a.status))) break;
+                        k_next = true;
                     }
+                    if (!(ok = wait_ab(&B->pv_done[x], j & 1, abort, a.status))) break;
+                    tc::fence_after_sync();
+                    issue_S(x, j + 1);
+                    tc::mma_commit(&B->s_full[x]);
                 }
+                if (!ok) break;
+                tc::mma_commit(&B->v_empty[j % VST]);
+                if (k_next) tc::mma_commit(&B->k_empty[(j + 1) % KST]);
             }
             // all issued MMAs complete before TMEM is released
             tc::mma_commit(&B->drain);
             mbar_wait(&B->drain, 0, nullptr);
         }
-    } else if (warp >= 4) {
+      }
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_SOFTMAX));
         // ------------------------------------------------ softmax warpgroups
-        const int x = (warp >= 8) ? 1 : 0;
-        if (x == 0 || paired) {
-            const int h = hA + x;
-            const int row = (warp & 3) * 32 + lane;
-            const uint32_t lane_addr = tbase + ((uint32_t)((warp & 3) * 32) << 16);
-            const int qrow = q0 + row;
+        const int x = (warp - 4) >> 2;
+        const bool my_on = x ? on[1] : on[0];
+        const int my_q0 = x ? q0[1] : q0[0], my_nkv = x ? nkv[1] : nkv[0], h = x ? head[1] : head[0];
+        if (my_on) {
+            const int quad = warp & 3;
+            const int row = quad * 32 + lane;
+            const uint32_t lane_addr = tbase + ((uint32_t)(quad * 32) << 16);
+            const int qrow = my_q0 + row;
             const int limit = a.q_pos0 + qrow;          // last visible key of this row
-            unsigned char* P = sm + (x ? OFF_PB : OFF_PA);
-            unsigned char* prow = P + (row >> 3) * 1024 + (row & 7) * 128;
-            float m = -INFINITY, l = 0.f;
+            const float sl2 = a.sl2;
+            float m = -INFINITY, l = 0.f;               // m in scaled log2 units
             bool ok = true;
-            for (int j = 0; j < n_kv; ++j) {
+            for (int j = 0; j < my_nkv; ++j) {
                 if (!(ok = wait_ab(&B->s_full[x], j & 1, abort, a.status))) break;
                 tc::fence_after_sync();
-                uint32_t r0[32], r1[32];
-                tc::tmem_ld32(lane_addr + col_s(x), r0);
-                tc::tmem_ld32(lane_addr + col_s(x) + 32, r1);
-                tc::tmem_wait_ld();
-                float s[BN];
+                uint32_t u32[BN];
 #pragma unroll
-                for (int c = 0; c < 32; ++c) {
-                    s[c] = __uint_as_float(r0[c]) * a.sl2;
-                    s[32 + c] = __uint_as_float(r1[c]) * a.sl2;
-                }
+                for (int cb = 0; cb < BN / 32; ++cb) tc::tmem_ld32p(lane_addr + col_s(x) + cb * 32, u32 + cb * 32);
+                tc::tmem_wait_ld();
+                float* sc = reinterpret_cast<float*>(u32);
                 const int k0 = j * BN;
-                if (k0 + BN - 1 > a.q_pos0 + q0 || k0 + BN > a.Skv) {
+                if (k0 + BN - 1 > a.q_pos0 + my_q0 || k0 + BN > a.Skv) {
 #pragma unroll
                     for (int c = 0; c < BN; ++c)
-                        if (k0 + c > limit || k0 + c >= a.Skv) s[c] = -INFINITY;
+                        if (k0 + c > limit || k0 + c >= a.Skv) sc[c] = -INFINITY;
                 }
-                float mx = s[0];
+                // row max of the raw scores (scale > 0), independent chains
+                float mx[8];
 #pragma unroll
-                for (int c = 1; c < BN; ++c) mx = fmaxf(mx, s[c]);
+                for (int c = 0; c < 8; ++c) mx[c] = sc[c];
+#pragma unroll
+                for (int c = 8; c < BN; c += 8)
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) mx[i] = fmaxf(mx[i], sc[c + i]);
+                const float mxs = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                        fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sl2;
                 float alpha = 1.f;
-                if (mx > m + RESCALE_THRESHOLD || (m == -INFINITY && mx != -INFINITY)) {
-                    const float mn = fmaxf(mx, m);
+                if (mxs > m + RESCALE_THRESHOLD || (m == -INFINITY && mxs != -INFINITY)) {
+                    const float mn = fmaxf(mxs, m);
                     alpha = (m == -INFINITY) ? 0.f : ex2(m - mn);
                     m = mn;
                 }
-                const float mref = (m == -INFINITY) ? 0.f : m;
-                float ps = 0.f;
-#pragma unroll
-                for (int c = 0; c < BN; ++c) {
-                    s[c] = ex2(s[c] - mref);
-                    ps += s[c];
-                }
-                l = l * alpha + ps;
-                // rescale this row's O accumulator (warp-collective TMEM access)
+                // rescale this row's O accumulator (warp-collective TMEM access);
+                // the P.V of tile j-1 completed before S(j) was issued
                 if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
                     for (int cb = 0; cb < D / 32; ++cb) {
@@ -311,21 +368,27 @@ prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                         for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
                         tc::tmem_st32(lane_addr + col_o(x) + cb * 32, o);
                     }
-                    tc::tmem_wait_st();
                 }
-                // P row (bf16) into the K-major 128-byte-swizzled operand layout
+                const float nm = (m == -INFINITY) ? 0.f : -m;
+                // P (bf16 pairs) over the upper half of S, 64 scores at a time
+                float ps[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    uint4 v;
-                    v.x = pack_bf16(s[c * 8 + 0], s[c * 8 + 1]);
-                    v.y = pack_bf16(s[c * 8 + 2], s[c * 8 + 3]);
-                    v.z = pack_bf16(s[c * 8 + 4], s[c * 8 + 5]);
-                    v.w = pack_bf16(s[c * 8 + 6], s[c * 8 + 7]);
-                    *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = v;
+                for (int hf = 0; hf < 2; ++hf) {
+                    uint32_t pk[32];
+#pragma unroll
+                    for (int c = hf * 64; c < hf * 64 + 64; c += 2) {
+                        const float e0 = exp2_mix<POLY>(fmaf(sc[c], sl2, nm), c);
+                        const float e1 = exp2_mix<POLY>(fmaf(sc[c + 1], sl2, nm), c + 1);
+                        ps[(c >> 1) & 3] += e0 + e1;
+                        pk[(c >> 1) & 31] = pack_bf16(e0, e1);
+                    }
+                    tc::tmem_st32(lane_addr + col_p(x) + hf * 32, pk);
                 }
-                fence_proxy_async_smem();
+                l = l * alpha + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
+                tc::tmem_wait_st();
                 tc::fence_before_sync();
-                mbar_arrive(&B->p_full[x]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&B->p_full[x]);
             }
             if (ok && wait_ab(&B->o_full[x], 0, abort, a.status)) {
                 tc::fence_after_sync();
@@ -387,15 +450,20 @@ static int launch_prefill(sa_ctx* ctx, const void* q, const void* k, const void*
     pf::Args a;
     a.Sq = Sq; a.Skv = Skv; a.q_pos0 = q_pos0; a.hq = hq; a.hkv = hkv; a.G = hq / hkv;
     a.n_qtiles = (Sq + pf::BM - 1) / pf::BM;
-    a.upk = a.G >= 2 ? a.G / 2 : 1;
+    a.pair_heads = (a.G % 2 == 0) ? 1 : 0;
+    a.units_per_row = a.pair_heads ? hkv * (a.G / 2) : hq;
+    const int rows = a.pair_heads ? a.n_qtiles : (a.n_qtiles + 1) / 2;
     a.sl2 = scale * pf::LOG2E;
     a.out = out; a.o_tok = o_tok; a.o_head = pf::D;
     a.out_bf16 = out_dtype == SA_BF16;
     a.status = ctx->status;
-    SA_CUDA_TRY(cudaFuncSetAttribute(pf::prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     pf::SMEM_BYTES));
-    const int grid = a.n_qtiles * hkv * a.upk;
-    pf::prefill_kernel<<<grid, pf::THREADS, pf::SMEM_BYTES, ctx->stream>>>(mq, mk, mv, a);
+    // All exponentials on the SFU: with 128-key tiles the softmax is issue-bound,
+    // and moving every 8th/4th/3rd exponential to exp2_poly measured 3%/5%/9%
+    // slower on config 3 (S=8192, 16/8 heads).
+    auto kern = pf::prefill_kernel<0>;
+    SA_RC_TRY(set_smem_attr_once((const void*)kern, pf::SMEM_BYTES));
+    const int grid = rows * a.units_per_row;
+    kern<<<grid, pf::THREADS, pf::SMEM_BYTES, ctx->stream>>>(mq, mk, mv, a);
     SA_CUDA_TRY(cudaGetLastError());
     return SA_OK;
 }
@@ -415,8 +483,6 @@ SA_API int sa_attn_prefill(sa_ctx* ctx, const void* q, const void* k, const void
     SA_CHECK_ARG(q_pos0 + Sq <= Skv, "sa_attn_prefill: queries [%d, %d) need keys beyond Skv=%d", q_pos0,
                  q_pos0 + Sq, Skv);
     SA_CHECK_ARG(hkv > 0 && hq % hkv == 0, "sa_attn_prefill: hq=%d hkv=%d", hq, hkv);
-    const int G = hq / hkv;
-    SA_CHECK_ARG(G == 1 || G % 2 == 0, "sa_attn_prefill: hq/hkv = %d (1 or even)", G);
     SA_CHECK_ARG(out_dtype == SA_F32 || out_dtype == SA_BF16, "sa_attn_prefill: out_dtype %d", out_dtype);
     SA_CHECK_ARG(q_tok_stride >= (long long)hq * d && kv_tok_stride >= (long long)hkv * d &&
                  o_tok_stride >= (long long)hq * d, "sa_attn_prefill: token strides too small");

@@ -42,7 +42,7 @@ def test_prefill_golden(ctx):
 
 
 @pytest.mark.parametrize("S", [1, 63, 64, 65, 127, 128, 129, 300, 777])
-@pytest.mark.parametrize("hq,hkv", [(2, 1), (4, 2), (2, 2), (16, 8), (8, 2)])
+@pytest.mark.parametrize("hq,hkv", [(2, 1), (4, 2), (2, 2), (16, 8), (8, 2), (3, 1), (1, 1)])
 def test_prefill_vs_oracle(ctx, oracle, S, hq, hkv):
     import torch
     from streaming_attention_b200 import attn_prefill
@@ -119,10 +119,15 @@ def test_config3_full_size_vs_torch_fp32(ctx):
 def test_prefill_argument_errors(ctx):
     import torch
     from streaming_attention_b200 import SAError, attn_prefill
-    q = torch.zeros(10, 3, 128, device="cuda", dtype=torch.bfloat16)
-    k = torch.zeros(10, 1, 128, device="cuda", dtype=torch.bfloat16)
+    q = torch.zeros(10, 3, 64, device="cuda", dtype=torch.bfloat16)
+    k = torch.zeros(10, 1, 64, device="cuda", dtype=torch.bfloat16)
     with pytest.raises(SAError):
-        attn_prefill(q, k, k, 1.0, ctx=ctx)            # hq/hkv = 3
+        attn_prefill(q, k, k, 1.0, ctx=ctx)            # d = 64
+    q = torch.zeros(10, 3, 128, device="cuda", dtype=torch.bfloat16)
+    k = torch.zeros(10, 2, 128, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(SAError):
+        attn_prefill(q, k, k, 1.0, ctx=ctx)            # hq % hkv != 0
     q = torch.zeros(10, 2, 128, device="cuda", dtype=torch.bfloat16)
+    k = torch.zeros(10, 1, 128, device="cuda", dtype=torch.bfloat16)
     with pytest.raises(SAError):
         attn_prefill(q, k[:5], k[:5], 1.0, ctx=ctx)    # Sq > Skv
