@@ -26,13 +26,21 @@
 //  * S = Q K^T: M=128, N=128, K=128 (8 MMAs of K=16, A and B K-major from
 //    shared memory).  O += P V: M=128, N=128, K=128 (8 MMAs), A = P read from
 //    TMEM, B = V MN-major from shared memory (the V tile as loaded: keys x d).
-//    MMAs into different accumulators are not ordered by the hardware, so S
-//    of the next tile (which overwrites P) is issued only once the P.V that
-//    reads P has completed.
+//    S of the next tile overwrites the TMEM columns that the P.V just issued
+//    reads P from; it is issued right behind that P.V by the same thread, and
+//    the tensor core executes one thread's MMAs in issue order (the same
+//    reliance as NVIDIA's CUTLASS sm100 FMHA forward mainloop, which issues
+//    P.V and the next Q.K^T over shared TMEM columns back to back).  The
+//    commit that signals S(j+1) also covers the P.V of tile j, so the softmax
+//    may rescale O as soon as it sees S(j+1).
 //  * Online softmax in the exp2 domain (scale*log2 e folded into the scores)
 //    with a lazy rescale: the running max used for the exponent only moves
 //    when a row's max grows by more than 8 (2^8 headroom in P), and only then
-//    is the row's O accumulator in TMEM loaded, scaled and stored back.  The
+//    is the row's O accumulator in TMEM loaded, scaled and stored back.  From
+//    the second tile on, the exponentials are computed speculatively against
+//    the running max while the tile's max is found in the same pass; the
+//    warp redoes the tile only when one of its rows crossed the threshold,
+//    which keeps the max reduction off the softmax's critical path.  The
 //    kernel can evaluate a fraction of the exponentials on the FMA pipe
 //    (exp2_poly, template parameter POLY); the shipped instance keeps them all
 //    on the SFU, which measured fastest.
@@ -83,7 +91,7 @@ struct Args {
 struct Bars {
     uint64_t q_full;
     uint64_t k_full[KST], k_empty[KST], v_full[VST], v_empty[VST];
-    uint64_t s_full[2], p_full[2], pv_done[2], o_full[2];
+    uint64_t s_full[2], p_full[2], o_full[2];
     uint64_t drain;
     uint32_t tmem_base;
     int abort;
@@ -131,6 +139,51 @@ __device__ __forceinline__ float exp2_mix(float x, int c) {
         if ((c % POLY) == POLY - 1) return exp2_poly(x);
     }
     return ex2(x);
+}
+
+// Max of a row's 128 raw scores (eight independent chains).
+__device__ __forceinline__ float row_max(const float* sc) {
+    float mx[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) mx[c] = sc[c];
+#pragma unroll
+    for (int c = 8; c < BN; c += 8)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx[i] = fmaxf(mx[i], sc[c + i]);
+    return fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+}
+
+// P = 2^(sc*sl2 + nm) for one row's 128 scores, written to TMEM at p_addr as
+// 64 columns of bf16 pairs (two tcgen05.st of 32 columns, not waited for);
+// returns the fp32 row sum.  With TRACK_MAX the max of the raw scores is
+// found in the same pass and written to *mx_out.
+template <int POLY, bool TRACK_MAX>
+__device__ __forceinline__ float emit_p(const float* sc, float sl2, float nm, uint32_t p_addr, float* mx_out) {
+    float ps[4] = {0.f, 0.f, 0.f, 0.f};
+    float mx[8];
+    if constexpr (TRACK_MAX) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx[i] = sc[i];
+    }
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int c = hf * 64; c < hf * 64 + 64; c += 2) {
+            if constexpr (TRACK_MAX) {
+                mx[c & 7] = fmaxf(mx[c & 7], sc[c]);
+                mx[(c + 1) & 7] = fmaxf(mx[(c + 1) & 7], sc[c + 1]);
+            }
+            const float e0 = exp2_mix<POLY>(fmaf(sc[c], sl2, nm), c);
+            const float e1 = exp2_mix<POLY>(fmaf(sc[c + 1], sl2, nm), c + 1);
+            ps[(c >> 1) & 3] += e0 + e1;
+            pk[(c >> 1) & 31] = pack_bf16(e0, e1);
+        }
+        tc::tmem_st32(p_addr + hf * 32, pk);
+    }
+    if constexpr (TRACK_MAX)
+        *mx_out = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+    return (ps[0] + ps[1]) + (ps[2] + ps[3]);
 }
 
 template <int POLY>
@@ -189,7 +242,6 @@ prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
         for (int x = 0; x < 2; ++x) {
             mbar_init(&B->s_full[x], 1);
             mbar_init(&B->p_full[x], 4);      // one arrival per softmax warp
-            mbar_init(&B->pv_done[x], 1);
             mbar_init(&B->o_full[x], 1);
         }
         mbar_init(&B->drain, 1);
@@ -244,9 +296,9 @@ prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
-        // Per KV tile j and slot x: P.V(j) once the slot's P is in TMEM, then,
-        // after that P.V has completed, S(j+1) over the same TMEM columns.
-        // The other slot's softmax runs meanwhile.
+        // Per KV tile j and slot x: P.V(j) once the slot's P is in TMEM, then
+        // S(j+1) over the same TMEM columns, issued right behind it.  The
+        // other slot's softmax runs meanwhile.
         if (lane == 0) {
             constexpr uint32_t idS = tc::idesc_bf16_f32(BM, BN, false, false);
             constexpr uint32_t idO = tc::idesc_bf16_f32(BM, D, false, true);
@@ -287,7 +339,6 @@ prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                     if (!(ok = wait_ab(&B->p_full[x], j & 1, abort, a.status))) break;
                     tc::fence_after_sync();
                     issue_PV(x, j);
-                    tc::mma_commit(&B->pv_done[x]);
                     if (j + 1 == nkv[x]) {
                         tc::mma_commit(&B->o_full[x]);
                         continue;
@@ -297,8 +348,6 @@ prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                         if (!(ok = wait_ab(&B->k_full[j1 % KST], (j1 / KST) & 1, abort, a.status))) break;
                         k_next = true;
                     }
-                    if (!(ok = wait_ab(&B->pv_done[x], j & 1, abort, a.status))) break;
-                    tc::fence_after_sync();
                     issue_S(x, j + 1);
                     tc::mma_commit(&B->s_full[x]);
                 }
@@ -340,51 +389,42 @@ prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                     for (int c = 0; c < BN; ++c)
                         if (k0 + c > limit || k0 + c >= a.Skv) sc[c] = -INFINITY;
                 }
-                // row max of the raw scores (scale > 0), independent chains
-                float mx[8];
-#pragma unroll
-                for (int c = 0; c < 8; ++c) mx[c] = sc[c];
-#pragma unroll
-                for (int c = 8; c < BN; c += 8)
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) mx[i] = fmaxf(mx[i], sc[c + i]);
-                const float mxs = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                        fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sl2;
-                float alpha = 1.f;
-                if (mxs > m + RESCALE_THRESHOLD || (m == -INFINITY && mxs != -INFINITY)) {
-                    const float mn = fmaxf(mxs, m);
-                    alpha = (m == -INFINITY) ? 0.f : ex2(m - mn);
-                    m = mn;
-                }
-                // rescale this row's O accumulator (warp-collective TMEM access);
-                // the P.V of tile j-1 completed before S(j) was issued
-                if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+                const uint32_t p_addr = lane_addr + col_p(x);
+                float alpha = 1.f, sum;
+                if (j == 0) {
+                    // first tile: every row sees key 0, so its max is finite
+                    const float mxs = row_max(sc) * sl2;
+                    m = mxs;
+                    sum = emit_p<POLY, false>(sc, sl2, (m == -INFINITY) ? 0.f : -m, p_addr, nullptr);
+                } else {
+                    // speculative: exponentials against the running max while the
+                    // tile's max is found in the same pass; redone only if some row's
+                    // max grew by more than the rescale threshold
+                    float mxr;
+                    sum = emit_p<POLY, true>(sc, sl2, -m, p_addr, &mxr);
+                    const float mxs = mxr * sl2;
+                    const bool need = mxs > m + RESCALE_THRESHOLD;
+                    if (__any_sync(0xffffffffu, need)) {
+                        if (need) {
+                            alpha = ex2(m - mxs);
+                            m = mxs;
+                        }
+                        // rescale this row's O accumulator (warp-collective TMEM
+                        // access); the P.V of tile j-1 completed before S(j) was issued
 #pragma unroll 1
-                    for (int cb = 0; cb < D / 32; ++cb) {
-                        uint32_t o[32];
-                        tc::tmem_ld32(lane_addr + col_o(x) + cb * 32, o);
-                        tc::tmem_wait_ld();
+                        for (int cb = 0; cb < D / 32; ++cb) {
+                            uint32_t o[32];
+                            tc::tmem_ld32(lane_addr + col_o(x) + cb * 32, o);
+                            tc::tmem_wait_ld();
 #pragma unroll
-                        for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-                        tc::tmem_st32(lane_addr + col_o(x) + cb * 32, o);
+                            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+                            tc::tmem_st32(lane_addr + col_o(x) + cb * 32, o);
+                        }
+                        tc::tmem_wait_st();        // the first P stores land before they are replaced
+                        sum = emit_p<POLY, false>(sc, sl2, -m, p_addr, nullptr);
                     }
                 }
-                const float nm = (m == -INFINITY) ? 0.f : -m;
-                // P (bf16 pairs) over the upper half of S, 64 scores at a time
-                float ps[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
-                    uint32_t pk[32];
-#pragma unroll
-                    for (int c = hf * 64; c < hf * 64 + 64; c += 2) {
-                        const float e0 = exp2_mix<POLY>(fmaf(sc[c], sl2, nm), c);
-                        const float e1 = exp2_mix<POLY>(fmaf(sc[c + 1], sl2, nm), c + 1);
-                        ps[(c >> 1) & 3] += e0 + e1;
-                        pk[(c >> 1) & 31] = pack_bf16(e0, e1);
-                    }
-                    tc::tmem_st32(lane_addr + col_p(x) + hf * 32, pk);
-                }
-                l = l * alpha + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
+                l = l * alpha + sum;
                 tc::tmem_wait_st();
                 tc::fence_before_sync();
                 __syncwarp();

@@ -73,6 +73,38 @@ def test_prefill_query_offset(ctx, oracle, Sq, q_pos0):
     _check(out.cpu().numpy(), ref, f"offset {q_pos0}")
 
 
+@pytest.mark.parametrize("kind", ["wide", "negative", "ramp"])
+def test_prefill_extreme_logits(ctx, oracle, kind):
+    """Score ranges that exercise the running-max logic: logits with a spread
+    of hundreds (the max moves many times, O is rescaled), rows whose logits
+    are all far below zero (the first tile's max must replace the initial
+    running max), and keys whose logits grow along the sequence."""
+    import torch
+    from streaming_attention_b200 import attn_prefill
+    S, hq, hkv, d = 400, 4, 2, 128
+    rs = np.random.default_rng(11)
+    q = rs.standard_normal((S, hq, d)).astype(np.float32)
+    k = rs.standard_normal((S, hkv, d)).astype(np.float32)
+    v = rs.standard_normal((S, hkv, d)).astype(np.float32)
+    scale = 1.0 / np.sqrt(d)
+    if kind == "wide":
+        scale = 1.0                                   # logits ~ N(0, 128)
+    elif kind == "negative":
+        k = np.abs(k) + 1.0
+        q = -np.abs(q) - 2.0                          # every logit << 0
+        scale = 1.0
+    else:
+        k = k + np.linspace(0.0, 4.0, S, dtype=np.float32)[:, None, None]
+        q = np.abs(q)
+        scale = 0.25
+    q, k, v = bf16_round(q), bf16_round(k), bf16_round(v)
+    out = attn_prefill(_bf(q), _bf(k), _bf(v), scale, ctx=ctx)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    assert np.isfinite(got).all()
+    _check(got, oracle.causal_prefill(q, k, v, scale), kind)
+
+
 def test_prefill_strided_qkv_from_one_buffer(ctx, oracle):
     """Q, K, V as column slices of one fused [S, (hq+2*hkv)*d] projection output
     (the QKV GEMM's layout), read in place through their token strides."""
