@@ -57,6 +57,9 @@ const char* sa_last_error(void);
 /* Library version string. */
 const char* sa_version(void);
 
+/* Number of CUDA devices visible to the process (0 without a GPU). */
+int sa_device_count(int* out);
+
 /* Create a context on `device` with its own non-blocking stream. */
 int sa_ctx_create(int device, sa_ctx** out);
 /* Destroy a context (synchronises its stream first). */
@@ -152,8 +155,8 @@ int sa_attn_merge(sa_ctx* ctx, int n_parts, int hq, int d, const float* m, const
  * Replaces ops::self_attention with create_causal_mask
  * (tensor_cpp/src/ops.cpp:514-641, qwen3_ops.cpp:240-259) and
  * self_attention_streaming_blockwise (ops.cpp:1027-1112,1383-1450) after
- * repeat_kv (qwen3_ops.cpp:194-234).  Requirements: d = 128; hq/hkv = 1 or
- * even; q_pos0 + Sq <= Skv; device pointers (16-byte aligned, token strides
+ * repeat_kv (qwen3_ops.cpp:194-234).  Requirements: d = 128; hq a multiple
+ * of hkv; q_pos0 + Sq <= Skv; device pointers (16-byte aligned, token strides
  * multiples of 8 elements).
  */
 int sa_attn_prefill(sa_ctx* ctx, const void* q, const void* k, const void* v, int Sq, int Skv,
@@ -251,6 +254,21 @@ int sa_qwen3_set_layer(sa_qwen3* m, int layer, const float* in_norm, const float
 int sa_qwen3_reset(sa_qwen3* m);
 /* KVCache::current_seq_len. */
 int sa_qwen3_cache_len(sa_qwen3* m);
+
+/*
+ * Mirror of the host KVCache contents (kv_cache.h:60-70: one tensor per layer
+ * of [batch, num_kv_heads, max_seq_len, head_dim], here batch 1).
+ * sa_qwen3_read_kv copies rows 0..cache_len-1 of one layer's K and V cache
+ * (fp32) into host arrays laid out [hkv][seq_stride][head_dim]
+ * (seq_stride >= cache_len; KVCache uses its max_seq_len); blocking.
+ * sa_qwen3_write_kv uploads rows 0..len-1 of one layer from the same layout
+ * (len <= max_seq); blocking.  sa_qwen3_set_cache_len makes the first len
+ * rows the live cache (KVCache::current_seq_len = len), so a cache filled
+ * elsewhere (e.g. a CPU prefill) can be continued on the GPU.
+ */
+int sa_qwen3_read_kv(sa_qwen3* m, int layer, float* k_out, float* v_out, int seq_stride);
+int sa_qwen3_write_kv(sa_qwen3* m, int layer, const float* k, const float* v, int len, int seq_stride);
+int sa_qwen3_set_cache_len(sa_qwen3* m, int len);
 
 /*
  * Forward S tokens.  use_cache = 0: qwen3_forward (qwen3_ops.cpp:537-614),

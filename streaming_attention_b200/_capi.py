@@ -28,6 +28,7 @@ _fp = C.POINTER(C.c_float)
 SIGNATURES = {
     "sa_last_error": (C.c_char_p, []),
     "sa_version": (C.c_char_p, []),
+    "sa_device_count": (C.c_int, [C.POINTER(C.c_int)]),
     "sa_ctx_create": (C.c_int, [C.c_int, C.POINTER(_vp)]),
     "sa_ctx_destroy": (C.c_int, [_vp]),
     "sa_ctx_set_stream": (C.c_int, [_vp, _vp]),
@@ -52,6 +53,9 @@ SIGNATURES = {
     "sa_qwen3_set_layer": (C.c_int, [_vp, C.c_int] + [_fp] * 11),
     "sa_qwen3_reset": (C.c_int, [_vp]),
     "sa_qwen3_cache_len": (C.c_int, [_vp]),
+    "sa_qwen3_read_kv": (C.c_int, [_vp, C.c_int, _vp, _vp, C.c_int]),
+    "sa_qwen3_write_kv": (C.c_int, [_vp, C.c_int, _vp, _vp, C.c_int, C.c_int]),
+    "sa_qwen3_set_cache_len": (C.c_int, [_vp, C.c_int]),
     "sa_qwen3_forward": (C.c_int, [_vp, C.POINTER(C.c_int64), C.c_int, C.c_int, _fp, C.c_int,
                                    C.c_uint]),
     "sa_qwen3_generate": (C.c_int, [_vp, C.POINTER(C.c_int64), C.c_int, C.c_int,

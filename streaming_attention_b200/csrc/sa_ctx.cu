@@ -73,6 +73,18 @@ SA_API const char* sa_last_error(void) { return sa::g_last_error.c_str(); }
 
 SA_API const char* sa_version(void) { return "sa_cuda 0.1 (sm_100a)"; }
 
+SA_API int sa_device_count(int* out) {
+    sa::clear_error();
+    SA_CHECK_ARG(out != nullptr, "sa_device_count: out is NULL");
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+    }
+    *out = n;
+    return SA_OK;
+}
+
 SA_API int sa_ctx_create(int device, sa_ctx** out) {
     sa::clear_error();
     SA_CHECK_ARG(out != nullptr, "sa_ctx_create: out is NULL");

@@ -451,6 +451,55 @@ SA_API int sa_qwen3_reset(sa_qwen3* m) {
 
 SA_API int sa_qwen3_cache_len(sa_qwen3* m) { return m ? m->cache_len : -1; }
 
+// Host [hkv][seq_stride][D] <-> device rows 0..rows-1 of one layer's cache
+// ([hkv][max_seq][D]), one 2-D copy per tensor on the context's stream.
+static int copy_kv_layer(sa_qwen3* m, int layer, float* hk, float* hv, int rows, int seq_stride, bool to_host) {
+    const size_t D = m->c.head_dim;
+    const size_t layer_kv = (size_t)m->c.hkv * m->c.max_seq * D;
+    float* dk = m->kc + (size_t)layer * layer_kv;
+    float* dv = m->vc + (size_t)layer * layer_kv;
+    if (rows == 0) return SA_OK;
+    const size_t hpitch = (size_t)seq_stride * D * 4, dpitch = (size_t)m->c.max_seq * D * 4;
+    const size_t width = (size_t)rows * D * 4;
+    cudaStream_t st = m->ctx->stream;
+    if (to_host) {
+        SA_CUDA_TRY(cudaMemcpy2DAsync(hk, hpitch, dk, dpitch, width, m->c.hkv, cudaMemcpyDeviceToHost, st));
+        SA_CUDA_TRY(cudaMemcpy2DAsync(hv, hpitch, dv, dpitch, width, m->c.hkv, cudaMemcpyDeviceToHost, st));
+    } else {
+        SA_CUDA_TRY(cudaMemcpy2DAsync(dk, dpitch, hk, hpitch, width, m->c.hkv, cudaMemcpyHostToDevice, st));
+        SA_CUDA_TRY(cudaMemcpy2DAsync(dv, dpitch, hv, hpitch, width, m->c.hkv, cudaMemcpyHostToDevice, st));
+    }
+    return sync_and_check(m->ctx);
+}
+
+SA_API int sa_qwen3_read_kv(sa_qwen3* m, int layer, float* k_out, float* v_out, int seq_stride) {
+    clear_error();
+    SA_CHECK_ARG(m && k_out && v_out, "sa_qwen3_read_kv: null argument");
+    SA_CHECK_ARG(layer >= 0 && layer < m->c.n_layers, "sa_qwen3_read_kv: layer %d of %d", layer, m->c.n_layers);
+    SA_CHECK_ARG(seq_stride >= m->cache_len, "sa_qwen3_read_kv: seq_stride %d < cache length %d", seq_stride,
+                 m->cache_len);
+    DeviceGuard guard(m->ctx->device);
+    return copy_kv_layer(m, layer, k_out, v_out, m->cache_len, seq_stride, true);
+}
+
+SA_API int sa_qwen3_write_kv(sa_qwen3* m, int layer, const float* k, const float* v, int len, int seq_stride) {
+    clear_error();
+    SA_CHECK_ARG(m && (len == 0 || (k && v)), "sa_qwen3_write_kv: null argument");
+    SA_CHECK_ARG(layer >= 0 && layer < m->c.n_layers, "sa_qwen3_write_kv: layer %d of %d", layer, m->c.n_layers);
+    SA_CHECK_ARG(len >= 0 && len <= m->c.max_seq && seq_stride >= len,
+                 "sa_qwen3_write_kv: len %d (max_seq %d, seq_stride %d)", len, m->c.max_seq, seq_stride);
+    DeviceGuard guard(m->ctx->device);
+    return copy_kv_layer(m, layer, const_cast<float*>(k), const_cast<float*>(v), len, seq_stride, false);
+}
+
+SA_API int sa_qwen3_set_cache_len(sa_qwen3* m, int len) {
+    clear_error();
+    SA_CHECK_ARG(m, "sa_qwen3_set_cache_len: null model");
+    SA_CHECK_ARG(len >= 0 && len <= m->c.max_seq, "sa_qwen3_set_cache_len: len %d (max_seq %d)", len, m->c.max_seq);
+    m->cache_len = len;
+    return SA_OK;
+}
+
 // Run `body` on the model's own (capturable) stream, ordered after the
 // context's stream and before anything the caller issues on it afterwards.
 template <typename F>

@@ -102,6 +102,26 @@ class Qwen3:
     def cache_len(self) -> int:
         return lib().sa_qwen3_cache_len(self.h)
 
+    def read_kv(self, layer: int, seq_stride: int | None = None):
+        """(K, V) of one layer's live cache rows: float32 [hkv, seq_stride, head_dim]
+        (rows past cache_len are zero), the layout of KVCache's layer tensors."""
+        L = self.cache_len
+        stride = L if seq_stride is None else seq_stride
+        shape = (self.cfg["hkv"], stride, self.cfg["head_dim"])
+        k, v = np.zeros(shape, np.float32), np.zeros(shape, np.float32)
+        check(lib().sa_qwen3_read_kv(self.h, layer, k.ctypes.data, v.ctypes.data, stride))
+        return k, v
+
+    def write_kv(self, layer: int, k, v):
+        """Upload rows 0..len-1 of one layer's cache from float32 [hkv, len, head_dim]."""
+        k = np.ascontiguousarray(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        assert k.shape == v.shape and k.shape[0] == self.cfg["hkv"] and k.shape[2] == self.cfg["head_dim"]
+        check(lib().sa_qwen3_write_kv(self.h, layer, k.ctypes.data, v.ctypes.data, k.shape[1], k.shape[1]))
+
+    def set_cache_len(self, n: int):
+        check(lib().sa_qwen3_set_cache_len(self.h, n))
+
     def forward(self, ids, use_cache: bool = False, logits: str = "all"):
         ids = np.ascontiguousarray(ids, np.int64).ravel()
         S = ids.size

@@ -1,0 +1,67 @@
+"""The C++ host layer over the C ABI (CPU only): libsa_host.so provides every
+function include/sa_attention_cuda.h declares, the command-line drivers parse
+the reference drivers' argument forms, and the header-only Qwen3 adapter
+compiles against the reference's own headers when that tree is present."""
+import os
+import re
+import shutil
+import subprocess
+
+import pytest
+
+from conftest import ROOT
+
+PKG = os.path.join(ROOT, "streaming_attention_b200")
+BIN = os.path.join(PKG, "bin")
+REF = "/root/reference"
+CXX = "/usr/bin/g++" if os.path.exists("/usr/bin/g++") else shutil.which("g++")
+DRIVERS = ["test_naive_cuda", "test_streaming_cuda", "test_streaming_cuda_multi", "test_mpi_cuda"]
+
+
+def _declared_cpp():
+    src = open(os.path.join(ROOT, "include", "sa_attention_cuda.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return re.findall(r"^[\w:<>]+\s+\**(\w+)\s*\(", src, flags=re.M)
+
+
+def test_host_library_links_every_declared_function(tmp_path):
+    names = _declared_cpp()
+    assert {"naive_attention_cuda", "streaming_attention_cuda", "streaming_attention_cuda_multi"} <= set(names)
+    if CXX is None:
+        pytest.skip("no C++ compiler")
+    # a program that takes the address of each declared function links only if
+    # libsa_host.so defines all of them
+    prog = tmp_path / "link.cpp"
+    prog.write_text('#include "sa_attention_cuda.h"\n#include <cstdio>\nint main() {\n' +
+                    "".join(f'  std::printf("%p\\n", (void*)&{n});\n' for n in names) + "  return 0;\n}\n")
+    exe = tmp_path / "link"
+    subprocess.run([CXX, "-std=c++17", "-I", os.path.join(ROOT, "include"), str(prog), "-o", str(exe),
+                    "-L", PKG, "-lsa_host", "-lsa_cuda", f"-Wl,-rpath,{PKG}"], check=True)
+
+
+@pytest.mark.parametrize("name", DRIVERS)
+def test_driver_usage(name):
+    exe = os.path.join(BIN, name)
+    assert os.path.exists(exe), f"{exe} not built (make -C streaming_attention_b200)"
+    r = subprocess.run([exe, "--help"], capture_output=True, text=True, timeout=30)
+    assert r.returncode == 2 and "usage:" in r.stderr
+
+
+@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "tensor_cpp", "include")),
+                    reason="reference headers not present")
+def test_qwen3_adapter_compiles_against_reference_headers(tmp_path):
+    src = tmp_path / "use.cpp"
+    src.write_text(
+        '#include "tensor_cpp/qwen3_ops.h"\n#include "sa_qwen3_tensorcpp.hpp"\n'
+        "using namespace tensor_cpp;\n"
+        "Tensor f(const TensorL& ids, qwen3::KVCache* kv, const qwen3::Qwen3Weights* w) {\n"
+        "  return qwen3::cuda::qwen3_forward_cuda_with_cache(ids, kv, w->embed_tokens, w->layers,\n"
+        "      w->norm_weight, w->lm_head, w->num_layers, w->num_attention_heads, w->num_key_value_heads,\n"
+        "      w->head_dim, 1e-6f, qwen3::AttentionType::STREAMING);\n}\n"
+        "Tensor g(const TensorL& ids, const qwen3::Qwen3Weights& w) {\n"
+        "  return qwen3::cuda::qwen3_forward_cuda(ids, w.embed_tokens, w.layers, w.norm_weight, w.lm_head,\n"
+        "      w.num_layers, w.num_attention_heads, w.num_key_value_heads, w.head_dim, 1e-6f);\n}\n")
+    r = subprocess.run([CXX, "-std=c++17", "-fsyntax-only", "-w", "-I", os.path.join(REF, "tensor_cpp", "include"),
+                        "-I", os.path.join(ROOT, "include"), '-include', "tensor_cpp/qwen3_loader.h", str(src)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-2000:]

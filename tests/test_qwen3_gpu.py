@@ -100,6 +100,39 @@ def test_qwen3_cache_continuation_matches_full_prompt(ctx, oracle):
     _close(full[0], oracle.qwen3_forward(cfg, w, ids, all_logits=False)[0], "oracle")
 
 
+def test_qwen3_kv_mirror_read_write(ctx, oracle):
+    """The device cache read back after a cached prefill equals the oracle's
+    KVCache contents; a second model that adopts it (write_kv + set_cache_len,
+    the path for a host KVCache filled elsewhere) continues bit-identically."""
+    from streaming_attention_b200 import Qwen3
+    cfg = Qwen3Cfg(vocab=500, hidden=256, n_layers=2, hq=4, hkv=2, head_dim=128, inter=512,
+                   eps=1e-6, theta=1e6)
+    w = make_qwen3_weights(cfg, 5)
+    S, MS = 40, 64
+    ids = I.rng(9).integers(0, cfg.vocab, S)
+    m = Qwen3(_cfgdict(cfg), max_seq=MS, ctx=ctx)
+    m.load(w)
+    m.forward(ids, use_cache=True, logits="none")
+    kc = np.zeros((cfg.n_layers, cfg.hkv, MS, cfg.head_dim), np.float32)
+    vc = np.zeros_like(kc)
+    oracle.qwen3_forward(cfg, w, ids, kc=kc, vc=vc, max_seq=MS, all_logits=False)
+    m2 = Qwen3(_cfgdict(cfg), max_seq=MS, ctx=ctx)
+    m2.load(w)
+    for layer in range(cfg.n_layers):
+        k, v = m.read_kv(layer, seq_stride=MS)
+        assert not k[:, S:].any() and not v[:, S:].any()
+        _close(k[:, :S], kc[layer, :, :S], f"K layer {layer}")
+        _close(v[:, :S], vc[layer, :, :S], f"V layer {layer}")
+        k, v = m.read_kv(layer)
+        assert k.shape == (cfg.hkv, S, cfg.head_dim)
+        m2.write_kv(layer, k, v)
+    m2.set_cache_len(S)
+    a = m.forward(np.array([7]), use_cache=True, logits="last")
+    b = m2.forward(np.array([7]), use_cache=True, logits="last")
+    np.testing.assert_array_equal(a, b)
+    assert m.cache_len == m2.cache_len == S + 1
+
+
 def test_qwen3_errors(ctx):
     from streaming_attention_b200 import Qwen3, SAError
     cfg = dict(vocab=300, hidden=256, n_layers=1, hq=2, hkv=1, head_dim=128, inter=256)
