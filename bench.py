@@ -529,6 +529,56 @@ def load_bf16_peak(sustained=False):
         return (1400.0 if sustained else 1590.0), "fallback"
 
 
+def cpu_prefill_baseline(budget_s: float, reps: int = 1):
+    """The reference's ops::self_attention_streaming_blockwise_avx2 (ops.cpp:1453-1524,
+    q/kv blocks 128 as its driver uses) on the configs[2] head layout at a sample
+    sequence length sized to about budget_s / 3 per call; returns the cpu_baseline dict."""
+    import numpy as np
+    from oracle.oracle import Reference
+    R = Reference()
+    rng = np.random.default_rng(SEED)
+
+    def inputs(S):
+        return (rng.standard_normal((S, PF_HQ, D), dtype=np.float32),
+                rng.standard_normal((S, PF_HKV, D), dtype=np.float32),
+                rng.standard_normal((S, PF_HKV, D), dtype=np.float32))
+
+    q, k, v = inputs(1024)
+    t0 = time.perf_counter()
+    R.causal_prefill(q, k, v, SCALE, 128, 128, avx2=True)
+    t1 = time.perf_counter() - t0
+    S = int(min(PF_S, max(1024, 1024 * (max(budget_s, 1.0) / 3 / max(t1, 1e-3)) ** 0.5)) // 128 * 128)
+    q, k, v = inputs(S)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        R.causal_prefill(q, k, v, SCALE, 128, 128, avx2=True)
+    el = (time.perf_counter() - t0) / reps
+    tf = prefill_flops(S) / el / 1e12
+    cores = os.cpu_count() or 1
+    return {"value": round(tf, 5), "unit": "TFLOP/s", "cores": cores, "kind": "reference",
+            "sample": f"self_attention_streaming_blockwise_avx2 (q/kv blocks 128), S={S} of {PF_S}, "
+                      f"{PF_HQ}/{PF_HKV} heads, d {D}, {el:.2f} s per call, {cores} OpenMP threads"}
+
+
+def run_prefill_reference(args):
+    """--impl reference for the prefill workload: the reference's AVX2 block-wise
+    causal prefill on the host cores, each step a bounded sample."""
+    if env_int("RANK", 0) != 0:
+        return 0
+    per_step = max(2.0, 90.0 / (args.steps + args.warmup))
+    cb = cpu_prefill_baseline(per_step * 3, reps=max(1, args.steps))
+    print(json.dumps({
+        "impl": "reference", "metric": "attn TFLOP/s (causal prefill)", "value": cb["value"],
+        "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(prefill_flops() / (cb["value"] * 1e12) * 1e3, 3) if cb["value"] else None,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": PF_WORKLOAD, "parallelism": "cpu"},
+        "cpu_baseline": cb,
+        "e2e": {"value": cb["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+    return 0
+
+
 def run_prefill(args):
     import torch
     import streaming_attention_b200 as sa
@@ -557,6 +607,12 @@ def run_prefill(args):
     ms, tf = measure_prefill(ctx, dev, stream, args.steps, args.warmup)
     clk = clocks.stop()
     peak, kind = load_bf16_peak()
+    cpu = None
+    if not args.no_cpu:
+        try:
+            cpu = cpu_prefill_baseline(args.cpu_budget)
+        except Exception as e:    # the reference build is optional on the box
+            cpu = {"value": None, "unit": "TFLOP/s", "sample": f"unavailable: {e}"}
     print(json.dumps({
         "metric": "attn TFLOP/s (causal prefill)", "value": round(tf, 2), "unit": "TFLOP/s",
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
@@ -567,6 +623,7 @@ def run_prefill(args):
                      "frac": round(tf / peak, 4), "peak_kind": f"{kind} bf16_tflops (burst)",
                      "kernel": "sa::pf::prefill_kernel", "kernel_ms": round(ms, 4),
                      "traffic": load_traffic("prefill_S8192")},
+        "cpu_baseline": cpu,
         "clocks": clk, "gpu_launches": args.steps}), flush=True)
     ctx.close()
     return 0
@@ -674,11 +731,33 @@ def cpu_qwen3_baseline(weights, budget_tokens=16):
     t_dec = time.perf_counter() - t0
     m.free_cache(kv)
     m.close()
-    return {"prefill_tok_s": budget_tokens / t_pf, "decode_tok_s": steps / t_dec,
+    return {"value": round(budget_tokens / t_pf, 3), "unit": "tok/s",
+            "prefill_tok_s": budget_tokens / t_pf, "decode_tok_s": steps / t_dec,
             "cores": os.cpu_count(), "kind": "reference",
             "sample": f"avx2::qwen3_forward_avx on a {budget_tokens}-token prompt; "
                       f"{steps} cached decode steps (qwen3_forward_avx_with_cache) after it; "
                       f"{os.cpu_count()} OpenMP threads"}
+
+
+def run_qwen3_reference(args):
+    """--impl reference for the qwen3 workload: the reference's AVX2 Qwen3-0.6B
+    forward on the host cores with the same random-init weights (bounded prompt)."""
+    if env_int("RANK", 0) != 0:
+        return 0
+    import streaming_attention_b200 as sa
+    weights = sa.qwen3.random_weights(sa.QWEN3_0_6B, SEED)
+    cb = cpu_qwen3_baseline(weights)
+    print(json.dumps({
+        "impl": "reference", "metric": "Qwen3-0.6B tok/s (prefill)", "value": cb["value"], "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(Q3_PROMPT / cb["prefill_tok_s"] * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": Q3_WORKLOAD, "parallelism": "cpu"},
+        "decode": {"decode_tok_s": round(cb["decode_tok_s"], 3)},
+        "cpu_baseline": cb,
+        "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+    return 0
 
 
 def run_qwen3(args):
@@ -752,9 +831,9 @@ def main():
     if args.warmup < 3:
         args.warmup = 3
     if args.workload == "prefill":
-        return run_prefill(args)
+        return run_prefill_reference(args) if args.impl == "reference" else run_prefill(args)
     if args.workload == "qwen3":
-        return run_qwen3(args)
+        return run_qwen3_reference(args) if args.impl == "reference" else run_qwen3(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

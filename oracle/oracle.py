@@ -231,8 +231,11 @@ class Reference:
                                   scale, _p(out))
         return out
 
-    def causal_prefill(self, q, k, v, scale, q_block=32, kv_block=64, standard=False):
-        """q [Sq, hq, d]; k, v [S, hkv, d] (token-major, Sq == S) -> [S, hq, d]."""
+    def causal_prefill(self, q, k, v, scale, q_block=32, kv_block=64, standard=False, avx2=False):
+        """q [Sq, hq, d]; k, v [S, hkv, d] (token-major, Sq == S) -> [S, hq, d].
+        standard: ops::self_attention with the causal mask; avx2: the
+        reference's self_attention_streaming_blockwise_avx2; else the scalar
+        self_attention_streaming_blockwise."""
         q, k, v = _f32(q), _f32(k), _f32(v)
         S, hq, d = q.shape
         hkv = k.shape[1]
@@ -241,7 +244,7 @@ class Reference:
         vh = np.ascontiguousarray(v.transpose(1, 0, 2))
         out = np.empty_like(qh)
         if self.L.ref_causal_prefill(_p(qh), _p(kh), _p(vh), S, hq, hkv, d, scale, q_block,
-                                     kv_block, 1 if standard else 0, _p(out)):
+                                     kv_block, 1 if standard else (2 if avx2 else 0), _p(out)):
             self._err("ref_causal_prefill")
         return np.ascontiguousarray(out.transpose(1, 0, 2))
 

@@ -87,9 +87,11 @@ REF_EXPORT int ref_causal_prefill(const float* q, const float* k, const float* v
         Tensor kr = q3::repeat_kv(tk, hq / hkv);
         Tensor vr = q3::repeat_kv(tv, hq / hkv);
         Tensor o;
-        if (standard) {
+        if (standard == 1) {
             Tensor mask = q3::create_causal_mask(S).view(Shape({1, 1, (size_t)S, (size_t)S}));
             o = tensor_cpp::ops::self_attention(tq, kr, vr, &mask, scale);
+        } else if (standard == 2) {
+            o = tensor_cpp::ops::self_attention_streaming_blockwise_avx2(tq, kr, vr, scale, q_block, kv_block);
         } else {
             o = tensor_cpp::ops::self_attention_streaming_blockwise(tq, kr, vr, scale, q_block, kv_block);
         }
