@@ -579,9 +579,78 @@ def run_prefill_reference(args):
     return 0
 
 
+def run_prefill_sp(args):
+    """configs[2] on N GPUs: zig-zag sequence-parallel causal prefill (each rank
+    two query chunks, K/V all-gathered over NCCL, no output merge).  Total work is
+    fixed (strong scaling); time = max over ranks of CUDA-event time per step."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    import streaming_attention_b200 as sa
+    from streaming_attention_b200.sequence_parallel import sp_prefill, zigzag_shard
+    world, rank, local = env_int("WORLD_SIZE", 1), env_int("RANK", 0), env_int("LOCAL_RANK", 0)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    g = torch.Generator(device=dev).manual_seed(SEED)     # the same full tensors on every rank
+    q = torch.randn(PF_S, PF_HQ, D, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(PF_S, PF_HKV, D, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(PF_S, PF_HKV, D, device=dev, generator=g).to(torch.bfloat16)
+    ql, kl, vl = zigzag_shard(q, rank, world), zigzag_shard(k, rank, world), zigzag_shard(v, rank, world)
+    del q, k, v
+    ctx = sa.Context(local)
+    streams = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    main = torch.cuda.Stream(dev)
+
+    def pf(qc, kc, vc, s, q_pos0, out):
+        return sa.attn_prefill(qc, kc, vc, s, q_pos0, "bfloat16", ctx, out)
+
+    with torch.cuda.stream(main):
+        for _ in range(args.warmup):
+            sp_prefill(ql, kl, vl, SCALE, None, pf, streams, torch.bfloat16)
+    torch.cuda.synchronize(dev)
+    dist.barrier(device_ids=[local])
+    tot = 0.0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(args.steps):
+        with torch.cuda.stream(main):
+            flush.zero_()
+            dist.barrier(device_ids=[local])
+            e0.record(main)
+            sp_prefill(ql, kl, vl, SCALE, None, pf, streams, torch.bfloat16)
+            e1.record(main)
+        e1.synchronize()
+        tot += e0.elapsed_time(e1)
+    t = torch.tensor([tot / args.steps], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    tf = prefill_flops() / (ms / 1e3) / 1e12
+    if rank == 0:
+        peak, kind = load_bf16_peak()
+        print(json.dumps({
+            "metric": "attn TFLOP/s (causal prefill)", "value": round(tf, 2), "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": PF_WORKLOAD, "parallelism": f"sp{world} zig-zag (2 chunks/rank, "
+                                                             "K/V all-gather over NCCL)",
+                       "l2": "256 MB buffer written between timed steps"},
+            "roofline": {"bound": "tensor", "achieved": round(tf / world, 2), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(tf / world / peak, 4), "per": "GPU",
+                         "peak_kind": f"{kind} bf16_tflops (burst)"},
+            "gpu_launches": 2 * args.steps}), flush=True)
+    ctx.close()
+    dist.barrier(device_ids=[local])
+    dist.destroy_process_group()
+    return 0
+
+
 def run_prefill(args):
     import torch
     import streaming_attention_b200 as sa
+    if env_int("WORLD_SIZE", 1) > 1:
+        return run_prefill_sp(args)
     local = env_int("LOCAL_RANK", 0)
     if env_int("RANK", 0) != 0:
         return 0

@@ -1,4 +1,6 @@
-"""Sequence-parallel decode attention across ranks (one GPU per rank).
+"""Sequence-parallel attention across ranks (one GPU per rank).
+
+Decode (sp_decode):
 
 The reference splits the KV sequence over MPI ranks and merges the per-rank
 online-softmax states on rank 0 (streaming_attention_mpi_simple,
@@ -8,9 +10,19 @@ rank 0's query is broadcast, every rank reduces its contiguous KV slice to
 per-head partials (m, l, O) on its GPU, one all-gather moves hq*(d+2) floats
 per rank (NCCL over NVLink), and the merge runs on the device.
 
-``partial_fn`` / ``merge_fn`` default to the CUDA library; they are
-parameters so the orchestration (collective order, rank-0 semantics) can be
-exercised with other implementations.
+Causal prefill (sp_prefill): the sequence is cut into 2P equal chunks and
+rank r owns chunks r and 2P-1-r ("zig-zag"), so every rank gets the same
+amount of causal work (chunk c costs about c + 1/2 chunk-squares, so the two
+chunks of every rank add up to 2P).  One all-gather assembles the full K
+and V on every rank; each rank then runs the causal prefill of its two query
+chunks with their global offsets.  Outputs stay where their queries are: no
+merge.  This is the load-balanced causal chunking of configs[2] (the
+reference's sequence strategy, ops_mpi.cpp:1000-1212, without its
+statistics bug).
+
+``partial_fn`` / ``merge_fn`` / ``prefill_fn`` default to the CUDA library; they
+are parameters so the orchestration (collective order, rank-0 semantics,
+chunk placement) can be exercised with other implementations.
 """
 from __future__ import annotations
 
@@ -57,4 +69,87 @@ def sp_decode(q, k_local, v_local, scale: float = 1.0, block: int = 64, group=No
     out = merge_fn(gm, gl, go)
     if rank != 0 and not all_ranks:
         out = torch.zeros_like(out)
+    return out
+
+
+def zigzag_chunks(rank: int, world: int, S: int):
+    """(start, stop) of the two query chunks rank `rank` owns: chunks `rank`
+    and 2*world-1-rank of 2*world equal chunks (S must divide evenly)."""
+    n = 2 * world
+    if S % n:
+        raise ValueError(f"sp_prefill: S={S} is not a multiple of 2 x world size ({n})")
+    C = S // n
+    return [(rank * C, (rank + 1) * C), ((n - 1 - rank) * C, (n - rank) * C)]
+
+
+def zigzag_shard(x, rank: int, world: int):
+    """This rank's two zig-zag chunks of a token-major tensor x [S, ...],
+    concatenated (the layout sp_prefill expects)."""
+    import torch
+    (a0, a1), (b0, b1) = zigzag_chunks(rank, world, x.shape[0])
+    return torch.cat([x[a0:a1], x[b0:b1]]).contiguous()
+
+
+def _default_prefill(q, k, v, scale, q_pos0, out):
+    import torch
+    from .attention import attn_prefill
+    return attn_prefill(q, k, v, scale, q_pos0, "float32" if out.dtype == torch.float32 else "bfloat16",
+                        None, out)
+
+
+def sp_prefill(q_local, k_local, v_local, scale: float, group=None, prefill_fn=None, streams=None,
+               out_dtype=None):
+    """Causal prefill over a sequence sharded zig-zag across the group's ranks.
+
+    q_local [2C, hq, d], k_local / v_local [2C, hkv, d]: this rank's chunks
+    r and 2P-1-r of the sequence, concatenated (``zigzag_shard``).  Returns
+    out_local [2C, hq, d] for the same query rows, in ``out_dtype`` (default:
+    the dtype of q_local).  ``prefill_fn(q, k, v, scale, q_pos0, out)``
+    computes causal attention of queries at q_pos0.. against keys
+    0..len(k)-1 into ``out``; ``streams`` (two CUDA streams) let the two
+    chunks run concurrently.
+
+    One all-gather moves every rank's K and V chunks; the ranks' first chunks
+    are chunks 0..P-1 in rank order and their second chunks chunks 2P-1..P,
+    so two strided copies put the full K and V in sequence order.
+    """
+    import torch
+    import torch.distributed as dist
+
+    prefill_fn = prefill_fn or _default_prefill
+    rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
+    C2 = q_local.shape[0]
+    if C2 % 2 or k_local.shape[0] != C2 or v_local.shape[0] != C2:
+        raise ValueError("sp_prefill: q/k/v_local must hold two equal chunks of the same tokens")
+    C = C2 // 2
+    S = C2 * world
+    PC = world * C
+    (a0, a1), (b0, b1) = zigzag_chunks(rank, world, S)
+    # one all-gather of K and V together: [world, 2 (k, v), 2C, hkv, d]
+    kv = torch.stack([k_local, v_local]).contiguous()
+    flat = torch.empty((world * kv.shape[0],) + tuple(kv.shape[1:]), dtype=kv.dtype, device=kv.device)
+    dist.all_gather_into_tensor(flat, kv, group=group)
+    flat = flat.view((world,) + tuple(kv.shape))
+    kv_full = torch.empty((2, S) + tuple(kv.shape[2:]), dtype=kv.dtype, device=kv.device)
+    rest = tuple(kv.shape[2:])
+    # [2, S, ...] viewed as [2, 2 halves, world, C, ...]; sequence chunk c < P is
+    # rank c's first chunk, chunk P + i is rank P-1-i's second chunk
+    dst = kv_full.view((2, 2, world, C) + rest)
+    dst[:, 0].copy_(flat[:, :, :C].transpose(0, 1))
+    dst[:, 1].copy_(flat.flip(0)[:, :, C:].transpose(0, 1))
+    k_full, v_full = kv_full[0], kv_full[1]
+    out = torch.empty((C2,) + tuple(q_local.shape[1:]), dtype=out_dtype or q_local.dtype, device=q_local.device)
+    jobs = [(q_local[:C], a0, a1, out[:C]), (q_local[C:], b0, b1, out[C:])]
+    if streams is None:
+        for qc, q0, q1, oc in jobs:
+            prefill_fn(qc, k_full[:q1], v_full[:q1], scale, q0, oc)
+    else:
+        cur = torch.cuda.current_stream()
+        for st, (qc, q0, q1, oc) in zip(streams, jobs):
+            st.wait_stream(cur)
+            with torch.cuda.stream(st):
+                prefill_fn(qc, k_full[:q1], v_full[:q1], scale, q0, oc)
+        for st in streams:
+            cur.wait_stream(st)
     return out
