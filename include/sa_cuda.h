@@ -250,6 +250,25 @@ int sa_qwen3_set_layer(sa_qwen3* m, int layer, const float* in_norm, const float
                        const float* post_norm, const float* w_gate, const float* w_up,
                        const float* w_down);
 
+/*
+ * Qwen3 weights from a safetensors checkpoint (load_qwen3_weights,
+ * tensor_cpp/src/qwen3_loader.cpp:140-297): the file is memory-mapped and
+ * each tensor is uploaded from its stored bytes (BF16 as it is; F16 / F32
+ * rounded to bf16), without the reference's widening to fp32.  Tensor names
+ * are the Hugging Face Qwen3 ones (model.embed_tokens.weight,
+ * model.layers.{i}.self_attn.q_proj.weight, ...); lm_head.weight may be
+ * absent (tied to the embedding).  The configuration is inferred from the
+ * shapes; eps / theta <= 0 select Qwen3's 1e-6 / 1e6.
+ * sa_safetensors_inspect validates the file and reports the configuration
+ * (max_seq 0) without touching a GPU; sa_qwen3_load_safetensors creates the
+ * model on the context's GPU with room for max_seq cached tokens and uploads
+ * the weights (blocking).  Malformed files, missing tensors and wrong shapes
+ * are SA_ERR_ARG with the tensor named in the message.
+ */
+int sa_safetensors_inspect(const char* path, sa_qwen3_config* out);
+int sa_qwen3_load_safetensors(sa_ctx* ctx, const char* path, int max_seq, float eps, float theta,
+                              sa_qwen3** out);
+
 /* KVCache::reset (kv_cache.h:142-153): the cache length returns to 0. */
 int sa_qwen3_reset(sa_qwen3* m);
 /* KVCache::current_seq_len. */

@@ -259,6 +259,19 @@ class RefQwen3:
         self.h = ref.L.ref_qwen3_create(C.byref(cfg), _p(w["embed"]), _p(w["layers"]),
                                         _p(w["final_norm"]), _p(w["lm_head"]))
 
+    @classmethod
+    def from_safetensors(cls, ref: Reference, path: str) -> "RefQwen3":
+        """Weights read by the reference's own load_qwen3_weights
+        (qwen3_loader.cpp:140-297)."""
+        self = cls.__new__(cls)
+        self.ref, self.cfg = ref, Qwen3Cfg()
+        ref.L.ref_qwen3_load.restype = C.c_void_p
+        ref.L.ref_qwen3_load.argtypes = [C.c_char_p, C.c_void_p]
+        self.h = ref.L.ref_qwen3_load(os.fsencode(path), C.byref(self.cfg))
+        if not self.h:
+            ref._err("ref_qwen3_load")
+        return self
+
     def close(self):
         if self.h:
             self.ref.L.ref_qwen3_destroy(self.h)

@@ -20,6 +20,7 @@
 #include "attention.h"                 // attention/src/attention.h
 #include "tensor_cpp/ops.h"            // tensor_cpp/include/tensor_cpp/ops.h
 #include "tensor_cpp/qwen3_ops.h"
+#include "tensor_cpp/qwen3_loader.h"
 #include "tensor_cpp/qwen3_ops_avx.h"
 #include "tensor_cpp/kv_cache.h"
 
@@ -155,6 +156,35 @@ REF_EXPORT void* ref_qwen3_create(const RefCfg* c, const float* embed, const flo
         m->layers.push_back(std::move(w));
     }
     return m;
+}
+
+// The reference's own safetensors loader (load_qwen3_weights,
+// qwen3_loader.cpp:140-297): weights and the configuration it implies (the
+// loader fixes 28 layers, 16/8 heads, head_dim 128; eps / theta are the
+// forwards' 1e-6 / 1e6).
+REF_EXPORT void* ref_qwen3_load(const char* path, RefCfg* out_cfg) {
+    try {
+        q3::Qwen3Weights w = q3::load_qwen3_weights(path);
+        auto* m = new RefModel();
+        m->c.vocab = (int)w.vocab_size;
+        m->c.hidden = (int)w.hidden_size;
+        m->c.n_layers = (int)w.num_layers;
+        m->c.hq = (int)w.num_attention_heads;
+        m->c.hkv = (int)w.num_key_value_heads;
+        m->c.head_dim = (int)w.head_dim;
+        m->c.inter = (int)w.layers[0].gate_proj.shape()[0];
+        m->c.eps = 1e-6f;
+        m->c.theta = 1000000.0f;
+        m->embed = std::move(w.embed_tokens);
+        m->norm = std::move(w.norm_weight);
+        m->lm_head = std::move(w.lm_head);
+        m->layers = std::move(w.layers);
+        if (out_cfg) *out_cfg = m->c;
+        return m;
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return nullptr;
+    }
 }
 
 REF_EXPORT void ref_qwen3_destroy(void* h) { delete static_cast<RefModel*>(h); }

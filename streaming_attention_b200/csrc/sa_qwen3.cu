@@ -106,14 +106,7 @@ static uint16_t f2bf(float f) {
     return (uint16_t)(u >> 16);
 }
 
-// Upload `rows` x `cols` fp32 host values as bf16 into dst at row offset.
-static int upload_bf16(__nv_bfloat16* dst, const float* src, size_t n, cudaStream_t st) {
-    std::vector<uint16_t> tmp(n);
-    for (size_t i = 0; i < n; ++i) tmp[i] = f2bf(src[i]);
-    SA_CUDA_TRY(cudaMemcpyAsync(dst, tmp.data(), n * 2, cudaMemcpyHostToDevice, st));
-    SA_CUDA_TRY(cudaStreamSynchronize(st));
-    return SA_OK;
-}
+// Copy n fp32 host values to the device (blocking).
 static int upload_f32(float* dst, const float* src, size_t n, cudaStream_t st) {
     SA_CUDA_TRY(cudaMemcpyAsync(dst, src, n * 4, cudaMemcpyHostToDevice, st));
     SA_CUDA_TRY(cudaStreamSynchronize(st));
@@ -386,25 +379,117 @@ SA_API int sa_qwen3_destroy(sa_qwen3* m) {
     return SA_OK;
 }
 
-SA_API int sa_qwen3_set_embed(sa_qwen3* m, const float* embed, const float* final_norm, const float* lm_head) {
-    clear_error();
-    SA_CHECK_ARG(m && embed && final_norm, "sa_qwen3_set_embed: null argument");
-    DeviceGuard guard(m->ctx->device);
-    const size_t VH = (size_t)m->c.vocab * m->c.hidden;
+namespace sa {
+
+static float h2f(uint16_t h) {   // IEEE half -> float (exact)
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    uint32_t exp = (h >> 10) & 0x1Fu, man = h & 0x3FFu;
+    uint32_t bits;
+    if (exp == 0x1Fu) {
+        bits = sign | 0x7F800000u | (man << 13);
+    } else if (exp == 0) {
+        if (man == 0) {
+            bits = sign;
+        } else {   // subnormal: renormalise
+            int e = -1;
+            do { man <<= 1; ++e; } while (!(man & 0x400u));
+            bits = sign | ((uint32_t)(127 - 15 - e) << 23) | ((man & 0x3FFu) << 13);
+        }
+    } else {
+        bits = sign | ((exp + 127 - 15) << 23) | (man << 13);
+    }
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+
+static float src_at(QwSrc s, size_t i) {
+    if (s.type == QW_SRC_F32) return static_cast<const float*>(s.p)[i];
+    const uint16_t u = static_cast<const uint16_t*>(s.p)[i];
+    if (s.type == QW_SRC_F16) return h2f(u);
+    uint32_t bits = (uint32_t)u << 16;
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+
+// rows x cols elements of `src` starting at element `off` -> device bf16 rows
+// of pitch dpitch_elems (2-D copy; bf16 sources go straight from host memory).
+static int upload_rows(__nv_bfloat16* dst, size_t dpitch_elems, QwSrc src, size_t off, size_t rows,
+                       size_t cols, size_t spitch_elems, cudaStream_t st) {
+    if (src.type == QW_SRC_BF16) {
+        SA_CUDA_TRY(cudaMemcpy2DAsync(dst, dpitch_elems * 2, static_cast<const uint16_t*>(src.p) + off,
+                                      spitch_elems * 2, cols * 2, rows, cudaMemcpyHostToDevice, st));
+        SA_CUDA_TRY(cudaStreamSynchronize(st));
+        return SA_OK;
+    }
+    std::vector<uint16_t> tmp(rows * cols);
+    for (size_t r = 0; r < rows; ++r)
+        for (size_t c = 0; c < cols; ++c) tmp[r * cols + c] = f2bf(src_at(src, off + r * spitch_elems + c));
+    SA_CUDA_TRY(cudaMemcpy2DAsync(dst, dpitch_elems * 2, tmp.data(), cols * 2, cols * 2, rows,
+                                  cudaMemcpyHostToDevice, st));
+    SA_CUDA_TRY(cudaStreamSynchronize(st));
+    return SA_OK;
+}
+
+static int upload_gain(float* dst, QwSrc src, size_t n, cudaStream_t st) {
+    std::vector<float> tmp(n);
+    for (size_t i = 0; i < n; ++i) tmp[i] = src_at(src, i);
+    return upload_f32(dst, tmp.data(), n, st);
+}
+
+int qwen3_upload_embed(sa_qwen3* m, QwSrc embed, QwSrc final_norm, QwSrc lm_head) {
+    const size_t V = m->c.vocab, H = m->c.hidden;
     cudaStream_t st = m->ctx->stream;
-    SA_RC(upload_bf16(m->embed, embed, VH, st));
-    SA_RC(upload_f32(m->final_norm, final_norm, m->c.hidden, st));
-    const bool tied = lm_head == nullptr || lm_head == embed ||
-                      std::memcmp(lm_head, embed, VH * sizeof(float)) == 0;
+    SA_RC(upload_rows(m->embed, H, embed, 0, V, H, H, st));
+    SA_RC(upload_gain(m->final_norm, final_norm, H, st));
+    bool tied = lm_head.p == nullptr || lm_head.p == embed.p;
+    if (!tied && lm_head.type == embed.type) {
+        const size_t bytes = V * H * (embed.type == QW_SRC_F32 ? 4 : 2);
+        tied = std::memcmp(lm_head.p, embed.p, bytes) == 0;
+    }
     if (tied) {
         if (m->lm_head != m->embed) cudaFree(m->lm_head);
         m->lm_head = m->embed;
     } else {
-        if (m->lm_head == m->embed) SA_RC(dalloc(&m->lm_head, VH));
-        SA_RC(upload_bf16(m->lm_head, lm_head, VH, st));
+        if (m->lm_head == m->embed) SA_RC(dalloc(&m->lm_head, V * H));
+        SA_RC(upload_rows(m->lm_head, H, lm_head, 0, V, H, H, st));
     }
     m->loaded_embed = true;
     return SA_OK;
+}
+
+int qwen3_upload_layer(sa_qwen3* m, int layer, QwSrc in_norm, QwSrc wq, QwSrc wk, QwSrc wv, QwSrc q_norm,
+                       QwSrc k_norm, QwSrc wo, QwSrc post_norm, QwSrc w_gate, QwSrc w_up, QwSrc w_down) {
+    const sa_qwen3_config& c = m->c;
+    const size_t H = c.hidden, I = c.inter, D = c.head_dim;
+    auto& L = m->layers[layer];
+    cudaStream_t st = m->ctx->stream;
+    SA_RC(upload_gain(L.in_norm, in_norm, H, st));
+    SA_RC(upload_gain(L.post_norm, post_norm, H, st));
+    SA_RC(upload_gain(L.q_norm, q_norm, D, st));
+    SA_RC(upload_gain(L.k_norm, k_norm, D, st));
+    // [q; k; v] rows, as qwen3_loader.cpp builds qkv_projs
+    SA_RC(upload_rows(L.wqkv, H, wq, 0, m->QD, H, H, st));
+    SA_RC(upload_rows(L.wqkv + (size_t)m->QD * H, H, wk, 0, m->KD, H, H, st));
+    SA_RC(upload_rows(L.wqkv + (size_t)(m->QD + m->KD) * H, H, wv, 0, m->KD, H, H, st));
+    SA_RC(upload_rows(L.wo, m->QD, wo, 0, H, m->QD, m->QD, st));
+    // gate/up interleaved in blocks of 32 rows: [gate 32b..32b+31 ; up 32b..32b+31]:
+    // the blocks of gate land at even block slots, those of up at odd ones
+    SA_RC(upload_rows(L.wgu, 2 * 32 * H, w_gate, 0, I / 32, 32 * H, 32 * H, st));
+    SA_RC(upload_rows(L.wgu + 32 * H, 2 * 32 * H, w_up, 0, I / 32, 32 * H, 32 * H, st));
+    SA_RC(upload_rows(L.wd, I, w_down, 0, H, I, I, st));
+    m->loaded_layer[layer] = true;
+    return SA_OK;
+}
+
+}  // namespace sa
+
+SA_API int sa_qwen3_set_embed(sa_qwen3* m, const float* embed, const float* final_norm, const float* lm_head) {
+    clear_error();
+    SA_CHECK_ARG(m && embed && final_norm, "sa_qwen3_set_embed: null argument");
+    DeviceGuard guard(m->ctx->device);
+    return qwen3_upload_embed(m, {embed, QW_SRC_F32}, {final_norm, QW_SRC_F32}, {lm_head, QW_SRC_F32});
 }
 
 SA_API int sa_qwen3_set_layer(sa_qwen3* m, int layer, const float* in_norm, const float* wq, const float* wk,
@@ -415,31 +500,9 @@ SA_API int sa_qwen3_set_layer(sa_qwen3* m, int layer, const float* in_norm, cons
     SA_CHECK_ARG(in_norm && wq && wk && wv && q_norm && k_norm && wo && post_norm && w_gate && w_up && w_down,
                  "sa_qwen3_set_layer: null weight");
     DeviceGuard guard(m->ctx->device);
-    const sa_qwen3_config& c = m->c;
-    const size_t H = c.hidden, I = c.inter, D = c.head_dim;
-    auto& L = m->layers[layer];
-    cudaStream_t st = m->ctx->stream;
-    SA_RC(upload_f32(L.in_norm, in_norm, H, st));
-    SA_RC(upload_f32(L.post_norm, post_norm, H, st));
-    SA_RC(upload_f32(L.q_norm, q_norm, D, st));
-    SA_RC(upload_f32(L.k_norm, k_norm, D, st));
-    // [q; k; v] rows, as qwen3_loader.cpp builds qkv_projs
-    std::vector<float> qkv((size_t)m->NQKV * H);
-    std::memcpy(qkv.data(), wq, (size_t)m->QD * H * 4);
-    std::memcpy(qkv.data() + (size_t)m->QD * H, wk, (size_t)m->KD * H * 4);
-    std::memcpy(qkv.data() + (size_t)(m->QD + m->KD) * H, wv, (size_t)m->KD * H * 4);
-    SA_RC(upload_bf16(L.wqkv, qkv.data(), qkv.size(), st));
-    SA_RC(upload_bf16(L.wo, wo, H * m->QD, st));
-    // gate/up interleaved in blocks of 32 rows: [gate 32b..32b+31 ; up 32b..32b+31]
-    std::vector<float> gu(2 * I * H);
-    for (size_t b = 0; b < I / 32; ++b) {
-        std::memcpy(gu.data() + (2 * b) * 32 * H, w_gate + b * 32 * H, 32 * H * 4);
-        std::memcpy(gu.data() + (2 * b + 1) * 32 * H, w_up + b * 32 * H, 32 * H * 4);
-    }
-    SA_RC(upload_bf16(L.wgu, gu.data(), gu.size(), st));
-    SA_RC(upload_bf16(L.wd, w_down, H * I, st));
-    m->loaded_layer[layer] = true;
-    return SA_OK;
+    auto F = [](const float* p) { return QwSrc{p, QW_SRC_F32}; };
+    return qwen3_upload_layer(m, layer, F(in_norm), F(wq), F(wk), F(wv), F(q_norm), F(k_norm), F(wo),
+                              F(post_norm), F(w_gate), F(w_up), F(w_down));
 }
 
 SA_API int sa_qwen3_reset(sa_qwen3* m) {

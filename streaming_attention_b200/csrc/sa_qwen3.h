@@ -49,4 +49,18 @@ int launch_gemv2(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, i
                  const float* nw, float eps, float* y, unsigned long long* amax);
 int launch_amax_to_token(cudaStream_t st, unsigned long long* amax, int64_t* tok);
 
+// A host weight array in one of the element types a checkpoint may hold.
+enum : int { QW_SRC_F32 = 0, QW_SRC_BF16 = 1, QW_SRC_F16 = 2 };
+struct QwSrc {
+    const void* p;
+    int type;   // QW_SRC_*
+};
+// Upload the embedding / final norm / lm_head (lm_head.p NULL = tied) and one
+// layer's weights from host arrays of any QW_SRC type; bf16 arrays are copied
+// to the device as they are, others are rounded to bf16 on the host.  Shapes
+// as sa_qwen3_set_embed / sa_qwen3_set_layer.  Blocking.
+int qwen3_upload_embed(sa_qwen3* m, QwSrc embed, QwSrc final_norm, QwSrc lm_head);
+int qwen3_upload_layer(sa_qwen3* m, int layer, QwSrc in_norm, QwSrc wq, QwSrc wk, QwSrc wv, QwSrc q_norm,
+                       QwSrc k_norm, QwSrc wo, QwSrc post_norm, QwSrc w_gate, QwSrc w_up, QwSrc w_down);
+
 }  // namespace sa

@@ -9,6 +9,7 @@ Weights come as fp32 host arrays in the reference's shapes.
 from __future__ import annotations
 
 import ctypes as C
+import os
 
 import numpy as np
 
@@ -51,7 +52,37 @@ def _fp(a: np.ndarray):
     return a.ctypes.data_as(C.POINTER(C.c_float))
 
 
+_CFG_FIELDS = ("vocab", "hidden", "n_layers", "hq", "hkv", "head_dim", "inter", "eps", "theta")
+
+
+def inspect_safetensors(path: str) -> dict:
+    """The Qwen3 configuration a safetensors checkpoint implies (no GPU needed;
+    sa_safetensors_inspect).  Raises SAError for malformed files."""
+    c = Qwen3Config()
+    check(lib().sa_safetensors_inspect(os.fsencode(path), C.byref(c)))
+    return {f: getattr(c, f) for f in _CFG_FIELDS}
+
+
 class Qwen3:
+    @classmethod
+    def from_safetensors(cls, path: str, max_seq: int = 4096, ctx: Context | None = None,
+                         eps: float = 0.0, theta: float = 0.0) -> "Qwen3":
+        """A model whose weights are uploaded straight from a safetensors
+        checkpoint (sa_qwen3_load_safetensors: bf16 bytes to the GPU, no fp32
+        round trip).  eps / theta <= 0 select Qwen3's 1e-6 / 1e6."""
+        self = cls.__new__(cls)
+        self.cfg = inspect_safetensors(path)
+        if eps > 0:
+            self.cfg["eps"] = eps
+        if theta > 0:
+            self.cfg["theta"] = theta
+        self.ctx = ctx or default_context(0)
+        h = C.c_void_p()
+        check(lib().sa_qwen3_load_safetensors(self.ctx.h, os.fsencode(path), max_seq, eps, theta, C.byref(h)))
+        self.h = h
+        self.max_seq = max_seq
+        return self
+
     def __init__(self, cfg: dict, max_seq: int = 4096, ctx: Context | None = None):
         self.cfg = dict(cfg)
         self.ctx = ctx or default_context(0)

@@ -7,6 +7,8 @@ max |logit| (the prompt GEMMs carry ~16 bits of activation mantissa, the
 decode GEMVs full fp32), greedy tokens identical to the reference's.
 """
 import numpy as np
+
+from oracle.oracle import bf16_round
 import pytest
 
 import _inputs as I
@@ -131,6 +133,35 @@ def test_qwen3_kv_mirror_read_write(ctx, oracle):
     b = m2.forward(np.array([7]), use_cache=True, logits="last")
     np.testing.assert_array_equal(a, b)
     assert m.cache_len == m2.cache_len == S + 1
+
+
+@pytest.mark.parametrize("dtype,tied", [("BF16", True), ("BF16", False), ("F32", True), ("F16", True)])
+def test_qwen3_from_safetensors_equals_load(ctx, tmp_path, dtype, tied):
+    """A model uploaded straight from a safetensors checkpoint (bf16 bytes to
+    the GPU) computes exactly what the same weights uploaded through
+    sa_qwen3_set_layer compute; F16 checkpoints hold the weights rounded to
+    fp16, so they agree within the logits bar."""
+    from streaming_attention_b200 import Qwen3
+    from streaming_attention_b200.checkpoint import write_qwen3_safetensors
+    from streaming_attention_b200.qwen3 import random_weights
+    cfg = dict(vocab=600, hidden=256, n_layers=2, hq=4, hkv=2, head_dim=128, inter=512, eps=1e-6, theta=1e6)
+    w = random_weights(cfg, 21)
+    w["final_norm"] = bf16_round(np.linspace(0.5, 1.5, cfg["hidden"], dtype=np.float32))
+    if not tied:
+        w["lm_head"] = random_weights(cfg, 22)["embed"]
+    path = str(tmp_path / "m.safetensors")
+    write_qwen3_safetensors(path, cfg, w, dtype=dtype, tied=tied)
+    a = Qwen3(cfg, max_seq=64, ctx=ctx)
+    a.load(w)
+    b = Qwen3.from_safetensors(path, max_seq=64, ctx=ctx)
+    assert b.cfg["n_layers"] == 2 and b.cfg["hq"] == 4
+    ids = I.rng(5).integers(0, cfg["vocab"], 20)
+    la, lb = a.forward(ids), b.forward(ids)
+    if dtype == "F16":
+        _close(lb, la, "f16 checkpoint")
+    else:
+        np.testing.assert_array_equal(lb, la)
+    assert [int(t) for t in a.generate(ids, 5)] == [int(t) for t in b.generate(ids, 5)]
 
 
 def test_qwen3_errors(ctx):
