@@ -79,6 +79,13 @@ struct sa_qwen3 {
     float* dec_scratch = nullptr;        // split partials for the decode step (max plan)
     unsigned* dec_cnt = nullptr;         // [hkv]
     unsigned long long* d_amax = nullptr;  // argmax key of the last lm_head GEMV (0 between uses)
+    // single-launch decode step (sa_qwen3_mega.cu): set up on first use;
+    // mega_grid < 0 once found unsupported
+    int mega_grid = 0;
+    sa::MegaLayer* d_mlayers = nullptr;  // [L]
+    float* mpart = nullptr;              // attention split partials
+    unsigned* mhead_cnt = nullptr;       // [hkv]
+    unsigned* mgbar = nullptr;           // grid barrier words [4]
     // CUDA graphs: the single-token decode step; cache-free prefill per (S, logits mode)
     cudaGraphExec_t dec_graph = nullptr;
     std::map<std::pair<int, int>, cudaGraphExec_t> pf_graphs;
@@ -126,6 +133,7 @@ static void free_model(sa_qwen3* m) {
     cudaFree(m->a_hi); cudaFree(m->a_lo); cudaFree(m->b_hi); cudaFree(m->b_lo);
     cudaFree(m->logits); cudaFree(m->ids); cudaFree(m->gemm_ws); cudaFree(m->gemm_cnt);
     cudaFree(m->d_state); cudaFree(m->d_toks); cudaFree(m->dec_scratch); cudaFree(m->dec_cnt); cudaFree(m->d_amax);
+    cudaFree(m->d_mlayers); cudaFree(m->mpart); cudaFree(m->mhead_cnt); cudaFree(m->mgbar);
     if (m->dec_graph) cudaGraphExecDestroy(m->dec_graph);
     for (auto& kv : m->pf_graphs) cudaGraphExecDestroy(kv.second);
     if (m->ev_in) cudaEventDestroy(m->ev_in);
@@ -669,6 +677,56 @@ static int decode_step_dev(sa_qwen3* m) {
     return SA_OK;
 }
 
+// The single-launch decode step's buffers and per-layer weight table; false
+// when this model or device cannot use it (the graph of separate kernels
+// serves then).
+static bool mega_ready(sa_qwen3* m) {
+    if (m->mega_grid < 0) return false;
+    if (m->mega_grid > 0) return true;
+    const sa_qwen3_config& c = m->c;
+    const int grid = mega_supported(c, m->ctx->num_sms) ? mega_grid(m->ctx->device) : 0;
+    if (grid < c.hkv) {
+        m->mega_grid = -1;
+        return false;
+    }
+    std::vector<MegaLayer> ls(c.n_layers);
+    for (int l = 0; l < c.n_layers; ++l) {
+        const auto& L = m->layers[l];
+        ls[l] = MegaLayer{L.wqkv, L.wo, L.wgu, L.wd, L.in_norm, L.post_norm, L.q_norm, L.k_norm};
+    }
+    const size_t part = (size_t)c.hkv * (grid / c.hkv) * (c.hq / c.hkv) * (c.head_dim + 2);
+    bool ok = dmalloc(reinterpret_cast<void**>(&m->d_mlayers), ls.size() * sizeof(MegaLayer)) == SA_OK &&
+              dalloc(&m->mpart, part) == SA_OK && dalloc(&m->mhead_cnt, (size_t)c.hkv) == SA_OK &&
+              dalloc(&m->mgbar, 4) == SA_OK;
+    ok = ok && cudaMemcpy(m->d_mlayers, ls.data(), ls.size() * sizeof(MegaLayer), cudaMemcpyHostToDevice) ==
+                   cudaSuccess &&
+         cudaMemset(m->mhead_cnt, 0, (size_t)c.hkv * sizeof(unsigned)) == cudaSuccess &&
+         cudaMemset(m->mgbar, 0, 4 * sizeof(unsigned)) == cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+        clear_error();
+        m->mega_grid = -1;
+        return false;
+    }
+    m->mega_grid = grid;
+    return true;
+}
+
+static int launch_mega_step(sa_qwen3* m, cudaStream_t st) {
+    const sa_qwen3_config& c = m->c;
+    MegaParams q;
+    q.layers = m->d_mlayers;
+    q.L = c.n_layers; q.H = c.hidden; q.I = c.inter; q.hq = c.hq; q.hkv = c.hkv; q.V = c.vocab;
+    q.max_seq = c.max_seq; q.eps = c.eps;
+    q.embed = m->embed; q.lm_head = m->lm_head; q.final_norm = m->final_norm;
+    q.kc = m->kc; q.vc = m->vc; q.cos_t = m->cos_t; q.sin_t = m->sin_t;
+    q.x = m->x; q.qkv = m->qkv; q.attn = m->attn; q.act = m->act; q.part = m->mpart;
+    q.head_cnt = m->mhead_cnt; q.amax = m->d_amax; q.gbar = m->mgbar;
+    q.state = m->d_state; q.ids = m->ids; q.toks = m->d_toks; q.toks_cap = m->toks_cap;
+    q.status = m->ctx->status;
+    return launch_decode_mega(st, m->mega_grid, q);
+}
+
 SA_API int sa_qwen3_generate(sa_qwen3* m, const int64_t* prompt, int S, int n_new, int64_t* out_tokens,
                              unsigned flags) {
     clear_error();
@@ -699,8 +757,15 @@ SA_API int sa_qwen3_generate(sa_qwen3* m, const int64_t* prompt, int S, int n_ne
         const int state[2] = {pos0 + S, 0};
         SA_CUDA_TRY(cudaMemcpyAsync(m->d_state, state, sizeof(state), cudaMemcpyHostToDevice, st));
         SA_RC(launch_advance(st, m->d_state, m->ids, m->d_toks, m->toks_cap, 0, false));   // first new token
-        if (n_new > 1 && !m->dec_graph) SA_RC(capture(m, &m->dec_graph, [&]() { return decode_step_dev(m); }));
-        for (int t = 1; t < n_new; ++t) SA_CUDA_TRY(cudaGraphLaunch(m->dec_graph, st));
+        if (n_new > 1 && mega_ready(m)) {
+            // one cooperative launch per token (sa_qwen3_mega.cu)
+            SA_CUDA_TRY(cudaMemsetAsync(m->mgbar, 0, 4 * sizeof(unsigned), st));
+            for (int t = 1; t < n_new; ++t) SA_RC(launch_mega_step(m, st));
+        } else {
+            if (n_new > 1 && !m->dec_graph)
+                SA_RC(capture(m, &m->dec_graph, [&]() { return decode_step_dev(m); }));
+            for (int t = 1; t < n_new; ++t) SA_CUDA_TRY(cudaGraphLaunch(m->dec_graph, st));
+        }
         SA_CUDA_TRY(cudaMemcpyAsync(out_tokens, m->d_toks, (size_t)n_new * 8,
                                     host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, st));
         return SA_OK;

@@ -49,6 +49,35 @@ int launch_gemv2(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, i
                  const float* nw, float eps, float* y, unsigned long long* amax);
 int launch_amax_to_token(cudaStream_t st, unsigned long long* amax, int64_t* tok);
 
+// ---- single-launch decode step (sa_qwen3_mega.cu) ---------------------------
+struct MegaLayer {
+    const __nv_bfloat16 *wqkv, *wo, *wgu, *wd;
+    const float *in_norm, *post_norm, *q_norm, *k_norm;
+};
+struct MegaParams {
+    const MegaLayer* layers;   // device array [L]
+    int L, H, I, hq, hkv, V, max_seq;
+    float eps;
+    const __nv_bfloat16* embed;
+    const __nv_bfloat16* lm_head;
+    const float* final_norm;
+    float *kc, *vc;
+    const float *cos_t, *sin_t;
+    float *x, *qkv, *attn, *act;
+    float* part;               // [hkv][grid / hkv][hq / hkv][130]
+    unsigned* head_cnt;        // [hkv], zeroed
+    unsigned long long* amax;  // zeroed
+    unsigned* gbar;            // [4], zeroed before a run of launches
+    int* state;
+    int64_t* ids;
+    int64_t* toks;
+    int toks_cap;
+    int* status;
+};
+bool mega_supported(const sa_qwen3_config& c, int num_sms);
+int mega_grid(int device);   // CTAs of one launch (one per SM), 0 if the device cannot run it
+int launch_decode_mega(cudaStream_t st, int grid, const MegaParams& q);
+
 // A host weight array in one of the element types a checkpoint may hold.
 enum : int { QW_SRC_F32 = 0, QW_SRC_BF16 = 1, QW_SRC_F16 = 2 };
 struct QwSrc {

@@ -164,6 +164,39 @@ def test_qwen3_from_safetensors_equals_load(ctx, tmp_path, dtype, tied):
     assert [int(t) for t in a.generate(ids, 5)] == [int(t) for t in b.generate(ids, 5)]
 
 
+@pytest.mark.parametrize("prompt_len,n_new", [(5, 40), (300, 24)])
+def test_qwen3_single_launch_step_matches_kernel_graph(ctx, monkeypatch, prompt_len, n_new):
+    """Greedy decode through the single-launch step (one cooperative kernel per
+    token, SA_QWEN3_MEGA=1) yields the tokens of the multi-kernel CUDA-graph
+    step (the default) on a model with Qwen3-0.6B's layer shapes, and leaves
+    the same KV cache."""
+    from streaming_attention_b200 import Qwen3
+    from streaming_attention_b200.qwen3 import random_weights
+    cfg = dict(vocab=32000, hidden=1024, n_layers=4, hq=16, hkv=8, head_dim=128, inter=3072, eps=1e-6, theta=1e6)
+    w = random_weights(cfg, 31)
+    ids = I.rng(prompt_len).integers(0, cfg["vocab"], prompt_len)
+    monkeypatch.setenv("SA_QWEN3_MEGA", "1")
+    a = Qwen3(cfg, max_seq=512, ctx=ctx)
+    a.load(w)
+    ta = [int(t) for t in a.generate(ids, n_new)]
+    monkeypatch.delenv("SA_QWEN3_MEGA")
+    b = Qwen3(cfg, max_seq=512, ctx=ctx)
+    b.load(w)
+    tb = [int(t) for t in b.generate(ids, n_new)]
+    assert ta == tb
+    assert a.cache_len == b.cache_len == prompt_len + n_new - 1
+    for layer in (0, cfg["n_layers"] - 1):
+        ka, va = a.read_kv(layer)
+        kb, vb = b.read_kv(layer)
+        _close(ka, kb, f"K cache layer {layer}")
+        _close(va, vb, f"V cache layer {layer}")
+    # and a second generate on the same model continues from its cache
+    monkeypatch.setenv("SA_QWEN3_MEGA", "1")
+    more = [int(t) for t in a.generate(np.array([ta[-1]]), 4)]
+    monkeypatch.delenv("SA_QWEN3_MEGA")
+    assert len(more) == 4 and a.cache_len == prompt_len + n_new - 1 + 4
+
+
 def test_qwen3_errors(ctx):
     from streaming_attention_b200 import Qwen3, SAError
     cfg = dict(vocab=300, hidden=256, n_layers=1, hq=2, hkv=1, head_dim=128, inter=256)
