@@ -123,6 +123,7 @@ template <typename KT, int D, int G>
 __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
     using S = Shape<KT, D>;
     constexpr int SR = S::STAGE_ROWS, RB = S::ROW_BYTES, CPL = S::CPL, CH = S::CH, VEC = S::VEC;
+    constexpr int DYN_ROWS = 2 * SR;   // rows per CTA when the length is read on the device
 
     pdl_trigger();
     pdl_wait();
@@ -136,9 +137,21 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int kvh = blockIdx.y, split = blockIdx.x, qz = blockIdx.z;
-    const int t0 = split * a.rows_per_split;
     const int T = a.len_dev ? (*a.len_dev + 1) : a.T;
-    const int nrows = max(0, min(T + qz - t0, a.rows_per_split));
+    // With the length read on the device the grid is planned for the cache's
+    // capacity; the rows actually present are re-split here into about
+    // DYN_ROWS rows per CTA, and CTAs past the last such split leave at once
+    // (the merge then counts only the splits in use).
+    int rps = a.rows_per_split, nsplit = a.n_splits;
+    if (a.len_dev) {
+        int want = (T + DYN_ROWS - 1) / DYN_ROWS;
+        want = want < 1 ? 1 : (want > a.n_splits ? a.n_splits : want);
+        rps = ((T + want - 1) / want + SR - 1) / SR * SR;
+        nsplit = (T + rps - 1) / rps;
+        if (split >= nsplit) return;
+    }
+    const int t0 = split * rps;
+    const int nrows = max(0, min(T + qz - t0, rps));
     const int nst = (nrows + SR - 1) / SR;
     const KT* kg = static_cast<const KT*>(a.k) + (size_t)kvh * a.kv_head_stride + (size_t)t0 * D;
     const KT* vg = static_cast<const KT*>(a.v) + (size_t)kvh * a.kv_head_stride + (size_t)t0 * D;
@@ -326,7 +339,7 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
             O += red_o[(w * G + g) * D + col] * wt;
         }
         const int h = kvh * G + g;
-        if (a.n_splits == 1) {
+        if (nsplit == 1) {
             // one split: this CTA holds the whole state; finalise in place
             a.out[(size_t)qz * a.o_stride + (size_t)h * D + col] = L > 0.f ? O / L : 0.f;
             if (col == 0 && a.out_m) {
@@ -342,28 +355,28 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
             a.part_l[pi] = L;
         }
     }
-    if (a.n_splits == 1) return;
+    if (nsplit == 1) return;
     __threadfence();
     __syncthreads();
-    if (tid == 0) s_last = (atomicAdd(&a.counters[kvh], 1u) == (unsigned)(a.n_splits - 1));
+    if (tid == 0) s_last = (atomicAdd(&a.counters[kvh], 1u) == (unsigned)(nsplit - 1));
     __syncthreads();
     if (!s_last) return;
     __threadfence();
 
     // ---------------- last CTA of this KV head: merge the split partials
-    float* wts = reinterpret_cast<float*>(smem);                 // [G][n_splits]
+    float* wts = reinterpret_cast<float*>(smem);                 // [G][nsplit]
     float* hdr = wts + G * a.n_splits;                           // [G]: M, L
-    const int ns = a.n_splits;
+    const int ns = nsplit, pstride = a.n_splits;                  // splits in use; partials' row stride
     for (int g = warp; g < G; g += THREADS / 32) {
         const int h = kvh * G + g;
         float M = -INFINITY;
-        for (int i = lane; i < ns; i += 32) M = fmaxf(M, __ldcg(a.part_m + (size_t)h * ns + i));
+        for (int i = lane; i < ns; i += 32) M = fmaxf(M, __ldcg(a.part_m + (size_t)h * pstride + i));
 #pragma unroll
         for (int off = 16; off; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
         float L = 0.f;
         for (int i = lane; i < ns; i += 32) {
-            const float mi = __ldcg(a.part_m + (size_t)h * ns + i);
-            const float wi = (mi == -INFINITY) ? 0.f : __ldcg(a.part_l + (size_t)h * ns + i) * ex2(mi - M);
+            const float mi = __ldcg(a.part_m + (size_t)h * pstride + i);
+            const float wi = (mi == -INFINITY) ? 0.f : __ldcg(a.part_l + (size_t)h * pstride + i) * ex2(mi - M);
             wts[g * ns + i] = wi;
             L += wi;
         }
@@ -380,7 +393,7 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
         const int h = kvh * G + g;
         const float L = hdr[2 * g + 1];
         float O = 0.f;
-        for (int i = 0; i < ns; ++i) O += wts[g * ns + i] * __ldcg(a.part_o + ((size_t)h * ns + i) * D + col);
+        for (int i = 0; i < ns; ++i) O += wts[g * ns + i] * __ldcg(a.part_o + ((size_t)h * pstride + i) * D + col);
         a.out[(size_t)h * D + col] = L > 0.f ? O / L : 0.f;
         if (col == 0 && a.out_m) {
             a.out_m[h] = L > 0.f ? hdr[2 * g] * LN2 : -INFINITY;

@@ -77,7 +77,7 @@ struct sa_qwen3 {
     int64_t* d_toks = nullptr;           // [toks_cap]
     int toks_cap = 0;
     float* dec_scratch = nullptr;        // split partials for the decode step (max plan)
-    unsigned* dec_cnt = nullptr;         // [hkv]
+    unsigned* dec_cnt = nullptr;         // [hkv] attention + [hq + hkv] QKV-epilogue arrival counters
     unsigned long long* d_amax = nullptr;  // argmax key of the last lm_head GEMV (0 between uses)
     // single-launch decode step (sa_qwen3_mega.cu): set up on first use;
     // mega_grid < 0 once found unsupported
@@ -255,9 +255,13 @@ static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr
         const float* ka = kc + (size_t)shift * D;             // attention view of this sequence
         const float* va = vc + (size_t)shift * D;
         if (M == 1) {
-            SA_RC(launch_gemv2(st, QW_EPI_STORE, true, L.wqkv, m->NQKV, H, m->x, L.in_norm, c.eps, m->qkv, nullptr));
-            SA_RC(launch_qknorm_rope_append(st, m->qkv, 1, c.hq, c.hkv, L.q_norm, L.k_norm, m->cos_t, m->sin_t, pos0,
-                                            pos_dev, shift, m->q, kc, vc, c.max_seq));
+            QkvEpi e;
+            e.hq = c.hq; e.hkv = c.hkv; e.max_seq = c.max_seq; e.pos0 = pos0; e.row_shift = shift;
+            e.pos_dev = pos_dev;
+            e.qn = L.q_norm; e.kn = L.k_norm; e.cos_t = m->cos_t; e.sin_t = m->sin_t;
+            e.q_out = m->q; e.kc = kc; e.vc = vc;
+            e.cnt = m->dec_cnt + c.hkv;
+            SA_RC(launch_gemv2(st, QW_EPI_QKV, true, L.wqkv, m->NQKV, H, m->x, L.in_norm, c.eps, m->qkv, nullptr, &e));
             SA_RC(decode_dev_launch(st, m->ctx->status, m->ctx->num_sms, m->q, ka, va, (long long)c.max_seq * D,
                                     pos_dev, pos0 + 1, c.max_seq - shift, D, c.hq, c.hkv, scale, m->attn,
                                     m->dec_scratch, m->dec_cnt));
@@ -355,11 +359,11 @@ SA_API int sa_qwen3_create(sa_ctx* ctx, const sa_qwen3_config* cfg, sa_qwen3** o
     if (!rc) rc = dalloc(&m->d_toks, (size_t)m->toks_cap);
     if (!rc) rc = dalloc(&m->dec_scratch,
                          decode_dev_scratch_floats(ctx->num_sms, c.max_seq, (int)D, c.hq, c.hkv, nullptr));
-    if (!rc) rc = dalloc(&m->dec_cnt, (size_t)c.hkv);
+    if (!rc) rc = dalloc(&m->dec_cnt, (size_t)(c.hq + 2 * c.hkv));
     if (!rc) rc = dalloc(&m->d_amax, 1);
     if (!rc && cudaMemsetAsync(m->d_amax, 0, sizeof(unsigned long long), ctx->stream) != cudaSuccess)
         rc = set_error(SA_ERR_CUDA, "memset");
-    if (!rc && cudaMemsetAsync(m->dec_cnt, 0, c.hkv * sizeof(unsigned), ctx->stream) != cudaSuccess)
+    if (!rc && cudaMemsetAsync(m->dec_cnt, 0, (c.hq + 2 * c.hkv) * sizeof(unsigned), ctx->stream) != cudaSuccess)
         rc = set_error(SA_ERR_CUDA, "memset");
     m->cur = ctx->stream;
     if (!rc) rc = launch_rope_table(ctx->stream, c.max_seq, (int)D, c.theta, m->cos_t, m->sin_t);

@@ -9,8 +9,19 @@
 #define QW_EPI_STORE  0   // y = W x
 #define QW_EPI_RESID  1   // y += W x          (residual stream)
 #define QW_EPI_SWIGLU 2   // y_i = silu(g_i) * u_i over [gate(32); up(32)] row blocks
+#define QW_EPI_QKV    3   // decode QKV projection + QK-norm + RoPE + KV-cache append (head_dim 128)
 
 namespace sa {
+
+// Operands of the QW_EPI_QKV epilogue: one token at RoPE position
+// (pos_dev ? *pos_dev : pos0), written to cache row position + row_shift.
+struct QkvEpi {
+    int hq = 0, hkv = 0, max_seq = 0, pos0 = 0, row_shift = 0;
+    const int* pos_dev = nullptr;
+    const float *qn = nullptr, *kn = nullptr, *cos_t = nullptr, *sin_t = nullptr;
+    float *q_out = nullptr, *kc = nullptr, *vc = nullptr;
+    unsigned* cnt = nullptr;   // [hq + hkv] arrival counters, zero between launches
+};
 
 int gemm_launch(cudaStream_t st, int* status, const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo,
                 long long lda, const __nv_bfloat16* w, int M, int N, int K, int mode, float* C,
@@ -46,7 +57,7 @@ int launch_gemv(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, in
                 const float* nw, float eps, float* y, int num_sms);
 int launch_argmax(cudaStream_t st, const float* v, int n, int64_t* out);
 int launch_gemv2(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, int N_out, int K, const float* x,
-                 const float* nw, float eps, float* y, unsigned long long* amax);
+                 const float* nw, float eps, float* y, unsigned long long* amax, const QkvEpi* qkv = nullptr);
 int launch_amax_to_token(cudaStream_t st, unsigned long long* amax, int64_t* tok);
 
 // ---- single-launch decode step (sa_qwen3_mega.cu) ---------------------------

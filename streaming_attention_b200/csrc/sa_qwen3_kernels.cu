@@ -110,6 +110,33 @@ __global__ void rope_table_kernel(int n_pos, int D, float theta, float* cos_t, f
 // times q_norm, then rotate-half RoPE at position pos0 + m
 // (qwen3_ops.cpp:110-188) -> q_out [M, hq, 128].  K heads: the same with
 // k_norm -> K cache row pos0 + m.  V heads: copied to the V cache.
+// RMS-normalise one 128-wide head held by a warp (lane l: elements 4l..4l+3)
+// with gain nw, then rotate-half RoPE with the position's cos/sin rows.
+__device__ __forceinline__ float4 head_norm_rope(const float (&e_in)[4], const float* nw, const float* cr,
+                                                 const float* sr, int lane) {
+    constexpr int D = 128;
+    float e[4] = {e_in[0], e_in[1], e_in[2], e_in[3]};
+    float ss = e[0] * e[0] + e[1] * e[1] + e[2] * e[2] + e[3] * e[3];
+    ss = warp_sum(ss);
+    const float rms = sqrtf(ss / (float)D + 1e-6f);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) e[j] = (e[j] / rms) * nw[4 * lane + j];
+    // rotate-half: element i pairs with i + 64 (lanes l and l ^ 16)
+    float p[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) p[j] = __shfl_xor_sync(0xffffffffu, e[j], 16);
+    const bool first = lane < 16;
+    float o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int i = (4 * lane + j) & (D / 2 - 1);
+        const float c = cr[i], s = sr[i];
+        // first half: x1*c + (-x2)*s ; second half: x2*c + x1*s
+        o[j] = first ? e[j] * c + (-p[j]) * s : e[j] * c + p[j] * s;
+    }
+    return make_float4(o[0], o[1], o[2], o[3]);
+}
+
 __global__ void qknorm_rope_append_kernel(const float* qkv, int M, int hq, int hkv, const float* qn,
                                           const float* kn, const float* cos_t, const float* sin_t, int pos0,
                                           const int* pos_dev, int row_shift, float* q_out, float* kc, float* vc,
@@ -133,28 +160,8 @@ __global__ void qknorm_rope_append_kernel(const float* qkv, int M, int hq, int h
         *reinterpret_cast<float4*>(dst + 4 * lane) = v4;
         return;
     }
-    const float* nw = h < hq ? qn : kn;
-    float ss = e[0] * e[0] + e[1] * e[1] + e[2] * e[2] + e[3] * e[3];
-    ss = warp_sum(ss);
-    const float rms = sqrtf(ss / (float)D + 1e-6f);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) e[j] = (e[j] / rms) * nw[4 * lane + j];
-    // rotate-half: element i pairs with i + 64 (lanes l and l ^ 16)
-    float p[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) p[j] = __shfl_xor_sync(0xffffffffu, e[j], 16);
-    const bool first = lane < 16;
-    const float* cr = cos_t + (size_t)pos * (D / 2);
-    const float* sr = sin_t + (size_t)pos * (D / 2);
-    float o[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int i = (4 * lane + j) & (D / 2 - 1);
-        const float c = cr[i], s = sr[i];
-        // first half: x1*c + (-x2)*s ; second half: x2*c + x1*s
-        o[j] = first ? e[j] * c + (-p[j]) * s : e[j] * c + p[j] * s;
-    }
-    const float4 r4 = make_float4(o[0], o[1], o[2], o[3]);
+    const float4 r4 = head_norm_rope(e, h < hq ? qn : kn, cos_t + (size_t)pos * (D / 2),
+                                     sin_t + (size_t)pos * (D / 2), lane);
     if (h < hq) {
         *reinterpret_cast<float4*>(q_out + ((size_t)m * hq + h) * D + 4 * lane) = r4;
     } else {
@@ -243,10 +250,17 @@ __device__ __forceinline__ uint32_t ordered_f32(float f) {
 // Activations (x, and y in RESID mode) come from the previous kernel, which may
 // still be draining when this one starts (programmatic launch): they are read
 // through L2 (ld.global.cg) after pdl_wait, never through the read-only path.
+//
+// QW_EPI_QKV (the decode step's fused QKV projection): rows are the
+// [q heads; k heads; v heads] x 128 outputs, R rows per CTA, so 128 / R CTAs
+// make one head.  V outputs go straight to the V cache row.  Q and K outputs
+// go to y; the last CTA of a head to arrive (per-head counter) reads the
+// head back, applies QK-norm and RoPE (as qknorm_rope_append_kernel) and
+// writes the query (e.q_out) or the K cache row, then re-arms the counter.
 template <int MODE, bool NORM, int R, bool ARGMAX>
 __global__ void gemv2_kernel(const __nv_bfloat16* __restrict__ W, int N_out, int K,
                              const float* x, const float* __restrict__ nw, float eps,
-                             float* y, unsigned long long* amax) {
+                             float* y, unsigned long long* amax, const QkvEpi e) {
     constexpr int NV = R + 1;                      // R dot products + sum of squares
     __shared__ float red[32][NV];
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5, nwarp = blockDim.x >> 5;
@@ -264,12 +278,18 @@ __global__ void gemv2_kernel(const __nv_bfloat16* __restrict__ W, int N_out, int
             rows[r] = min(o0 + r, N_out - 1);
         }
     }
+    static_assert(MODE != QW_EPI_QKV || (128 % R == 0 && !ARGMAX), "QKV epilogue: whole heads of R rows");
     pdl_trigger();
     uint4 w[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) w[r] = __ldg(reinterpret_cast<const uint4*>(W + (size_t)rows[r] * K) + t);
     // weights do not depend on the previous kernel; the activations do
     pdl_wait();
+    int q_pos = 0, q_row = 0;      // QKV epilogue: RoPE position and cache row
+    if (MODE == QW_EPI_QKV) {
+        q_pos = e.pos_dev ? __ldcg(e.pos_dev) : e.pos0;
+        q_row = q_pos + e.row_shift;
+    }
     const float4 xa = __ldcg(reinterpret_cast<const float4*>(x) + 2 * t);
     const float4 xb = __ldcg(reinterpret_cast<const float4*>(x) + 2 * t + 1);
     float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
@@ -325,7 +345,16 @@ __global__ void gemv2_kernel(const __nv_bfloat16* __restrict__ W, int N_out, int
                     }
                 }
             }
-            if (n < N_out) {
+            if (MODE == QW_EPI_QKV) {
+                if (n < N_out) {
+                    const int h = n / 128, vh = h - e.hq - e.hkv;
+                    if (vh >= 0) {
+                        if (q_row < e.max_seq) e.vc[((size_t)vh * e.max_seq + q_row) * 128 + n % 128] = out;
+                    } else {
+                        y[n] = out;
+                    }
+                }
+            } else if (n < N_out) {
                 if (MODE == QW_EPI_RESID) y[n] = __ldcg(y + n) + out;
                 else y[n] = out;
                 if (ARGMAX)
@@ -339,6 +368,29 @@ __global__ void gemv2_kernel(const __nv_bfloat16* __restrict__ W, int N_out, int
                 best = o > best ? o : best;
             }
             if (lane == 0) atomicMax(amax, best);
+        }
+        if (MODE == QW_EPI_QKV) {
+            const int h = o0 / 128;
+            if (h < e.hq + e.hkv) {
+                // publish this CTA's outputs, then count it in
+                __threadfence();
+                __syncwarp();
+                unsigned last = 0;
+                if (lane == 0) last = atomicAdd(e.cnt + h, 1u) == (unsigned)(128 / R - 1);
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (last && q_row < e.max_seq) {
+                    __threadfence();
+                    const float4 v4 = __ldcg(reinterpret_cast<const float4*>(y + (size_t)h * 128) + lane);
+                    const float ev[4] = {v4.x, v4.y, v4.z, v4.w};
+                    const float* cr = e.cos_t + (size_t)q_pos * 64;
+                    const float* sr = e.sin_t + (size_t)q_pos * 64;
+                    const float4 r4 = head_norm_rope(ev, h < e.hq ? e.qn : e.kn, cr, sr, lane);
+                    float* dst = h < e.hq ? e.q_out + (size_t)h * 128
+                                          : e.kc + ((size_t)(h - e.hq) * e.max_seq + q_row) * 128;
+                    reinterpret_cast<float4*>(dst)[lane] = r4;
+                }
+                if (last && lane == 0) e.cnt[h] = 0u;
+            }
         }
     }
 }
@@ -469,7 +521,7 @@ int launch_gemv(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, in
     return SA_OK;
 }
 int launch_gemv2(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, int N_out, int K, const float* x,
-                 const float* nw, float eps, float* y, unsigned long long* amax) {
+                 const float* nw, float eps, float* y, unsigned long long* amax, const QkvEpi* qkv) {
     SA_CHECK_ARG(K % 256 == 0 && K / 8 <= 1024, "gemv2: K=%d (multiple of 256, <= 8192)", K);
     const int threads = K / 8;
     // rows per CTA: enough CTAs to cover the SMs several times over
@@ -477,10 +529,15 @@ int launch_gemv2(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, i
     const int R = rows >= 8 * 1024 ? 8 : (rows >= 4 * 512 ? 4 : 2);
     const int outs = mode == QW_EPI_SWIGLU ? R / 2 : R;
     const int grid = (N_out + outs - 1) / outs;
+    const QkvEpi e = qkv ? *qkv : QkvEpi{};
 #define SA_G2(M, N, RR, A) SA_CUDA_TRY(launch_pdl_k(0, qk::gemv2_kernel<M, N, RR, A>, dim3(grid), dim3(threads), 0, st, \
-                                                  W, N_out, K, x, nw, eps, y, amax))
+                                                  W, N_out, K, x, nw, eps, y, amax, e))
 #define SA_G2R(M, N, A) do { if (R == 8) SA_G2(M, N, 8, A); else if (R == 4) SA_G2(M, N, 4, A); else SA_G2(M, N, 2, A); } while (0)
-    if (amax) {
+    if (mode == QW_EPI_QKV) {
+        SA_CHECK_ARG(qkv && norm && !amax && qkv->cnt && N_out == 128 * (qkv->hq + 2 * qkv->hkv),
+                     "gemv2: QKV epilogue needs its operands, the input norm and N_out = 128 (hq + 2 hkv)");
+        SA_G2R(QW_EPI_QKV, true, false);
+    } else if (amax) {
         SA_CHECK_ARG(mode == QW_EPI_STORE && norm, "gemv2: argmax only with the normed STORE head");
         SA_G2R(QW_EPI_STORE, true, true);
     } else if (mode == QW_EPI_STORE) {
