@@ -705,8 +705,11 @@ Q3_WORKLOAD = ("configs[3]/[4] Qwen3-0.6B random-init (bf16-exact N(0,0.02) weig
                "decode of 100 greedy tokens after a 128-token prompt with the KV cache")
 
 
-def measure_qwen3(ctx, dev, stream, steps, warmup, weights=None, long_prompt=False):
-    """Returns dict with prefill / decode tok/s (device-resident and e2e)."""
+def measure_qwen3(ctx, dev, stream, steps, warmup, weights=None, long_prompt=False, rank=0, world=1):
+    """Returns dict with prefill / decode tok/s (device-resident and e2e).
+    With world > 1 every rank runs its head-parallel share (sa_qwen3_create_tp)
+    of the same calls; each timed region starts after a barrier and its time
+    is the maximum over the ranks."""
     import ctypes as C
     import torch
     import streaming_attention_b200 as sa
@@ -715,8 +718,24 @@ def measure_qwen3(ctx, dev, stream, steps, warmup, weights=None, long_prompt=Fal
     if weights is None:
         weights = sa.qwen3.random_weights(cfg, SEED)
     max_seq = 4096 + Q3_GEN + 8 if long_prompt else 512
-    m = sa.Qwen3(cfg, max_seq=max_seq, ctx=ctx)
+    m = sa.Qwen3(cfg, max_seq=max_seq, ctx=ctx, rank=rank, world=world)
     m.load(weights)
+
+    def sync():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def tmax(v):
+        if world == 1:
+            return v
+        import torch.distributed as dist
+        t = torch.tensor([v], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    if world > 1:
+        m.connect()
     L = _capi.lib()
     rng = __import__("numpy").random.default_rng(SEED)
     ids = rng.integers(0, cfg["vocab"], Q3_PROMPT).astype("int64")
@@ -732,13 +751,15 @@ def measure_qwen3(ctx, dev, stream, steps, warmup, weights=None, long_prompt=Fal
                                            C.cast(P(logits_d), C.POINTER(C.c_float)), 0, 0))
         for _ in range(warmup):
             pf()
+        stream.synchronize()
+        sync()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(steps):
             pf()
         e1.record(stream)
         e1.synchronize()
-        pms = e0.elapsed_time(e1) / steps
+        pms = tmax(e0.elapsed_time(e1) / steps)
         out["prefill_tok_s"] = Q3_PROMPT / (pms / 1e3)
         out["prefill_ms"] = pms
         # ---- prefill e2e: pinned host ids in, pinned host logits [128, V] out,
@@ -750,17 +771,19 @@ def measure_qwen3(ctx, dev, stream, steps, warmup, weights=None, long_prompt=Fal
                                            C.cast(P(logits_h), C.POINTER(C.c_float)), 0,
                                            _capi.SA_HOST_PTRS))
         pf_host()
+        sync()
         t0 = time.perf_counter()
         ne = max(2, min(steps, 5))
         for _ in range(ne):
             pf_host()
-        out["prefill_e2e_tok_s"] = Q3_PROMPT * ne / (time.perf_counter() - t0)
+        out["prefill_e2e_tok_s"] = Q3_PROMPT * ne / tmax(time.perf_counter() - t0)
         # ---- decode: generate(101) - generate(1) = 100 decode steps (same prefill)
         def gen(n, prompt):
             m.reset()
+            sync()
             t0 = time.perf_counter()
             toks = m.generate(prompt, n)
-            return time.perf_counter() - t0, toks
+            return tmax(time.perf_counter() - t0), toks
         for p_len, key in ([(Q3_PROMPT, "decode")] + ([(4096, "decode_4096")] if long_prompt else [])):
             prompt = rng.integers(0, cfg["vocab"], p_len).astype("int64")
             gen(Q3_GEN + 1, prompt)                       # warm-up
@@ -832,8 +855,14 @@ def run_qwen3_reference(args):
 def run_qwen3(args):
     import torch
     import streaming_attention_b200 as sa
-    local = env_int("LOCAL_RANK", 0)
-    if env_int("RANK", 0) != 0:
+    local, rank, world = env_int("LOCAL_RANK", 0), env_int("RANK", 0), env_int("WORLD_SIZE", 1)
+    if world > 1:
+        # head-parallel over the ranks; gloo carries only the exchange-buffer
+        # handles, barriers and the max over ranks of each timing
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("gloo", timeout=timedelta(seconds=600))
+    elif rank != 0:
         return 0
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -855,26 +884,39 @@ def run_qwen3(args):
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     clocks = ClockSampler(vis.split(",")[local].strip() if vis else str(local))
     clocks.start()
-    res, weights = measure_qwen3(ctx, dev, stream, args.steps, args.warmup, long_prompt=args.long_prompt)
+    res, weights = measure_qwen3(ctx, dev, stream, args.steps, args.warmup, long_prompt=args.long_prompt,
+                                 rank=rank, world=world)
     clk = clocks.stop()
+    if rank != 0:
+        ctx.close()
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+        return 0
     line = {
         "metric": "Qwen3-0.6B tok/s (prefill)", "value": round(res["prefill_tok_s"], 1), "unit": "tok/s",
-        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(res["prefill_ms"], 4), "higher_is_better": True, "scaling": "weak",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(res["prefill_ms"], 4), "higher_is_better": True,
+        "scaling": "weak" if world == 1 else "strong",
         "vs_baseline": None, "dtype": "bf16 weights, fp32 activations", "data": "synthetic",
-        "config": {"workload": Q3_WORKLOAD},
+        "config": {"workload": Q3_WORKLOAD,
+                   "parallelism": "single" if world == 1 else f"head-parallel over {world} GPUs"},
         "decode": {k: round(v, 3) for k, v in res.items() if k.startswith("decode")},
         "e2e": {"value": round(res["prefill_e2e_tok_s"], 1), "unit": "tok/s",
                 "h2d_bytes_per_step": Q3_PROMPT * 8, "d2h_bytes_per_step": Q3_PROMPT * 151936 * 4},
         "clocks": clk,
     }
-    if not args.no_cpu:
+    if not args.no_cpu and world == 1:
         try:
             line["cpu_baseline"] = cpu_qwen3_baseline(weights)
         except Exception as e:
             line["cpu_baseline"] = {"value": None, "sample": f"unavailable: {e}"}
     print(json.dumps(line), flush=True)
     ctx.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
     return 0
 
 

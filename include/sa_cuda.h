@@ -314,6 +314,44 @@ int sa_qwen3_forward(sa_qwen3* m, const int64_t* ids, int S, int use_cache, floa
 int sa_qwen3_generate(sa_qwen3* m, const int64_t* prompt, int S, int n_new, int64_t* out_tokens,
                       unsigned flags);
 
+/*
+ * Head-parallel Qwen3 over `world` GPUs (1..8), one model per GPU, usually
+ * one process per GPU.  Replaces the reference's head-wise MPI model path
+ * (qwen3_ops_mpi.cpp, ParallelStrategy HEADWISE, qwen3_ops_mpi.h:30-50) for
+ * qwen3_forward / qwen3_forward_with_cache / greedy decode.
+ *
+ * Rank r keeps q heads [r*hq/world, (r+1)*hq/world), the KV heads, o_proj
+ * columns and KV cache of those heads, gate/up rows and down_proj columns of
+ * intermediate features [r*inter/world, ...), and the whole embedding and
+ * lm_head.  Each layer's o_proj and down_proj give partial sums that every
+ * rank sends to every rank's exchange buffer over NVLink (peer stores from
+ * the projection kernels); the next normed projection adds them, in rank
+ * order, so the residual stream is the same on every rank.  Greedy decode
+ * splits the lm_head over the vocabulary and exchanges the ranks' argmax.
+ *
+ * sa_qwen3_create_tp: as sa_qwen3_create for rank `rank` of `world`
+ *   (hkv divisible by world, inter by 64 * world).  Weights are set with
+ *   the same full tensors on every rank (sa_qwen3_set_embed / _set_layer, or
+ *   sa_qwen3_load_safetensors_tp); each rank keeps its share.
+ * sa_qwen3_tp_handle: SA_TP_HANDLE_BYTES bytes naming this rank's exchange
+ *   buffer (a CUDA IPC handle), to be passed to every rank.
+ * sa_qwen3_tp_connect: the world handles in rank order (world *
+ *   SA_TP_HANDLE_BYTES bytes); maps the other ranks' buffers.  Required
+ *   before forward / generate.
+ * Every rank then calls sa_qwen3_forward / sa_qwen3_generate with the same
+ * arguments in the same order; logits and tokens come back on every rank.
+ * Head-parallel forwards take at most min(max_seq, 8192) tokens per call.
+ * A rank that stops taking part makes the others' waits give up after a few
+ * seconds (SA_ERR_TIMEOUT at the next synchronising call).
+ * sa_qwen3_read_kv / _write_kv address this rank's KV heads only.
+ */
+#define SA_TP_HANDLE_BYTES 64
+int sa_qwen3_create_tp(sa_ctx* ctx, const sa_qwen3_config* cfg, int rank, int world, sa_qwen3** out);
+int sa_qwen3_load_safetensors_tp(sa_ctx* ctx, const char* path, int max_seq, float eps, float theta, int rank,
+                                 int world, sa_qwen3** out);
+int sa_qwen3_tp_handle(sa_qwen3* m, void* handle);
+int sa_qwen3_tp_connect(sa_qwen3* m, const void* handles);
+
 #ifdef __cplusplus
 }
 #endif

@@ -50,6 +50,11 @@ SIGNATURES = {
     "sa_qwen3_create": (C.c_int, [_vp, _vp, C.POINTER(_vp)]),
     "sa_safetensors_inspect": (C.c_int, [C.c_char_p, _vp]),
     "sa_qwen3_load_safetensors": (C.c_int, [_vp, C.c_char_p, C.c_int, C.c_float, C.c_float, C.POINTER(_vp)]),
+    "sa_qwen3_create_tp": (C.c_int, [_vp, _vp, C.c_int, C.c_int, C.POINTER(_vp)]),
+    "sa_qwen3_load_safetensors_tp": (C.c_int, [_vp, C.c_char_p, C.c_int, C.c_float, C.c_float, C.c_int, C.c_int,
+                                               C.POINTER(_vp)]),
+    "sa_qwen3_tp_handle": (C.c_int, [_vp, _vp]),
+    "sa_qwen3_tp_connect": (C.c_int, [_vp, _vp]),
     "sa_qwen3_destroy": (C.c_int, [_vp]),
     "sa_qwen3_set_embed": (C.c_int, [_vp, _fp, _fp, _fp]),
     "sa_qwen3_set_layer": (C.c_int, [_vp, C.c_int] + [_fp] * 11),

@@ -27,7 +27,13 @@ struct sa_qwen3 {
     sa_ctx* ctx = nullptr;
     int device = 0;                      // the context's GPU (the model may outlive the context object)
     sa_qwen3_config c{};
-    int QD = 0, KD = 0, NQKV = 0;
+    // head-parallel rank (sa_qwen3_create_tp; world 1 = the whole model):
+    // this rank's q heads, KV heads and intermediate features, and the
+    // vocabulary rows [v0, v0 + vn) of its share of the decode lm_head
+    int tp_rank = 0, tp_world = 1;
+    int hq = 0, hkv = 0, inter = 0;
+    int v0 = 0, vn = 0;
+    int QD = 0, KD = 0, NQKV = 0;        // local: hq * D, hkv * D, QD + 2 KD
     // weights (device)
     __nv_bfloat16* embed = nullptr;      // [V, H]
     __nv_bfloat16* lm_head = nullptr;    // [V, H] (== embed when tied)
@@ -90,6 +96,19 @@ struct sa_qwen3 {
     cudaGraphExec_t dec_graph = nullptr;
     std::map<std::pair<int, int>, cudaGraphExec_t> pf_graphs;
     std::set<std::pair<int, int>> pf_seen;
+    // head-parallel exchange: this rank's buffer (flags [2][world], then
+    // blocks [2][world][tp_rows * hidden]) and the peers' (CUDA IPC mappings)
+    void* tp_buf = nullptr;
+    size_t tp_flag_bytes = 0;            // flags + word areas, the offset of the receive blocks
+    int tp_rows = 0;
+    void* tp_peer[sa::TP_MAX] = {};
+    bool tp_connected = false;
+    unsigned* tp_seq = nullptr;          // [1] exchange instances completed
+    unsigned* tp_cnt = nullptr;          // [1] producer arrival counter
+    float* tp_part = nullptr;            // [cap_m, hidden] prompt-path partial sums
+    float* tp_x2 = nullptr;              // [hidden] decode-path residual, other half of the ping-pong
+    float* x_last = nullptr;             // residual after the last run_layers (m->x or tp_x2)
+    bool x_last_ll = false;              // its pending exchange came as words (single-token path)
 };
 
 namespace sa {
@@ -134,6 +153,9 @@ static void free_model(sa_qwen3* m) {
     cudaFree(m->logits); cudaFree(m->ids); cudaFree(m->gemm_ws); cudaFree(m->gemm_cnt);
     cudaFree(m->d_state); cudaFree(m->d_toks); cudaFree(m->dec_scratch); cudaFree(m->dec_cnt); cudaFree(m->d_amax);
     cudaFree(m->d_mlayers); cudaFree(m->mpart); cudaFree(m->mhead_cnt); cudaFree(m->mgbar);
+    for (int r = 0; r < sa::TP_MAX; ++r)
+        if (m->tp_peer[r] && r != m->tp_rank) cudaIpcCloseMemHandle(m->tp_peer[r]);
+    cudaFree(m->tp_buf); cudaFree(m->tp_seq); cudaFree(m->tp_cnt); cudaFree(m->tp_part); cudaFree(m->tp_x2);
     if (m->dec_graph) cudaGraphExecDestroy(m->dec_graph);
     for (auto& kv : m->pf_graphs) cudaGraphExecDestroy(kv.second);
     if (m->ev_in) cudaEventDestroy(m->ev_in);
@@ -158,14 +180,17 @@ static int ensure_acts(sa_qwen3* m, int M) {
     invalidate_graphs(m);
     cudaFree(m->x); cudaFree(m->qkv); cudaFree(m->q); cudaFree(m->attn); cudaFree(m->act); cudaFree(m->xn);
     cudaFree(m->a_hi); cudaFree(m->a_lo); cudaFree(m->b_hi); cudaFree(m->b_lo); cudaFree(m->ids);
+    cudaFree(m->tp_part);
+    m->tp_part = nullptr;
     const sa_qwen3_config& c = m->c;
-    const size_t wmax = (size_t)std::max(std::max(m->QD, c.inter), c.hidden);
+    const size_t wmax = (size_t)std::max(std::max(m->QD, m->inter), c.hidden);
     int rc = SA_OK;
     if (!rc) rc = dalloc(&m->x, (size_t)M * c.hidden);
     if (!rc) rc = dalloc(&m->qkv, (size_t)M * m->NQKV);
     if (!rc) rc = dalloc(&m->q, (size_t)M * m->QD);
     if (!rc) rc = dalloc(&m->attn, (size_t)M * m->QD);
-    if (!rc) rc = dalloc(&m->act, (size_t)M * c.inter);
+    if (!rc) rc = dalloc(&m->act, (size_t)M * m->inter);
+    if (!rc && m->tp_world > 1) rc = dalloc(&m->tp_part, (size_t)M * c.hidden);
     if (!rc) rc = dalloc(&m->xn, (size_t)M * c.hidden);
     if (!rc) rc = dalloc(&m->a_hi, (size_t)M * wmax);
     if (!rc) rc = dalloc(&m->a_lo, (size_t)M * wmax);
@@ -239,13 +264,43 @@ static int gemm(sa_qwen3* m, const __nv_bfloat16* hi, const __nv_bfloat16* lo, l
 // cache-free forward (positions from 0) uses the rows after the live prefix
 // as scratch, kv_row0 = cache length, so the cache is left as it was.
 // M == 1 uses the GEMV path; pos_dev makes the position a device value.
+// Exchange operands of instance k of the current segment (head-parallel).
+static TpArgs tp_args(sa_qwen3* m, int k) {
+    TpArgs t;
+    t.rank = m->tp_rank;
+    t.world = m->tp_world;
+    for (int r = 0; r < m->tp_world; ++r) {
+        char* base = static_cast<char*>(m->tp_peer[r]);
+        t.flags[r] = reinterpret_cast<unsigned*>(base);
+        t.ll[r] = reinterpret_cast<unsigned long long*>(base + 256);
+        t.recv[r] = reinterpret_cast<float*>(base + m->tp_flag_bytes);
+    }
+    t.ll_stride = m->c.hidden;
+    t.slot_floats = (long long)m->tp_rows * m->c.hidden;
+    t.seq = m->tp_seq;
+    t.k = k;
+    t.cnt = m->tp_cnt;
+    t.status = m->ctx->status;
+    return t;
+}
+
+// Head-parallel ranks run the same schedule on their share of the heads and
+// intermediate features; each layer exchanges two partial sums of the
+// residual update (o_proj, down_proj: instances 2l and 2l + 1 of the
+// segment), which the next normed projection adds in before its norm.  In
+// the single-token path the residual alternates between m->x and m->tp_x2
+// (the consuming GEMV reads one and writes the other); m->x_last records
+// where it ends.  The prompt path updates m->x in place.
 static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr, int kv_row0 = -1) {
     if (kv_row0 < 0) kv_row0 = pos0;
     const sa_qwen3_config& c = m->c;
     cudaStream_t st = m->cur;
-    const int H = c.hidden, I = c.inter, D = c.head_dim;
+    const int H = c.hidden, I = m->inter, D = c.head_dim;
     const float scale = 1.0f / sqrtf((float)D);
-    const size_t layer_kv = (size_t)c.hkv * c.max_seq * D;
+    const size_t layer_kv = (size_t)m->hkv * c.max_seq * D;
+    const bool tp = m->tp_world > 1;
+    float* xc = m->x;          // single-token path: the residual the next consumer reads
+    float* xo = m->tp_x2;
     SA_RC(launch_embedding(st, m->ids, M, m->embed, c.vocab, H, m->x, m->ctx->status));
     for (int l = 0; l < c.n_layers; ++l) {
         const sa_qwen3::Layer& L = m->layers[l];
@@ -256,42 +311,111 @@ static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr
         const float* va = vc + (size_t)shift * D;
         if (M == 1) {
             QkvEpi e;
-            e.hq = c.hq; e.hkv = c.hkv; e.max_seq = c.max_seq; e.pos0 = pos0; e.row_shift = shift;
+            e.hq = m->hq; e.hkv = m->hkv; e.max_seq = c.max_seq; e.pos0 = pos0; e.row_shift = shift;
             e.pos_dev = pos_dev;
             e.qn = L.q_norm; e.kn = L.k_norm; e.cos_t = m->cos_t; e.sin_t = m->sin_t;
             e.q_out = m->q; e.kc = kc; e.vc = vc;
-            e.cnt = m->dec_cnt + c.hkv;
-            SA_RC(launch_gemv2(st, QW_EPI_QKV, true, L.wqkv, m->NQKV, H, m->x, L.in_norm, c.eps, m->qkv, nullptr, &e));
+            e.cnt = m->dec_cnt + m->hkv;
+            if (tp && l > 0) {
+                TpArgs t = tp_args(m, 2 * l - 1);
+                t.x_out = xo;
+                t.use_ll = 1;
+                SA_RC(launch_gemv2_tp(st, QW_EPI_QKV, true, L.wqkv, m->NQKV, H, xc, L.in_norm, c.eps, m->qkv,
+                                      nullptr, &e, t, true));
+                std::swap(xc, xo);
+            } else {
+                SA_RC(launch_gemv2(st, QW_EPI_QKV, true, L.wqkv, m->NQKV, H, xc, L.in_norm, c.eps, m->qkv, nullptr,
+                                   &e));
+            }
             SA_RC(decode_dev_launch(st, m->ctx->status, m->ctx->num_sms, m->q, ka, va, (long long)c.max_seq * D,
-                                    pos_dev, pos0 + 1, c.max_seq - shift, D, c.hq, c.hkv, scale, m->attn,
+                                    pos_dev, pos0 + 1, c.max_seq - shift, D, m->hq, m->hkv, scale, m->attn,
                                     m->dec_scratch, m->dec_cnt));
-            SA_RC(launch_gemv2(st, QW_EPI_RESID, false, L.wo, H, m->QD, m->attn, nullptr, 0.f, m->x, nullptr));
-            SA_RC(launch_gemv2(st, QW_EPI_SWIGLU, true, L.wgu, I, H, m->x, L.post_norm, c.eps, m->act, nullptr));
-            SA_RC(launch_gemv2(st, QW_EPI_RESID, false, L.wd, H, I, m->act, nullptr, 0.f, m->x, nullptr));
+            if (tp) {
+                SA_RC(launch_gemv2_tp(st, QW_EPI_XCHG, false, L.wo, H, m->QD, m->attn, nullptr, 0.f, nullptr, nullptr,
+                                      nullptr, tp_args(m, 2 * l), false));
+                TpArgs t = tp_args(m, 2 * l);
+                t.x_out = xo;
+                t.use_ll = 1;
+                SA_RC(launch_gemv2_tp(st, QW_EPI_SWIGLU, true, L.wgu, I, H, xc, L.post_norm, c.eps, m->act, nullptr,
+                                      nullptr, t, true));
+                std::swap(xc, xo);
+                SA_RC(launch_gemv2_tp(st, QW_EPI_XCHG, false, L.wd, H, I, m->act, nullptr, 0.f, nullptr, nullptr,
+                                      nullptr, tp_args(m, 2 * l + 1), false));
+            } else {
+                SA_RC(launch_gemv2(st, QW_EPI_RESID, false, L.wo, H, m->QD, m->attn, nullptr, 0.f, m->x, nullptr));
+                SA_RC(launch_gemv2(st, QW_EPI_SWIGLU, true, L.wgu, I, H, m->x, L.post_norm, c.eps, m->act, nullptr));
+                SA_RC(launch_gemv2(st, QW_EPI_RESID, false, L.wd, H, I, m->act, nullptr, 0.f, m->x, nullptr));
+            }
         } else {
-            SA_RC(launch_rmsnorm_hilo(st, m->x, L.in_norm, M, H, c.eps, m->a_hi, m->a_lo));
+            if (tp && l > 0)
+                SA_RC(launch_rmsnorm_hilo_tp(st, m->x, L.in_norm, M, H, c.eps, m->a_hi, m->a_lo, tp_args(m, 2 * l - 1)));
+            else
+                SA_RC(launch_rmsnorm_hilo(st, m->x, L.in_norm, M, H, c.eps, m->a_hi, m->a_lo));
             SA_RC(gemm(m, m->a_hi, m->a_lo, H, L.wqkv, M, m->NQKV, H, QW_EPI_STORE, m->qkv, m->NQKV, nullptr, nullptr, 0));
-            SA_RC(launch_qknorm_rope_append(st, m->qkv, M, c.hq, c.hkv, L.q_norm, L.k_norm, m->cos_t, m->sin_t, pos0,
+            SA_RC(launch_qknorm_rope_append(st, m->qkv, M, m->hq, m->hkv, L.q_norm, L.k_norm, m->cos_t, m->sin_t, pos0,
                                             nullptr, shift, m->q, kc, vc, c.max_seq));
             SA_RC(decode_multi_launch(st, m->ctx->status, m->q, m->QD, ka, va, (long long)c.max_seq * D, pos0 + 1, M, D,
-                                      c.hq, c.hkv, scale, m->attn, m->QD));
+                                      m->hq, m->hkv, scale, m->attn, m->QD));
             SA_RC(launch_split_hilo(st, m->attn, (size_t)M * m->QD, m->a_hi, m->a_lo));
-            SA_RC(gemm(m, m->a_hi, m->a_lo, m->QD, L.wo, M, H, m->QD, QW_EPI_RESID, m->x, H, nullptr, nullptr, 0));
-            SA_RC(launch_rmsnorm_hilo(st, m->x, L.post_norm, M, H, c.eps, m->a_hi, m->a_lo));
+            if (tp) {
+                SA_RC(gemm(m, m->a_hi, m->a_lo, m->QD, L.wo, M, H, m->QD, QW_EPI_STORE, m->tp_part, H, nullptr, nullptr,
+                           0));
+                SA_RC(launch_tp_scatter(st, m->tp_part, M, H, tp_args(m, 2 * l), m->ctx->num_sms));
+                SA_RC(launch_rmsnorm_hilo_tp(st, m->x, L.post_norm, M, H, c.eps, m->a_hi, m->a_lo, tp_args(m, 2 * l)));
+            } else {
+                SA_RC(gemm(m, m->a_hi, m->a_lo, m->QD, L.wo, M, H, m->QD, QW_EPI_RESID, m->x, H, nullptr, nullptr, 0));
+                SA_RC(launch_rmsnorm_hilo(st, m->x, L.post_norm, M, H, c.eps, m->a_hi, m->a_lo));
+            }
             SA_RC(gemm(m, m->a_hi, m->a_lo, H, L.wgu, M, 2 * I, H, QW_EPI_SWIGLU, nullptr, 0, m->b_hi, m->b_lo, I));
-            SA_RC(gemm(m, m->b_hi, m->b_lo, I, L.wd, M, H, I, QW_EPI_RESID, m->x, H, nullptr, nullptr, 0));
+            if (tp) {
+                SA_RC(gemm(m, m->b_hi, m->b_lo, I, L.wd, M, H, I, QW_EPI_STORE, m->tp_part, H, nullptr, nullptr, 0));
+                SA_RC(launch_tp_scatter(st, m->tp_part, M, H, tp_args(m, 2 * l + 1), m->ctx->num_sms));
+            } else {
+                SA_RC(gemm(m, m->b_hi, m->b_lo, I, L.wd, M, H, I, QW_EPI_RESID, m->x, H, nullptr, nullptr, 0));
+            }
         }
     }
+    m->x_last = M == 1 ? xc : m->x;
+    m->x_last_ll = M == 1;
     return SA_OK;
 }
 
 // Final norm + lm_head for rows [r0, r0 + n) of the residual stream.  With
 // `token` (n == 1 only) the argmax of the logits is also written there
-// (first index of the maximum, as ops::argmax).
+// (first index of the maximum, as ops::argmax).  Head-parallel ranks first
+// add the last layer's exchanged down_proj sums (instance 2L - 1); with
+// `token` each rank takes the argmax over its vocabulary slice and the
+// ranks' maxima are exchanged (instance 2L), which also closes the segment.
 static int run_head(sa_qwen3* m, int r0, int n, int64_t* token = nullptr) {
     const sa_qwen3_config& c = m->c;
     cudaStream_t st = m->cur;
+    const size_t H = c.hidden;
     SA_RC(ensure_logits(m, n));
+    if (m->tp_world > 1) {
+        const int L2 = 2 * c.n_layers;
+        TpArgs t = tp_args(m, L2 - 1);
+        t.row = r0;
+        t.use_ll = m->x_last_ll ? 1 : 0;
+        if (n == 1) {
+            const float* xin = m->x_last + (m->x_last == m->x ? (size_t)r0 * H : 0);
+            t.x_out = m->x_last == m->tp_x2 ? m->x : m->tp_x2;
+            if (token) {
+                t.n_base = m->v0;
+                SA_RC(launch_gemv2_tp(st, QW_EPI_STORE, true, m->lm_head + (size_t)m->v0 * H, m->vn, (int)H, xin,
+                                      m->final_norm, c.eps, m->logits, m->d_amax, nullptr, t, true));
+                SA_RC(launch_tp_amax_token(st, m->d_amax, token, tp_args(m, L2), L2 + 1));
+            } else {
+                SA_RC(launch_gemv2_tp(st, QW_EPI_STORE, true, m->lm_head, c.vocab, (int)H, xin, m->final_norm, c.eps,
+                                      m->logits, nullptr, nullptr, t, true));
+            }
+        } else {
+            SA_RC(launch_rmsnorm_hilo_tp(st, m->x + (size_t)r0 * H, m->final_norm, n, (int)H, c.eps, m->a_hi, m->a_lo,
+                                         t));
+            SA_RC(gemm(m, m->a_hi, m->a_lo, c.hidden, m->lm_head, n, c.vocab, c.hidden, QW_EPI_STORE, m->logits,
+                       c.vocab, nullptr, nullptr, 0));
+        }
+        return SA_OK;
+    }
     if (n == 1) {
         SA_RC(launch_gemv2(st, QW_EPI_STORE, true, m->lm_head, c.vocab, c.hidden, m->x + (size_t)r0 * c.hidden,
                            m->final_norm, c.eps, m->logits, token ? m->d_amax : nullptr));
@@ -304,32 +428,53 @@ static int run_head(sa_qwen3* m, int r0, int n, int64_t* token = nullptr) {
     return SA_OK;
 }
 
+// Close a head-parallel segment that did not end with the token exchange
+// (which closes its own): the sequence word advances by the 2L instances.
+static int tp_close_segment(sa_qwen3* m) {
+    if (m->tp_world > 1) SA_RC(launch_tp_seq_add(m->cur, m->tp_seq, 2 * m->c.n_layers));
+    return SA_OK;
+}
+
 }  // namespace sa
 
 using namespace sa;
 
-SA_API int sa_qwen3_create(sa_ctx* ctx, const sa_qwen3_config* cfg, sa_qwen3** out) {
-    clear_error();
+namespace sa {
+
+// Allocate rank `rank` of a `world`-way head-parallel model (world 1: the
+// whole model).
+int qwen3_create_model(sa_ctx* ctx, const sa_qwen3_config* cfg, int rank, int world, sa_qwen3** out) {
     SA_CHECK_ARG(ctx && cfg && out, "sa_qwen3_create: null argument");
     *out = nullptr;
     const sa_qwen3_config& c = *cfg;
     SA_CHECK_ARG(c.head_dim == 128, "sa_qwen3_create: head_dim %d (128 supported)", c.head_dim);
-    SA_CHECK_ARG(c.hidden > 0 && c.hidden % 64 == 0 && c.inter % 64 == 0 && c.vocab > 0 && c.n_layers > 0,
+    SA_CHECK_ARG(c.hidden > 0 && c.hidden % 256 == 0 && c.inter % 64 == 0 && c.vocab > 0 && c.n_layers > 0,
                  "sa_qwen3_create: hidden=%d inter=%d vocab=%d layers=%d", c.hidden, c.inter, c.vocab, c.n_layers);
     SA_CHECK_ARG(c.hkv > 0 && c.hq % c.hkv == 0 && (c.hq / c.hkv == 1 || c.hq / c.hkv == 2 || c.hq / c.hkv == 4),
                  "sa_qwen3_create: hq=%d hkv=%d", c.hq, c.hkv);
     SA_CHECK_ARG(c.max_seq > 0, "sa_qwen3_create: max_seq=%d", c.max_seq);
+    SA_CHECK_ARG(world >= 1 && world <= TP_MAX && rank >= 0 && rank < world,
+                 "sa_qwen3_create_tp: rank %d of world %d (1..%d)", rank, world, TP_MAX);
+    SA_CHECK_ARG(c.hkv % world == 0 && c.inter % (64 * world) == 0 && c.vocab >= world,
+                 "sa_qwen3_create_tp: hkv=%d and inter/64=%d must divide over %d ranks", c.hkv, c.inter / 64, world);
     DeviceGuard guard(ctx->device);
     sa_qwen3* m = new sa_qwen3();
     m->ctx = ctx;
     m->device = ctx->device;
     m->c = c;
-    m->QD = c.hq * c.head_dim;
-    m->KD = c.hkv * c.head_dim;
+    m->tp_rank = rank;
+    m->tp_world = world;
+    m->hq = c.hq / world;
+    m->hkv = c.hkv / world;
+    m->inter = c.inter / world;
+    m->v0 = (int)((long long)c.vocab * rank / world);
+    m->vn = (int)((long long)c.vocab * (rank + 1) / world) - m->v0;
+    m->QD = m->hq * c.head_dim;
+    m->KD = m->hkv * c.head_dim;
     m->NQKV = m->QD + 2 * m->KD;
     m->layers.resize(c.n_layers);
     m->loaded_layer.assign(c.n_layers, false);
-    const size_t H = c.hidden, I = c.inter, D = c.head_dim;
+    const size_t H = c.hidden, I = m->inter, D = c.head_dim;
     int rc = SA_OK;
     if (!rc) rc = dalloc(&m->embed, (size_t)c.vocab * H);
     if (!rc) rc = dalloc(&m->final_norm, H);
@@ -344,7 +489,7 @@ SA_API int sa_qwen3_create(sa_ctx* ctx, const sa_qwen3_config* cfg, sa_qwen3** o
         if (!rc) rc = dalloc(&L.wgu, 2 * I * H);
         if (!rc) rc = dalloc(&L.wd, H * I);
     }
-    const size_t kv = (size_t)c.n_layers * c.hkv * c.max_seq * D;
+    const size_t kv = (size_t)c.n_layers * m->hkv * c.max_seq * D;
     if (!rc) rc = dalloc(&m->kc, kv);
     if (!rc) rc = dalloc(&m->vc, kv);
     if (!rc) rc = dalloc(&m->cos_t, (size_t)c.max_seq * D / 2);
@@ -358,13 +503,28 @@ SA_API int sa_qwen3_create(sa_ctx* ctx, const sa_qwen3_config* cfg, sa_qwen3** o
     if (!rc) rc = dalloc(&m->d_state, 2);
     if (!rc) rc = dalloc(&m->d_toks, (size_t)m->toks_cap);
     if (!rc) rc = dalloc(&m->dec_scratch,
-                         decode_dev_scratch_floats(ctx->num_sms, c.max_seq, (int)D, c.hq, c.hkv, nullptr));
-    if (!rc) rc = dalloc(&m->dec_cnt, (size_t)(c.hq + 2 * c.hkv));
+                         decode_dev_scratch_floats(ctx->num_sms, c.max_seq, (int)D, m->hq, m->hkv, nullptr));
+    if (!rc) rc = dalloc(&m->dec_cnt, (size_t)(m->hq + 2 * m->hkv));
     if (!rc) rc = dalloc(&m->d_amax, 1);
     if (!rc && cudaMemsetAsync(m->d_amax, 0, sizeof(unsigned long long), ctx->stream) != cudaSuccess)
         rc = set_error(SA_ERR_CUDA, "memset");
-    if (!rc && cudaMemsetAsync(m->dec_cnt, 0, (c.hq + 2 * c.hkv) * sizeof(unsigned), ctx->stream) != cudaSuccess)
+    if (!rc && cudaMemsetAsync(m->dec_cnt, 0, (m->hq + 2 * m->hkv) * sizeof(unsigned), ctx->stream) != cudaSuccess)
         rc = set_error(SA_ERR_CUDA, "memset");
+    if (!rc && world > 1) {
+        // exchange buffer: flags, then two slots of `world` blocks of tp_rows rows
+        m->tp_rows = std::min(c.max_seq, 8192);
+        m->tp_flag_bytes = 256 + 2 * (size_t)world * H * sizeof(unsigned long long);
+        const size_t bytes = m->tp_flag_bytes + 2 * (size_t)world * m->tp_rows * H * sizeof(float);
+        rc = dmalloc(&m->tp_buf, bytes);
+        if (!rc && cudaMemsetAsync(m->tp_buf, 0, bytes, ctx->stream) != cudaSuccess)
+            rc = set_error(SA_ERR_CUDA, "memset");
+        if (!rc) rc = dalloc(&m->tp_seq, 1);
+        if (!rc) rc = dalloc(&m->tp_cnt, 1);
+        if (!rc) rc = dalloc(&m->tp_x2, H);
+        if (!rc && (cudaMemsetAsync(m->tp_seq, 0, sizeof(unsigned), ctx->stream) != cudaSuccess ||
+                    cudaMemsetAsync(m->tp_cnt, 0, sizeof(unsigned), ctx->stream) != cudaSuccess))
+            rc = set_error(SA_ERR_CUDA, "memset");
+    }
     m->cur = ctx->stream;
     if (!rc) rc = launch_rope_table(ctx->stream, c.max_seq, (int)D, c.theta, m->cos_t, m->sin_t);
     if (!rc && cudaMemsetAsync(m->kc, 0, kv * 4, ctx->stream) != cudaSuccess) rc = set_error(SA_ERR_CUDA, "memset");
@@ -377,6 +537,61 @@ SA_API int sa_qwen3_create(sa_ctx* ctx, const sa_qwen3_config* cfg, sa_qwen3** o
     }
     m->lm_head = m->embed;
     *out = m;
+    return SA_OK;
+}
+
+}  // namespace sa
+
+SA_API int sa_qwen3_create(sa_ctx* ctx, const sa_qwen3_config* cfg, sa_qwen3** out) {
+    clear_error();
+    return qwen3_create_model(ctx, cfg, 0, 1, out);
+}
+
+SA_API int sa_qwen3_create_tp(sa_ctx* ctx, const sa_qwen3_config* cfg, int rank, int world, sa_qwen3** out) {
+    clear_error();
+    return qwen3_create_model(ctx, cfg, rank, world, out);
+}
+
+SA_API int sa_qwen3_tp_handle(sa_qwen3* m, void* handle) {
+    clear_error();
+    SA_CHECK_ARG(m && handle, "sa_qwen3_tp_handle: null argument");
+    SA_CHECK_ARG(m->tp_world > 1, "sa_qwen3_tp_handle: not a head-parallel model (world 1)");
+    static_assert(sizeof(cudaIpcMemHandle_t) <= SA_TP_HANDLE_BYTES, "IPC handle size");
+    DeviceGuard guard(m->device);
+    cudaIpcMemHandle_t h;
+    SA_CUDA_TRY(cudaIpcGetMemHandle(&h, m->tp_buf));
+    std::memset(handle, 0, SA_TP_HANDLE_BYTES);
+    std::memcpy(handle, &h, sizeof(h));
+    return SA_OK;
+}
+
+SA_API int sa_qwen3_tp_connect(sa_qwen3* m, const void* handles) {
+    clear_error();
+    SA_CHECK_ARG(m && handles, "sa_qwen3_tp_connect: null argument");
+    SA_CHECK_ARG(m->tp_world > 1, "sa_qwen3_tp_connect: not a head-parallel model (world 1)");
+    SA_CHECK_ARG(!m->tp_connected, "sa_qwen3_tp_connect: already connected");
+    DeviceGuard guard(m->device);
+    const unsigned char* hb = static_cast<const unsigned char*>(handles);
+    for (int r = 0; r < m->tp_world; ++r) {
+        if (r == m->tp_rank) {
+            m->tp_peer[r] = m->tp_buf;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, hb + (size_t)r * SA_TP_HANDLE_BYTES, sizeof(h));
+        void* p = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            for (int q = 0; q < r; ++q)
+                if (q != m->tp_rank && m->tp_peer[q]) cudaIpcCloseMemHandle(m->tp_peer[q]);
+            std::fill(m->tp_peer, m->tp_peer + TP_MAX, nullptr);
+            return set_error(SA_ERR_CUDA, "sa_qwen3_tp_connect: opening rank %d's buffer failed: %s", r,
+                             cudaGetErrorString(e));
+        }
+        m->tp_peer[r] = p;
+    }
+    m->tp_connected = true;
     return SA_OK;
 }
 
@@ -475,6 +690,9 @@ int qwen3_upload_layer(sa_qwen3* m, int layer, QwSrc in_norm, QwSrc wq, QwSrc wk
                        QwSrc k_norm, QwSrc wo, QwSrc post_norm, QwSrc w_gate, QwSrc w_up, QwSrc w_down) {
     const sa_qwen3_config& c = m->c;
     const size_t H = c.hidden, I = c.inter, D = c.head_dim;
+    // this rank's share: q / k / v rows of its heads, the matching o_proj
+    // columns, gate / up rows and down_proj columns of its intermediate features
+    const size_t QDl = m->QD, KDl = m->KD, Il = m->inter, QDg = (size_t)c.hq * D, r = m->tp_rank;
     auto& L = m->layers[layer];
     cudaStream_t st = m->ctx->stream;
     SA_RC(upload_gain(L.in_norm, in_norm, H, st));
@@ -482,15 +700,15 @@ int qwen3_upload_layer(sa_qwen3* m, int layer, QwSrc in_norm, QwSrc wq, QwSrc wk
     SA_RC(upload_gain(L.q_norm, q_norm, D, st));
     SA_RC(upload_gain(L.k_norm, k_norm, D, st));
     // [q; k; v] rows, as qwen3_loader.cpp builds qkv_projs
-    SA_RC(upload_rows(L.wqkv, H, wq, 0, m->QD, H, H, st));
-    SA_RC(upload_rows(L.wqkv + (size_t)m->QD * H, H, wk, 0, m->KD, H, H, st));
-    SA_RC(upload_rows(L.wqkv + (size_t)(m->QD + m->KD) * H, H, wv, 0, m->KD, H, H, st));
-    SA_RC(upload_rows(L.wo, m->QD, wo, 0, H, m->QD, m->QD, st));
+    SA_RC(upload_rows(L.wqkv, H, wq, r * QDl * H, QDl, H, H, st));
+    SA_RC(upload_rows(L.wqkv + QDl * H, H, wk, r * KDl * H, KDl, H, H, st));
+    SA_RC(upload_rows(L.wqkv + (QDl + KDl) * H, H, wv, r * KDl * H, KDl, H, H, st));
+    SA_RC(upload_rows(L.wo, QDl, wo, r * QDl, H, QDl, QDg, st));
     // gate/up interleaved in blocks of 32 rows: [gate 32b..32b+31 ; up 32b..32b+31]:
     // the blocks of gate land at even block slots, those of up at odd ones
-    SA_RC(upload_rows(L.wgu, 2 * 32 * H, w_gate, 0, I / 32, 32 * H, 32 * H, st));
-    SA_RC(upload_rows(L.wgu + 32 * H, 2 * 32 * H, w_up, 0, I / 32, 32 * H, 32 * H, st));
-    SA_RC(upload_rows(L.wd, I, w_down, 0, H, I, I, st));
+    SA_RC(upload_rows(L.wgu, 2 * 32 * H, w_gate, r * Il * H, Il / 32, 32 * H, 32 * H, st));
+    SA_RC(upload_rows(L.wgu + 32 * H, 2 * 32 * H, w_up, r * Il * H, Il / 32, 32 * H, 32 * H, st));
+    SA_RC(upload_rows(L.wd, Il, w_down, r * Il, H, Il, I, st));
     m->loaded_layer[layer] = true;
     return SA_OK;
 }
@@ -530,7 +748,7 @@ SA_API int sa_qwen3_cache_len(sa_qwen3* m) { return m ? m->cache_len : -1; }
 // ([hkv][max_seq][D]), one 2-D copy per tensor on the context's stream.
 static int copy_kv_layer(sa_qwen3* m, int layer, float* hk, float* hv, int rows, int seq_stride, bool to_host) {
     const size_t D = m->c.head_dim;
-    const size_t layer_kv = (size_t)m->c.hkv * m->c.max_seq * D;
+    const size_t layer_kv = (size_t)m->hkv * m->c.max_seq * D;
     float* dk = m->kc + (size_t)layer * layer_kv;
     float* dv = m->vc + (size_t)layer * layer_kv;
     if (rows == 0) return SA_OK;
@@ -538,11 +756,11 @@ static int copy_kv_layer(sa_qwen3* m, int layer, float* hk, float* hv, int rows,
     const size_t width = (size_t)rows * D * 4;
     cudaStream_t st = m->ctx->stream;
     if (to_host) {
-        SA_CUDA_TRY(cudaMemcpy2DAsync(hk, hpitch, dk, dpitch, width, m->c.hkv, cudaMemcpyDeviceToHost, st));
-        SA_CUDA_TRY(cudaMemcpy2DAsync(hv, hpitch, dv, dpitch, width, m->c.hkv, cudaMemcpyDeviceToHost, st));
+        SA_CUDA_TRY(cudaMemcpy2DAsync(hk, hpitch, dk, dpitch, width, m->hkv, cudaMemcpyDeviceToHost, st));
+        SA_CUDA_TRY(cudaMemcpy2DAsync(hv, hpitch, dv, dpitch, width, m->hkv, cudaMemcpyDeviceToHost, st));
     } else {
-        SA_CUDA_TRY(cudaMemcpy2DAsync(dk, dpitch, hk, hpitch, width, m->c.hkv, cudaMemcpyHostToDevice, st));
-        SA_CUDA_TRY(cudaMemcpy2DAsync(dv, dpitch, hv, hpitch, width, m->c.hkv, cudaMemcpyHostToDevice, st));
+        SA_CUDA_TRY(cudaMemcpy2DAsync(dk, dpitch, hk, hpitch, width, m->hkv, cudaMemcpyHostToDevice, st));
+        SA_CUDA_TRY(cudaMemcpy2DAsync(dv, dpitch, hv, hpitch, width, m->hkv, cudaMemcpyHostToDevice, st));
     }
     return sync_and_check(m->ctx);
 }
@@ -621,6 +839,9 @@ SA_API int sa_qwen3_forward(sa_qwen3* m, const int64_t* ids, int S, int use_cach
     SA_CHECK_ARG(m->loaded_embed, "sa_qwen3_forward: embedding not loaded");
     for (int l = 0; l < m->c.n_layers; ++l)
         SA_CHECK_ARG(m->loaded_layer[l], "sa_qwen3_forward: layer %d not loaded", l);
+    SA_CHECK_ARG(m->tp_world == 1 || m->tp_connected, "sa_qwen3_forward: head-parallel ranks not connected");
+    SA_CHECK_ARG(m->tp_world == 1 || S <= m->tp_rows, "sa_qwen3_forward: S = %d > %d rows per head-parallel forward",
+                 S, m->tp_rows);
     DeviceGuard guard(m->ctx->device);
     m->cur = m->ctx->stream;
     const int pos0 = use_cache ? m->cache_len : 0;
@@ -642,7 +863,7 @@ SA_API int sa_qwen3_forward(sa_qwen3* m, const int64_t* ids, int S, int use_cach
         auto body = [&]() -> int {
             SA_RC(run_layers(m, S, pos0, nullptr, kv_row0));
             if (logits_mode != 2) SA_RC(run_head(m, r0, n));
-            return SA_OK;
+            return tp_close_segment(m);
         };
         if (use_cache) return body();
         // qwen3_forward without a cache has a fixed schedule per (S, logits
@@ -685,7 +906,7 @@ static int decode_step_dev(sa_qwen3* m) {
 // when this model or device cannot use it (the graph of separate kernels
 // serves then).
 static bool mega_ready(sa_qwen3* m) {
-    if (m->mega_grid < 0) return false;
+    if (m->mega_grid < 0 || m->tp_world > 1) return false;
     if (m->mega_grid > 0) return true;
     const sa_qwen3_config& c = m->c;
     const int grid = mega_supported(c, m->ctx->num_sms) ? mega_grid(m->ctx->device) : 0;
@@ -738,6 +959,9 @@ SA_API int sa_qwen3_generate(sa_qwen3* m, const int64_t* prompt, int S, int n_ne
     SA_CHECK_ARG(m->loaded_embed, "sa_qwen3_generate: embedding not loaded");
     for (int l = 0; l < m->c.n_layers; ++l)
         SA_CHECK_ARG(m->loaded_layer[l], "sa_qwen3_generate: layer %d not loaded", l);
+    SA_CHECK_ARG(m->tp_world == 1 || m->tp_connected, "sa_qwen3_generate: head-parallel ranks not connected");
+    SA_CHECK_ARG(m->tp_world == 1 || S <= m->tp_rows, "sa_qwen3_generate: S = %d > %d prompt rows (head-parallel)",
+                 S, m->tp_rows);
     DeviceGuard guard(m->ctx->device);
     m->cur = m->ctx->stream;
     if (m->cache_len + S + n_new > m->c.max_seq + 1)
@@ -756,7 +980,10 @@ SA_API int sa_qwen3_generate(sa_qwen3* m, const int64_t* prompt, int S, int n_ne
         SA_CUDA_TRY(cudaMemcpyAsync(m->ids, prompt, (size_t)S * 8,
                                     host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, st));
         SA_RC(run_layers(m, S, pos0));
-        if (n_new == 0) return run_head(m, S - 1, 1);
+        if (n_new == 0) {
+            SA_RC(run_head(m, S - 1, 1));
+            return tp_close_segment(m);
+        }
         SA_RC(run_head(m, S - 1, 1, m->ids));
         const int state[2] = {pos0 + S, 0};
         SA_CUDA_TRY(cudaMemcpyAsync(m->d_state, state, sizeof(state), cudaMemcpyHostToDevice, st));

@@ -10,6 +10,7 @@
 #define QW_EPI_RESID  1   // y += W x          (residual stream)
 #define QW_EPI_SWIGLU 2   // y_i = silu(g_i) * u_i over [gate(32); up(32)] row blocks
 #define QW_EPI_QKV    3   // decode QKV projection + QK-norm + RoPE + KV-cache append (head_dim 128)
+#define QW_EPI_XCHG   4   // partial sums sent to every rank's receive block (head-parallel)
 
 namespace sa {
 
@@ -58,6 +59,53 @@ int launch_gemv(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, in
 int launch_argmax(cudaStream_t st, const float* v, int n, int64_t* out);
 int launch_gemv2(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, int N_out, int K, const float* x,
                  const float* nw, float eps, float* y, unsigned long long* amax, const QkvEpi* qkv = nullptr);
+
+// ---- head-parallel exchange (sa_qwen3_create_tp) ---------------------------
+// Every rank owns one exchange buffer: flag words [2 slots][world], word
+// areas [2 slots][world sources][ll_stride] (single-token exchanges), then
+// receive blocks [2 slots][world sources][slot_floats] (prompt exchanges).  Exchange instance i
+// (counted over the whole run, the same on every rank) uses slot i & 1; the
+// source rank writes its partial sums into block [slot][source] of every
+// rank (itself included) and then sets flag [slot][source] on every rank to
+// i + 1.  A consumer waits until all `world` flags of its slot reach i + 1
+// and adds the blocks in rank order, so every rank computes the same sums.
+// Two slots suffice: a rank can only start instance i + 2 after every rank
+// published instance i + 1, which each does after consuming instance i.
+constexpr int TP_MAX = 8;
+struct TpArgs {
+    int rank = 0, world = 1;
+    float* recv[TP_MAX] = {};       // receive blocks of every rank (own at [rank])
+    unsigned* flags[TP_MAX] = {};   // flag words of every rank
+    long long slot_floats = 0;      // floats per (slot, source) block
+    const unsigned* seq = nullptr;  // instances completed before this segment (device)
+    int k = 0;                      // this instance's index within the segment
+    unsigned* cnt = nullptr;        // producer grid's arrival counter (zero between launches)
+    int* status = nullptr;
+    float* x_out = nullptr;         // consumer GEMV: residual + exchanged sums are written here
+    int row = 0;                    // consumer / producer: row of the receive block
+    int n_base = 0;                 // argmax: index of output 0 in the full vocabulary
+    // Single-token exchanges use self-validating words instead of blocks and
+    // flags: word = (epoch << 32) | value bits, stored with one 8-byte store,
+    // so a reader that sees the epoch also sees the value.
+    unsigned long long* ll[TP_MAX] = {};   // word areas [2 slots][world][ll_stride] of every rank
+    int ll_stride = 0;
+    int use_ll = 0;                 // consumer: the producer wrote words (single-token path)
+};
+int launch_gemv2_tp(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, int N_out, int K,
+                    const float* x, const float* nw, float eps, float* y, unsigned long long* amax,
+                    const QkvEpi* qkv, const TpArgs& tp, bool consume);
+// Copy rows [0, M) x H of `part` to every rank's receive block and publish.
+int launch_tp_scatter(cudaStream_t st, const float* part, int M, int H, const TpArgs& tp, int grid);
+// RMSNorm (as launch_rmsnorm_hilo) of rows r0.. of x after adding the exchanged sums
+// (rows r0 + m of the receive blocks) into x in place.
+int launch_rmsnorm_hilo_tp(cudaStream_t st, float* x, const float* w, int M, int H, float eps,
+                           __nv_bfloat16* hi, __nv_bfloat16* lo, const TpArgs& tp);
+// Greedy token over the ranks' vocabulary slices: max of the argmax keys,
+// then *seq += seg (the segment's instances).
+int launch_tp_amax_token(cudaStream_t st, unsigned long long* amax, int64_t* tok, const TpArgs& tp, int seg);
+int launch_tp_seq_add(cudaStream_t st, unsigned* seq, int n);
+// Model allocation for rank `rank` of `world` (sa_qwen3.cu).
+int qwen3_create_model(sa_ctx* ctx, const sa_qwen3_config* cfg, int rank, int world, sa_qwen3** out);
 int launch_amax_to_token(cudaStream_t st, unsigned long long* amax, int64_t* tok);
 
 // ---- single-launch decode step (sa_qwen3_mega.cu) ---------------------------

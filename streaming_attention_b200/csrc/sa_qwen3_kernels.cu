@@ -247,9 +247,99 @@ __device__ __forceinline__ uint32_t ordered_f32(float f) {
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// ---- head-parallel exchange primitives --------------------------------------
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Slot and epoch of this launch's exchange instance (read after pdl_wait:
+// the sequence word is advanced by an earlier kernel of the stream).
+__device__ __forceinline__ void tp_instance(const TpArgs& t, int& slot, unsigned& epoch) {
+    const unsigned i = __ldcg(t.seq) + (unsigned)t.k;
+    slot = (int)(i & 1u);
+    epoch = i + 1u;
+}
+
+// Wait until source `src` has published `epoch` into this rank's flag of
+// `slot`.  Bounded: after the limit (or when an earlier wait already failed)
+// the status word is set and the caller continues with whatever is there.
+__device__ __forceinline__ void tp_wait(const TpArgs& t, int slot, unsigned epoch, int src) {
+    const unsigned* f = t.flags[t.rank] + slot * t.world + src;
+    if ((int)(ld_acquire_sys(f) - epoch) >= 0) return;
+    if (*reinterpret_cast<volatile int*>(t.status) != 0) return;
+    const unsigned long long t0 = globaltimer();
+    while ((int)(ld_acquire_sys(f) - epoch) < 0) {
+        if (globaltimer() - t0 > kWaitLimitNs) {
+            atomicExch(t.status, SA_STATUS_TIMEOUT);
+            return;
+        }
+    }
+}
+
+__device__ __forceinline__ void st_word_sys(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_word_sys(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned long long ll_word(unsigned epoch, uint32_t bits) {
+    return ((unsigned long long)epoch << 32) | bits;
+}
+__device__ __forceinline__ ulonglong2 ld_words2_sys(const unsigned long long* p) {
+    ulonglong2 v;
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+    return v;
+}
+// Word area [slot][src] of rank `dst`.
+__device__ __forceinline__ unsigned long long* tp_words(const TpArgs& t, int dst, int slot, int src) {
+    return t.ll[dst] + ((long long)slot * t.world + src) * t.ll_stride;
+}
+// Wait for a self-validating word of `epoch` (bounded as tp_wait) and return its value bits.
+__device__ __forceinline__ uint32_t ll_wait(const TpArgs& t, const unsigned long long* p, unsigned epoch) {
+    unsigned long long w = ld_word_sys(p);
+    if ((unsigned)(w >> 32) == epoch) return (uint32_t)w;
+    if (*reinterpret_cast<volatile int*>(t.status) != 0) return (uint32_t)w;
+    const unsigned long long t0 = globaltimer();
+    while ((unsigned)((w = ld_word_sys(p)) >> 32) != epoch) {
+        if (globaltimer() - t0 > kWaitLimitNs) {
+            atomicExch(t.status, SA_STATUS_TIMEOUT);
+            break;
+        }
+    }
+    return (uint32_t)w;
+}
+
+// Receive block [slot][src] of rank `dst`.
+__device__ __forceinline__ float* tp_block(const TpArgs& t, int dst, int slot, int src) {
+    return t.recv[dst] + ((long long)slot * t.world + src) * t.slot_floats;
+}
+
+// Called by one warp of every CTA of a producing grid after its stores to
+// the receive blocks: the last CTA to arrive publishes the instance on every
+// rank (lane r sets this rank's flag on rank r) and re-arms the counter.
+__device__ __forceinline__ void tp_arrive_publish(const TpArgs& t, int slot, unsigned epoch, int lane) {
+    __threadfence_system();
+    __syncwarp();
+    unsigned last = 0;
+    if (lane == 0) last = atomicAdd(t.cnt, 1u) == gridDim.x - 1;
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    __threadfence_system();
+    if (lane < t.world) st_release_sys(t.flags[lane] + slot * t.world + t.rank, epoch);
+    if (lane == 0) *t.cnt = 0u;
+}
+
 // Activations (x, and y in RESID mode) come from the previous kernel, which may
 // still be draining when this one starts (programmatic launch): they are read
 // through L2 (ld.global.cg) after pdl_wait, never through the read-only path.
+// blockDim = K/8 rounded up to whole warps; threads past K/8 contribute zero.
 //
 // QW_EPI_QKV (the decode step's fused QKV projection): rows are the
 // [q heads; k heads; v heads] x 128 outputs, R rows per CTA, so 128 / R CTAs
@@ -257,13 +347,23 @@ __device__ __forceinline__ uint32_t ordered_f32(float f) {
 // go to y; the last CTA of a head to arrive (per-head counter) reads the
 // head back, applies QK-norm and RoPE (as qknorm_rope_append_kernel) and
 // writes the query (e.q_out) or the K cache row, then re-arms the counter.
-template <int MODE, bool NORM, int R, bool ARGMAX>
+//
+// Head-parallel ranks: QW_EPI_XCHG sends the outputs (this rank's partial
+// sums of o_proj / down_proj) as self-validating words to word area
+// [slot][rank] of every rank: no fence, counter or flag.  CONSUME adds the
+// exchanged sums of the previous instance to the residual before anything
+// else: x + the sum over ranks r, in rank order, of word area [slot][r]
+// (tp.use_ll; each thread waits for its own 8 words per rank) or of block
+// [slot][r] row tp.row after the flags (after a prompt-path exchange); CTA 0
+// stores the result at tp.x_out (the other CTAs still read x).
+template <int MODE, bool NORM, int R, bool ARGMAX, bool CONSUME>
 __global__ void gemv2_kernel(const __nv_bfloat16* __restrict__ W, int N_out, int K,
                              const float* x, const float* __restrict__ nw, float eps,
-                             float* y, unsigned long long* amax, const QkvEpi e) {
+                             float* y, unsigned long long* amax, const QkvEpi e, const TpArgs tp) {
     constexpr int NV = R + 1;                      // R dot products + sum of squares
     __shared__ float red[32][NV];
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5, nwarp = blockDim.x >> 5;
+    const bool act = t < K / 8;                    // thread owns a K-chunk
     const int OUT_PER_CTA = MODE == QW_EPI_SWIGLU ? R / 2 : R;
     const int o0 = blockIdx.x * OUT_PER_CTA;
     // rows of this CTA
@@ -282,7 +382,8 @@ __global__ void gemv2_kernel(const __nv_bfloat16* __restrict__ W, int N_out, int
     pdl_trigger();
     uint4 w[R];
 #pragma unroll
-    for (int r = 0; r < R; ++r) w[r] = __ldg(reinterpret_cast<const uint4*>(W + (size_t)rows[r] * K) + t);
+    for (int r = 0; r < R; ++r)
+        w[r] = act ? __ldg(reinterpret_cast<const uint4*>(W + (size_t)rows[r] * K) + t) : make_uint4(0, 0, 0, 0);
     // weights do not depend on the previous kernel; the activations do
     pdl_wait();
     int q_pos = 0, q_row = 0;      // QKV epilogue: RoPE position and cache row
@@ -290,19 +391,95 @@ __global__ void gemv2_kernel(const __nv_bfloat16* __restrict__ W, int N_out, int
         q_pos = e.pos_dev ? __ldcg(e.pos_dev) : e.pos0;
         q_row = q_pos + e.row_shift;
     }
-    const float4 xa = __ldcg(reinterpret_cast<const float4*>(x) + 2 * t);
-    const float4 xb = __ldcg(reinterpret_cast<const float4*>(x) + 2 * t + 1);
-    float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+    float xv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (act) {
+        const float4 xa = __ldcg(reinterpret_cast<const float4*>(x) + 2 * t);
+        const float4 xb = __ldcg(reinterpret_cast<const float4*>(x) + 2 * t + 1);
+        xv[0] = xa.x; xv[1] = xa.y; xv[2] = xa.z; xv[3] = xa.w;
+        xv[4] = xb.x; xv[5] = xb.y; xv[6] = xb.z; xv[7] = xb.w;
+    }
+    if (CONSUME) {
+        __shared__ int s_slot;
+        __shared__ unsigned s_epoch;
+        if (t == 0) {
+            int slot;
+            unsigned epoch;
+            tp_instance(tp, slot, epoch);
+            s_slot = slot;
+            s_epoch = epoch;
+            if (!tp.use_ll)
+                for (int r = 0; r < tp.world; ++r) tp_wait(tp, slot, epoch, r);
+        }
+        __syncthreads();
+        if (act && tp.use_ll) {
+            // this thread's 8 words from each source, loaded two sources at a
+            // time before any is checked (one round trip per pair when the
+            // words are there); words that are not yet there are waited for
+            float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            for (int r0 = 0; r0 < tp.world; r0 += 2) {
+                ulonglong2 wv[2][4];
+#pragma unroll
+                for (int g = 0; g < 2; ++g)
+                    if (r0 + g < tp.world) {
+                        const unsigned long long* wd = tp_words(tp, tp.rank, s_slot, r0 + g) + 8 * t;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) wv[g][i] = ld_words2_sys(wd + 2 * i);
+                    }
+#pragma unroll
+                for (int g = 0; g < 2; ++g)
+                    if (r0 + g < tp.world) {
+                        const unsigned long long* wd = tp_words(tp, tp.rank, s_slot, r0 + g) + 8 * t;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            unsigned long long a = wv[g][i].x, b = wv[g][i].y;
+                            if ((unsigned)(a >> 32) != s_epoch) a = ll_wait(tp, wd + 2 * i, s_epoch);
+                            if ((unsigned)(b >> 32) != s_epoch) b = ll_wait(tp, wd + 2 * i + 1, s_epoch);
+                            const float va = __uint_as_float((uint32_t)a), vb = __uint_as_float((uint32_t)b);
+                            sum[2 * i] = r0 + g == 0 ? va : sum[2 * i] + va;
+                            sum[2 * i + 1] = r0 + g == 0 ? vb : sum[2 * i + 1] + vb;
+                        }
+                    }
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) xv[i] += sum[i];
+            if (blockIdx.x == 0) {
+                reinterpret_cast<float4*>(tp.x_out)[2 * t] = make_float4(xv[0], xv[1], xv[2], xv[3]);
+                reinterpret_cast<float4*>(tp.x_out)[2 * t + 1] = make_float4(xv[4], xv[5], xv[6], xv[7]);
+            }
+        } else if (act) {
+            float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            for (int r = 0; r < tp.world; ++r) {
+                float pv[8];
+                {
+                    const float* b = tp_block(tp, tp.rank, s_slot, r) + (size_t)tp.row * K;
+                    const float4 pa = __ldcg(reinterpret_cast<const float4*>(b) + 2 * t);
+                    const float4 pb = __ldcg(reinterpret_cast<const float4*>(b) + 2 * t + 1);
+                    pv[0] = pa.x; pv[1] = pa.y; pv[2] = pa.z; pv[3] = pa.w;
+                    pv[4] = pb.x; pv[5] = pb.y; pv[6] = pb.z; pv[7] = pb.w;
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i) sum[i] = r == 0 ? pv[i] : sum[i] + pv[i];
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) xv[i] += sum[i];
+            if (blockIdx.x == 0) {
+                reinterpret_cast<float4*>(tp.x_out)[2 * t] = make_float4(xv[0], xv[1], xv[2], xv[3]);
+                reinterpret_cast<float4*>(tp.x_out)[2 * t + 1] = make_float4(xv[4], xv[5], xv[6], xv[7]);
+            }
+        }
+    }
     float v[NV];
     v[R] = 0.f;
     if (NORM) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[R] = fmaf(xv[e], xv[e], v[R]);
-        const float4 ga = __ldg(reinterpret_cast<const float4*>(nw) + 2 * t);
-        const float4 gb = __ldg(reinterpret_cast<const float4*>(nw) + 2 * t + 1);
-        const float gv[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+        for (int i = 0; i < 8; ++i) v[R] = fmaf(xv[i], xv[i], v[R]);
+        if (act) {
+            const float4 ga = __ldg(reinterpret_cast<const float4*>(nw) + 2 * t);
+            const float4 gb = __ldg(reinterpret_cast<const float4*>(nw) + 2 * t + 1);
+            const float gv[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) xv[e] *= gv[e];
+            for (int i = 0; i < 8; ++i) xv[i] *= gv[i];
+        }
     }
 #pragma unroll
     for (int r = 0; r < R; ++r) {
@@ -330,6 +507,9 @@ __global__ void gemv2_kernel(const __nv_bfloat16* __restrict__ W, int N_out, int
         }
         float scale = 1.f;
         if (NORM) scale = 1.f / sqrtf(v[R] / (float)K + eps);
+        int x_slot = 0;
+        unsigned x_epoch = 0;
+        if (MODE == QW_EPI_XCHG) tp_instance(tp, x_slot, x_epoch);
         unsigned long long best = 0ull;
         if (lane < OUT_PER_CTA) {
             const int n = o0 + lane;
@@ -354,11 +534,17 @@ __global__ void gemv2_kernel(const __nv_bfloat16* __restrict__ W, int N_out, int
                         y[n] = out;
                     }
                 }
+            } else if (MODE == QW_EPI_XCHG) {
+                // one self-validating word per output to every rank
+                if (n < N_out)
+                    for (int r = 0; r < tp.world; ++r)
+                        st_word_sys(tp_words(tp, r, x_slot, tp.rank) + n, ll_word(x_epoch, __float_as_uint(out)));
             } else if (n < N_out) {
                 if (MODE == QW_EPI_RESID) y[n] = __ldcg(y + n) + out;
                 else y[n] = out;
                 if (ARGMAX)
-                    best = ((unsigned long long)ordered_f32(out) << 32) | (unsigned long long)(0xffffffffu - (uint32_t)n);
+                    best = ((unsigned long long)ordered_f32(out) << 32) |
+                           (unsigned long long)(0xffffffffu - (uint32_t)(n + tp.n_base));
             }
         }
         if (ARGMAX) {
@@ -393,6 +579,107 @@ __global__ void gemv2_kernel(const __nv_bfloat16* __restrict__ W, int N_out, int
             }
         }
     }
+}
+
+// ---- head-parallel: prompt-path exchange ------------------------------------
+// Producer: rows [0, M) x H of `part` (this rank's o_proj / down_proj partial
+// sums from the tensor-core GEMM) go to block [slot][rank] of every rank.
+__global__ void tp_scatter_kernel(const float* part, size_t n4, const TpArgs tp) {
+    pdl_trigger();
+    pdl_wait();
+    int slot;
+    unsigned epoch;
+    tp_instance(tp, slot, epoch);
+    const float4* src = reinterpret_cast<const float4*>(part);
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        const float4 v = __ldcg(src + i);
+        for (int r = 0; r < tp.world; ++r) reinterpret_cast<float4*>(tp_block(tp, r, slot, tp.rank))[i] = v;
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < 32) tp_arrive_publish(tp, slot, epoch, threadIdx.x);
+}
+
+// Consumer: x[m] += sum over ranks of block row (tp.row + m), then RMSNorm of
+// the row split into bf16 hi/lo terms (as rmsnorm_hilo_kernel).  One CTA per
+// row; each updates only its own row of x.
+__global__ void rmsnorm_hilo_tp_kernel(float* x, const float* w, int H, float eps, __nv_bfloat16* hi,
+                                       __nv_bfloat16* lo, const TpArgs tp) {
+    __shared__ float red[32];
+    __shared__ int s_slot;
+    pdl_trigger();
+    pdl_wait();
+    const int m = blockIdx.x;
+    if (threadIdx.x == 0) {
+        int slot;
+        unsigned epoch;
+        tp_instance(tp, slot, epoch);
+        s_slot = slot;
+        for (int r = 0; r < tp.world; ++r) tp_wait(tp, slot, epoch, r);
+    }
+    __syncthreads();
+    float* xr = x + (size_t)m * H;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+        float sum = 0.f;
+        for (int r = 0; r < tp.world; ++r) {
+            const float p = __ldcg(tp_block(tp, tp.rank, s_slot, r) + (size_t)(tp.row + m) * H + i);
+            sum = r == 0 ? p : sum + p;
+        }
+        const float v = xr[i] + sum;
+        xr[i] = v;
+        ss += v * v;
+    }
+    ss = block_sum(ss, red);
+    const float rms = sqrtf(ss / (float)H + eps);
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+        const float y = (xr[i] / rms) * w[i];
+        const __nv_bfloat16 h = __float2bfloat16_rn(y);
+        hi[(size_t)m * H + i] = h;
+        lo[(size_t)m * H + i] = __float2bfloat16_rn(y - __bfloat162float(h));
+    }
+}
+
+// Greedy token across the ranks' vocabulary slices: every rank sends its
+// argmax key (largest value, first index; indices are global) to every rank
+// as self-validating words,
+// takes the maximum of the `world` keys and decodes it; then the segment's
+// instance count is added to the sequence word.  One warp.
+__global__ void tp_amax_token_kernel(unsigned long long* amax, int64_t* tok, const TpArgs tp, int seg) {
+    pdl_trigger();
+    pdl_wait();
+    const int lane = threadIdx.x;
+    int slot;
+    unsigned epoch;
+    tp_instance(tp, slot, epoch);
+    const unsigned long long mine = __ldcg(amax);            // folded in by the lm_head GEMV
+    if (lane < tp.world) {   // the key as two self-validating words (high, low half)
+        unsigned long long* w = tp_words(tp, lane, slot, tp.rank);
+        st_word_sys(w, ll_word(epoch, (uint32_t)(mine >> 32)));
+        st_word_sys(w + 1, ll_word(epoch, (uint32_t)mine));
+    }
+    unsigned long long best = 0ull;
+    if (lane < tp.world) {
+        const unsigned long long* w = tp_words(tp, tp.rank, slot, lane);
+        const uint32_t hi = ll_wait(tp, w, epoch), lo = ll_wait(tp, w + 1, epoch);
+        best = ((unsigned long long)hi << 32) | lo;
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) {
+        const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
+        best = o > best ? o : best;
+    }
+    if (lane == 0) {
+        *tok = (int64_t)(0xffffffffu - (uint32_t)(best & 0xffffffffull));
+        *amax = 0ull;
+        *const_cast<unsigned*>(tp.seq) = __ldcg(tp.seq) + (unsigned)seg;
+    }
+}
+
+__global__ void tp_seq_add_kernel(unsigned* seq, int n) {
+    pdl_trigger();
+    pdl_wait();
+    *seq = __ldcg(seq) + (unsigned)n;
 }
 
 // Decode the argmax key into a token id and clear the key for the next step.
@@ -520,35 +807,89 @@ int launch_gemv(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, in
     SA_CUDA_TRY(cudaGetLastError());
     return SA_OK;
 }
-int launch_gemv2(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, int N_out, int K, const float* x,
-                 const float* nw, float eps, float* y, unsigned long long* amax, const QkvEpi* qkv) {
-    SA_CHECK_ARG(K % 256 == 0 && K / 8 <= 1024, "gemv2: K=%d (multiple of 256, <= 8192)", K);
-    const int threads = K / 8;
+int launch_gemv2_tp(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, int N_out, int K,
+                    const float* x, const float* nw, float eps, float* y, unsigned long long* amax,
+                    const QkvEpi* qkv, const TpArgs& tp, bool consume) {
+    SA_CHECK_ARG(K % 64 == 0 && K / 8 <= 1024, "gemv2: K=%d (multiple of 64, <= 8192)", K);
+    const int threads = (K / 8 + 31) / 32 * 32;
     // rows per CTA: enough CTAs to cover the SMs several times over
     const int rows = mode == QW_EPI_SWIGLU ? 2 * N_out : N_out;
     const int R = rows >= 8 * 1024 ? 8 : (rows >= 4 * 512 ? 4 : 2);
     const int outs = mode == QW_EPI_SWIGLU ? R / 2 : R;
     const int grid = (N_out + outs - 1) / outs;
     const QkvEpi e = qkv ? *qkv : QkvEpi{};
-#define SA_G2(M, N, RR, A) SA_CUDA_TRY(launch_pdl_k(0, qk::gemv2_kernel<M, N, RR, A>, dim3(grid), dim3(threads), 0, st, \
-                                                  W, N_out, K, x, nw, eps, y, amax, e))
-#define SA_G2R(M, N, A) do { if (R == 8) SA_G2(M, N, 8, A); else if (R == 4) SA_G2(M, N, 4, A); else SA_G2(M, N, 2, A); } while (0)
-    if (mode == QW_EPI_QKV) {
+    const bool xchg = tp.world > 1 && (mode == QW_EPI_XCHG || consume);
+    SA_CHECK_ARG(!xchg || (tp.seq && tp.status && tp.world <= TP_MAX), "gemv2: exchange operands missing");
+    SA_CHECK_ARG(!consume || (tp.x_out && K % 256 == 0 && K / 8 == threads),
+                 "gemv2: the consuming GEMV needs x_out and whole warps of K-chunks");
+    SA_CHECK_ARG(mode != QW_EPI_XCHG || (tp.ll_stride >= N_out && tp.row == 0 && !norm && !amax),
+                 "gemv2: exchange epilogue operands");
+    SA_CHECK_ARG(!consume || !tp.use_ll || tp.ll_stride >= K, "gemv2: word area smaller than the residual");
+#define SA_G2(M, N, RR, A, C) SA_CUDA_TRY(launch_pdl_k(0, qk::gemv2_kernel<M, N, RR, A, C>, dim3(grid), dim3(threads), \
+                                                     0, st, W, N_out, K, x, nw, eps, y, amax, e, tp))
+#define SA_G2R(M, N, A, C) do { if (R == 8) SA_G2(M, N, 8, A, C); else if (R == 4) SA_G2(M, N, 4, A, C); \
+                                else SA_G2(M, N, 2, A, C); } while (0)
+    if (consume) {
+        SA_CHECK_ARG(norm, "gemv2: the consuming GEMV applies the norm");
+        if (mode == QW_EPI_QKV) {
+            SA_CHECK_ARG(qkv && !amax && qkv->cnt && N_out == 128 * (qkv->hq + 2 * qkv->hkv), "gemv2: QKV operands");
+            SA_G2R(QW_EPI_QKV, true, false, true);
+        } else if (mode == QW_EPI_SWIGLU) {
+            SA_G2R(QW_EPI_SWIGLU, true, false, true);
+        } else if (mode == QW_EPI_STORE) {
+            if (amax) SA_G2R(QW_EPI_STORE, true, true, true); else SA_G2R(QW_EPI_STORE, true, false, true);
+        } else {
+            return set_error(SA_ERR_ARG, "gemv2: mode %d cannot consume an exchange", mode);
+        }
+    } else if (mode == QW_EPI_XCHG) {
+        SA_G2R(QW_EPI_XCHG, false, false, false);
+    } else if (mode == QW_EPI_QKV) {
         SA_CHECK_ARG(qkv && norm && !amax && qkv->cnt && N_out == 128 * (qkv->hq + 2 * qkv->hkv),
                      "gemv2: QKV epilogue needs its operands, the input norm and N_out = 128 (hq + 2 hkv)");
-        SA_G2R(QW_EPI_QKV, true, false);
+        SA_G2R(QW_EPI_QKV, true, false, false);
     } else if (amax) {
         SA_CHECK_ARG(mode == QW_EPI_STORE && norm, "gemv2: argmax only with the normed STORE head");
-        SA_G2R(QW_EPI_STORE, true, true);
+        SA_G2R(QW_EPI_STORE, true, true, false);
     } else if (mode == QW_EPI_STORE) {
-        if (norm) SA_G2R(QW_EPI_STORE, true, false); else SA_G2R(QW_EPI_STORE, false, false);
+        if (norm) SA_G2R(QW_EPI_STORE, true, false, false); else SA_G2R(QW_EPI_STORE, false, false, false);
     } else if (mode == QW_EPI_RESID) {
-        if (norm) SA_G2R(QW_EPI_RESID, true, false); else SA_G2R(QW_EPI_RESID, false, false);
+        if (norm) SA_G2R(QW_EPI_RESID, true, false, false); else SA_G2R(QW_EPI_RESID, false, false, false);
     } else {
-        if (norm) SA_G2R(QW_EPI_SWIGLU, true, false); else SA_G2R(QW_EPI_SWIGLU, false, false);
+        if (norm) SA_G2R(QW_EPI_SWIGLU, true, false, false); else SA_G2R(QW_EPI_SWIGLU, false, false, false);
     }
 #undef SA_G2R
 #undef SA_G2
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
+int launch_gemv2(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, int N_out, int K, const float* x,
+                 const float* nw, float eps, float* y, unsigned long long* amax, const QkvEpi* qkv) {
+    SA_CHECK_ARG(mode != QW_EPI_XCHG, "gemv2: the exchange epilogue needs launch_gemv2_tp");
+    return launch_gemv2_tp(st, mode, norm, W, N_out, K, x, nw, eps, y, amax, qkv, TpArgs{}, false);
+}
+int launch_tp_scatter(cudaStream_t st, const float* part, int M, int H, const TpArgs& tp, int grid) {
+    SA_CHECK_ARG(tp.world > 1 && tp.seq && tp.cnt && (size_t)M * H <= (size_t)tp.slot_floats && H % 4 == 0,
+                 "tp_scatter: M=%d H=%d", M, H);
+    qk::tp_scatter_kernel<<<grid, 256, 0, st>>>(part, (size_t)M * H / 4, tp);
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
+int launch_rmsnorm_hilo_tp(cudaStream_t st, float* x, const float* w, int M, int H, float eps,
+                           __nv_bfloat16* hi, __nv_bfloat16* lo, const TpArgs& tp) {
+    SA_CHECK_ARG(tp.world > 1 && tp.seq && tp.status && (size_t)(tp.row + M) * H <= (size_t)tp.slot_floats,
+                 "rmsnorm_hilo_tp: rows %d..%d", tp.row, tp.row + M);
+    qk::rmsnorm_hilo_tp_kernel<<<M, 256, 0, st>>>(x, w, H, eps, hi, lo, tp);
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
+int launch_tp_amax_token(cudaStream_t st, unsigned long long* amax, int64_t* tok, const TpArgs& tp, int seg) {
+    SA_CHECK_ARG(tp.world > 1 && tp.seq && tp.status, "tp_amax_token: exchange operands missing");
+    SA_CUDA_TRY(launch_pdl_k(3, qk::tp_amax_token_kernel, dim3(1), dim3(32), 0, st, amax, tok, tp, seg));
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
+int launch_tp_seq_add(cudaStream_t st, unsigned* seq, int n) {
+    SA_CUDA_TRY(launch_pdl_k(3, qk::tp_seq_add_kernel, dim3(1), dim3(1), 0, st, seq, n));
     SA_CUDA_TRY(cudaGetLastError());
     return SA_OK;
 }

@@ -385,6 +385,11 @@ SA_API int sa_safetensors_inspect(const char* path, sa_qwen3_config* out) {
 
 SA_API int sa_qwen3_load_safetensors(sa_ctx* ctx, const char* path, int max_seq, float eps, float theta,
                                      sa_qwen3** out) {
+    return sa_qwen3_load_safetensors_tp(ctx, path, max_seq, eps, theta, 0, 1, out);
+}
+
+SA_API int sa_qwen3_load_safetensors_tp(sa_ctx* ctx, const char* path, int max_seq, float eps, float theta, int rank,
+                                        int world, sa_qwen3** out) {
     using namespace sa;
     clear_error();
     SA_CHECK_ARG(ctx && out, "sa_qwen3_load_safetensors: null argument");
@@ -397,7 +402,7 @@ SA_API int sa_qwen3_load_safetensors(sa_ctx* ctx, const char* path, int max_seq,
     st::Sources s;
     SA_RC_TRY(st::collect(f, c, &s));   // every tensor checked before the model is allocated
     sa_qwen3* m = nullptr;
-    SA_RC_TRY(sa_qwen3_create(ctx, &c, &m));
+    SA_RC_TRY(qwen3_create_model(ctx, &c, rank, world, &m));
     int rc;
     {
         DeviceGuard guard(ctx->device);

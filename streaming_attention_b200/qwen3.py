@@ -63,10 +63,19 @@ def inspect_safetensors(path: str) -> dict:
     return {f: getattr(c, f) for f in _CFG_FIELDS}
 
 
+SA_TP_HANDLE_BYTES = 64
+
+
 class Qwen3:
+    """One Qwen3 model on one GPU, or (rank, world) of a head-parallel model
+    over `world` GPUs (sa_qwen3_create_tp): every rank is given the same full
+    weights and keeps its share; after ``connect`` every rank calls
+    ``forward`` / ``generate`` with the same arguments and gets the same
+    results."""
+
     @classmethod
     def from_safetensors(cls, path: str, max_seq: int = 4096, ctx: Context | None = None,
-                         eps: float = 0.0, theta: float = 0.0) -> "Qwen3":
+                         eps: float = 0.0, theta: float = 0.0, rank: int = 0, world: int = 1) -> "Qwen3":
         """A model whose weights are uploaded straight from a safetensors
         checkpoint (sa_qwen3_load_safetensors: bf16 bytes to the GPU, no fp32
         round trip).  eps / theta <= 0 select Qwen3's 1e-6 / 1e6."""
@@ -77,22 +86,49 @@ class Qwen3:
         if theta > 0:
             self.cfg["theta"] = theta
         self.ctx = ctx or default_context(0)
+        self.rank, self.world = rank, world
         h = C.c_void_p()
-        check(lib().sa_qwen3_load_safetensors(self.ctx.h, os.fsencode(path), max_seq, eps, theta, C.byref(h)))
+        check(lib().sa_qwen3_load_safetensors_tp(self.ctx.h, os.fsencode(path), max_seq, eps, theta, rank, world,
+                                                 C.byref(h)))
         self.h = h
         self.max_seq = max_seq
         return self
 
-    def __init__(self, cfg: dict, max_seq: int = 4096, ctx: Context | None = None):
+    def __init__(self, cfg: dict, max_seq: int = 4096, ctx: Context | None = None, rank: int = 0, world: int = 1):
         self.cfg = dict(cfg)
         self.ctx = ctx or default_context(0)
+        self.rank, self.world = rank, world
         c = Qwen3Config(vocab=cfg["vocab"], hidden=cfg["hidden"], n_layers=cfg["n_layers"],
                         hq=cfg["hq"], hkv=cfg["hkv"], head_dim=cfg["head_dim"], inter=cfg["inter"],
                         eps=cfg.get("eps", 1e-6), theta=cfg.get("theta", 1e6), max_seq=max_seq)
         h = C.c_void_p()
-        check(lib().sa_qwen3_create(self.ctx.h, C.byref(c), C.byref(h)))
+        if world == 1:
+            check(lib().sa_qwen3_create(self.ctx.h, C.byref(c), C.byref(h)))
+        else:
+            check(lib().sa_qwen3_create_tp(self.ctx.h, C.byref(c), rank, world, C.byref(h)))
         self.h = h
         self.max_seq = max_seq
+
+    # -- head-parallel ranks ------------------------------------------------
+    def tp_handle(self) -> bytes:
+        """This rank's exchange-buffer handle (sa_qwen3_tp_handle)."""
+        buf = C.create_string_buffer(SA_TP_HANDLE_BYTES)
+        check(lib().sa_qwen3_tp_handle(self.h, buf))
+        return buf.raw
+
+    def tp_connect(self, handles) -> None:
+        """Map the other ranks' exchange buffers: `handles` in rank order."""
+        assert len(handles) == self.world and all(len(x) == SA_TP_HANDLE_BYTES for x in handles)
+        blob = b"".join(handles)
+        check(lib().sa_qwen3_tp_connect(self.h, C.create_string_buffer(blob, len(blob))))
+
+    def connect(self, group=None) -> None:
+        """Exchange handles over a torch.distributed group (one rank per
+        process, ranks in group order) and connect."""
+        import torch.distributed as dist
+        handles = [None] * self.world
+        dist.all_gather_object(handles, self.tp_handle(), group=group)
+        self.tp_connect(handles)
 
     def close(self):
         if getattr(self, "h", None):
@@ -138,7 +174,7 @@ class Qwen3:
         (rows past cache_len are zero), the layout of KVCache's layer tensors."""
         L = self.cache_len
         stride = L if seq_stride is None else seq_stride
-        shape = (self.cfg["hkv"], stride, self.cfg["head_dim"])
+        shape = (self.cfg["hkv"] // self.world, stride, self.cfg["head_dim"])
         k, v = np.zeros(shape, np.float32), np.zeros(shape, np.float32)
         check(lib().sa_qwen3_read_kv(self.h, layer, k.ctypes.data, v.ctypes.data, stride))
         return k, v
@@ -147,7 +183,7 @@ class Qwen3:
         """Upload rows 0..len-1 of one layer's cache from float32 [hkv, len, head_dim]."""
         k = np.ascontiguousarray(k, np.float32)
         v = np.ascontiguousarray(v, np.float32)
-        assert k.shape == v.shape and k.shape[0] == self.cfg["hkv"] and k.shape[2] == self.cfg["head_dim"]
+        assert k.shape == v.shape and k.shape[0] == self.cfg["hkv"] // self.world and k.shape[2] == self.cfg["head_dim"]
         check(lib().sa_qwen3_write_kv(self.h, layer, k.ctypes.data, v.ctypes.data, k.shape[1], k.shape[1]))
 
     def set_cache_len(self, n: int):
