@@ -8,9 +8,10 @@
 //
 // Tile 128 (M) x 64 (N) x 64 (K), 4-stage TMA ring (128-byte swizzle), one
 // lane issues tcgen05.mma into a 64-column TMEM accumulator, four warps run
-// the epilogue (one row each per TMEM lane).  Split-K over gridDim.z writes
-// fp32 partials to scratch; the last CTA of a tile (arrival counter) sums them
-// in split order -- deterministic -- and applies the epilogue:
+// the epilogue (TMEM -> shared memory, then coalesced global accesses).
+// Split-K over gridDim.z writes fp32 partials to scratch; the last CTA of a
+// tile (arrival counter) sums them in split order -- deterministic -- and
+// applies the epilogue:
 //   STORE   C = acc                                  (fp32)
 //   RESID   C += acc       (the residual stream, qwen3_ops.cpp:514,527)
 //   SWIGLU  W holds [gate(32) ; up(32)] row blocks; out[:, n0/2 + i] =
@@ -143,71 +144,119 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ C
         }
     } else {
         // ------------------------------------------------ epilogue warps 2..5
+        // The accumulator tile goes TMEM -> registers (thread = row) -> shared
+        // memory (the pipeline stages are idle once `done` fired), and every
+        // global access after that is coalesced: a warp covers contiguous
+        // columns of a row, or contiguous float4s of a split partial.
+        const int et = tid - 64;                       // 0..127
         const int quad = warp & 3;
         const int row = quad * 32 + lane;
-        const int m = m0 + row;
-        float acc[BN];
+        float* T = reinterpret_cast<float*>(sm);       // [BM][TP] fp32
+        constexpr int TP = BN + 1;                     // padded row: conflict-free column writes
         const bool ok = wait_ab(&B->done, 0, abort, a.status);
         tc::fence_after_sync();
         {
             uint32_t r[32];
-            tc::tmem_ld32(tacc + ((uint32_t)(quad * 32) << 16), r);
-            tc::tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 32; ++c) acc[c] = nkb > 0 ? __uint_as_float(r[c]) : 0.f;
-            tc::tmem_ld32(tacc + ((uint32_t)(quad * 32) << 16) + 32, r);
-            tc::tmem_wait_ld();
+            for (int h = 0; h < 2; ++h) {
+                tc::tmem_ld32(tacc + ((uint32_t)(quad * 32) << 16) + 32 * h, r);
+                tc::tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 32; ++c) acc[32 + c] = nkb > 0 ? __uint_as_float(r[c]) : 0.f;
+                for (int c = 0; c < 32; ++c) T[row * TP + 32 * h + c] = nkb > 0 ? __uint_as_float(r[c]) : 0.f;
+            }
         }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
         const int tile = blockIdx.y * gridDim.x + blockIdx.x;
         bool finish = ok;
         if (ok && a.splits > 1) {
-            float* mine = a.part + ((size_t)tile * a.splits + kz) * (BM * BN) + (size_t)row * BN;
-#pragma unroll
-            for (int c = 0; c < BN; c += 4)
-                *reinterpret_cast<float4*>(mine + c) = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
+            // partial [BM][BN] row-major, written as 2048 float4 by 128 threads
+            float4* mine = reinterpret_cast<float4*>(a.part + ((size_t)tile * a.splits + kz) * (BM * BN));
+#pragma unroll 4
+            for (int i = 0; i < BM * BN / 4 / 128; ++i) {
+                const int e4 = i * 128 + et, rr = e4 / (BN / 4), c4 = (e4 % (BN / 4)) * 4;
+                const float* t = T + rr * TP + c4;
+                mine[e4] = make_float4(t[0], t[1], t[2], t[3]);
+            }
             __threadfence();
-            // named barrier over the 4 epilogue warps (128 threads)
             asm volatile("bar.sync 1, 128;" ::: "memory");
-            if (warp == 2 && lane == 0)
-                B->last = atomicAdd(&a.counters[tile], 1u) == (unsigned)(a.splits - 1);
+            if (et == 0) B->last = atomicAdd(&a.counters[tile], 1u) == (unsigned)(a.splits - 1);
             asm volatile("bar.sync 1, 128;" ::: "memory");
             finish = B->last;
             if (finish) {
                 __threadfence();
+                // sum the partials in split order into T
+                const float4* base = reinterpret_cast<const float4*>(a.part + (size_t)tile * a.splits * (BM * BN));
+                for (int i = 0; i < BM * BN / 4 / 128; i += 4) {
+                    float4 sacc[4];
 #pragma unroll
-                for (int c = 0; c < BN; ++c) acc[c] = 0.f;
-                for (int z = 0; z < a.splits; ++z) {
-                    const float* p = a.part + ((size_t)tile * a.splits + z) * (BM * BN) + (size_t)row * BN;
+                    for (int u = 0; u < 4; ++u) sacc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int z = 0; z < a.splits; ++z) {
+                        float4 v[4];
 #pragma unroll
-                    for (int c = 0; c < BN; c += 4) {
-                        const float4 v = __ldcg(reinterpret_cast<const float4*>(p + c));
-                        acc[c] += v.x; acc[c + 1] += v.y; acc[c + 2] += v.z; acc[c + 3] += v.w;
+                        for (int u = 0; u < 4; ++u) v[u] = __ldcg(base + (size_t)z * (BM * BN / 4) + (i + u) * 128 + et);
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            sacc[u].x += v[u].x; sacc[u].y += v[u].y; sacc[u].z += v[u].z; sacc[u].w += v[u].w;
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int e4 = (i + u) * 128 + et, rr = e4 / (BN / 4), c4 = (e4 % (BN / 4)) * 4;
+                        float* t = T + rr * TP + c4;
+                        t[0] = sacc[u].x; t[1] = sacc[u].y; t[2] = sacc[u].z; t[3] = sacc[u].w;
                     }
                 }
-                if (warp == 2 && lane == 0) a.counters[tile] = 0u;
+                if (et == 0) a.counters[tile] = 0u;
+                asm volatile("bar.sync 1, 128;" ::: "memory");
             }
         }
-        if (finish && m < a.M) {
+        if (finish) {
             if (a.mode == QW_EPI_SWIGLU) {
+                // 32 outputs per row: a warp writes one row's 32 consecutive bf16 pairs
                 const int i0 = n0 / 2;
-#pragma unroll
-                for (int c = 0; c < BN / 2; ++c) {
-                    const float val = silu(acc[c]) * acc[BN / 2 + c];
-                    store_hilo(a.out_hi + (size_t)m * a.ldo + i0 + c, a.out_lo + (size_t)m * a.ldo + i0 + c, val);
+#pragma unroll 4
+                for (int i = 0; i < BM * (BN / 2) / 128; ++i) {
+                    const int e = i * 128 + et, rr = e / (BN / 2), c = e % (BN / 2), m = m0 + rr;
+                    if (m < a.M) {
+                        const float val = silu(T[rr * TP + c]) * T[rr * TP + BN / 2 + c];
+                        store_hilo(a.out_hi + (size_t)m * a.ldo + i0 + c, a.out_lo + (size_t)m * a.ldo + i0 + c, val);
+                    }
                 }
             } else {
-                float* crow = a.C + (size_t)m * a.ldc + n0;
-                const int nv = min(BN, a.N - n0);
-                if (a.mode == QW_EPI_RESID) {
-                    for (int c = 0; c < nv; ++c) crow[c] += acc[c];
-                } else if (nv == BN) {
+                // a warp covers one row's BN columns as float2; loads of the
+                // residual are issued 8 rows at a time before any store
+                const int c2 = (et & 31) * 2, nv = a.N - n0;
+                const bool full = nv >= BN && (a.ldc & 1) == 0;
+                for (int i = 0; i < BM * (BN / 2) / 128; i += 8) {
+                    float2 old[8];
+                    if (a.mode == QW_EPI_RESID) {
 #pragma unroll
-                    for (int c = 0; c < BN; c += 4)
-                        *reinterpret_cast<float4*>(crow + c) = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
-                } else {
-                    for (int c = 0; c < nv; ++c) crow[c] = acc[c];
+                        for (int u = 0; u < 8; ++u) {
+                            const int rr = ((i + u) * 128 + et) / (BN / 2), m = m0 + rr;
+                            old[u] = make_float2(0.f, 0.f);
+                            if (m < a.M) {
+                                const float* cp = a.C + (size_t)m * a.ldc + n0 + c2;
+                                if (full) old[u] = __ldcg(reinterpret_cast<const float2*>(cp));
+                                else {
+                                    if (c2 < nv) old[u].x = __ldcg(cp);
+                                    if (c2 + 1 < nv) old[u].y = __ldcg(cp + 1);
+                                }
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        const int rr = ((i + u) * 128 + et) / (BN / 2), m = m0 + rr;
+                        if (m >= a.M) continue;
+                        float2 v = make_float2(T[rr * TP + c2], T[rr * TP + c2 + 1]);
+                        if (a.mode == QW_EPI_RESID) { v.x += old[u].x; v.y += old[u].y; }
+                        float* cp = a.C + (size_t)m * a.ldc + n0 + c2;
+                        if (full) *reinterpret_cast<float2*>(cp) = v;
+                        else {
+                            if (c2 < nv) cp[0] = v.x;
+                            if (c2 + 1 < nv) cp[1] = v.y;
+                        }
+                    }
                 }
             }
         }
