@@ -69,10 +69,6 @@ struct sa_qwen3 {
     float* logits = nullptr;             // [logits_rows, V]
     int logits_rows = 0;
     int64_t* ids = nullptr;              // [M]
-    float* gemm_ws = nullptr;            // split-K partials
-    size_t gemm_ws_floats = 0;
-    unsigned* gemm_cnt = nullptr;
-    size_t gemm_cnt_n = 0;
     // streams: `cur` is where launches go (the context's stream, or the
     // model's own capturable stream inside graph-using calls)
     cudaStream_t own = nullptr;
@@ -150,7 +146,7 @@ static void free_model(sa_qwen3* m) {
     cudaFree(m->kc); cudaFree(m->vc); cudaFree(m->cos_t); cudaFree(m->sin_t);
     cudaFree(m->x); cudaFree(m->qkv); cudaFree(m->q); cudaFree(m->attn); cudaFree(m->act); cudaFree(m->xn);
     cudaFree(m->a_hi); cudaFree(m->a_lo); cudaFree(m->b_hi); cudaFree(m->b_lo);
-    cudaFree(m->logits); cudaFree(m->ids); cudaFree(m->gemm_ws); cudaFree(m->gemm_cnt);
+    cudaFree(m->logits); cudaFree(m->ids);
     cudaFree(m->d_state); cudaFree(m->d_toks); cudaFree(m->dec_scratch); cudaFree(m->dec_cnt); cudaFree(m->d_amax);
     cudaFree(m->d_mlayers); cudaFree(m->mpart); cudaFree(m->mhead_cnt); cudaFree(m->mgbar);
     for (int r = 0; r < sa::TP_MAX; ++r)
@@ -214,46 +210,12 @@ static int ensure_logits(sa_qwen3* m, int rows) {
     return rc;
 }
 
-// Split-K so that a GEMM of this shape fills the GPU with >= ~1 CTA per SM.
-static int pick_splits(const sa_qwen3* m, int M, int N, int K) {
-    const int tiles = ((N + 63) / 64) * ((M + 127) / 128);
-    // at most 4 splits: the last CTA of a tile sums every split's partial
-    int s = 1;
-    while (tiles * s < m->ctx->num_sms && s * 2 <= K / 64 / 2 && s < 4) s *= 2;
-    return s;
-}
-
+// Prompt projection on the tensor cores with the tile / split plan for its shape.
 static int gemm(sa_qwen3* m, const __nv_bfloat16* hi, const __nv_bfloat16* lo, long long lda,
                 const __nv_bfloat16* w, int M, int N, int K, int mode, float* C, long long ldc,
                 __nv_bfloat16* ohi, __nv_bfloat16* olo, long long ldo) {
-    const int splits = mode == QW_EPI_SWIGLU ? 1 : pick_splits(m, M, N, K);
-    const size_t tiles = (size_t)((N + 63) / 64) * ((M + 127) / 128);
-    if (splits > 1) {
-        const size_t need = tiles * splits * 128 * 64;
-        if (need > m->gemm_ws_floats) {
-            SA_CUDA_TRY(cudaStreamSynchronize(m->cur));
-            invalidate_graphs(m);
-            cudaFree(m->gemm_ws);
-            m->gemm_ws = nullptr;
-            m->gemm_ws_floats = 0;
-            int rc = dalloc(&m->gemm_ws, need);
-            if (rc) return rc;
-            m->gemm_ws_floats = need;
-        }
-        if (tiles > m->gemm_cnt_n) {
-            SA_CUDA_TRY(cudaStreamSynchronize(m->cur));
-            invalidate_graphs(m);
-            cudaFree(m->gemm_cnt);
-            m->gemm_cnt = nullptr;
-            m->gemm_cnt_n = 0;
-            int rc = dalloc(&m->gemm_cnt, tiles);
-            if (rc) return rc;
-            SA_CUDA_TRY(cudaMemsetAsync(m->gemm_cnt, 0, tiles * sizeof(unsigned), m->cur));
-            m->gemm_cnt_n = tiles;
-        }
-    }
-    return gemm_launch(m->cur, m->ctx->status, hi, lo, lda, w, M, N, K, mode, C, ldc, ohi, olo, ldo,
-                       splits, m->gemm_ws, m->gemm_ws_floats, m->gemm_cnt, m->gemm_cnt_n);
+    const GemmPlan plan = gemm_plan(m->ctx->device, M, N, K, mode);
+    return gemm_launch(m->cur, m->ctx->status, hi, lo, lda, w, M, N, K, mode, C, ldc, ohi, olo, ldo, plan);
 }
 
 #define SA_RC(expr) do { int rc_ = (expr); if (rc_) return rc_; } while (0)
@@ -354,9 +316,8 @@ static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr
             SA_RC(gemm(m, m->a_hi, m->a_lo, H, L.wqkv, M, m->NQKV, H, QW_EPI_STORE, m->qkv, m->NQKV, nullptr, nullptr, 0));
             SA_RC(launch_qknorm_rope_append(st, m->qkv, M, m->hq, m->hkv, L.q_norm, L.k_norm, m->cos_t, m->sin_t, pos0,
                                             nullptr, shift, m->q, kc, vc, c.max_seq));
-            SA_RC(decode_multi_launch(st, m->ctx->status, m->q, m->QD, ka, va, (long long)c.max_seq * D, pos0 + 1, M, D,
-                                      m->hq, m->hkv, scale, m->attn, m->QD));
-            SA_RC(launch_split_hilo(st, m->attn, (size_t)M * m->QD, m->a_hi, m->a_lo));
+            SA_RC(prompt_attn_launch(st, m->q, m->QD, ka, va, (long long)c.max_seq * D, pos0 + 1, M, D, m->hq, m->hkv,
+                                     scale, nullptr, m->QD, m->a_hi, m->a_lo));
             if (tp) {
                 SA_RC(gemm(m, m->a_hi, m->a_lo, m->QD, L.wo, M, H, m->QD, QW_EPI_STORE, m->tp_part, H, nullptr, nullptr,
                            0));
@@ -458,6 +419,7 @@ int qwen3_create_model(sa_ctx* ctx, const sa_qwen3_config* cfg, int rank, int wo
     SA_CHECK_ARG(c.hkv % world == 0 && c.inter % (64 * world) == 0 && c.vocab >= world,
                  "sa_qwen3_create_tp: hkv=%d and inter/64=%d must divide over %d ranks", c.hkv, c.inter / 64, world);
     DeviceGuard guard(ctx->device);
+    gemm_prepare(ctx->device);   // occupancy queries outside any later stream capture
     sa_qwen3* m = new sa_qwen3();
     m->ctx = ctx;
     m->device = ctx->device;

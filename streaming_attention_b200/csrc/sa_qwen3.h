@@ -24,10 +24,18 @@ struct QkvEpi {
     unsigned* cnt = nullptr;   // [hq + hkv] arrival counters, zero between launches
 };
 
+// Prompt GEMM (sa_gemm.cu): output tile width and the number of CTAs of a
+// cluster that split K.
+struct GemmPlan {
+    int bn, splits;
+};
+// Query (once per device) how many clusters of each GEMM variant fit on the
+// device; call before any stream capture.
+void gemm_prepare(int device);
+GemmPlan gemm_plan(int device, int M, int N, int K, int mode);
 int gemm_launch(cudaStream_t st, int* status, const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo,
                 long long lda, const __nv_bfloat16* w, int M, int N, int K, int mode, float* C,
-                long long ldc, __nv_bfloat16* out_hi, __nv_bfloat16* out_lo, long long ldo, int splits,
-                float* ws, size_t ws_floats, unsigned* counters, size_t n_counters);
+                long long ldc, __nv_bfloat16* out_hi, __nv_bfloat16* out_lo, long long ldo, GemmPlan plan);
 
 // Multi-query causal attention over a head-major fp32 KV cache: query m of
 // n_q (q at q + m*q_stride, [hq, d]) attends rows [0, T0 + m] of each KV head;
@@ -37,6 +45,13 @@ int decode_multi_launch(cudaStream_t st, int* status, const float* q, long long 
                         const float* v, long long kv_head_stride, int T0, int n_q, int d, int hq, int hkv,
                         float scale, float* out, long long o_stride);
 
+// Causal attention of M prompt queries (q at q + m*q_stride, [hq, 128]) over
+// rows [0, T0 + m) of each KV head of a head-major fp32 cache; output fp32
+// (out) and/or bf16 hi/lo planes (out_hi/out_lo), row m at m*o_stride.
+// Defined in sa_prompt_attn.cu.
+int prompt_attn_launch(cudaStream_t st, const float* q, long long q_stride, const float* k, const float* v,
+                       long long kv_head_stride, int T0, int M, int d, int hq, int hkv, float scale, float* out,
+                       long long o_stride, __nv_bfloat16* out_hi, __nv_bfloat16* out_lo);
 // element-wise / GEMV launchers (sa_qwen3_kernels.cu)
 int launch_embedding(cudaStream_t st, const int64_t* ids, int M, const __nv_bfloat16* E, int V, int H, float* x,
                      int* status);
