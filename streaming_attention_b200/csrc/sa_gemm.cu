@@ -1,4 +1,4 @@
-// sa_gemm.cu -- tcgen05 GEMM for the Qwen3 projections:
+// sa_gemm.cu -- tcgen05 GEMM for the Qwen3 prompt projections:
 //     C[M, N] = A[M, K] . W[N, K]^T        (the reference's ops::linear,
 //                                           tensor_cpp/src/ops.cpp:315-369)
 // with W in bf16 (the weights) and A given as two bf16 terms A = A_hi + A_lo
@@ -10,18 +10,20 @@
 // 128-byte-swizzled stages; one lane issues tcgen05.mma into a BN-column TMEM
 // accumulator; four warps run the epilogue.
 //
-// Split-K runs inside a thread-block cluster: the `s` CTAs of a cluster share
-// one output tile, each accumulates a contiguous range of K blocks, parks its
-// fp32 partial tile in its own shared memory, and after a cluster barrier CTA
-// r sums rows [128 r / s, 128 (r + 1) / s) of all s partials through
-// distributed shared memory, in rank order (deterministic), and applies the
-// epilogue to those rows.  No global scratch and no single-CTA reduction.
-// Prompt GEMMs have M = 128 .. a few thousand rows, so at short prompts a
-// tile's weights are the only large operand: the host picks BN and s per
-// shape so that one wave of clusters covers the SMs with the fewest bytes per
-// CTA (weights + the activation block + the partial exchange).
+// Split-K: at prompt lengths of a few hundred tokens one 128-row tile per
+// weight slice cannot fill 148 SMs, so gridDim.z = s CTAs share a tile, each
+// accumulating a contiguous range of K blocks.  Their fp32 partial sums go to
+// s stacked planes part[z][M][N] by TMA tensor stores (staged in 128-byte
+// swizzled shared memory, so the TMEM -> shared writes are conflict-free),
+// and the NEXT kernel adds the s planes in plane order while it reads its
+// input anyway (qknorm_rope_append for QKV, the residual RMSNorm for o_proj /
+// down_proj, swiglu_hilo for gate/up; sa_qwen3_kernels.cu).  So a split GEMM
+// needs no cross-CTA synchronisation and the sum is deterministic.
+// (Exchanging partials inside a thread-block cluster measured 20-33 GB/s per
+// SM through distributed shared memory on B200; ~3-5 us per GEMM.)
 //
-// Epilogues:
+// Epilogues of unsplit GEMMs (s = 1), through a padded shared-memory tile so
+// every global access is coalesced:
 //   STORE   C = acc                                  (fp32)
 //   RESID   C += acc       (the residual stream, qwen3_ops.cpp:514,527)
 //   SWIGLU  W holds [gate(32) ; up(32)] row blocks; out[:, n0/2 + i] =
@@ -33,9 +35,8 @@
 // to global memory comes after it.
 #include <cuda_bf16.h>
 #include <cmath>
-#include <mutex>
 #include <map>
-#include <tuple>
+#include <mutex>
 
 #include "sa_internal.h"
 #include "sa_tc.cuh"
@@ -52,10 +53,11 @@ struct Cfg {
     static constexpr int STAGES = BN == 256 ? 3 : 4;
     static constexpr int W_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = 2 * A_BYTES + W_BYTES;
-    static constexpr int TP = BN + 4;                        // partial-tile row pitch (floats)
+    static constexpr int TP = BN + 4;                        // padded epilogue tile row pitch (floats)
     static constexpr int T_BYTES = BM * TP * 4;
     static constexpr int PIPE = STAGES * STAGE_BYTES;
-    static constexpr int OFF_BAR = ((PIPE > T_BYTES ? PIPE : T_BYTES) + 1023) / 1024 * 1024;
+    static_assert(T_BYTES <= PIPE && BN * BM * 4 <= PIPE, "epilogue staging must fit in the pipeline stages");
+    static constexpr int OFF_BAR = (PIPE + 1023) / 1024 * 1024;
     static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;  // + barriers + alignment slack
 };
 
@@ -75,27 +77,6 @@ struct Bars {
     uint32_t tmem_base;
     int abort;
 };
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// shared::cluster address of the same shared-memory offset in CTA `rank`
-__device__ __forceinline__ uint32_t map_rank(uint32_t saddr, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-    return r;
-}
-__device__ __forceinline__ float4 ld_dsmem4(uint32_t caddr) {
-    float4 v;
-    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(caddr) : "memory");
-    return v;
-}
 
 __device__ __forceinline__ bool wait_ab(uint64_t* bar, uint32_t parity, volatile int* abort, int* status) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -125,23 +106,10 @@ __device__ __forceinline__ void store_hilo4(__nv_bfloat16* hi, __nv_bfloat16* lo
     *reinterpret_cast<uint2*>(lo) = ul;
 }
 
-// Sum of the s partial tiles' float4 at byte offset `off` (rank order).
-__device__ __forceinline__ float4 cluster_sum4(uint32_t t_base, uint32_t off, int s) {
-    float4 v[MAX_SPLIT];
-#pragma unroll
-    for (int z = 0; z < MAX_SPLIT; ++z)
-        if (z < s) v[z] = ld_dsmem4(map_rank(t_base + off, (uint32_t)z));
-    float4 acc = v[0];
-#pragma unroll
-    for (int z = 1; z < MAX_SPLIT; ++z)
-        if (z < s) { acc.x += v[z].x; acc.y += v[z].y; acc.z += v[z].z; acc.w += v[z].w; }
-    return acc;
-}
-
 template <int BN>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
-            const __grid_constant__ CUtensorMap tw, const Args a) {
+            const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tpart, const Args a) {
     using C_ = Cfg<BN>;
     constexpr int STAGES = C_::STAGES, STAGE_BYTES = C_::STAGE_BYTES, TP = C_::TP;
     extern __shared__ unsigned char smem_raw[];
@@ -151,11 +119,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ C
     volatile int* abort = &B->abort;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
-    const int s = gridDim.z;                        // the cluster spans the split dimension
-    const int rank = s > 1 ? (int)cluster_rank() : 0;
+    const int s = gridDim.z, z = blockIdx.z;
     const int kblocks = a.K / BK, kbase = kblocks / s, krem = kblocks % s;
-    const int nkb = kbase + (rank < krem ? 1 : 0);
-    const int kb0 = rank * kbase + min(rank, krem);
+    const int nkb = kbase + (z < krem ? 1 : 0);
+    const int kb0 = z * kbase + min(z, krem);
 
     if (tid == 0) {
         for (int i = 0; i < STAGES; ++i) {
@@ -233,190 +200,207 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ C
         __syncwarp();
     } else {
         // ------------------------------------------------ epilogue warps 2..5
-        // accumulator: TMEM -> registers (thread = row) -> partial tile T in
-        // this CTA's shared memory (the pipeline stages are idle once `done`
-        // fired: every MMA, and so every load it consumed, has completed)
+        // The accumulator goes TMEM -> registers (thread = row) -> shared
+        // memory; the pipeline stages are idle once `done` fired (every MMA,
+        // and so every load it consumed, has completed).
         pdl_wait();
+        const int et = tid - 64;                       // 0..127
         const int quad = warp & 3;
         const int row = quad * 32 + lane;
-        float* T = reinterpret_cast<float*>(sm);       // [BM][TP] fp32
         const bool ok = wait_ab(&B->done, 0, abort, a.status);
         tc::fence_after_sync();
-        if (ok) {
-            uint32_t r[32];
+        if (s > 1) {
+            // split partial: 32-column boxes of 128 rows x 128 bytes, 128-byte
+            // swizzle (16-byte chunk q of row r at chunk q ^ (r % 8)), stored
+            // to plane z by TMA
+            if (ok) {
+                uint32_t r[32];
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 32) {
-                tc::tmem_ld32(tacc + ((uint32_t)(quad * 32) << 16) + c0, r);
-                tc::tmem_wait_ld();
-                float4* dst = reinterpret_cast<float4*>(T + row * TP + c0);
+                for (int j = 0; j < BN / 32; ++j) {
+                    tc::tmem_ld32(tacc + ((uint32_t)(quad * 32) << 16) + 32 * j, r);
+                    tc::tmem_wait_ld();
+                    unsigned char* box = sm + j * (BM * 128) + row * 128;
 #pragma unroll
-                for (int c = 0; c < 8; ++c)
-                    dst[c] = nkb > 0 ? make_float4(__uint_as_float(r[4 * c]), __uint_as_float(r[4 * c + 1]),
-                                                   __uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3]))
-                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int q = 0; q < 8; ++q)
+                        *reinterpret_cast<float4*>(box + ((q ^ (row & 7)) << 4)) =
+                            make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                        __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+                }
+                tc::fence_proxy_async_all();
             }
-        }
-    }
-    // every partial tile of the cluster is in place after this barrier
-    tc::fence_before_sync();
-    if (s > 1) cluster_sync_all();
-    else __syncthreads();
-
-    if (warp >= 2 && !*abort) {
-        const int et = tid - 64;                       // 0..127
-        const uint32_t t_base = smem_u32(sm);
-        const float* T = reinterpret_cast<const float*>(sm);
-        const int r0 = BM * rank / s, r1 = BM * (rank + 1) / s;
-        if (a.mode == QW_EPI_SWIGLU) {
-            // item = (row, 4 outputs); output j of the tile pairs gate column
-            // 64 (j / 32) + j % 32 with up column 64 (j / 32) + 32 + j % 32
-            constexpr int J4 = BN / 8;
-            const int items = (r1 - r0) * J4;
-            for (int it = et; it < items; it += 128) {
-                const int rr = r0 + it / J4, j = (it % J4) * 4, m = m0 + rr;
-                const int gc = (j / 32) * 64 + (j % 32);
-                float4 g, u;
-                if (s > 1) {
-                    g = cluster_sum4(t_base, (uint32_t)(rr * TP + gc) * 4u, s);
-                    u = cluster_sum4(t_base, (uint32_t)(rr * TP + gc + 32) * 4u, s);
-                } else {
-                    g = *reinterpret_cast<const float4*>(T + rr * TP + gc);
-                    u = *reinterpret_cast<const float4*>(T + rr * TP + gc + 32);
-                }
-                if (m < a.M) {
-                    const float4 v = make_float4(silu(g.x) * u.x, silu(g.y) * u.y, silu(g.z) * u.z, silu(g.w) * u.w);
-                    const size_t o = (size_t)m * a.ldo + n0 / 2 + j;
-                    store_hilo4(a.out_hi + o, a.out_lo + o, v);
-                }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (et == 0 && ok && !*abort) {
+                for (int j = 0; j < BN / 32; ++j) tc::tma_store_3d(&tpart, sm + j * (BM * 128), n0 + 32 * j, m0, z);
+                tc::bulk_commit_wait_read();
             }
         } else {
-            constexpr int C4 = BN / 4;
-            const int items = (r1 - r0) * C4, nv = a.N - n0;
-            const bool vec = (a.ldc & 3) == 0;
-            for (int it = et; it < items; it += 128) {
-                const int rr = r0 + it / C4, c = (it % C4) * 4, m = m0 + rr;
-                const float4 v = s > 1 ? cluster_sum4(t_base, (uint32_t)(rr * TP + c) * 4u, s)
-                                       : *reinterpret_cast<const float4*>(T + rr * TP + c);
-                if (m >= a.M || c >= nv) continue;
-                float* cp = a.C + (size_t)m * a.ldc + n0 + c;
-                if (vec && c + 4 <= nv) {
-                    float4 o = v;
-                    if (a.mode == QW_EPI_RESID) {
-                        const float4 old = __ldcg(reinterpret_cast<const float4*>(cp));
-                        o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+            float* T = reinterpret_cast<float*>(sm);   // [BM][TP] fp32
+            if (ok) {
+                uint32_t r[32];
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    tc::tmem_ld32(tacc + ((uint32_t)(quad * 32) << 16) + c0, r);
+                    tc::tmem_wait_ld();
+                    float4* dst = reinterpret_cast<float4*>(T + row * TP + c0);
+#pragma unroll
+                    for (int c = 0; c < 8; ++c)
+                        dst[c] = make_float4(__uint_as_float(r[4 * c]), __uint_as_float(r[4 * c + 1]),
+                                             __uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3]));
+                }
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (ok && !*abort) {
+                if (a.mode == QW_EPI_SWIGLU) {
+                    // item = (row, 4 outputs); output j of the tile pairs gate
+                    // column 64 (j / 32) + j % 32 with up column + 32
+                    constexpr int J4 = BN / 8;
+                    for (int it = et; it < BM * J4; it += 128) {
+                        const int rr = it / J4, j = (it % J4) * 4, m = m0 + rr;
+                        if (m >= a.M) continue;
+                        const int gc = (j / 32) * 64 + (j % 32);
+                        const float4 g = *reinterpret_cast<const float4*>(T + rr * TP + gc);
+                        const float4 u = *reinterpret_cast<const float4*>(T + rr * TP + gc + 32);
+                        const float4 v = make_float4(silu(g.x) * u.x, silu(g.y) * u.y, silu(g.z) * u.z,
+                                                     silu(g.w) * u.w);
+                        const size_t o = (size_t)m * a.ldo + n0 / 2 + j;
+                        store_hilo4(a.out_hi + o, a.out_lo + o, v);
                     }
-                    *reinterpret_cast<float4*>(cp) = o;
                 } else {
-                    const float vv[4] = {v.x, v.y, v.z, v.w};
-                    for (int u = 0; u < 4 && c + u < nv; ++u)
-                        cp[u] = a.mode == QW_EPI_RESID ? cp[u] + vv[u] : vv[u];
+                    // a warp covers one row's BN columns as float4; residual
+                    // loads are issued four rows at a time before any store
+                    constexpr int C4 = BN / 4;
+                    const int nv = a.N - n0;
+                    const bool vec = (a.ldc & 3) == 0;
+                    const bool resid = a.mode == QW_EPI_RESID;
+                    for (int it0 = et; it0 < BM * C4; it0 += 4 * 128) {
+                        float4 old[4];
+#pragma unroll
+                        for (int b = 0; b < 4; ++b) {
+                            const int it = it0 + b * 128, rr = it / C4, c = (it % C4) * 4, m = m0 + rr;
+                            old[b] = make_float4(0.f, 0.f, 0.f, 0.f);
+                            if (resid && vec && it < BM * C4 && m < a.M && c + 4 <= nv)
+                                old[b] = __ldcg(reinterpret_cast<const float4*>(a.C + (size_t)m * a.ldc + n0 + c));
+                        }
+#pragma unroll
+                        for (int b = 0; b < 4; ++b) {
+                            const int it = it0 + b * 128, rr = it / C4, c = (it % C4) * 4, m = m0 + rr;
+                            if (it >= BM * C4 || m >= a.M || c >= nv) continue;
+                            const float4 v = *reinterpret_cast<const float4*>(T + rr * TP + c);
+                            float* cp = a.C + (size_t)m * a.ldc + n0 + c;
+                            if (vec && c + 4 <= nv) {
+                                float4 o = v;
+                                if (resid) { o.x += old[b].x; o.y += old[b].y; o.z += old[b].z; o.w += old[b].w; }
+                                *reinterpret_cast<float4*>(cp) = o;
+                            } else {
+                                const float vv[4] = {v.x, v.y, v.z, v.w};
+                                for (int q = 0; q < 4 && c + q < nv; ++q) cp[q] = resid ? cp[q] + vv[q] : vv[q];
+                            }
+                        }
+                    }
                 }
             }
         }
     }
-    // no CTA leaves (freeing its partial tile) while a peer may still read it
     tc::fence_before_sync();
-    if (s > 1) cluster_sync_all();
-    else __syncthreads();
+    __syncthreads();
     if (warp == 1) {
         tc::fence_after_sync();
         tc::tmem_dealloc(tacc, BN);
     }
 }
 
-// ---------------------------------------------------------------- planning
-// Clusters of `s` CTAs of the BN variant that fit on the device at once
-// (cudaOccupancyMaxActiveClusters), cached per device.
+// CTAs of the BN variant that fit on one SM, cached per device.
 template <int BN>
-int max_clusters(int device, int s) {
+int ctas_per_sm(int device) {
     static std::mutex mu;
-    static std::map<std::pair<int, int>, int> cache;
+    static std::map<int, int> cache;
     std::lock_guard<std::mutex> lk(mu);
-    auto it = cache.find({device, s});
+    auto it = cache.find(device);
     if (it != cache.end()) return it->second;
     int n = 0;
-    if (set_smem_attr_once((const void*)gemm_kernel<BN>, Cfg<BN>::SMEM_BYTES) == SA_OK) {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(1, 1, s);
-        cfg.blockDim = dim3(THREADS);
-        cfg.dynamicSmemBytes = Cfg<BN>::SMEM_BYTES;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 1;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = s;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        if (cudaOccupancyMaxActiveClusters(&n, gemm_kernel<BN>, &cfg) != cudaSuccess) n = 0;
+    if (set_smem_attr_once((const void*)gemm_kernel<BN>, Cfg<BN>::SMEM_BYTES) != SA_OK ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemm_kernel<BN>, THREADS, Cfg<BN>::SMEM_BYTES) !=
+            cudaSuccess) {
         cudaGetLastError();
-    } else {
         clear_error();
+        n = 0;
     }
-    cache[{device, s}] = n;
+    cache[device] = n;
     return n;
 }
 
-int max_clusters_bn(int bn, int device, int s) {
-    return bn == 64 ? max_clusters<64>(device, s) : bn == 128 ? max_clusters<128>(device, s)
-                                                             : max_clusters<256>(device, s);
+int ctas_per_sm_bn(int bn, int device) {
+    return bn == 64 ? ctas_per_sm<64>(device) : bn == 128 ? ctas_per_sm<128>(device) : ctas_per_sm<256>(device);
 }
 
 }  // namespace gm
 
 void gemm_prepare(int device) {
-    for (int bn : {64, 128, 256})
-        for (int s = 1; s <= gm::MAX_SPLIT; ++s) gm::max_clusters_bn(bn, device, s);
+    for (int bn : {64, 128, 256}) gm::ctas_per_sm_bn(bn, device);
 }
 
-// Tile width and split count for one GEMM: the fewest bytes a CTA moves per
-// wave of co-resident clusters (activation block + weight tile per K block,
-// plus its share of the partial-tile exchange), times the number of waves.
-GemmPlan gemm_plan(int device, int M, int N, int K, int mode) {
+// Tile width and split count for one GEMM.  Cost per wave of resident CTAs =
+// the bytes one CTA streams (activation block + weight tile per K block) plus,
+// for split plans, the partial planes the next kernel reads back (spread over
+// the SMs, charged twice: plain loads run at about half the bulk-copy rate).
+// `split_ok` is false where the consumer of the output cannot add planes.
+GemmPlan gemm_plan(int device, int num_sms, int M, int N, int K, bool split_ok) {
     GemmPlan best{64, 1};
     double best_cost = 1e30;
     const int mt = (M + gm::BM - 1) / gm::BM, kb = K / gm::BK;
     for (int bn : {64, 128, 256}) {
+        const int per_sm = gm::ctas_per_sm_bn(bn, device);
+        if (per_sm <= 0) continue;
         const int nt = (N + bn - 1) / bn;
-        for (int s = 1; s <= gm::MAX_SPLIT && s <= kb; ++s) {
-            const int cap = gm::max_clusters_bn(bn, device, s);
-            if (cap <= 0) continue;
-            const long long clusters = (long long)nt * mt;
-            const long long waves = (clusters + cap - 1) / cap;
+        for (int s = 1; s <= (split_ok ? gm::MAX_SPLIT : 1) && s <= kb; ++s) {
+            const long long ctas = (long long)nt * mt * s;
+            const long long slots = (long long)num_sms * per_sm;
+            const long long waves = (ctas + slots - 1) / slots;
             const double kbs = (double)((kb + s - 1) / s);
             const double main_b = kbs * gm::BK * (gm::BM * 4.0 + bn * 2.0);
-            const double red_b = s > 1 ? gm::BM * bn * 4.0 * (s - 1) / s : 0.0;
-            const double cost = (double)waves * (main_b + red_b + 65536.0);
+            const double planes = s > 1 ? 2.0 * s * (double)M * N * 4.0 / num_sms : 0.0;
+            const double cost = (double)waves * (main_b + 65536.0) + planes;
             if (cost < best_cost * 0.98) {
                 best_cost = cost;
                 best = GemmPlan{bn, s};
             }
         }
     }
-    (void)mode;
     return best;
 }
 
 // C-side launcher used by the Qwen3 forward.  a_hi/a_lo: [M, K] bf16 row-major
-// (lda elements per row); w: [N, K] bf16.  No scratch memory: split-K partials
-// are exchanged inside the cluster.
+// (lda elements per row); w: [N, K] bf16.  plan.splits > 1 writes the split
+// partials to planes part[z][M][N] (part_floats >= splits * M * N) instead of
+// applying `mode`.
 int gemm_launch(cudaStream_t st, int* status, const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo,
                 long long lda, const __nv_bfloat16* w, int M, int N, int K, int mode, float* C,
-                long long ldc, __nv_bfloat16* out_hi, __nv_bfloat16* out_lo, long long ldo, GemmPlan plan) {
+                long long ldc, __nv_bfloat16* out_hi, __nv_bfloat16* out_lo, long long ldo, GemmPlan plan,
+                float* part, size_t part_floats) {
     SA_CHECK_ARG(M > 0 && N > 0 && K > 0 && K % gm::BK == 0, "gemm: M=%d N=%d K=%d", M, N, K);
     SA_CHECK_ARG(plan.bn == 64 || plan.bn == 128 || plan.bn == 256, "gemm: tile width %d", plan.bn);
     SA_CHECK_ARG(plan.splits >= 1 && plan.splits <= gm::MAX_SPLIT && plan.splits <= K / gm::BK,
                  "gemm: %d splits", plan.splits);
-    SA_CHECK_ARG(mode != QW_EPI_SWIGLU || N % plan.bn == 0, "gemm: SwiGLU needs N %% %d == 0", plan.bn);
-    SA_CHECK_ARG(mode == QW_EPI_SWIGLU ? (ldo % 4 == 0 && ((uintptr_t)out_hi & 7) == 0 && ((uintptr_t)out_lo & 7) == 0)
-                                       : (((uintptr_t)C & 15) == 0),
-                 "gemm: output alignment");
+    const bool split = plan.splits > 1;
+    if (split) {
+        SA_CHECK_ARG(part && ((uintptr_t)part & 15) == 0 && (size_t)plan.splits * M * N <= part_floats && N % 4 == 0,
+                     "gemm: partial planes too small (%d x %d x %d)", plan.splits, M, N);
+    } else {
+        SA_CHECK_ARG(mode != QW_EPI_SWIGLU || N % plan.bn == 0, "gemm: SwiGLU needs N %% %d == 0", plan.bn);
+        SA_CHECK_ARG(mode == QW_EPI_SWIGLU
+                         ? (ldo % 4 == 0 && ((uintptr_t)out_hi & 7) == 0 && ((uintptr_t)out_lo & 7) == 0)
+                         : (C && ((uintptr_t)C & 15) == 0),
+                     "gemm: output alignment");
+    }
     const int bn = plan.bn, s = plan.splits;
     const int nt = (N + bn - 1) / bn, mt = (M + gm::BM - 1) / gm::BM;
-    CUtensorMap mh, ml, mw;
+    CUtensorMap mh, ml, mw, mp;
     int rc = cached_tmap_2d_bf16(&mh, a_hi, (uint64_t)M, (uint64_t)K, (uint64_t)lda, gm::BM, gm::BK);
     if (!rc) rc = cached_tmap_2d_bf16(&ml, a_lo, (uint64_t)M, (uint64_t)K, (uint64_t)lda, gm::BM, gm::BK);
     if (!rc) rc = cached_tmap_2d_bf16(&mw, w, (uint64_t)N, (uint64_t)K, (uint64_t)K, (uint32_t)bn, gm::BK);
+    if (!rc && split) rc = cached_tmap_3d_f32_planes(&mp, part, (uint64_t)M, (uint64_t)N, (uint64_t)s);
     if (rc) return rc;
+    if (!split) mp = mw;   // unused by unsplit launches
     gm::Args a;
     a.M = M; a.N = N; a.K = K; a.mode = mode;
     a.C = C; a.ldc = ldc; a.out_hi = out_hi; a.out_lo = out_lo; a.ldo = ldo;
@@ -431,22 +415,13 @@ int gemm_launch(cudaStream_t st, int* status, const __nv_bfloat16* a_hi, const _
     cfg.blockDim = dim3(gm::THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[2];
-    int na = 0;
-    attr[na].id = cudaLaunchAttributeClusterDimension;
-    attr[na].val.clusterDim.x = 1;
-    attr[na].val.clusterDim.y = 1;
-    attr[na].val.clusterDim.z = s;
-    ++na;
-    static const bool no_pdl = std::getenv("SA_NO_PDL") != nullptr;
-    if (!no_pdl) {
-        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[na].val.programmaticStreamSerializationAllowed = 1;
-        ++na;
-    }
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = na;
-    void* args[] = {(void*)&mh, (void*)&ml, (void*)&mw, (void*)&a};
+    static const bool no_pdl = std::getenv("SA_NO_PDL") != nullptr;
+    cfg.numAttrs = no_pdl ? 0 : 1;
+    void* args[] = {(void*)&mh, (void*)&ml, (void*)&mw, (void*)&mp, (void*)&a};
     SA_CUDA_TRY(cudaLaunchKernelExC(&cfg, fn, args));
     return SA_OK;
 }

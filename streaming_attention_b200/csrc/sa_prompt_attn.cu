@@ -4,17 +4,17 @@
 // create_causal_mask, :240-259; GQA by head index as repeat_kv, :194-234).
 //
 // Query m of the prompt (RoPE position pos0 + m) attends cache rows
-// [0, T0 + m) with T0 = pos0 + 1.  One CTA serves QV = 16 query vectors that
-// read the same KV head: 16 / G consecutive prompt rows x the G = hq / hkv
-// query heads of that KV head.  The CTA streams the KV head's rows once, in
+// [0, T0 + m) with T0 = pos0 + 1.  One CTA serves QV = 8 query vectors that
+// read the same KV head: 8 / G consecutive prompt rows x the G = hq / hkv
+// query heads of that KV head (two vectors per warp, four warps).  The CTA streams the KV head's rows once, in
 // 32-row tiles (cp.async, double-buffered), for all 16 vectors:
-//   * scores: warp w owns vectors 4w..4w+3, lane = key of the tile; q rows are
+//   * scores: warp w owns vectors 2w, 2w+1, lane = key of the tile; q rows are
 //     shared-memory broadcasts, K rows are padded to 132 floats so the 32
 //     lanes' float4 reads hit distinct banks;
 //   * online softmax in the exp2 domain (scale * log2 e folded into q), per
 //     vector, reduced across the warp with shuffles;
-//   * P.V: lane owns 4 consecutive output dims of the warp's 4 vectors; each
-//     key is one float4 of V and one broadcast float4 of the 4 vectors' p.
+//   * P.V: lane owns 4 consecutive output dims of the warp's 2 vectors; each
+//     key is one float4 of V and one broadcast float2 of the 2 vectors' p.
 // fp32 throughout (CUDA cores), like the reference.  The output is written as
 // fp32 and/or as the bf16 hi/lo planes the o_proj GEMM reads.
 #include <cuda_bf16.h>
@@ -28,9 +28,9 @@
 namespace sa {
 namespace pa {
 
-constexpr int D = 128, QV = 16, KT = 32, KP = D + 4, THREADS = 128;
+constexpr int D = 128, VPW = 2, NWARP = 4, QV = VPW * NWARP, KT = 32, KP = D + 4, THREADS = 32 * NWARP;
 constexpr float LOG2E = 1.4426950408889634f;
-constexpr int SMEM_FLOATS = QV * D + 2 * KT * KP + 2 * KT * D + 4 * KT * 4;
+constexpr int SMEM_FLOATS = QV * D + 2 * KT * KP + 2 * KT * D + NWARP * KT * VPW;
 constexpr int SMEM_BYTES = SMEM_FLOATS * 4;
 
 struct Args {
@@ -60,7 +60,7 @@ prompt_attn_kernel(const Args a) {
     float* Qs = reinterpret_cast<float*>(smem4);     // [QV][D]
     float* Ks = Qs + QV * D;                          // [2][KT][KP]
     float* Vs = Ks + 2 * KT * KP;                     // [2][KT][D]
-    float* Ps = Vs + 2 * KT * D;                      // [4 warps][KT][4]
+    float* Ps = Vs + 2 * KT * D;                      // [NWARP][KT][VPW]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int h = blockIdx.y;
     // heaviest (latest) query blocks first
@@ -102,16 +102,16 @@ prompt_attn_kernel(const Args a) {
     };
     load_tile(0, 0);
 
-    // per warp: vectors 4w + i; per lane: output dims 4 lane .. 4 lane + 3
-    float mrun[4], lrun[4];
-    float4 o[4];
-    int lim[4];   // keys vector i may attend
+    // per warp: vectors VPW w + i; per lane: output dims 4 lane .. 4 lane + 3
+    float mrun[VPW], lrun[VPW];
+    float4 o[VPW];
+    int lim[VPW];   // keys vector i may attend
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < VPW; ++i) {
         mrun[i] = -INFINITY;
         lrun[i] = 0.f;
         o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        const int j = warp * 4 + i, m = m0 + j / a.G;
+        const int j = warp * VPW + i, m = m0 + j / a.G;
         lim[i] = m < m_end ? a.T0 + m : 0;
     }
     for (int t = 0; t < n_tiles; ++t) {
@@ -125,13 +125,15 @@ prompt_attn_kernel(const Args a) {
         const float* kt = Ks + (t & 1) * KT * KP;
         const float* vt = Vs + (t & 1) * KT * D;
         // scores s[i] = q_i . k_lane
-        float s[4] = {0.f, 0.f, 0.f, 0.f};
-        const float* qw = Qs + warp * 4 * D;
+        float s[VPW];
+#pragma unroll
+        for (int i = 0; i < VPW; ++i) s[i] = 0.f;
+        const float* qw = Qs + warp * VPW * D;
 #pragma unroll 8
         for (int d = 0; d < D; d += 4) {
             const float4 kv = *reinterpret_cast<const float4*>(kt + lane * KP + d);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
+            for (int i = 0; i < VPW; ++i) {
                 const float4 qv = *reinterpret_cast<const float4*>(qw + i * D + d);
                 s[i] = fmaf(qv.x, kv.x, s[i]);
                 s[i] = fmaf(qv.y, kv.y, s[i]);
@@ -140,9 +142,9 @@ prompt_attn_kernel(const Args a) {
             }
         }
         const int key = t * KT + lane;
-        float p[4];
+        float p[VPW];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < VPW; ++i) {
             const float si = key < lim[i] ? s[i] : -INFINITY;
             float mx = si;
 #pragma unroll
@@ -158,27 +160,24 @@ prompt_attn_kernel(const Args a) {
             mrun[i] = mnew;
             o[i].x *= alpha; o[i].y *= alpha; o[i].z *= alpha; o[i].w *= alpha;
         }
-        float* pw = Ps + warp * KT * 4;
-        *reinterpret_cast<float4*>(pw + lane * 4) = make_float4(p[0], p[1], p[2], p[3]);
+        float* pw = Ps + warp * KT * VPW;
+        static_assert(VPW == 2, "p is stored as float2");
+        *reinterpret_cast<float2*>(pw + lane * VPW) = make_float2(p[0], p[1]);
         __syncwarp();
 #pragma unroll 8
         for (int kk = 0; kk < KT; ++kk) {
-            const float4 pk = *reinterpret_cast<const float4*>(pw + kk * 4);
+            const float2 pk = *reinterpret_cast<const float2*>(pw + kk * VPW);
             const float4 vv = *reinterpret_cast<const float4*>(vt + kk * D + lane * 4);
             o[0].x = fmaf(pk.x, vv.x, o[0].x); o[0].y = fmaf(pk.x, vv.y, o[0].y);
             o[0].z = fmaf(pk.x, vv.z, o[0].z); o[0].w = fmaf(pk.x, vv.w, o[0].w);
             o[1].x = fmaf(pk.y, vv.x, o[1].x); o[1].y = fmaf(pk.y, vv.y, o[1].y);
             o[1].z = fmaf(pk.y, vv.z, o[1].z); o[1].w = fmaf(pk.y, vv.w, o[1].w);
-            o[2].x = fmaf(pk.z, vv.x, o[2].x); o[2].y = fmaf(pk.z, vv.y, o[2].y);
-            o[2].z = fmaf(pk.z, vv.z, o[2].z); o[2].w = fmaf(pk.z, vv.w, o[2].w);
-            o[3].x = fmaf(pk.w, vv.x, o[3].x); o[3].y = fmaf(pk.w, vv.y, o[3].y);
-            o[3].z = fmaf(pk.w, vv.z, o[3].z); o[3].w = fmaf(pk.w, vv.w, o[3].w);
         }
         __syncthreads();   // the buffer of tile t is refilled at t + 2
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int j = warp * 4 + i, m = m0 + j / a.G, head = h * a.G + j % a.G;
+    for (int i = 0; i < VPW; ++i) {
+        const int j = warp * VPW + i, m = m0 + j / a.G, head = h * a.G + j % a.G;
         if (m >= m_end) continue;
         const float inv = lrun[i] > 0.f ? 1.f / lrun[i] : 0.f;
         const float4 r = make_float4(o[i].x * inv, o[i].y * inv, o[i].z * inv, o[i].w * inv);
@@ -207,7 +206,7 @@ int prompt_attn_launch(cudaStream_t st, const float* q, long long q_stride, cons
     SA_CHECK_ARG(M >= 1 && T0 >= 1 && hkv >= 1 && hq % hkv == 0, "prompt attention: M=%d T0=%d hq=%d hkv=%d", M, T0,
                  hq, hkv);
     const int G = hq / hkv;
-    SA_CHECK_ARG(G == 1 || G == 2 || G == 4 || G == 8 || G == 16, "prompt attention: hq/hkv=%d", G);
+    SA_CHECK_ARG(G == 1 || G == 2 || G == 4 || G == 8, "prompt attention: hq/hkv=%d", G);
     SA_CHECK_ARG(q_stride % 4 == 0 && kv_head_stride % 4 == 0 && o_stride % 4 == 0 && ((uintptr_t)q & 15) == 0 &&
                      ((uintptr_t)k & 15) == 0 && ((uintptr_t)v & 15) == 0 && ((uintptr_t)out & 15) == 0 &&
                      ((uintptr_t)out_hi & 7) == 0 && ((uintptr_t)out_lo & 7) == 0,

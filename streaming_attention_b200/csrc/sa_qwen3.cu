@@ -69,6 +69,8 @@ struct sa_qwen3 {
     float* logits = nullptr;             // [logits_rows, V]
     int logits_rows = 0;
     int64_t* ids = nullptr;              // [M]
+    float* gemm_ws = nullptr;            // split-K partial planes of the prompt GEMMs
+    size_t gemm_ws_floats = 0;
     // streams: `cur` is where launches go (the context's stream, or the
     // model's own capturable stream inside graph-using calls)
     cudaStream_t own = nullptr;
@@ -146,7 +148,7 @@ static void free_model(sa_qwen3* m) {
     cudaFree(m->kc); cudaFree(m->vc); cudaFree(m->cos_t); cudaFree(m->sin_t);
     cudaFree(m->x); cudaFree(m->qkv); cudaFree(m->q); cudaFree(m->attn); cudaFree(m->act); cudaFree(m->xn);
     cudaFree(m->a_hi); cudaFree(m->a_lo); cudaFree(m->b_hi); cudaFree(m->b_lo);
-    cudaFree(m->logits); cudaFree(m->ids);
+    cudaFree(m->logits); cudaFree(m->ids); cudaFree(m->gemm_ws);
     cudaFree(m->d_state); cudaFree(m->d_toks); cudaFree(m->dec_scratch); cudaFree(m->dec_cnt); cudaFree(m->d_amax);
     cudaFree(m->d_mlayers); cudaFree(m->mpart); cudaFree(m->mhead_cnt); cudaFree(m->mgbar);
     for (int r = 0; r < sa::TP_MAX; ++r)
@@ -210,15 +212,33 @@ static int ensure_logits(sa_qwen3* m, int rows) {
     return rc;
 }
 
-// Prompt projection on the tensor cores with the tile / split plan for its shape.
+// Prompt projection on the tensor cores with the tile / split plan for its
+// shape.  With split_ok the plan may split K: then the partial planes are left
+// in m->gemm_ws for the next kernel and *splits (when given) is the plane
+// count; otherwise `mode` is applied and *splits is 1.
 static int gemm(sa_qwen3* m, const __nv_bfloat16* hi, const __nv_bfloat16* lo, long long lda,
                 const __nv_bfloat16* w, int M, int N, int K, int mode, float* C, long long ldc,
-                __nv_bfloat16* ohi, __nv_bfloat16* olo, long long ldo) {
-    const GemmPlan plan = gemm_plan(m->ctx->device, M, N, K, mode);
-    return gemm_launch(m->cur, m->ctx->status, hi, lo, lda, w, M, N, K, mode, C, ldc, ohi, olo, ldo, plan);
+                __nv_bfloat16* ohi, __nv_bfloat16* olo, long long ldo, bool split_ok = false, int* splits = nullptr) {
+    const GemmPlan plan = gemm_plan(m->ctx->device, m->ctx->num_sms, M, N, K, split_ok && splits);
+    const size_t need = plan.splits > 1 ? (size_t)plan.splits * M * N : 0;
+    if (need > m->gemm_ws_floats) {
+        // grow-only; graphs captured with the old buffer are dropped
+        SA_CUDA_TRY(cudaStreamSynchronize(m->cur));
+        invalidate_graphs(m);
+        cudaFree(m->gemm_ws);
+        m->gemm_ws = nullptr;
+        m->gemm_ws_floats = 0;
+        int rc = dalloc(&m->gemm_ws, need);
+        if (rc) return rc;
+        m->gemm_ws_floats = need;
+    }
+    if (splits) *splits = plan.splits;
+    return gemm_launch(m->cur, m->ctx->status, hi, lo, lda, w, M, N, K, mode, C, ldc, ohi, olo, ldo, plan,
+                       m->gemm_ws, m->gemm_ws_floats);
 }
 
 #define SA_RC(expr) do { int rc_ = (expr); if (rc_) return rc_; } while (0)
+
 
 // Tokens ids (device) at positions pos0 .. pos0+M-1 through every layer.
 // Their K/V go to cache rows kv_row0 + (0 .. M-1) and attention reads rows
@@ -264,6 +284,7 @@ static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr
     float* xc = m->x;          // single-token path: the residual the next consumer reads
     float* xo = m->tp_x2;
     SA_RC(launch_embedding(st, m->ids, M, m->embed, c.vocab, H, m->x, m->ctx->status));
+    int resid = 0;   // partial planes of the last down_proj not yet added to x
     for (int l = 0; l < c.n_layers; ++l) {
         const sa_qwen3::Layer& L = m->layers[l];
         float* kc = m->kc + l * layer_kv;
@@ -309,13 +330,18 @@ static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr
                 SA_RC(launch_gemv2(st, QW_EPI_RESID, false, L.wd, H, I, m->act, nullptr, 0.f, m->x, nullptr));
             }
         } else {
+            // split GEMMs leave partial planes (m->gemm_ws) that the next
+            // kernel adds: `resid` counts the planes of a pending residual add
             if (tp && l > 0)
                 SA_RC(launch_rmsnorm_hilo_tp(st, m->x, L.in_norm, M, H, c.eps, m->a_hi, m->a_lo, tp_args(m, 2 * l - 1)));
             else
-                SA_RC(launch_rmsnorm_hilo(st, m->x, L.in_norm, M, H, c.eps, m->a_hi, m->a_lo));
-            SA_RC(gemm(m, m->a_hi, m->a_lo, H, L.wqkv, M, m->NQKV, H, QW_EPI_STORE, m->qkv, m->NQKV, nullptr, nullptr, 0));
-            SA_RC(launch_qknorm_rope_append(st, m->qkv, M, m->hq, m->hkv, L.q_norm, L.k_norm, m->cos_t, m->sin_t, pos0,
-                                            nullptr, shift, m->q, kc, vc, c.max_seq));
+                SA_RC(launch_rmsnorm_hilo(st, m->x, L.in_norm, M, H, c.eps, m->a_hi, m->a_lo, m->gemm_ws, resid));
+            resid = 0;
+            int sq = 1;
+            SA_RC(gemm(m, m->a_hi, m->a_lo, H, L.wqkv, M, m->NQKV, H, QW_EPI_STORE, m->qkv, m->NQKV, nullptr, nullptr, 0,
+                       true, &sq));
+            SA_RC(launch_qknorm_rope_append(st, sq > 1 ? m->gemm_ws : m->qkv, sq, M, m->hq, m->hkv, L.q_norm, L.k_norm,
+                                            m->cos_t, m->sin_t, pos0, nullptr, shift, m->q, kc, vc, c.max_seq));
             SA_RC(prompt_attn_launch(st, m->q, m->QD, ka, va, (long long)c.max_seq * D, pos0 + 1, M, D, m->hq, m->hkv,
                                      scale, nullptr, m->QD, m->a_hi, m->a_lo));
             if (tp) {
@@ -324,18 +350,27 @@ static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr
                 SA_RC(launch_tp_scatter(st, m->tp_part, M, H, tp_args(m, 2 * l), m->ctx->num_sms));
                 SA_RC(launch_rmsnorm_hilo_tp(st, m->x, L.post_norm, M, H, c.eps, m->a_hi, m->a_lo, tp_args(m, 2 * l)));
             } else {
-                SA_RC(gemm(m, m->a_hi, m->a_lo, m->QD, L.wo, M, H, m->QD, QW_EPI_RESID, m->x, H, nullptr, nullptr, 0));
-                SA_RC(launch_rmsnorm_hilo(st, m->x, L.post_norm, M, H, c.eps, m->a_hi, m->a_lo));
+                int so = 1;
+                SA_RC(gemm(m, m->a_hi, m->a_lo, m->QD, L.wo, M, H, m->QD, QW_EPI_RESID, m->x, H, nullptr, nullptr, 0,
+                           true, &so));
+                SA_RC(launch_rmsnorm_hilo(st, m->x, L.post_norm, M, H, c.eps, m->a_hi, m->a_lo, m->gemm_ws,
+                                          so > 1 ? so : 0));
             }
-            SA_RC(gemm(m, m->a_hi, m->a_lo, H, L.wgu, M, 2 * I, H, QW_EPI_SWIGLU, nullptr, 0, m->b_hi, m->b_lo, I));
+            int sg = 1;
+            SA_RC(gemm(m, m->a_hi, m->a_lo, H, L.wgu, M, 2 * I, H, QW_EPI_SWIGLU, nullptr, 0, m->b_hi, m->b_lo, I, true,
+                       &sg));
+            if (sg > 1) SA_RC(launch_swiglu_hilo(st, m->gemm_ws, sg, M, I, m->b_hi, m->b_lo, I, m->ctx->num_sms));
             if (tp) {
                 SA_RC(gemm(m, m->b_hi, m->b_lo, I, L.wd, M, H, I, QW_EPI_STORE, m->tp_part, H, nullptr, nullptr, 0));
                 SA_RC(launch_tp_scatter(st, m->tp_part, M, H, tp_args(m, 2 * l + 1), m->ctx->num_sms));
             } else {
-                SA_RC(gemm(m, m->b_hi, m->b_lo, I, L.wd, M, H, I, QW_EPI_RESID, m->x, H, nullptr, nullptr, 0));
+                int sd = 1;
+                SA_RC(gemm(m, m->b_hi, m->b_lo, I, L.wd, M, H, I, QW_EPI_RESID, m->x, H, nullptr, nullptr, 0, true, &sd));
+                resid = sd > 1 ? sd : 0;
             }
         }
     }
+    if (resid) SA_RC(launch_resid_add(st, m->x, m->gemm_ws, resid, M, H, m->ctx->num_sms));
     m->x_last = M == 1 ? xc : m->x;
     m->x_last_ll = M == 1;
     return SA_OK;

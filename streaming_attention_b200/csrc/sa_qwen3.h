@@ -29,13 +29,19 @@ struct QkvEpi {
 struct GemmPlan {
     int bn, splits;
 };
-// Query (once per device) how many clusters of each GEMM variant fit on the
-// device; call before any stream capture.
+// Occupancy queries of the GEMM variants, once per device; call before any
+// stream capture.
 void gemm_prepare(int device);
-GemmPlan gemm_plan(int device, int M, int N, int K, int mode);
+// Tile width and split count for C[M, N] = A[M, K] W^T; split plans (splits
+// > 1) leave partial planes for the next kernel, so `split_ok` says whether
+// the consumer of this output adds them.
+GemmPlan gemm_plan(int device, int num_sms, int M, int N, int K, bool split_ok);
+// plan.splits > 1: writes planes part[z][M][N] (z < splits) instead of
+// applying `mode`.
 int gemm_launch(cudaStream_t st, int* status, const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo,
                 long long lda, const __nv_bfloat16* w, int M, int N, int K, int mode, float* C,
-                long long ldc, __nv_bfloat16* out_hi, __nv_bfloat16* out_lo, long long ldo, GemmPlan plan);
+                long long ldc, __nv_bfloat16* out_hi, __nv_bfloat16* out_lo, long long ldo, GemmPlan plan,
+                float* part, size_t part_floats);
 
 // Multi-query causal attention over a head-major fp32 KV cache: query m of
 // n_q (q at q + m*q_stride, [hq, d]) attends rows [0, T0 + m] of each KV head;
@@ -55,12 +61,19 @@ int prompt_attn_launch(cudaStream_t st, const float* q, long long q_stride, cons
 // element-wise / GEMV launchers (sa_qwen3_kernels.cu)
 int launch_embedding(cudaStream_t st, const int64_t* ids, int M, const __nv_bfloat16* E, int V, int H, float* x,
                      int* status);
-int launch_rmsnorm_hilo(cudaStream_t st, const float* x, const float* w, int M, int H, float eps,
-                        __nv_bfloat16* hi, __nv_bfloat16* lo);
+// RMSNorm of rows [0, M) of x to bf16 hi / lo terms; with splits > 0 the
+// partial planes part[z][M][H] are first added to x (and x written back).
+int launch_rmsnorm_hilo(cudaStream_t st, float* x, const float* w, int M, int H, float eps,
+                        __nv_bfloat16* hi, __nv_bfloat16* lo, const float* part = nullptr, int splits = 0);
+// x[M, H] += sum of the partial planes part[z][M][H], z < splits.
+int launch_resid_add(cudaStream_t st, float* x, const float* part, int splits, int M, int H, int num_sms);
+// SwiGLU of the gate/up partial planes part[z][M][2I] to bf16 hi / lo [M, ldo].
+int launch_swiglu_hilo(cudaStream_t st, const float* part, int splits, int M, int I, __nv_bfloat16* hi,
+                       __nv_bfloat16* lo, long long ldo, int num_sms);
 int launch_rmsnorm_f32(cudaStream_t st, const float* x, const float* w, int M, int H, float eps, float* y);
 int launch_split_hilo(cudaStream_t st, const float* x, size_t n, __nv_bfloat16* hi, __nv_bfloat16* lo);
 int launch_rope_table(cudaStream_t st, int n_pos, int D, float theta, float* cos_t, float* sin_t);
-int launch_qknorm_rope_append(cudaStream_t st, const float* qkv, int M, int hq, int hkv, const float* qn,
+int launch_qknorm_rope_append(cudaStream_t st, const float* qkv, int splits, int M, int hq, int hkv, const float* qn,
                               const float* kn, const float* cos_t, const float* sin_t, int pos0, const int* pos_dev,
                               int row_shift, float* q_out, float* kc, float* vc, int max_seq);
 int launch_advance(cudaStream_t st, int* state, const int64_t* tok, int64_t* toks, int cap, int inc_len,

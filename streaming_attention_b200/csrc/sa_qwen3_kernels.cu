@@ -17,6 +17,8 @@
 namespace sa {
 namespace qk {
 
+constexpr int QK_MAX_PLANES = 8;   // split-K planes a consumer adds (the GEMM's largest split)
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -51,13 +53,39 @@ __global__ void embedding_kernel(const int64_t* ids, int M, const __nv_bfloat16*
 }
 
 // ---- RMSNorm (ops.cpp:375-418) to the two bf16 GEMM operand terms ---------
-__global__ void rmsnorm_hilo_kernel(const float* x, const float* w, int H, float eps, __nv_bfloat16* hi,
-                                    __nv_bfloat16* lo) {
+// With splits > 0, x first gets the `splits` partial planes of the previous
+// GEMM added (plane order; row m of plane z at part + z * plane + m * H) and
+// is written back: the residual add of a split o_proj / down_proj.
+__global__ void rmsnorm_hilo_kernel(float* x, const float* part, int splits, size_t plane, const float* w, int H,
+                                    float eps, __nv_bfloat16* hi, __nv_bfloat16* lo) {
     __shared__ float red[32];
+    // launched programmatically: the next kernel (a GEMM) may start streaming
+    // its weights now; x comes from the previous kernel
+    pdl_trigger();
+    pdl_wait();
     const int m = blockIdx.x;
-    const float* xr = x + (size_t)m * H;
+    float* xr = x + (size_t)m * H;
     float ss = 0.f;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) ss += xr[i] * xr[i];
+    if (splits > 0) {
+        // float4 columns; every plane's load issued before any is added
+        const float* pr = part + (size_t)m * H;
+        for (int i = 4 * threadIdx.x; i < H; i += 4 * blockDim.x) {
+            float4 pv[QK_MAX_PLANES];
+#pragma unroll
+            for (int z = 0; z < QK_MAX_PLANES; ++z)
+                if (z < splits) pv[z] = __ldcg(reinterpret_cast<const float4*>(pr + z * plane + i));
+            float4 v = *reinterpret_cast<const float4*>(xr + i);
+#pragma unroll
+            for (int z = 0; z < QK_MAX_PLANES; ++z)
+                if (z < splits) {
+                    v.x += pv[z].x; v.y += pv[z].y; v.z += pv[z].z; v.w += pv[z].w;
+                }
+            *reinterpret_cast<float4*>(xr + i) = v;
+            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+    } else {
+        for (int i = threadIdx.x; i < H; i += blockDim.x) ss += xr[i] * xr[i];
+    }
     ss = block_sum(ss, red);
     const float rms = sqrtf(ss / (float)H + eps);
     for (int i = threadIdx.x; i < H; i += blockDim.x) {
@@ -81,6 +109,64 @@ __global__ void rmsnorm_f32_kernel(const float* x, const float* w, int H, float 
 }
 
 // fp32 -> (hi, lo) bf16 split of an activation for the tensor-core GEMM.
+// x += the sum, in plane order, of `splits` partial planes (a split GEMM's
+// residual add when no RMSNorm follows).
+__global__ void resid_add_kernel(float* x, const float* part, int splits, size_t n4) {
+    pdl_trigger();
+    pdl_wait();
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        float4 pv[QK_MAX_PLANES];
+#pragma unroll
+        for (int z = 0; z < QK_MAX_PLANES; ++z)
+            if (z < splits) pv[z] = __ldcg(reinterpret_cast<const float4*>(part) + z * n4 + i);
+        float4 v = reinterpret_cast<float4*>(x)[i];
+#pragma unroll
+        for (int z = 0; z < QK_MAX_PLANES; ++z)
+            if (z < splits) { v.x += pv[z].x; v.y += pv[z].y; v.z += pv[z].z; v.w += pv[z].w; }
+        reinterpret_cast<float4*>(x)[i] = v;
+    }
+}
+
+// SwiGLU of a split gate/up GEMM (qwen3_mlp, qwen3_ops.cpp:265-296): the
+// planes hold [M, 2I] partial sums in [gate(32); up(32)] column blocks;
+// out[m, i] = silu(g) * u with g, u the plane sums (plane order) of columns
+// 64 (i / 32) + i % 32 and that + 32, written as bf16 hi / lo terms.
+__global__ void swiglu_hilo_kernel(const float* part, int splits, int M, int I, __nv_bfloat16* hi,
+                                   __nv_bfloat16* lo, long long ldo) {
+    pdl_trigger();
+    pdl_wait();
+    const size_t plane = (size_t)M * 2 * I;
+    const size_t n4 = (size_t)M * I / 4;
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n4; e += (size_t)gridDim.x * blockDim.x) {
+        const int m = (int)(e / (I / 4)), i = (int)(e % (I / 4)) * 4;
+        const size_t gc = (size_t)m * 2 * I + (i / 32) * 64 + (i % 32);
+        float4 pg[QK_MAX_PLANES], pu[QK_MAX_PLANES];
+#pragma unroll
+        for (int z = 0; z < QK_MAX_PLANES; ++z)
+            if (z < splits) {
+                pg[z] = __ldcg(reinterpret_cast<const float4*>(part + z * plane + gc));
+                pu[z] = __ldcg(reinterpret_cast<const float4*>(part + z * plane + gc + 32));
+            }
+        float4 g = pg[0], u = pu[0];
+#pragma unroll
+        for (int z = 1; z < QK_MAX_PLANES; ++z)
+            if (z < splits) {
+                g.x += pg[z].x; g.y += pg[z].y; g.z += pg[z].z; g.w += pg[z].w;
+                u.x += pu[z].x; u.y += pu[z].y; u.z += pu[z].z; u.w += pu[z].w;
+            }
+        const float v[4] = {(g.x / (1.f + expf(-g.x))) * u.x, (g.y / (1.f + expf(-g.y))) * u.y,
+                            (g.z / (1.f + expf(-g.z))) * u.z, (g.w / (1.f + expf(-g.w))) * u.w};
+        __nv_bfloat16* ho = hi + (size_t)m * ldo + i;
+        __nv_bfloat16* lw = lo + (size_t)m * ldo + i;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const __nv_bfloat16 h = __float2bfloat16_rn(v[k]);
+            ho[k] = h;
+            lw[k] = __float2bfloat16_rn(v[k] - __bfloat162float(h));
+        }
+    }
+}
+
 __global__ void split_hilo_kernel(const float* x, size_t n, __nv_bfloat16* hi, __nv_bfloat16* lo) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const float y = x[i];
@@ -137,10 +223,12 @@ __device__ __forceinline__ float4 head_norm_rope(const float (&e_in)[4], const f
     return make_float4(o[0], o[1], o[2], o[3]);
 }
 
-__global__ void qknorm_rope_append_kernel(const float* qkv, int M, int hq, int hkv, const float* qn,
-                                          const float* kn, const float* cos_t, const float* sin_t, int pos0,
-                                          const int* pos_dev, int row_shift, float* q_out, float* kc, float* vc,
-                                          int max_seq) {
+// qkv holds `splits` planes of `plane` floats (split-K partial sums of the
+// QKV GEMM, added here in plane order) or the finished projection (splits 1).
+__global__ void qknorm_rope_append_kernel(const float* qkv, int splits, size_t plane, int M, int hq, int hkv,
+                                          const float* qn, const float* kn, const float* cos_t, const float* sin_t,
+                                          int pos0, const int* pos_dev, int row_shift, float* q_out, float* kc,
+                                          float* vc, int max_seq) {
     constexpr int D = 128;
     pdl_trigger();
     pdl_wait();
@@ -153,7 +241,16 @@ __global__ void qknorm_rope_append_kernel(const float* qkv, int M, int hq, int h
     const int row = pos + row_shift;                       // cache row written
     if (row >= max_seq) return;       // the host checks capacity; never write past the cache
     const float* src = qkv + (size_t)m * nh * D + (size_t)h * D;
-    float4 v4 = __ldcg(reinterpret_cast<const float4*>(src + 4 * lane));   // produced by the previous kernel
+    // produced by the previous kernel; every plane's load is issued before
+    // any is added (an in-order add would wait on each load in turn)
+    float4 pv[QK_MAX_PLANES];
+#pragma unroll
+    for (int z = 0; z < QK_MAX_PLANES; ++z)
+        if (z < splits) pv[z] = __ldcg(reinterpret_cast<const float4*>(src + z * plane + 4 * lane));
+    float4 v4 = pv[0];
+#pragma unroll
+    for (int z = 1; z < QK_MAX_PLANES; ++z)
+        if (z < splits) { v4.x += pv[z].x; v4.y += pv[z].y; v4.z += pv[z].z; v4.w += pv[z].w; }
     float e[4] = {v4.x, v4.y, v4.z, v4.w};
     if (h >= hq + hkv) {  // V head
         float* dst = vc + ((size_t)(h - hq - hkv) * max_seq + row) * D;
@@ -759,15 +856,31 @@ int launch_embedding(cudaStream_t st, const int64_t* ids, int M, const __nv_bflo
     SA_CUDA_TRY(cudaGetLastError());
     return SA_OK;
 }
-int launch_rmsnorm_hilo(cudaStream_t st, const float* x, const float* w, int M, int H, float eps,
-                        __nv_bfloat16* hi, __nv_bfloat16* lo) {
-    qk::rmsnorm_hilo_kernel<<<M, 256, 0, st>>>(x, w, H, eps, hi, lo);
-    SA_CUDA_TRY(cudaGetLastError());
+int launch_rmsnorm_hilo(cudaStream_t st, float* x, const float* w, int M, int H, float eps,
+                        __nv_bfloat16* hi, __nv_bfloat16* lo, const float* part, int splits) {
+    SA_CHECK_ARG(splits == 0 || (part && splits <= qk::QK_MAX_PLANES && H % 4 == 0), "rmsnorm_hilo: partial planes");
+    SA_CUDA_TRY(launch_pdl_k(1, qk::rmsnorm_hilo_kernel, dim3(M), dim3(256), 0, st, x, part, splits,
+                             (size_t)M * H, w, H, eps, hi, lo));
     return SA_OK;
 }
 int launch_rmsnorm_f32(cudaStream_t st, const float* x, const float* w, int M, int H, float eps, float* y) {
     qk::rmsnorm_f32_kernel<<<M, 256, 0, st>>>(x, w, H, eps, y);
     SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
+int launch_resid_add(cudaStream_t st, float* x, const float* part, int splits, int M, int H, int num_sms) {
+    SA_CHECK_ARG(splits >= 1 && splits <= qk::QK_MAX_PLANES && part && H % 4 == 0, "resid_add: splits %d H %d", splits, H);
+    const size_t n4 = (size_t)M * H / 4;
+    const int grid = (int)std::min<size_t>((n4 + 255) / 256, (size_t)num_sms * 4);
+    SA_CUDA_TRY(launch_pdl_k(1, qk::resid_add_kernel, dim3(grid), dim3(256), 0, st, x, part, splits, n4));
+    return SA_OK;
+}
+int launch_swiglu_hilo(cudaStream_t st, const float* part, int splits, int M, int I, __nv_bfloat16* hi,
+                       __nv_bfloat16* lo, long long ldo, int num_sms) {
+    SA_CHECK_ARG(splits >= 1 && splits <= qk::QK_MAX_PLANES && part && I % 32 == 0, "swiglu_hilo: splits %d I %d", splits, I);
+    const size_t n4 = (size_t)M * I / 4;
+    const int grid = (int)std::min<size_t>((n4 + 255) / 256, (size_t)num_sms * 4);
+    SA_CUDA_TRY(launch_pdl_k(1, qk::swiglu_hilo_kernel, dim3(grid), dim3(256), 0, st, part, splits, M, I, hi, lo, ldo));
     return SA_OK;
 }
 int launch_split_hilo(cudaStream_t st, const float* x, size_t n, __nv_bfloat16* hi, __nv_bfloat16* lo) {
@@ -783,12 +896,14 @@ int launch_rope_table(cudaStream_t st, int n_pos, int D, float theta, float* cos
     SA_CUDA_TRY(cudaGetLastError());
     return SA_OK;
 }
-int launch_qknorm_rope_append(cudaStream_t st, const float* qkv, int M, int hq, int hkv, const float* qn,
+int launch_qknorm_rope_append(cudaStream_t st, const float* qkv, int splits, int M, int hq, int hkv, const float* qn,
                               const float* kn, const float* cos_t, const float* sin_t, int pos0, const int* pos_dev,
                               int row_shift, float* q_out, float* kc, float* vc, int max_seq) {
     const int warps = M * (hq + 2 * hkv);
-    SA_CUDA_TRY(launch_pdl_k(1, qk::qknorm_rope_append_kernel, dim3((warps + 7) / 8), dim3(256), 0, st, qkv, M, hq, hkv,
-                           qn, kn, cos_t, sin_t, pos0, pos_dev, row_shift, q_out, kc, vc, max_seq));
+    SA_CHECK_ARG(splits >= 1 && splits <= qk::QK_MAX_PLANES, "qknorm_rope_append: splits %d", splits);
+    SA_CUDA_TRY(launch_pdl_k(1, qk::qknorm_rope_append_kernel, dim3((warps + 7) / 8), dim3(256), 0, st, qkv, splits,
+                             (size_t)M * (hq + 2 * hkv) * 128, M, hq, hkv, qn, kn, cos_t, sin_t, pos0, pos_dev,
+                             row_shift, q_out, kc, vc, max_seq));
     SA_CUDA_TRY(cudaGetLastError());
     return SA_OK;
 }

@@ -127,6 +127,30 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
 }
 
+// 1-D bulk copy shared -> global (bulk async-group completion); both
+// addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_s2g(void* gdst, const void* ssrc, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+                 ::"l"(gdst), "r"(smem_u32(ssrc)), "r"(bytes) : "memory");
+}
+// 3-D tiled TMA store of a shared-memory box to (x, y, z) (bulk async-group).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
+                 ::"l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(src)) : "memory");
+}
+// Wait until the shared-memory sources of this thread's committed bulk copies
+// have been read (the buffer may be reused; the writes may still be in flight).
+__device__ __forceinline__ void bulk_commit_wait_read() {
+    asm volatile("cp.async.bulk.commit_group;\n\tcp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Wait until every bulk copy this thread committed has completed its writes.
+__device__ __forceinline__ void bulk_commit_wait_all() {
+    asm volatile("cp.async.bulk.commit_group;\n\tcp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Order this thread's generic-proxy memory accesses with async-proxy ones
+// (bulk copies / TMA) in every state space.
+__device__ __forceinline__ void fence_proxy_async_all() { asm volatile("fence.proxy.async;" ::: "memory"); }
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
@@ -140,6 +164,7 @@ int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_
                       uint64_t row_stride_elems, uint32_t box_rows, uint32_t box_cols);
 int cached_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
                         uint64_t row_stride_elems, uint32_t box_rows, uint32_t box_cols);
+int cached_tmap_3d_f32_planes(CUtensorMap* map, void* base, uint64_t rows, uint64_t cols, uint64_t splits);
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (function, device).
 int set_smem_attr_once(const void* fn, int bytes);
 

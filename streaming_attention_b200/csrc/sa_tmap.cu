@@ -47,6 +47,47 @@ int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_
     return SA_OK;
 }
 
+// 3-D fp32 tensor map over `splits` stacked row-major [rows, cols] planes
+// (split partial sums), box 128 rows x 32 columns x 1 plane, 128-byte swizzle:
+// the tensor-store destination of the prompt GEMM's split partials.
+int make_tmap_3d_f32_planes(CUtensorMap* map, void* base, uint64_t rows, uint64_t cols, uint64_t splits) {
+    int rc = get_encode();
+    if (rc) return rc;
+    SA_CHECK_ARG(((uintptr_t)base & 15) == 0 && (cols * 4) % 16 == 0, "partial-plane tensor map alignment");
+    cuuint64_t dims[3] = {cols, rows, splits};
+    cuuint64_t strides[2] = {cols * 4, rows * cols * 4};
+    cuuint32_t box[3] = {32, 128, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(SA_ERR_ARG, "cuTensorMapEncodeTiled failed (%d): planes %llu x %llu x %llu", (int)r,
+                         (unsigned long long)splits, (unsigned long long)rows, (unsigned long long)cols);
+    return SA_OK;
+}
+
+int cached_tmap_3d_f32_planes(CUtensorMap* map, void* base, uint64_t rows, uint64_t cols, uint64_t splits) {
+    using Key = std::tuple<const void*, uint64_t, uint64_t, uint64_t>;
+    static std::mutex mu;
+    static std::map<Key, CUtensorMap> cache;
+    const Key key{base, rows, cols, splits};
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) {
+            *map = it->second;
+            return SA_OK;
+        }
+    }
+    int rc = make_tmap_3d_f32_planes(map, base, rows, cols, splits);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lk(mu);
+    if (cache.size() > 8192) cache.clear();
+    cache.emplace(key, *map);
+    return SA_OK;
+}
+
 // Tensor maps depend only on (address, shape, stride, box); the Qwen3 forward
 // reuses the same few hundred for its fixed buffers, so encode each once.
 int cached_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
