@@ -4,17 +4,22 @@
 // create_causal_mask, :240-259; GQA by head index as repeat_kv, :194-234).
 //
 // Query m of the prompt (RoPE position pos0 + m) attends cache rows
-// [0, T0 + m) with T0 = pos0 + 1.  One CTA serves QV = 8 query vectors that
-// read the same KV head: 8 / G consecutive prompt rows x the G = hq / hkv
-// query heads of that KV head (two vectors per warp, four warps).  The CTA streams the KV head's rows once, in
-// 32-row tiles (cp.async, double-buffered), for all 16 vectors:
-//   * scores: warp w owns vectors 2w, 2w+1, lane = key of the tile; q rows are
-//     shared-memory broadcasts, K rows are padded to 132 floats so the 32
-//     lanes' float4 reads hit distinct banks;
+// [0, T0 + m) with T0 = pos0 + 1.  One CTA serves QV = 16 query vectors that
+// read the same KV head: 16 / G consecutive prompt rows x the G = hq / hkv
+// query heads of that KV head.  The CTA streams the head's rows in rounds of
+// 128 (cp.async into shared memory, K before V) and its four warps split each
+// round's keys, 32 each, for all 16 vectors.  Every thread works on a
+// register tile so that shared memory is not the limit:
+//   * scores: lane = (vector quad vq, key group kg) computes the 4 x 4 tile
+//     of vectors vq + 4i and keys kg + 8j: 8 float4 reads per 64 FMAs (rows
+//     padded to 132 floats, so the 8 key rows / 4 query rows a read touches
+//     sit in distinct banks);
 //   * online softmax in the exp2 domain (scale * log2 e folded into q), per
-//     vector, reduced across the warp with shuffles;
-//   * P.V: lane owns 4 consecutive output dims of the warp's 2 vectors; each
-//     key is one float4 of V and one broadcast float2 of the 2 vectors' p.
+//     warp and vector, reduced over the 8 key-group lanes with shuffles;
+//   * P.V: lane owns 4 consecutive output dims of all 16 vectors; each key
+//     is one float4 of V and four broadcast float4 of the 16 vectors' p;
+//   * the four warps' (m, l, O) states are merged at the end (the merge of
+//     streaming_omp.cpp:27-48), in warp order.
 // fp32 throughout (CUDA cores), like the reference.  The output is written as
 // fp32 and/or as the bf16 hi/lo planes the o_proj GEMM reads.
 #include <cuda_bf16.h>
@@ -28,10 +33,15 @@
 namespace sa {
 namespace pa {
 
-constexpr int D = 128, VPW = 2, NWARP = 4, QV = VPW * NWARP, KT = 32, KP = D + 4, THREADS = 32 * NWARP;
+constexpr int D = 128, QV = 16, NWARP = 4, KW = 32, KR = NWARP * KW, KP = D + 4, THREADS = 32 * NWARP;
 constexpr float LOG2E = 1.4426950408889634f;
-constexpr int SMEM_FLOATS = QV * D + 2 * KT * KP + 2 * KT * D + NWARP * KT * VPW;
+constexpr int OFF_Q = 0;                           // [QV][KP]
+constexpr int OFF_K = OFF_Q + QV * KP;             // [KR][KP]
+constexpr int OFF_V = OFF_K + KR * KP;             // [KR][D]
+constexpr int OFF_P = OFF_V + KR * D;              // [NWARP][KW][QV]
+constexpr int SMEM_FLOATS = OFF_P + NWARP * KW * QV;
 constexpr int SMEM_BYTES = SMEM_FLOATS * 4;
+static_assert(NWARP * QV * (D + 2) <= KR * KP, "the merge area reuses the K rows");
 
 struct Args {
     const float* q;
@@ -54,14 +64,17 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 __device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-__global__ void __launch_bounds__(THREADS)
+__global__ void __launch_bounds__(THREADS, 1)
 prompt_attn_kernel(const Args a) {
     extern __shared__ float4 smem4[];
-    float* Qs = reinterpret_cast<float*>(smem4);     // [QV][D]
-    float* Ks = Qs + QV * D;                          // [2][KT][KP]
-    float* Vs = Ks + 2 * KT * KP;                     // [2][KT][D]
-    float* Ps = Vs + 2 * KT * D;                      // [NWARP][KT][VPW]
+    float* sm = reinterpret_cast<float*>(smem4);
+    float* Qs = sm + OFF_Q;
+    float* Ks = sm + OFF_K;
+    float* Vs = sm + OFF_V;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // score phase: lane = (vector quad vq, key group kg); vectors vq + 4 i,
+    // keys kg + 8 j of the warp's 32 (i, j < 4)
+    const int kg = lane & 7, vq = lane >> 3;
     const int h = blockIdx.y;
     // heaviest (latest) query blocks first
     const int blk = gridDim.x - 1 - blockIdx.x;
@@ -82,105 +95,168 @@ prompt_attn_kernel(const Args a) {
             x = __ldg(reinterpret_cast<const float4*>(a.q + (size_t)m * a.q_stride + (size_t)head * D + c));
             x.x *= a.qscale; x.y *= a.qscale; x.z *= a.qscale; x.w *= a.qscale;
         }
-        *reinterpret_cast<float4*>(Qs + j * D + c) = x;
+        *reinterpret_cast<float4*>(Qs + j * KP + c) = x;
     }
-    const int n_tiles = (n_keys + KT - 1) / KT;
-    auto load_tile = [&](int t, int buf) {
-        float* kd = Ks + buf * KT * KP;
-        float* vd = Vs + buf * KT * D;
-        for (int e = tid; e < KT * (D / 4); e += THREADS) {
-            const int r = e / (D / 4), c = (e % (D / 4)) * 4, row = t * KT + r;
-            if (row < n_keys) {
-                cp_async16(kd + r * KP + c, kh + (size_t)row * D + c);
-                cp_async16(vd + r * D + c, vh + (size_t)row * D + c);
-            } else {
-                *reinterpret_cast<float4*>(kd + r * KP + c) = make_float4(0.f, 0.f, 0.f, 0.f);
-                *reinterpret_cast<float4*>(vd + r * D + c) = make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-        }
-        cp_async_commit();
-    };
-    load_tile(0, 0);
-
-    // per warp: vectors VPW w + i; per lane: output dims 4 lane .. 4 lane + 3
-    float mrun[VPW], lrun[VPW];
-    float4 o[VPW];
-    int lim[VPW];   // keys vector i may attend
+    // keys of this lane's 4 vectors (0 for the unused vectors of a ragged block)
+    int lim[4];
 #pragma unroll
-    for (int i = 0; i < VPW; ++i) {
-        mrun[i] = -INFINITY;
-        lrun[i] = 0.f;
-        o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        const int j = warp * VPW + i, m = m0 + j / a.G;
+    for (int i = 0; i < 4; ++i) {
+        const int m = m0 + (vq + 4 * i) / a.G;
         lim[i] = m < m_end ? a.T0 + m : 0;
     }
-    for (int t = 0; t < n_tiles; ++t) {
-        if (t + 1 < n_tiles) {
-            load_tile(t + 1, (t + 1) & 1);
-            cp_async_wait_1();
-        } else {
-            cp_async_wait_0();
+    // per warp: the state of all 16 vectors; P.V lane = 4 output dims
+    float mrun[QV], lrun[QV];
+    float4 o[QV];
+#pragma unroll
+    for (int j = 0; j < QV; ++j) {
+        mrun[j] = -INFINITY;
+        lrun[j] = 0.f;
+        o[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float* Pw = sm + OFF_P + warp * KW * QV;          // [KW][QV]
+    const int n_rounds = (n_keys + KR - 1) / KR;
+    for (int rd = 0; rd < n_rounds; ++rd) {
+        const int base = rd * KR;
+        if (rd > 0) __syncthreads();                   // every warp is done with the previous round's rows
+        // K rows first (group 0), then V rows (group 1): the scores start
+        // while V is still arriving
+        for (int e = tid; e < KR * (D / 4); e += THREADS) {
+            const int r = e / (D / 4), c = (e % (D / 4)) * 4, row = base + r;
+            if (row < n_keys) cp_async16(Ks + r * KP + c, kh + (size_t)row * D + c);
+            else *reinterpret_cast<float4*>(Ks + r * KP + c) = make_float4(0.f, 0.f, 0.f, 0.f);
         }
+        cp_async_commit();
+        for (int e = tid; e < KR * (D / 4); e += THREADS) {
+            const int r = e / (D / 4), c = (e % (D / 4)) * 4, row = base + r;
+            if (row < n_keys) cp_async16(Vs + r * D + c, vh + (size_t)row * D + c);
+            else *reinterpret_cast<float4*>(Vs + r * D + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        cp_async_commit();
+        cp_async_wait_1();
         __syncthreads();
-        const float* kt = Ks + (t & 1) * KT * KP;
-        const float* vt = Vs + (t & 1) * KT * D;
-        // scores s[i] = q_i . k_lane
-        float s[VPW];
+        // scores s[i][j] = q_{vq + 4i} . k_{kg + 8j} over this warp's 32 keys
+        const float* kw = Ks + (warp * KW + kg) * KP;
+        const float* qv = Qs + vq * KP;
+        float sc[4][4];
 #pragma unroll
-        for (int i = 0; i < VPW; ++i) s[i] = 0.f;
-        const float* qw = Qs + warp * VPW * D;
-#pragma unroll 8
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) sc[i][j] = 0.f;
+#pragma unroll 4
         for (int d = 0; d < D; d += 4) {
-            const float4 kv = *reinterpret_cast<const float4*>(kt + lane * KP + d);
+            float4 kk[4], qq[4];
 #pragma unroll
-            for (int i = 0; i < VPW; ++i) {
-                const float4 qv = *reinterpret_cast<const float4*>(qw + i * D + d);
-                s[i] = fmaf(qv.x, kv.x, s[i]);
-                s[i] = fmaf(qv.y, kv.y, s[i]);
-                s[i] = fmaf(qv.z, kv.z, s[i]);
-                s[i] = fmaf(qv.w, kv.w, s[i]);
+            for (int j = 0; j < 4; ++j) kk[j] = *reinterpret_cast<const float4*>(kw + 8 * j * KP + d);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) qq[i] = *reinterpret_cast<const float4*>(qv + 4 * i * KP + d);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    sc[i][j] = fmaf(qq[i].x, kk[j].x, sc[i][j]);
+                    sc[i][j] = fmaf(qq[i].y, kk[j].y, sc[i][j]);
+                    sc[i][j] = fmaf(qq[i].z, kk[j].z, sc[i][j]);
+                    sc[i][j] = fmaf(qq[i].w, kk[j].w, sc[i][j]);
+                }
+        }
+        // online softmax of the warp's 32 keys per vector (over j in-thread,
+        // then the 8 key-group lanes), P to shared memory [key][vector]
+        float alpha[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int key = base + warp * KW + kg + 8 * j;
+                if (key >= lim[i]) sc[i][j] = -INFINITY;
+                mx = fmaxf(mx, sc[i][j]);
+            }
+#pragma unroll
+            for (int off = 1; off < 8; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            // every lane holds the state of all 16 vectors; this lane's vector i is vq + 4 i
+            float mold = mrun[0];
+#pragma unroll
+            for (int v = 0; v < 4; ++v) if (vq == v) mold = mrun[v + 4 * i];
+            const float mnew = fmaxf(mold, mx);
+            alpha[i] = mnew == -INFINITY ? 1.f : ex2(mold - mnew);
+            float sum = 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float p = mnew == -INFINITY ? 0.f : ex2(sc[i][j] - mnew);
+                Pw[(kg + 8 * j) * QV + vq + 4 * i] = p;
+                sum += p;
+            }
+#pragma unroll
+            for (int off = 1; off < 8; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+            // broadcast vector (v + 4 i)'s new state from the lanes of quad v
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+                const float a_v = __shfl_sync(0xffffffffu, alpha[i], 8 * v);
+                const float m_v = __shfl_sync(0xffffffffu, mnew, 8 * v);
+                const float s_v = __shfl_sync(0xffffffffu, sum, 8 * v);
+                const int jv = v + 4 * i;
+                lrun[jv] = lrun[jv] * a_v + s_v;
+                mrun[jv] = m_v;
+                o[jv].x *= a_v; o[jv].y *= a_v; o[jv].z *= a_v; o[jv].w *= a_v;
             }
         }
-        const int key = t * KT + lane;
-        float p[VPW];
+        cp_async_wait_0();
+        __syncthreads();                               // V rows landed; P of the warp visible
+        // P.V over this warp's 32 keys; lane = output dims 4 lane .. 4 lane + 3
+        const float* vw = Vs + warp * KW * D + lane * 4;
+#pragma unroll 2
+        for (int kk = 0; kk < KW; ++kk) {
+            const float4 vv = *reinterpret_cast<const float4*>(vw + kk * D);
+            const float* pk = Pw + kk * QV;
 #pragma unroll
-        for (int i = 0; i < VPW; ++i) {
-            const float si = key < lim[i] ? s[i] : -INFINITY;
-            float mx = si;
+            for (int q4 = 0; q4 < QV / 4; ++q4) {
+                const float4 pp = *reinterpret_cast<const float4*>(pk + 4 * q4);
+                const float pj[4] = {pp.x, pp.y, pp.z, pp.w};
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-            const float mnew = fmaxf(mrun[i], mx);
-            // rows with no valid key yet keep m = -inf: nothing to rescale
-            const float alpha = mnew == -INFINITY ? 1.f : ex2(mrun[i] - mnew);
-            p[i] = mnew == -INFINITY ? 0.f : ex2(si - mnew);
-            float sum = p[i];
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-            lrun[i] = lrun[i] * alpha + sum;
-            mrun[i] = mnew;
-            o[i].x *= alpha; o[i].y *= alpha; o[i].z *= alpha; o[i].w *= alpha;
+                for (int t = 0; t < 4; ++t) {
+                    float4& acc = o[4 * q4 + t];
+                    acc.x = fmaf(pj[t], vv.x, acc.x);
+                    acc.y = fmaf(pj[t], vv.y, acc.y);
+                    acc.z = fmaf(pj[t], vv.z, acc.z);
+                    acc.w = fmaf(pj[t], vv.w, acc.w);
+                }
+            }
         }
-        float* pw = Ps + warp * KT * VPW;
-        static_assert(VPW == 2, "p is stored as float2");
-        *reinterpret_cast<float2*>(pw + lane * VPW) = make_float2(p[0], p[1]);
         __syncwarp();
-#pragma unroll 8
-        for (int kk = 0; kk < KT; ++kk) {
-            const float2 pk = *reinterpret_cast<const float2*>(pw + kk * VPW);
-            const float4 vv = *reinterpret_cast<const float4*>(vt + kk * D + lane * 4);
-            o[0].x = fmaf(pk.x, vv.x, o[0].x); o[0].y = fmaf(pk.x, vv.y, o[0].y);
-            o[0].z = fmaf(pk.x, vv.z, o[0].z); o[0].w = fmaf(pk.x, vv.w, o[0].w);
-            o[1].x = fmaf(pk.y, vv.x, o[1].x); o[1].y = fmaf(pk.y, vv.y, o[1].y);
-            o[1].z = fmaf(pk.y, vv.z, o[1].z); o[1].w = fmaf(pk.y, vv.w, o[1].w);
-        }
-        __syncthreads();   // the buffer of tile t is refilled at t + 2
     }
+    // merge the warps' states (the K rows are free now): [warp][vector][m, l, O]
+    __syncthreads();
+    float* Ms = sm + OFF_K;
 #pragma unroll
-    for (int i = 0; i < VPW; ++i) {
-        const int j = warp * VPW + i, m = m0 + j / a.G, head = h * a.G + j % a.G;
+    for (int j = 0; j < QV; ++j) {
+        float* st = Ms + (warp * QV + j) * (D + 2);
+        if (lane == 0) { st[0] = mrun[j]; st[1] = lrun[j]; }
+        *reinterpret_cast<float2*>(st + 2 + lane * 4) = make_float2(o[j].x, o[j].y);
+        *reinterpret_cast<float2*>(st + 4 + lane * 4) = make_float2(o[j].z, o[j].w);
+    }
+    __syncthreads();
+    for (int j = warp; j < QV; j += NWARP) {
+        const int m = m0 + j / a.G, head = h * a.G + j % a.G;
         if (m >= m_end) continue;
-        const float inv = lrun[i] > 0.f ? 1.f / lrun[i] : 0.f;
-        const float4 r = make_float4(o[i].x * inv, o[i].y * inv, o[i].z * inv, o[i].w * inv);
+        float mw[NWARP], mx = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NWARP; ++w) {
+            mw[w] = Ms[(w * QV + j) * (D + 2)];
+            mx = fmaxf(mx, mw[w]);
+        }
+        float l = 0.f;
+        float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < NWARP; ++w) {
+            const float* st = Ms + (w * QV + j) * (D + 2);
+            const float f = mw[w] == -INFINITY ? 0.f : ex2(mw[w] - mx);
+            l += st[1] * f;
+            const float2 a01 = *reinterpret_cast<const float2*>(st + 2 + lane * 4);
+            const float2 a23 = *reinterpret_cast<const float2*>(st + 4 + lane * 4);
+            r.x += a01.x * f; r.y += a01.y * f; r.z += a23.x * f; r.w += a23.y * f;
+        }
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        r.x *= inv; r.y *= inv; r.z *= inv; r.w *= inv;
         const size_t off = (size_t)m * a.o_stride + (size_t)head * D + lane * 4;
         if (a.out) *reinterpret_cast<float4*>(a.out + off) = r;
         if (a.out_hi) {
@@ -206,7 +282,7 @@ int prompt_attn_launch(cudaStream_t st, const float* q, long long q_stride, cons
     SA_CHECK_ARG(M >= 1 && T0 >= 1 && hkv >= 1 && hq % hkv == 0, "prompt attention: M=%d T0=%d hq=%d hkv=%d", M, T0,
                  hq, hkv);
     const int G = hq / hkv;
-    SA_CHECK_ARG(G == 1 || G == 2 || G == 4 || G == 8, "prompt attention: hq/hkv=%d", G);
+    SA_CHECK_ARG(G == 1 || G == 2 || G == 4 || G == 8 || G == 16, "prompt attention: hq/hkv=%d", G);
     SA_CHECK_ARG(q_stride % 4 == 0 && kv_head_stride % 4 == 0 && o_stride % 4 == 0 && ((uintptr_t)q & 15) == 0 &&
                      ((uintptr_t)k & 15) == 0 && ((uintptr_t)v & 15) == 0 && ((uintptr_t)out & 15) == 0 &&
                      ((uintptr_t)out_hi & 7) == 0 && ((uintptr_t)out_lo & 7) == 0,
@@ -218,7 +294,7 @@ int prompt_attn_launch(cudaStream_t st, const float* q, long long q_stride, cons
     a.qscale = scale * pa::LOG2E;
     a.out = out; a.o_stride = o_stride; a.out_hi = out_hi; a.out_lo = out_lo;
     const int nblk = (M + a.qb - 1) / a.qb;
-    SA_CHECK_ARG(nblk <= 2147483647 && hkv <= 65535, "prompt attention: grid");
+    SA_CHECK_ARG(hkv <= 65535, "prompt attention: grid");
     SA_RC_TRY(set_smem_attr_once((const void*)pa::prompt_attn_kernel, pa::SMEM_BYTES));
     SA_CUDA_TRY(launch_pdl(pa::prompt_attn_kernel, dim3(nblk, hkv), dim3(pa::THREADS), pa::SMEM_BYTES, st, a));
     return SA_OK;

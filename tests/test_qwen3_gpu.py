@@ -83,6 +83,36 @@ def test_qwen3_vs_oracle_shapes(ctx, oracle, S):
     _close(got, ref, f"S={S}")
 
 
+@pytest.mark.parametrize("hq,hkv,S", [(4, 4, 33), (8, 2, 47), (8, 4, 16), (4, 1, 5)])
+def test_qwen3_prompt_gqa_ratios(ctx, oracle, hq, hkv, S):
+    """Prompt attention blocks hold 16 / G prompt rows of all G query heads of
+    a KV head: G = 1, 2, 4 and prompt lengths that leave ragged last blocks."""
+    from streaming_attention_b200 import Qwen3
+    cfg = Qwen3Cfg(vocab=700, hidden=256, n_layers=2, hq=hq, hkv=hkv, head_dim=128, inter=512,
+                   eps=1e-6, theta=1e6)
+    w = make_qwen3_weights(cfg, 29)
+    ids = I.rng(S + hq).integers(0, cfg.vocab, S)
+    m = Qwen3(_cfgdict(cfg), max_seq=128, ctx=ctx)
+    m.load(w)
+    _close(m.forward(ids), oracle.qwen3_forward(cfg, w, ids), f"hq={hq} hkv={hkv} S={S}")
+
+
+def test_qwen3_long_prefix_continuation(ctx, oracle):
+    """A 40-token prompt continued after 300 cached tokens: its attention runs
+    over several 128-row rounds of the cache."""
+    from streaming_attention_b200 import Qwen3
+    cfg = Qwen3Cfg(vocab=500, hidden=256, n_layers=2, hq=4, hkv=2, head_dim=128, inter=512,
+                   eps=1e-6, theta=1e6)
+    w = make_qwen3_weights(cfg, 41)
+    ids = I.rng(8).integers(0, cfg.vocab, 340)
+    m = Qwen3(_cfgdict(cfg), max_seq=400, ctx=ctx)
+    m.load(w)
+    m.forward(ids[:300], use_cache=True, logits="none")
+    part = m.forward(ids[300:], use_cache=True, logits="all")
+    ref = oracle.qwen3_forward(cfg, w, ids, all_logits=True)[300:]
+    _close(part, ref, "continuation after 300 cached rows")
+
+
 def test_qwen3_cache_continuation_matches_full_prompt(ctx, oracle):
     """A prompt fed in two chunks through the cache equals one pass over the
     whole prompt (the KVCache append/advance contract)."""
