@@ -342,8 +342,9 @@ static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr
                        true, &sq));
             SA_RC(launch_qknorm_rope_append(st, sq > 1 ? m->gemm_ws : m->qkv, sq, M, m->hq, m->hkv, L.q_norm, L.k_norm,
                                             m->cos_t, m->sin_t, pos0, nullptr, shift, m->q, kc, vc, c.max_seq));
-            SA_RC(prompt_attn_launch(st, m->q, m->QD, ka, va, (long long)c.max_seq * D, pos0 + 1, M, D, m->hq, m->hkv,
-                                     scale, nullptr, m->QD, m->a_hi, m->a_lo));
+            SA_RC(prompt_attn_launch(st, m->ctx->status, m->q, m->QD, ka, va, (long long)c.max_seq * D,
+                                     (long long)m->hkv * c.max_seq - shift, pos0 + 1, M, D, m->hq, m->hkv, scale,
+                                     nullptr, m->QD, m->a_hi, m->a_lo));
             if (tp) {
                 SA_RC(gemm(m, m->a_hi, m->a_lo, m->QD, L.wo, M, H, m->QD, QW_EPI_STORE, m->tp_part, H, nullptr, nullptr,
                            0));

@@ -52,12 +52,14 @@ int decode_multi_launch(cudaStream_t st, int* status, const float* q, long long 
                         float scale, float* out, long long o_stride);
 
 // Causal attention of M prompt queries (q at q + m*q_stride, [hq, 128]) over
-// rows [0, T0 + m) of each KV head of a head-major fp32 cache; output fp32
-// (out) and/or bf16 hi/lo planes (out_hi/out_lo), row m at m*o_stride.
-// Defined in sa_prompt_attn.cu.
-int prompt_attn_launch(cudaStream_t st, const float* q, long long q_stride, const float* k, const float* v,
-                       long long kv_head_stride, int T0, int M, int d, int hq, int hkv, float scale, float* out,
-                       long long o_stride, __nv_bfloat16* out_hi, __nv_bfloat16* out_lo);
+// rows [0, T0 + m) of each KV head of a head-major fp32 cache (head h at
+// k / v + h * kv_head_stride; kv_rows = rows of 128 floats addressable from
+// k); output fp32 (out) and/or bf16 hi/lo planes (out_hi/out_lo), row m at
+// m*o_stride.  Defined in sa_prompt_attn.cu.
+int prompt_attn_launch(cudaStream_t st, int* status, const float* q, long long q_stride, const float* k,
+                       const float* v, long long kv_head_stride, long long kv_rows, int T0, int M, int d, int hq,
+                       int hkv, float scale, float* out, long long o_stride, __nv_bfloat16* out_hi,
+                       __nv_bfloat16* out_lo);
 // element-wise / GEMV launchers (sa_qwen3_kernels.cu)
 int launch_embedding(cudaStream_t st, const int64_t* ids, int M, const __nv_bfloat16* E, int V, int H, float* x,
                      int* status);

@@ -56,43 +56,59 @@ __global__ void embedding_kernel(const int64_t* ids, int M, const __nv_bfloat16*
 // With splits > 0, x first gets the `splits` partial planes of the previous
 // GEMM added (plane order; row m of plane z at part + z * plane + m * H) and
 // is written back: the residual add of a split o_proj / down_proj.
-__global__ void rmsnorm_hilo_kernel(float* x, const float* part, int splits, size_t plane, const float* w, int H,
-                                    float eps, __nv_bfloat16* hi, __nv_bfloat16* lo) {
+constexpr int RN_THREADS = 256, RN_MAX4 = 4;   // rows of up to 4096 floats, one register float4 per 256
+__global__ void __launch_bounds__(RN_THREADS)
+rmsnorm_hilo_kernel(float* x, const float* part, int splits, size_t plane, const float* w, int H, float eps,
+                    __nv_bfloat16* hi, __nv_bfloat16* lo) {
     __shared__ float red[32];
+    const int m = blockIdx.x, t = threadIdx.x, n4 = H / 4;
     // launched programmatically: the next kernel (a GEMM) may start streaming
-    // its weights now; x comes from the previous kernel
+    // its weights now; the gains do not depend on the previous kernel, x does
     pdl_trigger();
+    float4 wv[RN_MAX4], v[RN_MAX4];
+#pragma unroll
+    for (int k = 0; k < RN_MAX4; ++k)
+        if (t + k * RN_THREADS < n4) wv[k] = __ldg(reinterpret_cast<const float4*>(w) + t + k * RN_THREADS);
     pdl_wait();
-    const int m = blockIdx.x;
-    float* xr = x + (size_t)m * H;
+    float4* xr = reinterpret_cast<float4*>(x + (size_t)m * H);
+    const float* pr = part ? part + (size_t)m * H : nullptr;
     float ss = 0.f;
-    if (splits > 0) {
-        // float4 columns; every plane's load issued before any is added
-        const float* pr = part + (size_t)m * H;
-        for (int i = 4 * threadIdx.x; i < H; i += 4 * blockDim.x) {
-            float4 pv[QK_MAX_PLANES];
 #pragma unroll
-            for (int z = 0; z < QK_MAX_PLANES; ++z)
-                if (z < splits) pv[z] = __ldcg(reinterpret_cast<const float4*>(pr + z * plane + i));
-            float4 v = *reinterpret_cast<const float4*>(xr + i);
+    for (int k = 0; k < RN_MAX4; ++k) {
+        const int i4 = t + k * RN_THREADS;
+        if (i4 >= n4) break;
+        // every plane's load issued before any is added
+        float4 pv[QK_MAX_PLANES];
 #pragma unroll
-            for (int z = 0; z < QK_MAX_PLANES; ++z)
-                if (z < splits) {
-                    v.x += pv[z].x; v.y += pv[z].y; v.z += pv[z].z; v.w += pv[z].w;
-                }
-            *reinterpret_cast<float4*>(xr + i) = v;
-            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-        }
-    } else {
-        for (int i = threadIdx.x; i < H; i += blockDim.x) ss += xr[i] * xr[i];
+        for (int z = 0; z < QK_MAX_PLANES; ++z)
+            if (z < splits) pv[z] = __ldcg(reinterpret_cast<const float4*>(pr + z * plane) + i4);
+        float4 a = xr[i4];
+#pragma unroll
+        for (int z = 0; z < QK_MAX_PLANES; ++z)
+            if (z < splits) { a.x += pv[z].x; a.y += pv[z].y; a.z += pv[z].z; a.w += pv[z].w; }
+        if (splits > 0) xr[i4] = a;
+        v[k] = a;
+        ss += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
     }
     ss = block_sum(ss, red);
     const float rms = sqrtf(ss / (float)H + eps);
-    for (int i = threadIdx.x; i < H; i += blockDim.x) {
-        const float y = (xr[i] / rms) * w[i];
-        const __nv_bfloat16 h = __float2bfloat16_rn(y);
-        hi[(size_t)m * H + i] = h;
-        lo[(size_t)m * H + i] = __float2bfloat16_rn(y - __bfloat162float(h));
+#pragma unroll
+    for (int k = 0; k < RN_MAX4; ++k) {
+        const int i4 = t + k * RN_THREADS;
+        if (i4 >= n4) break;
+        const float y[4] = {(v[k].x / rms) * wv[k].x, (v[k].y / rms) * wv[k].y, (v[k].z / rms) * wv[k].z,
+                            (v[k].w / rms) * wv[k].w};
+        __nv_bfloat162 h2[2], l2[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            h2[q] = __floats2bfloat162_rn(y[2 * q], y[2 * q + 1]);
+            const float2 f = __bfloat1622float2(h2[q]);
+            l2[q] = __floats2bfloat162_rn(y[2 * q] - f.x, y[2 * q + 1] - f.y);
+        }
+        *reinterpret_cast<uint2*>(hi + (size_t)m * H + 4 * i4) =
+            make_uint2(*reinterpret_cast<uint32_t*>(&h2[0]), *reinterpret_cast<uint32_t*>(&h2[1]));
+        *reinterpret_cast<uint2*>(lo + (size_t)m * H + 4 * i4) =
+            make_uint2(*reinterpret_cast<uint32_t*>(&l2[0]), *reinterpret_cast<uint32_t*>(&l2[1]));
     }
 }
 
@@ -858,8 +874,9 @@ int launch_embedding(cudaStream_t st, const int64_t* ids, int M, const __nv_bflo
 }
 int launch_rmsnorm_hilo(cudaStream_t st, float* x, const float* w, int M, int H, float eps,
                         __nv_bfloat16* hi, __nv_bfloat16* lo, const float* part, int splits) {
-    SA_CHECK_ARG(splits == 0 || (part && splits <= qk::QK_MAX_PLANES && H % 4 == 0), "rmsnorm_hilo: partial planes");
-    SA_CUDA_TRY(launch_pdl_k(1, qk::rmsnorm_hilo_kernel, dim3(M), dim3(256), 0, st, x, part, splits,
+    SA_CHECK_ARG(splits == 0 || (part && splits <= qk::QK_MAX_PLANES), "rmsnorm_hilo: partial planes");
+    SA_CHECK_ARG(H % 4 == 0 && H <= 4 * qk::RN_THREADS * qk::RN_MAX4, "rmsnorm_hilo: H=%d", H);
+    SA_CUDA_TRY(launch_pdl_k(1, qk::rmsnorm_hilo_kernel, dim3(M), dim3(qk::RN_THREADS), 0, st, x, part, splits,
                              (size_t)M * H, w, H, eps, hi, lo));
     return SA_OK;
 }

@@ -165,6 +165,8 @@ int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_
 int cached_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
                         uint64_t row_stride_elems, uint32_t box_rows, uint32_t box_cols);
 int cached_tmap_3d_f32_planes(CUtensorMap* map, void* base, uint64_t rows, uint64_t cols, uint64_t splits);
+int cached_tmap_2d_f32_sw128(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                             uint64_t row_stride_elems, uint32_t box_rows);
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (function, device).
 int set_smem_attr_once(const void* fn, int bytes);
 

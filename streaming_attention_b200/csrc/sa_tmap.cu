@@ -47,6 +47,51 @@ int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_
     return SA_OK;
 }
 
+// 2-D fp32 tensor map over a row-major [rows, cols] block (row stride
+// row_stride_elems), box [box_rows, 32 columns], 128-byte swizzle: KV-cache
+// rows for the prompt attention (16-byte chunk q of row r lands at chunk
+// q ^ (r % 8) of the row's 128 bytes in shared memory).
+int make_tmap_2d_f32_sw128(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                           uint64_t row_stride_elems, uint32_t box_rows) {
+    int rc = get_encode();
+    if (rc) return rc;
+    SA_CHECK_ARG(((uintptr_t)base & 15) == 0 && (row_stride_elems * 4) % 16 == 0 && cols % 32 == 0,
+                 "fp32 tensor map alignment");
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {row_stride_elems * 4};
+    cuuint32_t box[2] = {32, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(SA_ERR_ARG, "cuTensorMapEncodeTiled failed (%d): fp32 rows=%llu cols=%llu", (int)r,
+                         (unsigned long long)rows, (unsigned long long)cols);
+    return SA_OK;
+}
+
+int cached_tmap_2d_f32_sw128(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                             uint64_t row_stride_elems, uint32_t box_rows) {
+    using Key = std::tuple<const void*, uint64_t, uint64_t, uint64_t, uint32_t>;
+    static std::mutex mu;
+    static std::map<Key, CUtensorMap> cache;
+    const Key key{base, rows, cols, row_stride_elems, box_rows};
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) {
+            *map = it->second;
+            return SA_OK;
+        }
+    }
+    int rc = make_tmap_2d_f32_sw128(map, base, rows, cols, row_stride_elems, box_rows);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lk(mu);
+    if (cache.size() > 8192) cache.clear();
+    cache.emplace(key, *map);
+    return SA_OK;
+}
+
 // 3-D fp32 tensor map over `splits` stacked row-major [rows, cols] planes
 // (split partial sums), box 128 rows x 32 columns x 1 plane, 128-byte swizzle:
 // the tensor-store destination of the prompt GEMM's split partials.
