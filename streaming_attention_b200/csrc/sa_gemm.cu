@@ -214,19 +214,26 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ C
             // swizzle (16-byte chunk q of row r at chunk q ^ (r % 8)), stored
             // to plane z by TMA
             if (ok) {
-                uint32_t r[32];
+                // up to four 32-column TMEM loads in flight before one wait
+                constexpr int G = BN / 32 < 4 ? BN / 32 : 4;
+                uint32_t r[G][32];
 #pragma unroll 1
-                for (int j = 0; j < BN / 32; ++j) {
-                    tc::tmem_ld32(tacc + ((uint32_t)(quad * 32) << 16) + 32 * j, r);
-                    tc::tmem_wait_ld();
-                    unsigned char* box = sm + j * (BM * 128) + row * 128;
+                for (int j0 = 0; j0 < BN / 32; j0 += G) {
 #pragma unroll
-                    for (int q = 0; q < 8; ++q)
-                        *reinterpret_cast<float4*>(box + ((q ^ (row & 7)) << 4)) =
-                            make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
-                                        __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+                    for (int g = 0; g < G; ++g)
+                        tc::tmem_ld32(tacc + ((uint32_t)(quad * 32) << 16) + 32 * (j0 + g), r[g]);
+                    tc::tmem_wait_ld();
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        unsigned char* box = sm + (j0 + g) * (BM * 128) + row * 128;
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            *reinterpret_cast<float4*>(box + ((q ^ (row & 7)) << 4)) =
+                                make_float4(__uint_as_float(r[g][4 * q]), __uint_as_float(r[g][4 * q + 1]),
+                                            __uint_as_float(r[g][4 * q + 2]), __uint_as_float(r[g][4 * q + 3]));
+                    }
                 }
-                tc::fence_proxy_async_all();
+                fence_proxy_async_smem();              // the boxes' writes before the tensor stores read them
             }
             asm volatile("bar.sync 1, 128;" ::: "memory");
             if (et == 0 && ok && !*abort) {
