@@ -638,36 +638,6 @@ SA_API int sa_attn_merge(sa_ctx* ctx, int n_parts, int hq, int d, const float* m
 }
 
 namespace sa {
-// Multi-query causal attention (prompt processing of the Qwen3 forward): one
-// CTA per (query, KV head), each a single split, so no scratch or counters.
-int decode_multi_launch(cudaStream_t st, int* status, const float* q, long long q_stride, const float* k,
-                        const float* v, long long kv_head_stride, int T0, int n_q, int d, int hq, int hkv,
-                        float scale, float* out, long long o_stride) {
-    SA_CHECK_ARG(n_q >= 1 && n_q <= 65535 && T0 >= 1, "decode_multi: n_q=%d T0=%d", n_q, T0);
-    dec::Args a;
-    a.q = q; a.k = k; a.v = v;
-    a.kv_head_stride = kv_head_stride;
-    a.T = T0; a.hq = hq; a.hkv = hkv;
-    const int sr = dec::stage_rows(SA_F32, d);
-    a.rows_per_split = (T0 + n_q - 1 + sr - 1) / sr * sr;
-    a.n_splits = 1;
-    a.qscale = scale * dec::LOG2E;
-    a.part_m = a.part_l = a.part_o = nullptr;
-    a.counters = nullptr;
-    a.out = out; a.out_m = nullptr; a.out_l = nullptr;
-    a.status = status;
-    a.q_stride = q_stride; a.o_stride = o_stride;
-    a.len_dev = nullptr;
-    dec::KernelFn fn = dec::pick<float>(d, hq / hkv);
-    SA_CHECK_ARG(fn != nullptr, "decode_multi: hq/hkv=%d d=%d unsupported", hq / hkv, d);
-    SA_RC_TRY(set_smem_attr_once((const void*)fn, dec::SMEM_BYTES));
-    fn<<<dim3(1, hkv, n_q), dec::THREADS, dec::SMEM_BYTES, st>>>(a);
-    SA_CUDA_TRY(cudaGetLastError());
-    return SA_OK;
-}
-}  // namespace sa
-
-namespace sa {
 // Split-KV decode whose row count comes from device memory (T = *len_dev + 1)
 // with a split plan fixed for max_T rows: splits past the current length are
 // empty and drop out of the merge.  Scratch (partials, counters) is the

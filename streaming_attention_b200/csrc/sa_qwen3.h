@@ -43,13 +43,6 @@ int gemm_launch(cudaStream_t st, int* status, const __nv_bfloat16* a_hi, const _
                 long long ldc, __nv_bfloat16* out_hi, __nv_bfloat16* out_lo, long long ldo, GemmPlan plan,
                 float* part, size_t part_floats);
 
-// Multi-query causal attention over a head-major fp32 KV cache: query m of
-// n_q (q at q + m*q_stride, [hq, d]) attends rows [0, T0 + m] of each KV head;
-// out at out + m*o_stride.  One CTA per (query, KV head); defined in
-// sa_decode.cu.
-int decode_multi_launch(cudaStream_t st, int* status, const float* q, long long q_stride, const float* k,
-                        const float* v, long long kv_head_stride, int T0, int n_q, int d, int hq, int hkv,
-                        float scale, float* out, long long o_stride);
 
 // Causal attention of M prompt queries (q at q + m*q_stride, [hq, 128]) over
 // rows [0, T0 + m) of each KV head of a head-major fp32 cache (head h at
@@ -72,8 +65,6 @@ int launch_resid_add(cudaStream_t st, float* x, const float* part, int splits, i
 // SwiGLU of the gate/up partial planes part[z][M][2I] to bf16 hi / lo [M, ldo].
 int launch_swiglu_hilo(cudaStream_t st, const float* part, int splits, int M, int I, __nv_bfloat16* hi,
                        __nv_bfloat16* lo, long long ldo, int num_sms);
-int launch_rmsnorm_f32(cudaStream_t st, const float* x, const float* w, int M, int H, float eps, float* y);
-int launch_split_hilo(cudaStream_t st, const float* x, size_t n, __nv_bfloat16* hi, __nv_bfloat16* lo);
 int launch_rope_table(cudaStream_t st, int n_pos, int D, float theta, float* cos_t, float* sin_t);
 int launch_qknorm_rope_append(cudaStream_t st, const float* qkv, int splits, int M, int hq, int hkv, const float* qn,
                               const float* kn, const float* cos_t, const float* sin_t, int pos0, const int* pos_dev,
@@ -84,9 +75,6 @@ size_t decode_dev_scratch_floats(int num_sms, int max_T, int d, int hq, int hkv,
 int decode_dev_launch(cudaStream_t st, int* status, int num_sms, const float* q, const float* k, const float* v,
                       long long kv_head_stride, const int* len_dev, int T_host, int max_T, int d, int hq, int hkv,
                       float scale, float* out, float* scratch, unsigned* counters);
-int launch_gemv(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, int N_out, int K, const float* x,
-                const float* nw, float eps, float* y, int num_sms);
-int launch_argmax(cudaStream_t st, const float* v, int n, int64_t* out);
 int launch_gemv2(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, int N_out, int K, const float* x,
                  const float* nw, float eps, float* y, unsigned long long* amax, const QkvEpi* qkv = nullptr);
 

@@ -112,17 +112,6 @@ rmsnorm_hilo_kernel(float* x, const float* part, int splits, size_t plane, const
     }
 }
 
-// RMSNorm to fp32 (the final norm before the lm_head GEMV).
-__global__ void rmsnorm_f32_kernel(const float* x, const float* w, int H, float eps, float* y) {
-    __shared__ float red[32];
-    const int m = blockIdx.x;
-    const float* xr = x + (size_t)m * H;
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) ss += xr[i] * xr[i];
-    ss = block_sum(ss, red);
-    const float rms = sqrtf(ss / (float)H + eps);
-    for (int i = threadIdx.x; i < H; i += blockDim.x) y[(size_t)m * H + i] = (xr[i] / rms) * w[i];
-}
 
 // fp32 -> (hi, lo) bf16 split of an activation for the tensor-core GEMM.
 // x += the sum, in plane order, of `splits` partial planes (a split GEMM's
@@ -183,14 +172,6 @@ __global__ void swiglu_hilo_kernel(const float* part, int splits, int M, int I, 
     }
 }
 
-__global__ void split_hilo_kernel(const float* x, size_t n, __nv_bfloat16* hi, __nv_bfloat16* lo) {
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        const float y = x[i];
-        const __nv_bfloat16 h = __float2bfloat16_rn(y);
-        hi[i] = h;
-        lo[i] = __float2bfloat16_rn(y - __bfloat162float(h));
-    }
-}
 
 // ---- RoPE tables (qwen3_ops.cpp:70-104): cos/sin[pos, i], i < D/2 ----------
 __global__ void rope_table_kernel(int n_pos, int D, float theta, float* cos_t, float* sin_t) {
@@ -283,68 +264,6 @@ __global__ void qknorm_rope_append_kernel(const float* qkv, int splits, size_t p
     }
 }
 
-// ---- decode GEMV: y = W x with optional RMSNorm prologue --------------------
-// W [N, K] bf16 row-major, x [K] fp32.  8 warps per CTA; a warp produces one
-// output at a time, each lane streaming 16-byte chunks of the row(s).
-template <int MODE, bool NORM>
-__global__ void __launch_bounds__(256) gemv_kernel(const __nv_bfloat16* __restrict__ W, int N_out, int K,
-                                                   const float* __restrict__ x, const float* __restrict__ nw,
-                                                   float eps, float* __restrict__ y) {
-    extern __shared__ float xs[];          // [K]
-    __shared__ float red[32];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (NORM) {
-        float ss = 0.f;
-        for (int i = threadIdx.x; i < K; i += blockDim.x) ss += x[i] * x[i];
-        ss = block_sum(ss, red);
-        const float rms = sqrtf(ss / (float)K + eps);
-        for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = (x[i] / rms) * nw[i];
-    } else {
-        for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = x[i];
-    }
-    __syncthreads();
-    const int nchunk = K / 8;                      // 16-byte chunks per row
-    for (int n = blockIdx.x * 8 + warp; n < N_out; n += gridDim.x * 8) {
-        int r0 = n, r1 = -1;
-        if (MODE == QW_EPI_SWIGLU) {
-            r0 = (n / 32) * 64 + (n % 32);
-            r1 = r0 + 32;
-        }
-        float acc0 = 0.f, acc1 = 0.f;
-        const uint4* w0 = reinterpret_cast<const uint4*>(W + (size_t)r0 * K);
-        const uint4* w1 = reinterpret_cast<const uint4*>(W + (size_t)(MODE == QW_EPI_SWIGLU ? r1 : r0) * K);
-#pragma unroll 4
-        for (int c = lane; c < nchunk; c += 32) {
-            const uint4 a = __ldg(w0 + c);
-            uint4 b;
-            if (MODE == QW_EPI_SWIGLU) b = __ldg(w1 + c);
-            const float4 xa = *reinterpret_cast<const float4*>(xs + c * 8);
-            const float4 xb = *reinterpret_cast<const float4*>(xs + c * 8 + 4);
-            const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-            const uint32_t wa[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                acc0 = fmaf(__uint_as_float(wa[j] << 16), xv[2 * j], acc0);
-                acc0 = fmaf(__uint_as_float(wa[j] & 0xffff0000u), xv[2 * j + 1], acc0);
-            }
-            if (MODE == QW_EPI_SWIGLU) {
-                const uint32_t wb[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    acc1 = fmaf(__uint_as_float(wb[j] << 16), xv[2 * j], acc1);
-                    acc1 = fmaf(__uint_as_float(wb[j] & 0xffff0000u), xv[2 * j + 1], acc1);
-                }
-            }
-        }
-        acc0 = warp_sum(acc0);
-        if (MODE == QW_EPI_SWIGLU) acc1 = warp_sum(acc1);
-        if (lane == 0) {
-            if (MODE == QW_EPI_SWIGLU) y[n] = (acc0 / (1.f + expf(-acc0))) * acc1;
-            else if (MODE == QW_EPI_RESID) y[n] += acc0;
-            else y[n] = acc0;
-        }
-    }
-}
 
 // ---- decode GEMV v2: one 16-byte chunk column per thread, R rows per CTA ----
 // blockDim = K/8: thread t owns K-chunk t (8 bf16) of each of the CTA's R
@@ -804,37 +723,6 @@ __global__ void amax_to_token_kernel(unsigned long long* amax, int64_t* tok) {
     *amax = 0ull;
 }
 
-// ---- argmax (ops.cpp:213-272): first index of the maximum ------------------
-__global__ void argmax_kernel(const float* __restrict__ v, int n, int64_t* out) {
-    __shared__ float sv[32];
-    __shared__ int si[32];
-    float best = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float x = v[i];
-        if (x > best) { best = x; bi = i; }   // ascending i: keeps the first maximum
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
-    }
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    if (lane == 0) { sv[w] = best; si[w] = bi; }
-    __syncthreads();
-    if (w == 0) {
-        best = lane < (int)(blockDim.x / 32) ? sv[lane] : -INFINITY;
-        bi = lane < (int)(blockDim.x / 32) ? si[lane] : 0x7fffffff;
-#pragma unroll
-        for (int o = 16; o; o >>= 1) {
-            const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
-        }
-        if (lane == 0) *out = bi == 0x7fffffff ? 0 : bi;
-    }
-}
 
 // Decode-loop bookkeeping after a token was chosen: record it and advance the
 // step counter; with inc_len the token just processed is now in the cache.
@@ -880,11 +768,6 @@ int launch_rmsnorm_hilo(cudaStream_t st, float* x, const float* w, int M, int H,
                              (size_t)M * H, w, H, eps, hi, lo));
     return SA_OK;
 }
-int launch_rmsnorm_f32(cudaStream_t st, const float* x, const float* w, int M, int H, float eps, float* y) {
-    qk::rmsnorm_f32_kernel<<<M, 256, 0, st>>>(x, w, H, eps, y);
-    SA_CUDA_TRY(cudaGetLastError());
-    return SA_OK;
-}
 int launch_resid_add(cudaStream_t st, float* x, const float* part, int splits, int M, int H, int num_sms) {
     SA_CHECK_ARG(splits >= 1 && splits <= qk::QK_MAX_PLANES && part && H % 4 == 0, "resid_add: splits %d H %d", splits, H);
     const size_t n4 = (size_t)M * H / 4;
@@ -898,12 +781,6 @@ int launch_swiglu_hilo(cudaStream_t st, const float* part, int splits, int M, in
     const size_t n4 = (size_t)M * I / 4;
     const int grid = (int)std::min<size_t>((n4 + 255) / 256, (size_t)num_sms * 4);
     SA_CUDA_TRY(launch_pdl_k(1, qk::swiglu_hilo_kernel, dim3(grid), dim3(256), 0, st, part, splits, M, I, hi, lo, ldo));
-    return SA_OK;
-}
-int launch_split_hilo(cudaStream_t st, const float* x, size_t n, __nv_bfloat16* hi, __nv_bfloat16* lo) {
-    const int grid = (int)std::min<size_t>((n + 255) / 256, 4096);
-    qk::split_hilo_kernel<<<grid, 256, 0, st>>>(x, n, hi, lo);
-    SA_CUDA_TRY(cudaGetLastError());
     return SA_OK;
 }
 int launch_rope_table(cudaStream_t st, int n_pos, int D, float theta, float* cos_t, float* sin_t) {
@@ -921,21 +798,6 @@ int launch_qknorm_rope_append(cudaStream_t st, const float* qkv, int splits, int
     SA_CUDA_TRY(launch_pdl_k(1, qk::qknorm_rope_append_kernel, dim3((warps + 7) / 8), dim3(256), 0, st, qkv, splits,
                              (size_t)M * (hq + 2 * hkv) * 128, M, hq, hkv, qn, kn, cos_t, sin_t, pos0, pos_dev,
                              row_shift, q_out, kc, vc, max_seq));
-    SA_CUDA_TRY(cudaGetLastError());
-    return SA_OK;
-}
-int launch_gemv(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, int N_out, int K, const float* x,
-                const float* nw, float eps, float* y, int num_sms) {
-    SA_CHECK_ARG(K % 8 == 0, "gemv: K=%d", K);
-    const size_t smem = (size_t)K * sizeof(float);
-    int grid = (N_out + 7) / 8;
-    const int cap = num_sms * 8;
-    if (grid > cap) grid = cap;
-#define SA_GEMV(MODE, NORM) qk::gemv_kernel<MODE, NORM><<<grid, 256, smem, st>>>(W, N_out, K, x, nw, eps, y)
-    if (mode == QW_EPI_STORE) { if (norm) SA_GEMV(QW_EPI_STORE, true); else SA_GEMV(QW_EPI_STORE, false); }
-    else if (mode == QW_EPI_RESID) { if (norm) SA_GEMV(QW_EPI_RESID, true); else SA_GEMV(QW_EPI_RESID, false); }
-    else { if (norm) SA_GEMV(QW_EPI_SWIGLU, true); else SA_GEMV(QW_EPI_SWIGLU, false); }
-#undef SA_GEMV
     SA_CUDA_TRY(cudaGetLastError());
     return SA_OK;
 }
@@ -1027,11 +889,6 @@ int launch_tp_seq_add(cudaStream_t st, unsigned* seq, int n) {
 }
 int launch_amax_to_token(cudaStream_t st, unsigned long long* amax, int64_t* tok) {
     SA_CUDA_TRY(launch_pdl_k(3, qk::amax_to_token_kernel, dim3(1), dim3(1), 0, st, amax, tok));
-    SA_CUDA_TRY(cudaGetLastError());
-    return SA_OK;
-}
-int launch_argmax(cudaStream_t st, const float* v, int n, int64_t* out) {
-    qk::argmax_kernel<<<1, 1024, 0, st>>>(v, n, out);
     SA_CUDA_TRY(cudaGetLastError());
     return SA_OK;
 }
