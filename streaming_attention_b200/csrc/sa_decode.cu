@@ -123,10 +123,17 @@ template <typename KT, int D, int G>
 __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
     using S = Shape<KT, D>;
     constexpr int SR = S::STAGE_ROWS, RB = S::ROW_BYTES, CPL = S::CPL, CH = S::CH, VEC = S::VEC;
-    constexpr int DYN_ROWS = 2 * SR;   // rows per CTA when the length is read on the device
+    constexpr int DYN_ROWS = 8 * SR;   // rows per CTA when the length is read on the device
 
     pdl_trigger();
-    pdl_wait();
+    // Launched inside the captured decode step (a.len_dev set), the kernel
+    // plans its split from the cache length and streams the rows cached by
+    // earlier steps before griddepcontrol.wait: the length and those rows
+    // were written before the step's first kernel, an ordinary (not
+    // programmatic) launch, so they are complete and visible here; only the
+    // newest row (appended by the QKV kernel this kernel follows) and q need
+    // the wait.  Otherwise every input may come from the previous kernel.
+    if (!a.len_dev) pdl_wait();
     extern __shared__ __align__(128) unsigned char smem[];
     unsigned char* kbuf = smem;
     unsigned char* vbuf = smem + STAGES * SR * RB;
@@ -172,9 +179,21 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
 
     if (warp == NW) {
         // ---------------- producer: one elected lane issues the bulk copies
+        // device-length launches: the first stages whose rows all precede
+        // the newest row go out before the wait for the previous kernel
+        const int pre = a.len_dev ? min(STAGES, min(nst, (T - 1 - t0) / SR)) : 0;
+        const uint64_t pol = policy_evict_first();
+        if (lane == 0)
+            for (int it = 0; it < pre; ++it) {
+                const uint32_t bytes = (uint32_t)(SR * RB);
+                mbar_arrive_expect_tx(full + it, 2 * bytes);
+                bulk_g2s_hint(kbuf + it * SR * RB, kg + (size_t)it * SR * D, bytes, full + it, pol);
+                bulk_g2s_hint(vbuf + it * SR * RB, vg + (size_t)it * SR * D, bytes, full + it, pol);
+            }
+        __syncwarp();
+        if (a.len_dev) pdl_wait();
         if (lane == 0) {
-            const uint64_t pol = policy_evict_first();
-            int it = 0;
+            int it = pre;
             for (; it < nst; ++it) {
                 const int s = it % STAGES;
                 if (it >= STAGES && !mbar_wait(empty + s, ((it / STAGES) & 1) ^ 1, a.status)) break;
@@ -187,7 +206,8 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
             s_issued = it;
         }
     } else {
-        // ---------------- consumers
+        // ---------------- consumers (q comes from the previous kernel)
+        if (a.len_dev) pdl_wait();
         float qr[G][CPL];
 #pragma unroll
         for (int g = 0; g < G; ++g) {
