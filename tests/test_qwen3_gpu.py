@@ -97,6 +97,19 @@ def test_qwen3_prompt_gqa_ratios(ctx, oracle, hq, hkv, S):
     _close(m.forward(ids), oracle.qwen3_forward(cfg, w, ids), f"hq={hq} hkv={hkv} S={S}")
 
 
+def test_qwen3_long_prompt(ctx, oracle):
+    """A 1000-token prompt: eight 128-row GEMM tiles (the last ragged), so the
+    projections run unsplit with 256-wide tiles, and eight attention rounds."""
+    from streaming_attention_b200 import Qwen3
+    cfg = Qwen3Cfg(vocab=600, hidden=256, n_layers=2, hq=4, hkv=2, head_dim=128, inter=512,
+                   eps=1e-6, theta=1e6)
+    w = make_qwen3_weights(cfg, 53)
+    ids = I.rng(9).integers(0, cfg.vocab, 1000)
+    m = Qwen3(_cfgdict(cfg), max_seq=1024, ctx=ctx)
+    m.load(w)
+    _close(m.forward(ids, logits="all"), oracle.qwen3_forward(cfg, w, ids, all_logits=True), "S=1000")
+
+
 def test_qwen3_long_prefix_continuation(ctx, oracle):
     """A 40-token prompt continued after 300 cached tokens: its attention runs
     over several 128-row rounds of the cache."""
