@@ -463,7 +463,7 @@ def run_ours(args):
                 "ms": round(pms, 4), "frac_of_bf16_peak": round(ptf / bpk, 4),
                 "peak": f"{bpk} ({bkind} bf16_tflops)", "workload": PF_WORKLOAD}}
             try:
-                q3, weights = measure_qwen3(ctx, dev, stream, 5, 2)
+                q3, weights = measure_qwen3(ctx, dev, stream, 20, 3)
                 q3line = {"metric": "Qwen3-0.6B tok/s", "workload": Q3_WORKLOAD,
                           **{k: round(v, 3) for k, v in q3.items()}}
                 if not args.no_cpu:
