@@ -36,8 +36,11 @@ namespace dec {
 constexpr int NW = 4;                      // consumer warps
 constexpr int THREADS = (NW + 1) * 32;     // + one producer warp
 constexpr int STAGE_BYTES = 32768;         // K + V bytes per stage
-constexpr int STAGES = 3;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 2 * STAGES * 8 + 16;
+constexpr int STAGES = 3;                  // ring depth of the general kernel (2 CTAs per SM)
+constexpr int DEV_STAGES = 6;              // the decode step's kernel: 192 cached rows in flight
+template <int NST>
+constexpr int smem_bytes() { return NST * STAGE_BYTES + 2 * NST * 8 + 16; }
+constexpr int SMEM_BYTES = smem_bytes<STAGES>();
 constexpr int MAX_SPLITS = 1024;
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
@@ -119,8 +122,8 @@ __device__ __forceinline__ void combine_weights(float m, float m2, float& a, flo
     b = (m2 == -INFINITY) ? 0.f : ex2(m2 - M);
 }
 
-template <typename KT, int D, int G>
-__global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
+template <typename KT, int D, int G, int NST = STAGES>
+__global__ void __launch_bounds__(THREADS, NST <= 3 ? 2 : 1) decode_kernel(const Args a) {
     using S = Shape<KT, D>;
     constexpr int SR = S::STAGE_ROWS, RB = S::ROW_BYTES, CPL = S::CPL, CH = S::CH, VEC = S::VEC;
     constexpr int DYN_ROWS = 8 * SR;   // rows per CTA when the length is read on the device
@@ -136,9 +139,9 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
     if (!a.len_dev) pdl_wait();
     extern __shared__ __align__(128) unsigned char smem[];
     unsigned char* kbuf = smem;
-    unsigned char* vbuf = smem + STAGES * SR * RB;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-    uint64_t* empty = full + STAGES;
+    unsigned char* vbuf = smem + NST * SR * RB;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + NST * STAGE_BYTES);
+    uint64_t* empty = full + NST;
     __shared__ float red_m[NW][G], red_l[NW][G];
     __shared__ int s_issued, s_consumed, s_last;
 
@@ -164,7 +167,7 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
     const KT* vg = static_cast<const KT*>(a.v) + (size_t)kvh * a.kv_head_stride + (size_t)t0 * D;
 
     if (tid == 0) {
-        for (int s = 0; s < STAGES; ++s) {
+        for (int s = 0; s < NST; ++s) {
             mbar_init(full + s, 1);
             mbar_init(empty + s, NW);
         }
@@ -179,24 +182,46 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
 
     if (warp == NW) {
         // ---------------- producer: one elected lane issues the bulk copies
-        // device-length launches: the first stages whose rows all precede
-        // the newest row go out before the wait for the previous kernel
-        const int pre = a.len_dev ? min(STAGES, min(nst, (T - 1 - t0) / SR)) : 0;
+        // device-length launches: every stage of rows cached by earlier steps
+        // that fits the ring goes out before the wait for the previous
+        // kernel, including the rows of the newest row's stage before it;
+        // the newest row (appended by that kernel) follows the wait
+        const int rel_new = T - 1 - t0;                       // >= 0
+        const bool has_new = a.len_dev && rel_new < nrows;     // then it is the split's last row
+        const int st_new = has_new ? rel_new / SR : nst;
+        const int pre = a.len_dev ? min(NST, min(nst, st_new)) : 0;
+        const bool split_new = has_new && st_new < NST;
         const uint64_t pol = policy_evict_first();
-        if (lane == 0)
+        if (lane == 0) {
             for (int it = 0; it < pre; ++it) {
-                const uint32_t bytes = (uint32_t)(SR * RB);
+                const uint32_t bytes = (uint32_t)(min(SR, nrows - it * SR) * RB);
                 mbar_arrive_expect_tx(full + it, 2 * bytes);
                 bulk_g2s_hint(kbuf + it * SR * RB, kg + (size_t)it * SR * D, bytes, full + it, pol);
                 bulk_g2s_hint(vbuf + it * SR * RB, vg + (size_t)it * SR * D, bytes, full + it, pol);
             }
+            if (split_new) {
+                const int rows = rel_new - st_new * SR + 1;         // the stage's rows, newest last
+                mbar_arrive_expect_tx(full + st_new, 2 * (uint32_t)(rows * RB));
+                if (rows > 1) {
+                    const uint32_t bytes = (uint32_t)((rows - 1) * RB);
+                    bulk_g2s_hint(kbuf + st_new * SR * RB, kg + (size_t)st_new * SR * D, bytes, full + st_new, pol);
+                    bulk_g2s_hint(vbuf + st_new * SR * RB, vg + (size_t)st_new * SR * D, bytes, full + st_new, pol);
+                }
+            }
+        }
         __syncwarp();
         if (a.len_dev) pdl_wait();
         if (lane == 0) {
             int it = pre;
+            if (split_new) {
+                const int r = rel_new - st_new * SR;
+                bulk_g2s_hint(kbuf + (st_new * SR + r) * RB, kg + (size_t)rel_new * D, RB, full + st_new, pol);
+                bulk_g2s_hint(vbuf + (st_new * SR + r) * RB, vg + (size_t)rel_new * D, RB, full + st_new, pol);
+                it = st_new + 1;
+            }
             for (; it < nst; ++it) {
-                const int s = it % STAGES;
-                if (it >= STAGES && !mbar_wait(empty + s, ((it / STAGES) & 1) ^ 1, a.status)) break;
+                const int s = it % NST;
+                if (it >= NST && !mbar_wait(empty + s, ((it / NST) & 1) ^ 1, a.status)) break;
                 const int rows = min(SR, nrows - it * SR);
                 const uint32_t bytes = (uint32_t)(rows * RB);
                 mbar_arrive_expect_tx(full + s, 2 * bytes);
@@ -226,8 +251,8 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
 
         int it = 0;
         for (; it < nst; ++it) {
-            const int s = it % STAGES;
-            if (!mbar_wait(full + s, (it / STAGES) & 1, a.status)) break;
+            const int s = it % NST;
+            if (!mbar_wait(full + s, (it / NST) & 1, a.status)) break;
             const int valid_rows = min(SR, nrows - it * SR);
             const unsigned char* ks = kbuf + s * SR * RB;
             const unsigned char* vs = vbuf + s * SR * RB;
@@ -324,7 +349,7 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
     // the stage buffers are reused or the CTA exits.
     if (tid == 0 && s_consumed < s_issued) {
         for (int it = s_consumed; it < s_issued; ++it)
-            mbar_wait(full + it % STAGES, (it / STAGES) & 1, nullptr);
+            mbar_wait(full + it % NST, (it / NST) & 1, nullptr);
     }
     __syncthreads();
 
@@ -476,6 +501,17 @@ static KernelFn pick(int d, int G) {
 }
 
 static int stage_rows(int dtype, int d) { return STAGE_BYTES / (2 * d * (dtype == SA_F32 ? 4 : 2)); }
+
+// The decode step's kernel (fp32 cache, head_dim 128): a DEV_STAGES-deep ring.
+static KernelFn pick_dev(int d, int G) {
+    if (d != 128) return nullptr;
+    switch (G) {
+        case 1: return decode_kernel<float, 128, 1, DEV_STAGES>;
+        case 2: return decode_kernel<float, 128, 2, DEV_STAGES>;
+        case 4: return decode_kernel<float, 128, 4, DEV_STAGES>;
+        default: return nullptr;
+    }
+}
 
 }  // namespace dec
 
@@ -690,10 +726,15 @@ int decode_dev_launch(cudaStream_t st, int* status, int num_sms, const float* q,
     a.status = status;
     a.q_stride = 0; a.o_stride = 0;
     a.len_dev = len_dev;
-    dec::KernelFn fn = dec::pick<float>(d, hq / hkv);
+    dec::KernelFn fn = dec::pick_dev(d, hq / hkv);
+    int smem = dec::smem_bytes<dec::DEV_STAGES>();
+    if (!fn) {
+        fn = dec::pick<float>(d, hq / hkv);
+        smem = dec::SMEM_BYTES;
+    }
     SA_CHECK_ARG(fn != nullptr, "decode_dev: hq/hkv=%d d=%d unsupported", hq / hkv, d);
-    SA_RC_TRY(set_smem_attr_once((const void*)fn, dec::SMEM_BYTES));
-    SA_CUDA_TRY(launch_pdl_k(2, fn, dim3(ns, hkv), dim3(dec::THREADS), dec::SMEM_BYTES, st, a));
+    SA_RC_TRY(set_smem_attr_once((const void*)fn, smem));
+    SA_CUDA_TRY(launch_pdl_k(2, fn, dim3(ns, hkv), dim3(dec::THREADS), smem, st, a));
     return SA_OK;
 }
 }  // namespace sa
