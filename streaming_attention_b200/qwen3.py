@@ -23,7 +23,7 @@ class Qwen3Config(C.Structure):
                 ("theta", C.c_float), ("max_seq", C.c_int)]
 
 
-# Qwen3-0.6B (SURVEY/BASELINE configs[3], configs[4])
+# Qwen3-0.6B: the model of the benchmark configurations configs[3] and configs[4]
 QWEN3_0_6B = dict(vocab=151936, hidden=1024, n_layers=28, hq=16, hkv=8, head_dim=128, inter=3072,
                   eps=1e-6, theta=1e6)
 
