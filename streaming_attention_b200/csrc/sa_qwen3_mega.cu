@@ -573,10 +573,11 @@ __global__ void __launch_bounds__(THREADS, 1) decode_step_kernel(const __grid_co
 // Shapes the single-launch step handles: head_dim 128, one or two query heads
 // per KV head, activation vectors that fit its shared-memory buffer, and at
 // least one CTA per KV head.  (Rows of every matrix then fit a ring slot.)
-// It is selected with SA_QWEN3_MEGA=1: on Qwen3-0.6B it measures 1.40 ms per
-// token against 0.94 ms for the CUDA graph of separate kernels (the five grid
-// barriers and latency-bound phases of a layer cost ~48 us, the graph's
-// kernels ~33 us), so the graph is the default.
+// It is selected with SA_QWEN3_MEGA=1: on Qwen3-0.6B it measured 1.40 ms per
+// token against 0.94 ms for the CUDA graph of separate kernels at the time
+// (the five grid barriers and latency-bound phases of a layer cost ~48 us,
+// the graph's kernels ~33 us; the graph has since reached 0.74 ms), so the
+// graph is the default.
 bool mega_supported(const sa_qwen3_config& c, int num_sms) {
     const int G = c.hkv > 0 && c.hq % c.hkv == 0 ? c.hq / c.hkv : 0;
     const char* on = std::getenv("SA_QWEN3_MEGA");
