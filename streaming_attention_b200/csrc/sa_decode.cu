@@ -25,6 +25,7 @@
 #include <cuda_bf16.h>
 #include <cmath>
 
+#include "sa_decode_plan.h"
 #include "sa_internal.h"
 #include "sa_ptx.cuh"
 #include "sa_qwen3.h"
@@ -154,10 +155,9 @@ __global__ void __launch_bounds__(THREADS, NST <= 3 ? 2 : 1) decode_kernel(const
     // (the merge then counts only the splits in use).
     int rps = a.rows_per_split, nsplit = a.n_splits;
     if (a.len_dev) {
-        int want = (T + DYN_ROWS - 1) / DYN_ROWS;
-        want = want < 1 ? 1 : (want > a.n_splits ? a.n_splits : want);
-        rps = ((T + want - 1) / want + SR - 1) / SR * SR;
-        nsplit = (T + rps - 1) / rps;
+        const Split sp = dev_split(T, a.n_splits, SR, DYN_ROWS);
+        rps = sp.rps;
+        nsplit = sp.nsplit;
         if (split >= nsplit) return;
     }
     const int t0 = split * rps;
@@ -186,11 +186,9 @@ __global__ void __launch_bounds__(THREADS, NST <= 3 ? 2 : 1) decode_kernel(const
         // that fits the ring goes out before the wait for the previous
         // kernel, including the rows of the newest row's stage before it;
         // the newest row (appended by that kernel) follows the wait
-        const int rel_new = T - 1 - t0;                       // >= 0
-        const bool has_new = a.len_dev && rel_new < nrows;     // then it is the split's last row
-        const int st_new = has_new ? rel_new / SR : nst;
-        const int pre = a.len_dev ? min(NST, min(nst, st_new)) : 0;
-        const bool split_new = has_new && st_new < NST;
+        const PreWait pw = pre_wait_plan(a.len_dev != nullptr, T, t0, nrows, SR, NST);
+        const int pre = pw.pre, st_new = pw.st_new;
+        const bool split_new = pw.split_new;
         const uint64_t pol = policy_evict_first();
         if (lane == 0) {
             for (int it = 0; it < pre; ++it) {
@@ -200,7 +198,7 @@ __global__ void __launch_bounds__(THREADS, NST <= 3 ? 2 : 1) decode_kernel(const
                 bulk_g2s_hint(vbuf + it * SR * RB, vg + (size_t)it * SR * D, bytes, full + it, pol);
             }
             if (split_new) {
-                const int rows = rel_new - st_new * SR + 1;         // the stage's rows, newest last
+                const int rows = pw.head + 1;                        // the stage's rows, newest last
                 mbar_arrive_expect_tx(full + st_new, 2 * (uint32_t)(rows * RB));
                 if (rows > 1) {
                     const uint32_t bytes = (uint32_t)((rows - 1) * RB);
@@ -214,10 +212,10 @@ __global__ void __launch_bounds__(THREADS, NST <= 3 ? 2 : 1) decode_kernel(const
         if (lane == 0) {
             int it = pre;
             if (split_new) {
-                const int r = rel_new - st_new * SR;
-                bulk_g2s_hint(kbuf + (st_new * SR + r) * RB, kg + (size_t)rel_new * D, RB, full + st_new, pol);
-                bulk_g2s_hint(vbuf + (st_new * SR + r) * RB, vg + (size_t)rel_new * D, RB, full + st_new, pol);
-                it = st_new + 1;
+                const int r = st_new * SR + pw.head;                 // the newest row, T - 1 - t0
+                bulk_g2s_hint(kbuf + r * RB, kg + (size_t)r * D, RB, full + st_new, pol);
+                bulk_g2s_hint(vbuf + r * RB, vg + (size_t)r * D, RB, full + st_new, pol);
+                it = pw.post0;
             }
             for (; it < nst; ++it) {
                 const int s = it % NST;
