@@ -138,6 +138,52 @@ int sa_attn_merge(sa_ctx* ctx, int n_parts, int hq, int d, const float* m, const
                   const float* o, float* out, float* m_out, float* l_out, unsigned flags);
 
 /* ======================================================================== */
+/* Sequence-parallel decode over several GPUs                                */
+/* ======================================================================== */
+
+/*
+ * The KV sequence is split over `world` ranks (1..8), one GPU per rank, each
+ * holding a contiguous slice in rank order -- the partition of
+ * streaming_attention_mpi_simple (attention/src/streaming_mpi.cpp:252-309).
+ * Each rank's sa_attn_decode_sp launch reduces its slice to per-head (m, l, O)
+ * states, and the CTA that finishes each KV head stores those states into
+ * every rank's exchange buffer over NVLink and merges all ranks' states in
+ * rank order (merge_partial_results, streaming_omp.cpp:27-48): one launch per
+ * rank, no collective library, and the result on EVERY rank (the reference
+ * returns it on rank 0 only and zeros elsewhere, streaming_mpi.cpp:306-308).
+ *
+ * sa_sp_create: this rank's exchange object on the context's GPU, for calls
+ *   with hq <= max_hq and d <= max_d (d in {64, 128, 256}).
+ * sa_sp_handle: SA_SP_HANDLE_BYTES bytes naming this rank's exchange buffer
+ *   (a CUDA IPC handle and the GPU's UUID), to be sent to every rank over any
+ *   host channel.
+ * sa_sp_connect: the world handles in rank order; maps the other ranks'
+ *   buffers.  Ranks on one GPU are rejected (SA_ERR_ARG): the launches wait
+ *   for one another and must run on different GPUs.
+ * sa_sp_connect_local: the same for `n` ranks of ONE process (one sa_sp per
+ *   GPU, sps[i] rank i): enables peer access and links the buffers directly.
+ * sa_attn_decode_sp: sa_attn_decode_partial's arguments for this rank's
+ *   slice (T_local rows, may be 0), q identical on every rank.  out [hq, d]
+ *   (and m_out / l_out [hq] if non-NULL) receive the merged result of the
+ *   whole sequence on every rank.  Every rank must make the same calls, with
+ *   the same hq / hkv / d, in the same order; calls on one rank must not
+ *   overlap on different streams.  A rank that does not take part makes the
+ *   others' waits expire after a few seconds (NaN in out, SA_ERR_TIMEOUT at
+ *   their next synchronising call).  SA_HOST_PTRS is accepted (staged,
+ *   blocking).
+ */
+#define SA_SP_HANDLE_BYTES 128
+typedef struct sa_sp sa_sp;
+int sa_sp_create(sa_ctx* ctx, int rank, int world, int max_hq, int max_d, sa_sp** out);
+int sa_sp_handle(sa_sp* sp, void* handle);
+int sa_sp_connect(sa_sp* sp, const void* handles);
+int sa_sp_connect_local(sa_sp* const* sps, int n);
+int sa_sp_destroy(sa_sp* sp);
+int sa_attn_decode_sp(sa_sp* sp, int dtype, const void* q, const void* k, const void* v,
+                      long long kv_head_stride, int T_local, int d, int hq, int hkv, int block,
+                      float scale, float* out, float* m_out, float* l_out, unsigned flags);
+
+/* ======================================================================== */
 /* Causal prefill attention (tensor cores)                                   */
 /* ======================================================================== */
 
@@ -200,14 +246,16 @@ int sa_attn_decode_step(sa_ctx* ctx, int dtype, const void* q, const void* k_new
  *    ~ 2 * SMs / hkv) exceeds SA_NOALLOC_SCRATCH_BYTES are rejected with
  *    SA_ERR_ARG and a message naming the sizes.
  *  - The first call on a GPU looks up the array's device address
- *    (cudaGetSymbolAddress) with that GPU current and caches it; make that
- *    first call before any stream capture.
+ *    (cudaGetSymbolAddress) with that GPU current and caches it for the life
+ *    of the process; make that first call before any stream capture, and do
+ *    not reset the device (cudaDeviceReset) between calls.
  *  - All calls on a GPU share the array, which keeps the last call's
- *    contents; each call clears the counters it needs.  Calls whose
- *    executions overlap on the GPU (different streams, or host threads
- *    without ordering) race on the array and give wrong results.
- *  - Asynchronous: errors of the kernel itself (a device-side wait that
- *    expired) are not reported back; argument errors are.
+ *    contents; each call clears the counters and the status word it needs.
+ *    Calls whose executions overlap on the GPU (different streams, or host
+ *    threads without ordering) race on the array and give wrong results.
+ *  - Asynchronous: argument errors are returned; a device-side wait of the
+ *    kernel that expired (a fault of the GPU, not of the arguments) is not
+ *    reported by a return code but leaves NaN in `out`.
  */
 #define SA_NOALLOC_SCRATCH_BYTES (2u << 20)
 int sa_attn_decode_noalloc(void* stream, int dtype, const void* q, const void* k, const void* v,

@@ -17,6 +17,8 @@ SA_ERR_NCCL = -5
 SA_ERR_RANGE = -6
 SA_ERR_FULL = -7
 
+SA_SP_HANDLE_BYTES = 128
+
 SA_F32 = 0
 SA_BF16 = 1
 SA_HOST_PTRS = 1
@@ -67,6 +69,13 @@ SIGNATURES = {
                                    C.c_uint]),
     "sa_qwen3_generate": (C.c_int, [_vp, C.POINTER(C.c_int64), C.c_int, C.c_int,
                                     C.POINTER(C.c_int64), C.c_uint]),
+    "sa_sp_create": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]),
+    "sa_sp_handle": (C.c_int, [_vp, _vp]),
+    "sa_sp_connect": (C.c_int, [_vp, _vp]),
+    "sa_sp_connect_local": (C.c_int, [C.POINTER(_vp), C.c_int]),
+    "sa_sp_destroy": (C.c_int, [_vp]),
+    "sa_attn_decode_sp": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, C.c_longlong, C.c_int, C.c_int,
+                                    C.c_int, C.c_int, C.c_int, C.c_float, _vp, _vp, _vp, C.c_uint]),
     "sa_attn_decode_noalloc": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, C.c_longlong, C.c_int,
                                          C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, _vp]),
 }

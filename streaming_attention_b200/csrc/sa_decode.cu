@@ -46,6 +46,23 @@ constexpr int MAX_SPLITS = 1024;
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
 
+// Sequence-parallel exchange of one launch (world > 1): every rank holds a
+// contiguous slice of the sequence and runs this kernel on it; the merging
+// CTA of each KV head sends that head's (m, L, O/L) states as self-validating
+// words to every rank's word area and merges all ranks' states, in rank
+// order, into the output -- the Gather + merge of
+// streaming_attention_mpi_simple (attention/src/streaming_mpi.cpp:252-309),
+// with every rank ending up with the result.
+constexpr int SP_MAX = 8;
+struct SpArgs {
+    int rank, world;
+    // word areas of every rank (own at [rank]), each [2 slots][world][hq][d+2]:
+    // per source rank and query head d words of O/L, then m (log2 domain), L
+    unsigned long long* words[SP_MAX];
+    unsigned* seq;    // this rank's instance count: slot = seq & 1, epoch = seq + 1
+    unsigned* done;   // merging CTAs of this launch that finished (the last re-arms it)
+};
+
 struct Args {
     const void* q;
     const void* k;
@@ -69,6 +86,7 @@ struct Args {
     // KV-cache length before the token being decoded, plus that token), so a
     // captured launch stays valid as the cache grows
     const int* len_dev;
+    SpArgs sp;                  // sp.world > 1: sequence-parallel exchange after the merge
 };
 
 // Unpack one 16-byte chunk into VEC floats.
@@ -121,6 +139,80 @@ __device__ __forceinline__ void combine_weights(float m, float m2, float& a, flo
     M = fmaxf(m, m2);
     a = (m == -INFINITY) ? 0.f : ex2(m - M);
     b = (m2 == -INFINITY) ? 0.f : ex2(m2 - M);
+}
+
+// Shared-memory offsets of the final states [G][D+2] a sequence-parallel
+// launch exchanges (at most (G*D + 2G) * 4 <= 2112 bytes, G*D <= 512) and
+// of the sources' (m, L) (2 * G * world <= 128 floats): past the cross-warp
+// reduction (NW*G*D floats) and the split weights of the merge
+// (G*MAX_SPLITS + 2G floats), inside the stage ring (>= 96 KB).
+constexpr int FIN_OFF = 64 * 1024;
+constexpr int ML_OFF = FIN_OFF + 4096;
+static_assert(FIN_OFF >= (8 * MAX_SPLITS + 2 * 8) * 4 && FIN_OFF >= NW * 512 * 4 &&
+              ML_OFF + 2 * 8 * SP_MAX * 4 <= STAGES * STAGE_BYTES,
+              "exchange buffers inside the stage ring, past the reduction scratch");
+
+// The merging CTA of KV head kvh has the final (O/L, m, L) of its G query
+// heads in fin[G][D+2]; send them to every rank, wait for every rank's,
+// merge them in rank order and write out (and out_m / out_l).  The last
+// merging CTA of the launch advances the instance count.  Two slots
+// alternate: a rank writes instance i+2 into slot i&1 of a peer only after
+// it has read that peer's instance i+1 words, which the peer sends after its
+// launch i -- and so all its reads of slot i&1 -- completed.
+template <int G, int D>
+__device__ void sp_exchange(const Args& a, int kvh, const float* fin, float* ml) {
+    constexpr int RW = D + 2;
+    const SpArgs& s = a.sp;
+    const int W = s.world, tid = threadIdx.x;
+    const unsigned inst = __ldcg(s.seq);
+    const int slot = (int)(inst & 1u);
+    const unsigned epoch = inst + 1u;
+    const size_t src_stride = (size_t)a.hq * RW;
+    // send: consecutive threads store consecutive words of one destination
+    for (int idx = tid; idx < W * G * RW; idx += THREADS) {
+        const int r = idx / (G * RW), rem = idx - r * (G * RW);
+        const int g = rem / RW, c = rem - g * RW;
+        unsigned long long* dst = s.words[r] + ((size_t)slot * W + s.rank) * src_stride +
+                                  (size_t)(kvh * G + g) * RW + c;
+        st_u64_relaxed_sys(dst, epoch_word(epoch, fin[g * RW + c]));
+    }
+    // receive the sources' (m, L), then each output column from every source
+    const unsigned long long* own = s.words[s.rank] + (size_t)slot * W * src_stride;
+    for (int idx = tid; idx < G * W; idx += THREADS) {
+        const int g = idx / W, src = idx - g * W;
+        const unsigned long long* p = own + src * src_stride + (size_t)(kvh * G + g) * RW + D;
+        ml[2 * idx] = wait_epoch_word(p, epoch, a.status);
+        ml[2 * idx + 1] = wait_epoch_word(p + 1, epoch, a.status);
+    }
+    __syncthreads();
+    for (int idx = tid; idx < G * D; idx += THREADS) {
+        const int g = idx / D, col = idx - g * D;
+        const int h = kvh * G + g;
+        float M = -INFINITY;
+        for (int src = 0; src < W; ++src) M = fmaxf(M, ml[2 * (g * W + src)]);
+        float L = 0.f, O = 0.f;
+        for (int src = 0; src < W; ++src) {
+            const float ms = ml[2 * (g * W + src)];
+            const float wt = (ms == -INFINITY) ? 0.f : ml[2 * (g * W + src) + 1] * ex2(ms - M);
+            const float o = wait_epoch_word(own + src * src_stride + (size_t)h * RW + col, epoch, a.status);
+            L += wt;
+            O = fmaf(wt, o, O);
+        }
+        const bool failed = *reinterpret_cast<volatile int*>(a.status) != 0;
+        a.out[(size_t)h * D + col] = failed ? nanf("") : (L > 0.f ? O / L : 0.f);
+        if (col == 0 && a.out_m) {
+            a.out_m[h] = L > 0.f ? M * LN2 : -INFINITY;
+            a.out_l[h] = L > 0.f ? L : 1.f;
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        if (atomicAdd(s.done, 1u) == (unsigned)(a.hkv - 1)) {
+            *s.done = 0u;
+            __stcg(s.seq, inst + 1u);
+        }
+    }
 }
 
 template <typename KT, int D, int G, int NST = STAGES>
@@ -369,6 +461,13 @@ __global__ void __launch_bounds__(THREADS, NST <= 3 ? 2 : 1) decode_kernel(const
     }
     __syncthreads();
 
+    const bool sp = a.sp.world > 1;
+    float* fin = reinterpret_cast<float*>(smem + FIN_OFF);       // [G][D+2] (sequence-parallel)
+    // A device-side wait that expired (this CTA's, or one of a split that
+    // arrived before the merge) leaves NaN in the output, so a caller that
+    // never reads the status word still sees the failure.
+    const float bad = nanf("");
+    bool failed = *reinterpret_cast<volatile int*>(a.status) != 0;
     for (int idx = tid; idx < G * D; idx += THREADS) {
         const int g = idx / D, col = idx % D;
         float M = -INFINITY;
@@ -383,8 +482,16 @@ __global__ void __launch_bounds__(THREADS, NST <= 3 ? 2 : 1) decode_kernel(const
         }
         const int h = kvh * G + g;
         if (nsplit == 1) {
+            if (sp) {   // this rank's state of head h, exchanged below
+                fin[g * (D + 2) + col] = L > 0.f ? O / L : 0.f;
+                if (col == 0) {
+                    fin[g * (D + 2) + D] = M;
+                    fin[g * (D + 2) + D + 1] = L;
+                }
+                continue;
+            }
             // one split: this CTA holds the whole state; finalise in place
-            a.out[(size_t)qz * a.o_stride + (size_t)h * D + col] = L > 0.f ? O / L : 0.f;
+            a.out[(size_t)qz * a.o_stride + (size_t)h * D + col] = failed ? bad : (L > 0.f ? O / L : 0.f);
             if (col == 0 && a.out_m) {
                 a.out_m[h] = L > 0.f ? M * LN2 : -INFINITY;
                 a.out_l[h] = L > 0.f ? L : 1.f;
@@ -398,13 +505,20 @@ __global__ void __launch_bounds__(THREADS, NST <= 3 ? 2 : 1) decode_kernel(const
             a.part_l[pi] = L;
         }
     }
-    if (nsplit == 1) return;
+    if (nsplit == 1) {
+        if (sp) {
+            __syncthreads();
+            sp_exchange<G, D>(a, kvh, fin, reinterpret_cast<float*>(smem + ML_OFF));
+        }
+        return;
+    }
     __threadfence();
     __syncthreads();
     if (tid == 0) s_last = (atomicAdd(&a.counters[kvh], 1u) == (unsigned)(nsplit - 1));
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+    failed = *reinterpret_cast<volatile int*>(a.status) != 0;
 
     // ---------------- last CTA of this KV head: merge the split partials
     float* wts = reinterpret_cast<float*>(smem);                 // [G][nsplit]
@@ -437,13 +551,25 @@ __global__ void __launch_bounds__(THREADS, NST <= 3 ? 2 : 1) decode_kernel(const
         const float L = hdr[2 * g + 1];
         float O = 0.f;
         for (int i = 0; i < ns; ++i) O += wts[g * ns + i] * __ldcg(a.part_o + ((size_t)h * pstride + i) * D + col);
-        a.out[(size_t)h * D + col] = L > 0.f ? O / L : 0.f;
+        if (sp) {
+            fin[g * (D + 2) + col] = L > 0.f ? O / L : 0.f;
+            if (col == 0) {
+                fin[g * (D + 2) + D] = hdr[2 * g];
+                fin[g * (D + 2) + D + 1] = L;
+            }
+            continue;
+        }
+        a.out[(size_t)h * D + col] = failed ? bad : (L > 0.f ? O / L : 0.f);
         if (col == 0 && a.out_m) {
             a.out_m[h] = L > 0.f ? hdr[2 * g] * LN2 : -INFINITY;
             a.out_l[h] = L > 0.f ? L : 1.f;
         }
     }
     if (tid == 0) a.counters[kvh] = 0u;
+    if (sp) {
+        __syncthreads();
+        sp_exchange<G, D>(a, kvh, fin, reinterpret_cast<float*>(smem + ML_OFF));
+    }
 }
 
 // Merge n partial states given in the natural-log domain (API layout
@@ -555,8 +681,8 @@ static int check_decode_args(const char* fn, int dtype, const void* q, const voi
 // hq*n_splits*(d+2) floats for the plan the call computes.
 static int launch_decode(sa_ctx* ctx, int dtype, const void* q, const void* k, const void* v,
                          long long stride, int T, int d, int hq, int hkv, float scale, float* out,
-                         float* out_m, float* out_l) {
-    SA_CHECK_ARG((((uintptr_t)k | (uintptr_t)v) & 15) == 0, "decode: k/v not 16-byte aligned");
+                         float* out_m, float* out_l, const dec::SpArgs* sp = nullptr) {
+    SA_CHECK_ARG(T == 0 || (((uintptr_t)k | (uintptr_t)v) & 15) == 0, "decode: k/v not 16-byte aligned");
     SA_CHECK_ARG((((uintptr_t)q) & 15) == 0, "decode: q not 16-byte aligned");
     int ns, rps;
     const int sr = dec::stage_rows(dtype, d);
@@ -579,6 +705,9 @@ static int launch_decode(sa_ctx* ctx, int dtype, const void* q, const void* k, c
     a.status = ctx->status;
     a.q_stride = 0; a.o_stride = 0;
     a.len_dev = nullptr;
+    a.sp = {};
+    a.sp.world = 1;
+    if (sp) a.sp = *sp;
     dec::KernelFn fn = dtype == SA_F32 ? dec::pick<float>(d, hq / hkv) : dec::pick<__nv_bfloat16>(d, hq / hkv);
     SA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::SMEM_BYTES));
     fn<<<dim3(ns, hkv), dec::THREADS, dec::SMEM_BYTES, ctx->stream>>>(a);
@@ -588,7 +717,8 @@ static int launch_decode(sa_ctx* ctx, int dtype, const void* q, const void* k, c
 
 static int decode_common(const char* fn_name, sa_ctx* ctx, int dtype, const void* q, const void* k,
                          const void* v, long long stride, int T, int d, int hq, int hkv, int block,
-                         float scale, float* out, float* m_out, float* l_out, unsigned flags) {
+                         float scale, float* out, float* m_out, float* l_out, unsigned flags,
+                         const dec::SpArgs* sp = nullptr) {
     clear_error();
     SA_CHECK_ARG(ctx != nullptr, "%s: ctx is NULL", fn_name);
     SA_CHECK_ARG(out != nullptr, "%s: out is NULL", fn_name);
@@ -596,7 +726,7 @@ static int decode_common(const char* fn_name, sa_ctx* ctx, int dtype, const void
     if (rc) return rc;
     DeviceGuard guard(ctx->device);
     if (!(flags & SA_HOST_PTRS))
-        return launch_decode(ctx, dtype, q, k, v, stride, T, d, hq, hkv, scale, out, m_out, l_out);
+        return launch_decode(ctx, dtype, q, k, v, stride, T, d, hq, hkv, scale, out, m_out, l_out, sp);
 
     // Host buffers: stage through device memory on the context's stream.
     const int elt = dtype == SA_F32 ? 4 : 2;
@@ -622,7 +752,7 @@ static int decode_common(const char* fn_name, sa_ctx* ctx, int dtype, const void
         SA_CUDA_TRY(cudaMemcpy2DAsync(dv, row, v, pitch, row, hkv, cudaMemcpyHostToDevice, st));
     }
     rc = launch_decode(ctx, dtype, dq, dk, dv, (long long)T * d, T, d, hq, hkv, scale, dout,
-                       m_out ? dm : nullptr, m_out ? dl : nullptr);
+                       m_out ? dm : nullptr, m_out ? dl : nullptr, sp);
     if (rc) return rc;
     SA_CUDA_TRY(cudaMemcpyAsync(out, dout, (size_t)hq * d * 4, cudaMemcpyDeviceToHost, st));
     if (m_out) {
@@ -724,6 +854,8 @@ int decode_dev_launch(cudaStream_t st, int* status, int num_sms, const float* q,
     a.status = status;
     a.q_stride = 0; a.o_stride = 0;
     a.len_dev = len_dev;
+    a.sp = {};
+    a.sp.world = 1;
     dec::KernelFn fn = dec::pick_dev(d, hq / hkv);
     int smem = dec::smem_bytes<dec::DEV_STAGES>();
     if (!fn) {
@@ -821,8 +953,9 @@ SA_API int sa_attn_decode_noalloc(void* stream, int dtype, const void* q, const 
     float* part = reinterpret_cast<float*>(b + cnt_bytes + st_bytes);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     // The kernel's last CTA leaves the counters at zero, but a call that ended
-    // early could not; start every call from zero.
-    SA_CUDA_TRY(cudaMemsetAsync(counters, 0, (size_t)hkv * sizeof(unsigned), st));
+    // early could not; start every call from zero, status word included (it
+    // follows the counters), so that only this call's own failure shows.
+    SA_CUDA_TRY(cudaMemsetAsync(counters, 0, cnt_bytes + sizeof(int), st));
 
     dec::Args a;
     a.q = q; a.k = k; a.v = v;
@@ -838,6 +971,8 @@ SA_API int sa_attn_decode_noalloc(void* stream, int dtype, const void* q, const 
     a.status = status;
     a.q_stride = 0; a.o_stride = 0;
     a.len_dev = nullptr;
+    a.sp = {};
+    a.sp.world = 1;
     dec::KernelFn fn = dtype == SA_F32 ? dec::pick<float>(d, hq / hkv) : dec::pick<__nv_bfloat16>(d, hq / hkv);
     SA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::SMEM_BYTES));
     fn<<<dim3(ns, hkv), dec::THREADS, dec::SMEM_BYTES, st>>>(a);
@@ -893,4 +1028,223 @@ SA_API int sa_attn_decode_step(sa_ctx* ctx, int dtype, const void* q, const void
     if (rc) return rc;
     SA_CUDA_TRY(cudaMemcpyAsync(out, dout, (size_t)hq * d * 4, cudaMemcpyDeviceToHost, st));
     return sync_and_check(ctx);
+}
+
+// ===========================================================================
+// Sequence-parallel decode over several GPUs (one rank per GPU).
+//
+// streaming_attention_mpi_simple (attention/src/streaming_mpi.cpp:252-309)
+// splits the sequence over MPI ranks, gathers every rank's (m, l, O) on
+// rank 0 and merges them there.  Here each rank's decode launch does the
+// exchange itself: the merging CTA of every KV head stores its heads' states
+// as self-validating words into every rank's word area (plain 8-byte stores
+// over NVLink into CUDA IPC mappings, or peer pointers inside one process)
+// and merges all ranks' states in rank order.  No collective library, no
+// separate merge launch, and every rank gets the result.
+// ===========================================================================
+#include <cstring>
+
+struct sa_sp {
+    sa_ctx* ctx = nullptr;
+    int device = 0, rank = 0, world = 1;
+    int max_hq = 0, max_d = 0;
+    size_t words_bytes = 0;
+    unsigned long long* words = nullptr;       // own word area
+    unsigned* ctl = nullptr;                   // [0] instance count, [1] arrivals
+    unsigned long long* peer[sa::dec::SP_MAX] = {};
+    bool opened[sa::dec::SP_MAX] = {};         // peer[r] is an IPC mapping to close
+    bool connected = false;
+    unsigned char uuid[16] = {};
+};
+
+namespace sa {
+namespace {
+constexpr uint32_t SP_MAGIC = 0x50534153u;   // "SASP"
+struct SpHandle {                            // the SA_SP_HANDLE_BYTES blob
+    cudaIpcMemHandle_t ipc;
+    unsigned char uuid[16];
+    int32_t rank, world;
+    uint64_t words_bytes;
+    uint32_t magic;
+};
+static_assert(sizeof(SpHandle) <= SA_SP_HANDLE_BYTES, "handle size");
+
+void sp_close_peers(sa_sp* sp) {
+    for (int r = 0; r < dec::SP_MAX; ++r) {
+        if (sp->opened[r] && sp->peer[r]) cudaIpcCloseMemHandle(sp->peer[r]);
+        sp->opened[r] = false;
+        sp->peer[r] = nullptr;
+    }
+    sp->connected = false;
+}
+}  // namespace
+}  // namespace sa
+
+SA_API int sa_sp_create(sa_ctx* ctx, int rank, int world, int max_hq, int max_d, sa_sp** out) {
+    using namespace sa;
+    clear_error();
+    SA_CHECK_ARG(ctx && out, "sa_sp_create: null argument");
+    *out = nullptr;
+    SA_CHECK_ARG(world >= 1 && world <= dec::SP_MAX, "sa_sp_create: world = %d (1..%d)", world, dec::SP_MAX);
+    SA_CHECK_ARG(rank >= 0 && rank < world, "sa_sp_create: rank %d of %d", rank, world);
+    SA_CHECK_ARG(max_hq >= 1 && max_hq <= 4096 && (max_d == 64 || max_d == 128 || max_d == 256),
+                 "sa_sp_create: max_hq = %d, max_d = %d", max_hq, max_d);
+    DeviceGuard guard(ctx->device);
+    sa_sp* sp = new sa_sp();
+    sp->ctx = ctx;
+    sp->device = ctx->device;
+    sp->rank = rank;
+    sp->world = world;
+    sp->max_hq = max_hq;
+    sp->max_d = max_d;
+    sp->words_bytes = align_up((size_t)2 * world * max_hq * (max_d + 2) * sizeof(unsigned long long), 4096);
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, ctx->device) != cudaSuccess ||
+        cudaMalloc(&sp->words, sp->words_bytes) != cudaSuccess ||
+        cudaMalloc(&sp->ctl, 2 * sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(sp->words, 0, sp->words_bytes) != cudaSuccess ||
+        cudaMemset(sp->ctl, 0, 2 * sizeof(unsigned)) != cudaSuccess) {
+        const cudaError_t e = cudaGetLastError();
+        cudaFree(sp->words);
+        cudaFree(sp->ctl);
+        delete sp;
+        return set_error(SA_ERR_OOM, "sa_sp_create: %s", cudaGetErrorString(e));
+    }
+    std::memcpy(sp->uuid, &prop.uuid, sizeof(sp->uuid));
+    sp->peer[rank] = sp->words;
+    sp->connected = world == 1;
+    *out = sp;
+    return SA_OK;
+}
+
+SA_API int sa_sp_handle(sa_sp* sp, void* handle) {
+    using namespace sa;
+    clear_error();
+    SA_CHECK_ARG(sp && handle, "sa_sp_handle: null argument");
+    DeviceGuard guard(sp->device);
+    SpHandle h;
+    std::memset(&h, 0, sizeof(h));
+    SA_CUDA_TRY(cudaIpcGetMemHandle(&h.ipc, sp->words));
+    std::memcpy(h.uuid, sp->uuid, sizeof(h.uuid));
+    h.rank = sp->rank;
+    h.world = sp->world;
+    h.words_bytes = sp->words_bytes;
+    h.magic = SP_MAGIC;
+    std::memset(handle, 0, SA_SP_HANDLE_BYTES);
+    std::memcpy(handle, &h, sizeof(h));
+    return SA_OK;
+}
+
+SA_API int sa_sp_connect(sa_sp* sp, const void* handles) {
+    using namespace sa;
+    clear_error();
+    SA_CHECK_ARG(sp && handles, "sa_sp_connect: null argument");
+    if (sp->world == 1) return SA_OK;
+    SA_CHECK_ARG(!sp->connected, "sa_sp_connect: already connected");
+    DeviceGuard guard(sp->device);
+    const unsigned char* hb = static_cast<const unsigned char*>(handles);
+    for (int r = 0; r < sp->world; ++r) {
+        SpHandle h;
+        std::memcpy(&h, hb + (size_t)r * SA_SP_HANDLE_BYTES, sizeof(h));
+        const char* bad = nullptr;
+        if (h.magic != SP_MAGIC) bad = "is not an sa_sp handle";
+        else if (h.rank != r || h.world != sp->world) bad = "names another rank or world size";
+        else if (h.words_bytes != sp->words_bytes) bad = "was created with other max_hq / max_d";
+        else if (r != sp->rank && std::memcmp(h.uuid, sp->uuid, sizeof(h.uuid)) == 0)
+            bad = "is on this rank's GPU (the exchange waits across ranks: one GPU per rank)";
+        if (bad) {
+            sp_close_peers(sp);
+            sp->peer[sp->rank] = sp->words;
+            return set_error(SA_ERR_ARG, "sa_sp_connect: handle %d %s", r, bad);
+        }
+        if (r == sp->rank) continue;
+        void* p = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&p, h.ipc, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            sp_close_peers(sp);
+            sp->peer[sp->rank] = sp->words;
+            return set_error(SA_ERR_CUDA, "sa_sp_connect: opening rank %d's word area failed: %s", r,
+                             cudaGetErrorString(e));
+        }
+        sp->peer[r] = static_cast<unsigned long long*>(p);
+        sp->opened[r] = true;
+    }
+    sp->peer[sp->rank] = sp->words;
+    sp->connected = true;
+    return SA_OK;
+}
+
+SA_API int sa_sp_connect_local(sa_sp* const* sps, int n) {
+    using namespace sa;
+    clear_error();
+    SA_CHECK_ARG(sps && n >= 1 && n <= dec::SP_MAX, "sa_sp_connect_local: n = %d", n);
+    for (int i = 0; i < n; ++i) {
+        SA_CHECK_ARG(sps[i] && sps[i]->rank == i && sps[i]->world == n,
+                     "sa_sp_connect_local: entry %d is not rank %d of %d", i, i, n);
+        SA_CHECK_ARG(!sps[i]->connected || n == 1, "sa_sp_connect_local: rank %d already connected", i);
+        SA_CHECK_ARG(sps[i]->words_bytes == sps[0]->words_bytes,
+                     "sa_sp_connect_local: rank %d was created with other max_hq / max_d", i);
+        for (int j = 0; j < i; ++j)
+            SA_CHECK_ARG(sps[j]->device != sps[i]->device,
+                         "sa_sp_connect_local: ranks %d and %d share GPU %d (one GPU per rank)", j, i,
+                         sps[i]->device);
+    }
+    for (int i = 0; i < n; ++i) {
+        DeviceGuard guard(sps[i]->device);
+        for (int j = 0; j < n; ++j) {
+            if (j == i) continue;
+            int can = 0;
+            SA_CUDA_TRY(cudaDeviceCanAccessPeer(&can, sps[i]->device, sps[j]->device));
+            SA_CHECK_ARG(can, "sa_sp_connect_local: GPU %d cannot access GPU %d", sps[i]->device,
+                         sps[j]->device);
+            const cudaError_t e = cudaDeviceEnablePeerAccess(sps[j]->device, 0);
+            if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled)
+                return set_error(SA_ERR_CUDA, "sa_sp_connect_local: peer access %d -> %d: %s", sps[i]->device,
+                                 sps[j]->device, cudaGetErrorString(e));
+            cudaGetLastError();
+        }
+    }
+    for (int i = 0; i < n; ++i) {
+        for (int j = 0; j < n; ++j) sps[i]->peer[j] = sps[j]->words;
+        sps[i]->connected = true;
+    }
+    return SA_OK;
+}
+
+SA_API int sa_sp_destroy(sa_sp* sp) {
+    using namespace sa;
+    clear_error();
+    if (!sp) return SA_OK;
+    DeviceGuard guard(sp->device);
+    cudaDeviceSynchronize();
+    sp_close_peers(sp);
+    cudaFree(sp->words);
+    cudaFree(sp->ctl);
+    delete sp;
+    return SA_OK;
+}
+
+SA_API int sa_attn_decode_sp(sa_sp* sp, int dtype, const void* q, const void* k, const void* v,
+                             long long kv_head_stride, int T_local, int d, int hq, int hkv, int block,
+                             float scale, float* out, float* m_out, float* l_out, unsigned flags) {
+    using namespace sa;
+    clear_error();
+    SA_CHECK_ARG(sp != nullptr, "sa_attn_decode_sp: sp is NULL");
+    SA_CHECK_ARG(sp->connected, "sa_attn_decode_sp: rank %d of %d is not connected (sa_sp_connect)", sp->rank,
+                 sp->world);
+    SA_CHECK_ARG((m_out == nullptr) == (l_out == nullptr), "sa_attn_decode_sp: m_out/l_out must both be set or NULL");
+    SA_CHECK_ARG(hq <= sp->max_hq && d <= sp->max_d, "sa_attn_decode_sp: hq = %d, d = %d exceed the word area's "
+                 "max_hq = %d, max_d = %d", hq, d, sp->max_hq, sp->max_d);
+    if (sp->world == 1)
+        return decode_common("sa_attn_decode_sp", sp->ctx, dtype, q, k, v, kv_head_stride, T_local, d, hq, hkv,
+                             block, scale, out, m_out, l_out, flags);
+    dec::SpArgs a{};
+    a.rank = sp->rank;
+    a.world = sp->world;
+    for (int r = 0; r < sp->world; ++r) a.words[r] = sp->peer[r];
+    a.seq = sp->ctl;
+    a.done = sp->ctl + 1;
+    return decode_common("sa_attn_decode_sp", sp->ctx, dtype, q, k, v, kv_head_stride, T_local, d, hq, hkv,
+                         block, scale, out, m_out, l_out, flags, &a);
 }

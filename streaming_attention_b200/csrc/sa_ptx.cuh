@@ -99,6 +99,38 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Self-validating exchange words between GPUs: (epoch << 32) | 32 value bits,
+// written with one 8-byte store, so a reader that sees the epoch also sees
+// the value (aligned 8-byte accesses are single-copy atomic).  System scope:
+// the writer may be another GPU storing over NVLink.
+__device__ __forceinline__ void st_u64_relaxed_sys(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_u64_relaxed_sys(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned long long epoch_word(unsigned epoch, float x) {
+    return ((unsigned long long)epoch << 32) | __float_as_uint(x);
+}
+// Wait (bounded, as mbar_wait) until the word at p carries `epoch`; return
+// its value.  After an earlier expired wait (*status set) it does not wait
+// again, so one missing peer costs one limit, not one per word.
+__device__ __forceinline__ float wait_epoch_word(const unsigned long long* p, unsigned epoch, int* status) {
+    unsigned long long w = ld_u64_relaxed_sys(p);
+    if ((unsigned)(w >> 32) == epoch) return __uint_as_float((uint32_t)w);
+    if (*reinterpret_cast<volatile int*>(status) != 0) return __uint_as_float((uint32_t)w);
+    const unsigned long long t0 = globaltimer();
+    while ((unsigned)((w = ld_u64_relaxed_sys(p)) >> 32) != epoch) {
+        if (globaltimer() - t0 > kWaitLimitNs) {
+            atomicExch(status, SA_STATUS_TIMEOUT);
+            break;
+        }
+    }
+    return __uint_as_float((uint32_t)w);
+}
+
 // 2^x on the SFU (MUFU.EX2), flush-to-zero; 2^-inf = 0.
 __device__ __forceinline__ float ex2(float x) {
     float y;

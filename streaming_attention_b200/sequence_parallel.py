@@ -1,6 +1,13 @@
 """Sequence-parallel attention across ranks (one GPU per rank).
 
-Decode (sp_decode):
+Decode, fused (SpDecoder): one launch per rank.  Each rank's decode kernel
+reduces its contiguous KV slice; the CTA that finishes each KV head stores
+that head's (m, l, O) states into every rank's exchange buffer over NVLink
+(CUDA IPC mappings whose handles travel over any host channel) and merges all
+ranks' states in rank order, so every rank ends the launch with the result
+(sa_sp_* / sa_attn_decode_sp in include/sa_cuda.h).
+
+Decode through a collective library (sp_decode):
 
 The reference splits the KV sequence over MPI ranks and merges the per-rank
 online-softmax states on rank 0 (streaming_attention_mpi_simple,
@@ -153,3 +160,81 @@ def sp_prefill(q_local, k_local, v_local, scale: float, group=None, prefill_fn=N
         for st in streams:
             cur.wait_stream(st)
     return out
+
+
+class SpDecoder:
+    """This rank's share of the fused sequence-parallel decode.
+
+    Every rank creates one with the same ``world``, exchanges handles
+    (``connect_dist`` over torch.distributed, ``connect`` with handles from any
+    other channel, or ``connect_local`` for several GPUs of one process), then
+    calls ``decode`` with its own KV slice (rank order = sequence order) and
+    the same q; the merged attention over the whole sequence comes back on
+    every rank.  Ranks must be on distinct GPUs.
+    """
+
+    def __init__(self, ctx, rank: int, world: int, max_hq: int = 64, max_d: int = 128):
+        import ctypes as C
+        from ._capi import check, lib
+        self.ctx, self.rank, self.world = ctx, rank, world
+        h = C.c_void_p()
+        check(lib().sa_sp_create(ctx.h, rank, world, max_hq, max_d, C.byref(h)))
+        self.h = h
+
+    def handle(self) -> bytes:
+        import ctypes as C
+        from ._capi import SA_SP_HANDLE_BYTES, check, lib
+        buf = C.create_string_buffer(SA_SP_HANDLE_BYTES)
+        check(lib().sa_sp_handle(self.h, buf))
+        return buf.raw
+
+    def connect(self, handles) -> None:
+        import ctypes as C
+        from ._capi import check, lib
+        blob = b"".join(handles)
+        check(lib().sa_sp_connect(self.h, C.create_string_buffer(blob, len(blob))))
+
+    def connect_dist(self, group=None) -> None:
+        import torch.distributed as dist
+        hs = [None] * self.world
+        dist.all_gather_object(hs, self.handle(), group=group)
+        self.connect(hs)
+
+    @staticmethod
+    def connect_local(decoders) -> None:
+        import ctypes as C
+        from ._capi import check, lib
+        arr = (C.c_void_p * len(decoders))(*[d.h.value for d in decoders])
+        check(lib().sa_sp_connect_local(arr, len(decoders)))
+
+    def decode(self, q, k, v, scale: float = 1.0, block: int = 64, out=None, with_state: bool = False):
+        """q [hq, d]; k, v [hkv, T_local, d] (CUDA tensors, fp32 or bf16) ->
+        out [hq, d] fp32 (and the merged m, l [hq] with ``with_state``)."""
+        import ctypes as C
+        import torch
+        from ._capi import SA_BF16, SA_F32, check, lib
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        hq, d = q.shape
+        hkv, T, _ = k.shape
+        dt = SA_F32 if q.dtype == torch.float32 else SA_BF16
+        if out is None:
+            out = torch.empty(hq, d, dtype=torch.float32, device=q.device)
+        m = torch.empty(hq, dtype=torch.float32, device=q.device) if with_state else None
+        l = torch.empty(hq, dtype=torch.float32, device=q.device) if with_state else None
+        P = lambda t: C.c_void_p(t.data_ptr()) if t is not None else None
+        self.ctx.set_stream(torch.cuda.current_stream(q.device).cuda_stream)
+        check(lib().sa_attn_decode_sp(self.h, dt, P(q), P(k), P(v), T * d, T, d, hq, hkv, block, scale,
+                                      P(out), P(m), P(l), 0))
+        return (out, m, l) if with_state else out
+
+    def close(self) -> None:
+        from ._capi import lib
+        if getattr(self, "h", None):
+            lib().sa_sp_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
