@@ -4,27 +4,30 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 Workload (the multi-head GQA decode sweep at its
-largest single-GPU point): one decode step of attention for batch 1, 16 query
-heads sharing 8 KV heads, head_dim 128, KV length T = 262144 per GPU, fp32
-(the reference's element type), block 64, scale 1/sqrt(128); Q/K/V i.i.d.
-N(0,1) from a fixed seed.  K+V = 2 GiB per GPU > L2 (126 MB), so every timed
-step streams from HBM with no flush needed.
+largest point): one decode step of attention for batch 1, 16 query heads
+sharing 8 KV heads, head_dim 128, KV length T = 262144, fp32 (the reference's
+element type), block 64, scale 1/sqrt(128); Q/K/V i.i.d. N(0,1) from a fixed
+seed.  K+V = 2 GiB > L2 (126 MB), so every timed step streams from HBM with
+no flush needed.
 
-A step = one pass of the hot path over that KV: at N = 1 one sa_attn_decode
-launch; at N > 1 (torchrun, one rank per GPU) each rank owns its own T-row KV
-shard (weak scaling, total KV = N*T), reduces it to per-head partial
-(m, l, O) states (sa_attn_decode_partial), the partials are all-gathered with
-NCCL and merged on every rank (sa_attn_merge) -- the sequence-parallel
-decomposition of streaming_attention_mpi_simple.
+A step = one pass of the hot path over that sequence.  At N = 1 one
+sa_attn_decode launch.  At N > 1 (torchrun, one rank per GPU) the sequence is
+split evenly over the ranks (strong scaling, configs[1]'s "KV sequence split
+evenly over 1/2/4/8 GPUs"): each rank runs one sa_attn_decode_sp launch over
+its T/N rows, whose merging CTAs exchange the per-head (m, l, O) states over
+NVLink and merge them -- the sequence-parallel decomposition of
+streaming_attention_mpi_simple.  The weak-scaling figure (T rows on every
+GPU) is reported beside it.
 
 Metric: attention GB/s = algorithmic bytes (K + V + q + out, each read or
 written once) / time, whole job.  `e2e` is the same metric through the C ABI
-with pinned HOST buffers (the attention.h drop-in: H2D of q, K, V and D2H of
-the output inside the timed region).  `roofline` compares the decode kernel's
-own time with the measured HBM copy bandwidth.  `cpu_baseline` and
-`--impl reference` time the reference's own CPU implementation
-(streaming_attention_omp per query head, compiled from the reference's
-sources into oracle/_ref/libsa_ref.so) on the host cores.
+with pinned HOST buffers for the step's inputs and output.  `roofline`
+compares the decode kernel's own time with the measured HBM copy bandwidth.
+`graph` repeats the step as 100 calls replayed from one CUDA graph (median of
+5).  `cpu_baseline` and `--impl reference` time the reference's own CPU
+implementation (streaming_attention_omp per query head, compiled from the
+reference's sources into oracle/_ref/libsa_ref.so) on the host cores with an
+explicit thread count.
 """
 from __future__ import annotations
 
@@ -41,12 +44,13 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-HQ, HKV, D, T_PER_GPU, BLOCK = 16, 8, 128, 262144, 64
+HQ, HKV, D, T_GLOBAL, BLOCK = 16, 8, 128, 262144, 64
+GRAPH_CALLS = 100          # calls per CUDA-graph replay of the graph measurement
 SCALE = 1.0 / math.sqrt(D)
 SEED = 20261201
 METRIC = "attn GB/s"
-WORKLOAD = ("configs[1] GQA decode: B=1, hq=16, hkv=8, d=128, T=262144 per GPU, block 64, "
-            "scale 1/sqrt(128), fp32, N(0,1) seeded")
+WORKLOAD = ("configs[1] GQA decode: B=1, hq=16, hkv=8, d=128, T=262144 split evenly over the GPUs, "
+            "block 64, scale 1/sqrt(128), fp32, N(0,1) seeded")
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -146,71 +150,99 @@ def make_inputs(T: int, dtype, device, seed: int):
     return q, k, v
 
 
+def make_slice(T_total: int, t0: int, T: int, device, seed: int):
+    """q and rows [t0, t0 + T) of K and V of one seeded T_total-row sequence
+    (every rank generates the same sequence and keeps its slice)."""
+    import torch
+    q, k, v = make_inputs(T_total, torch.float32, device, seed)
+    if t0 == 0 and T == T_total:
+        return q, k, v
+    ks, vs = k[:, t0:t0 + T].contiguous(), v[:, t0:t0 + T].contiguous()
+    del k, v
+    return q, ks, vs
+
+
 def cpu_reference_time(q, k, v, T_sample: int, budget_s: float, min_reps: int = 3):
-    """Time the reference CPU path (per-head streaming_attention_omp) on a
-    T_sample-row slice of the workload; returns (s per step-of-sample, reps)."""
+    """Time the reference CPU path (per-head streaming_attention_omp, all host
+    threads) on a T_sample-row slice of the workload; returns (s per
+    step-of-sample, reps, threads)."""
     from oracle.oracle import Reference
     import numpy as np
     R = Reference()
+    cores = host_cores()
     ks = np.ascontiguousarray(k[:, :T_sample])
     vs = np.ascontiguousarray(v[:, :T_sample])
     out = np.empty((HQ, D), np.float32)
-    R.gqa_decode_omp(q, ks, vs, BLOCK, 0, SCALE, out)       # warm-up (page-in, threads)
+    R.gqa_decode_omp(q, ks, vs, BLOCK, cores, SCALE, out)       # warm-up (page-in, threads)
     times = []
     t_end = time.perf_counter() + budget_s
     while len(times) < min_reps or time.perf_counter() < t_end:
         t0 = time.perf_counter()
-        R.gqa_decode_omp(q, ks, vs, BLOCK, 0, SCALE, out)
+        R.gqa_decode_omp(q, ks, vs, BLOCK, cores, SCALE, out)
         times.append(time.perf_counter() - t0)
         if len(times) >= 1000:
             break
-    return statistics.median(times), len(times)
+    return statistics.median(times), len(times), cores
 
 
 # ---------------------------------------------------------------- reference arm
+def host_cores() -> int:
+    """Host threads this process may run on (torchrun does not restrict the
+    affinity, but it sets OMP_NUM_THREADS=1, so the count is passed to the
+    reference explicitly)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def decode_config(world: int) -> dict:
+    """The workload both arms report (identical dicts, so the two lines pair up)."""
+    return {"workload": WORKLOAD, "kv_len": T_GLOBAL, "kv_split": world,
+            "T_per_gpu": T_GLOBAL // world,
+            "parallelism": f"sp{world}" if world > 1 else "single",
+            "l2": "inputs (2 GiB K+V in total) exceed L2 (126 MB); no flush"}
+
+
+def make_inputs_np(T: int, seed: int):
+    """Host copy of the global sequence: the values the GPU arm generates (on
+    the GPU's generator when there is one)."""
+    import torch
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    q, k, v = make_inputs(T, torch.float32, dev, seed)
+    return q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy()
+
+
 def run_reference(args):
+    """--impl reference: the reference's streaming_attention_omp per query head
+    (attention/src/streaming_omp.cpp:99-154, compiled from its sources) over
+    the whole T_GLOBAL-row sequence, every step, with all host threads."""
     rank = env_int("RANK", 0)
     if rank != 0:
         return 0
     import numpy as np
-    import torch
-    dev = "cuda" if torch.cuda.is_available() else "cpu"
-    q, k, v = make_inputs(T_PER_GPU, torch.float32, dev, SEED)
-    q, k, v = q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy()
     from oracle.oracle import Reference
+    q, k, v = make_inputs_np(T_GLOBAL, SEED)
     R = Reference()
-    cores = os.cpu_count() or 1
+    cores = host_cores()
     out = np.empty((HQ, D), np.float32)
-    # size each step's sample so that warm-up + timed steps end within ~2 min
-    t0 = time.perf_counter()
-    R.gqa_decode_omp(q, k[:, :8192], v[:, :8192], BLOCK, 0, SCALE, out)
-    R.gqa_decode_omp(q, k[:, :8192], v[:, :8192], BLOCK, 0, SCALE, out)
-    t_small = (time.perf_counter() - t0) / 2
-    est_full = t_small * T_PER_GPU / 8192
-    n = args.steps + args.warmup
-    T_s = T_PER_GPU
-    if est_full * n > 120:
-        T_s = max(8192, int(T_PER_GPU * 120 / (est_full * n)) // 64 * 64)
-    ks, vs = np.ascontiguousarray(k[:, :T_s]), np.ascontiguousarray(v[:, :T_s])
     for _ in range(args.warmup):
-        R.gqa_decode_omp(q, ks, vs, BLOCK, 0, SCALE, out)
+        R.gqa_decode_omp(q, k, v, BLOCK, cores, SCALE, out)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        R.gqa_decode_omp(q, ks, vs, BLOCK, 0, SCALE, out)
+        R.gqa_decode_omp(q, k, v, BLOCK, cores, SCALE, out)
     el = time.perf_counter() - t0
-    gbs = algo_bytes(T_s) * args.steps / el / 1e9
+    gbs = algo_bytes(T_GLOBAL) * args.steps / el / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(el / args.steps * 1e3 * T_PER_GPU / T_s, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": {"workload": WORKLOAD, "parallelism": "cpu"},
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores,
-                         "kind": "reference",
-                         "sample": f"streaming_attention_omp per query head (16), T={T_s} of "
-                                   f"{T_PER_GPU} rows per step, {cores} OpenMP threads"},
-        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
+        "ms_per_step": round(el / args.steps * 1e3, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": decode_config(args.gpus),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "reference",
+                         "sample": f"streaming_attention_omp per query head (16) over all {T_GLOBAL} rows "
+                                   f"per step, num_threads={cores} passed explicitly"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -228,49 +260,56 @@ def run_ours(args):
     if world != args.gpus:
         print(f"bench.py: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
         return 2
+    if T_GLOBAL % (world * 64):
+        print(f"bench.py: T={T_GLOBAL} does not split into {world} x 64-row shares", file=sys.stderr)
+        return 2
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        # gloo carries only the exchange-buffer handles, barriers and the max
+        # over ranks of the timings; the attention exchange is the kernel's own
+        dist.init_process_group("gloo", timeout=timedelta(seconds=120))
 
     import streaming_attention_b200 as sa
     from streaming_attention_b200 import _capi
+    from streaming_attention_b200.sequence_parallel import SpDecoder
     ctx = sa.Context(local)
     stream = torch.cuda.Stream(dev)
     ctx.set_stream(stream.cuda_stream)
     L = _capi.lib()
+    sp = None
+    if world > 1:
+        sp = SpDecoder(ctx, rank, world, max_hq=HQ, max_d=D)
+        sp.connect_dist()
 
-    T = T_PER_GPU
-    q, k, v = make_inputs(T, torch.float32, dev, SEED + rank)
+    T = T_GLOBAL // world
+    # rank r holds rows [r*T, (r+1)*T) of one seeded global sequence
+    q, k, v = make_slice(T_GLOBAL, rank * T, T, dev, SEED)
     out = torch.empty(HQ, D, device=dev)
-    m = torch.empty(HQ, device=dev)
-    l = torch.empty(HQ, device=dev)
-    packed = torch.empty(HQ * (D + 2), device=dev)
-    gathered_flat = torch.empty(world * HQ * (D + 2), device=dev)
-    gathered = gathered_flat.view(world, HQ * (D + 2))
-    P = lambda t: _capi.C.c_void_p(t.data_ptr())
+    P = lambda t: _capi.C.c_void_p(t.data_ptr()) if t is not None else None
 
-    def step():
+    def decode_once(q_, k_, v_, T_, out_):
         if world == 1:
-            _capi.check(L.sa_attn_decode(ctx.h, 0, P(q), P(k), P(v), T * D, T, D, HQ, HKV, BLOCK,
-                                         SCALE, P(out), 0))
+            _capi.check(L.sa_attn_decode(ctx.h, 0, P(q_), P(k_), P(v_), T_ * D, T_, D, HQ, HKV, BLOCK,
+                                         SCALE, P(out_), 0))
         else:
-            _capi.check(L.sa_attn_decode_partial(ctx.h, 0, P(q), P(k), P(v), T * D, T, D, HQ, HKV,
-                                                 BLOCK, SCALE, P(packed[:HQ]), P(packed[HQ:2 * HQ]),
-                                                 P(packed[2 * HQ:]), 0))
-            with torch.cuda.stream(stream):
-                dist.all_gather_into_tensor(gathered_flat, packed)
-                gm = gathered[:, :HQ].contiguous()
-                gl = gathered[:, HQ:2 * HQ].contiguous()
-                go = gathered[:, 2 * HQ:].contiguous()
-            _capi.check(L.sa_attn_merge(ctx.h, world, HQ, D, P(gm), P(gl), P(go), P(out), None,
-                                        None, 0))
+            _capi.check(L.sa_attn_decode_sp(sp.h, 0, P(q_), P(k_), P(v_), T_ * D, T_, D, HQ, HKV, BLOCK,
+                                            SCALE, P(out_), None, None, 0))
+
+    step = lambda: decode_once(q, k, v, T, out)
 
     def barrier():
         torch.cuda.synchronize(dev)
         if world > 1:
-            dist.barrier(device_ids=[local])
+            dist.barrier()
         torch.cuda.synchronize(dev)
+
+    def tmax(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
     # warm-up, then a ~1 s soak under clock sampling that runs into the timed region
     for _ in range(args.warmup):
@@ -283,6 +322,8 @@ def run_ours(args):
         barrier()
         if rank == 0:
             print(json.dumps({"profile": True, "launches": args.warmup + args.steps}), flush=True)
+        if sp:
+            sp.close()
         ctx.close()
         if world > 1:
             dist.destroy_process_group()
@@ -291,14 +332,14 @@ def run_ours(args):
     smi_id = vis.split(",")[local].strip() if vis else str(local)
     clocks = ClockSampler(smi_id)
     clocks.start()
-    t_soak = time.perf_counter() + 1.0
-    while time.perf_counter() < t_soak:
+    s0 = time.perf_counter()
+    while tmax(time.perf_counter() - s0) < 1.0:   # one decision for all ranks: same step count everywhere
         for _ in range(50):
             step()
         torch.cuda.synchronize(dev)
     barrier()
 
-    # timed region: K steps, CUDA events on the launching stream
+    # timed region: K steps, CUDA events on the launching stream, max over ranks
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
@@ -307,58 +348,93 @@ def run_ours(args):
     ev1.record(stream)
     barrier()
     clk = clocks.stop()
-    ms = ev0.elapsed_time(ev1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = tmax(ev0.elapsed_time(ev1))
     ms_step = ms / args.steps
-    value = algo_bytes(T) * world * args.steps / (ms / 1e3) / 1e9
-    launches = args.steps * (1 if world == 1 else 2)
+    value = algo_bytes(T_GLOBAL) * args.steps / (ms / 1e3) / 1e9
 
-    # kernel-only timing for the roofline: decode launches back to back
+    # the same step as GRAPH_CALLS calls replayed from one CUDA graph, median of 5
+    graph, g_ms, graph_err = None, [], None
+    try:
+        gs = torch.cuda.Stream(dev)
+        ctx.set_stream(gs.cuda_stream)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=gs):
+            for _ in range(GRAPH_CALLS):
+                step()
+        graph = g
+    except Exception as e:          # reported, never required
+        graph_err = str(e)
+    ctx.set_stream(stream.cuda_stream)
+    # replay only if every rank captured (a rank alone would wait for the others)
+    if -tmax(-(1.0 if graph is not None else 0.0)) > 0:
+        for _ in range(2):
+            graph.replay()
+        for _ in range(5):
+            barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            cur = torch.cuda.current_stream(dev)
+            e0.record(cur)
+            graph.replay()
+            e1.record(cur)
+            torch.cuda.synchronize(dev)
+            g_ms.append(tmax(e0.elapsed_time(e1)) / GRAPH_CALLS)
+    elif graph_err is None:
+        graph_err = "another rank could not capture the step"
+    barrier()
+
+    # kernel-only timing for the roofline: this rank's decode launches back to back
+    # (at N > 1 the same fused launch: slice + exchange + merge)
     kt0 = torch.cuda.Event(enable_timing=True)
     kt1 = torch.cuda.Event(enable_timing=True)
     nk = max(20, args.steps)
+    barrier()
     kt0.record(stream)
     for _ in range(nk):
-        _capi.check(L.sa_attn_decode_partial(ctx.h, 0, P(q), P(k), P(v), T * D, T, D, HQ, HKV,
-                                             BLOCK, SCALE, P(m), P(l), P(out), 0))
+        step()
     kt1.record(stream)
     torch.cuda.synchronize(dev)
-    k_ms = kt0.elapsed_time(kt1) / nk
+    k_ms = tmax(kt0.elapsed_time(kt1) / nk)
 
     result = None
     if rank == 0:
         peak, peak_kind = load_peak()
         achieved = algo_bytes(T) / (k_ms / 1e3) / 1e9
         traffic = load_traffic("decode_f32_T262144")
+        if traffic is not None and world > 1:
+            traffic = traffic / world      # DRAM bytes scale with the rows a launch streams
         result = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic",
-            "config": {"workload": WORKLOAD, "global_kv_len": T * world, "T_per_gpu": T,
-                       "parallelism": f"sp{world}" if world > 1 else "single",
-                       "l2": "inputs (2 GiB K+V per GPU) exceed L2 (126 MB); no flush"},
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": decode_config(world),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_kind": f"{peak_kind} hbm_gbs (copy bandwidth)",
-                         "kernel": "sa::dec::decode_kernel<float,128,2>",
+                         "per": "GPU (this rank's slice: K + V + q + out bytes / launch time)",
+                         "kernel": "sa::dec::decode_kernel<float,128,2>" +
+                                   (" with the sequence-parallel exchange" if world > 1 else ""),
                          "kernel_ms": round(k_ms, 5), "traffic": traffic},
             "clocks": clk,
-            "gpu_launches": launches,
+            "gpu_launches": args.steps,
+            "gpu_launches_per": "rank (one launch per step per rank)",
         }
+        if g_ms:
+            med = statistics.median(g_ms)
+            result["graph"] = {"calls": GRAPH_CALLS, "repeats": 5, "ms_per_step_median": round(med, 5),
+                               "value_median": round(algo_bytes(T_GLOBAL) / (med / 1e3) / 1e9, 2),
+                               "ms_per_step_all": [round(x, 5) for x in g_ms]}
+        else:
+            result["graph"] = {"error": graph_err}
+    if graph is not None:
+        del graph
 
-    # ---- e2e through the C ABI with pinned host buffers (rank-local, N=1 style)
+    # ---- e2e through the C ABI with pinned host buffers
     hq_ = q.cpu().pin_memory()
-    hk = k.cpu().pin_memory()
-    hv = v.cpu().pin_memory()
     hout = torch.empty(HQ, D).pin_memory()
     HP = lambda t: _capi.C.c_void_p(t.data_ptr())
     ne = max(3, min(args.steps, 20))
-
-    # the new token's key/value rows, appended at the last cache slot every step
+    # the new token's key/value rows, appended at the last row of the sequence
+    # (which the last rank holds) every step
     hkn = k[:, T - 1].cpu().pin_memory()
     hvn = v[:, T - 1].cpu().pin_memory()
 
@@ -370,9 +446,9 @@ def run_ours(args):
                                               T - 1, D, HQ, HKV, BLOCK, SCALE, HP(hout),
                                               _capi.SA_HOST_PTRS))
         else:
-            # the same decode step sharded: q and the new token's k/v rows come
-            # from pinned host memory, the last rank (the sequence's tail)
-            # appends the row, all ranks reduce + all-gather + merge
+            # the same step sharded: q from pinned host memory on every rank,
+            # the new row appended by the last rank, one fused launch per rank,
+            # the output read back
             with torch.cuda.stream(stream):
                 q.copy_(hq_, non_blocking=True)
                 if rank == world - 1:
@@ -395,17 +471,15 @@ def run_ours(args):
     e1.record(stream)
     torch.cuda.synchronize(dev)
     wall = time.perf_counter() - w0
-    e_ms = max(e0.elapsed_time(e1), wall * 1e3)
-    if world > 1:
-        t = torch.tensor([e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e_ms = float(t.item())
-    e2e = algo_bytes(T) * world * ne / (e_ms / 1e3) / 1e9
+    e_ms = tmax(max(e0.elapsed_time(e1), wall * 1e3))
+    e2e = algo_bytes(T_GLOBAL) * ne / (e_ms / 1e3) / 1e9
 
     # the attention.h drop-in with every K/V byte copied from host memory per
     # call (PCIe-bound by construction), reported beside e2e
     e2e_kv = None
     if world == 1:
+        hk = k.cpu().pin_memory()
+        hv = v.cpu().pin_memory()
         nh = 3
         _capi.check(L.sa_attn_decode(ctx.h, 0, HP(hq_), HP(hk), HP(hv), T * D, T, D, HQ, HKV, BLOCK,
                                      SCALE, HP(hout), _capi.SA_HOST_PTRS))
@@ -418,6 +492,28 @@ def run_ours(args):
         h1.record(stream)
         torch.cuda.synchronize(dev)
         e2e_kv = algo_bytes(T) * nh / (h0.elapsed_time(h1) / 1e3) / 1e9
+        del hk, hv
+
+    # ---- weak scaling (extra): T_GLOBAL rows on EVERY GPU, the same fused step
+    weak = None
+    if world > 1 and not args.no_extra:
+        del q, k, v
+        torch.cuda.empty_cache()
+        qw, kw, vw = make_slice(T_GLOBAL * world, rank * T_GLOBAL, T_GLOBAL, dev, SEED)
+        wstep = lambda: decode_once(qw, kw, vw, T_GLOBAL, out)
+        for _ in range(args.warmup):
+            wstep()
+        barrier()
+        w0e, w1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0e.record(stream)
+        for _ in range(args.steps):
+            wstep()
+        w1e.record(stream)
+        barrier()
+        wms = tmax(w0e.elapsed_time(w1e))
+        weak = {"value": round(algo_bytes(T_GLOBAL) * world * args.steps / (wms / 1e3) / 1e9, 2),
+                "unit": "GB/s", "ms_per_step": round(wms / args.steps, 5), "kv_len": T_GLOBAL * world,
+                "T_per_gpu": T_GLOBAL, "scaling": "weak"}
 
     if rank == 0:
         if world == 1:
@@ -437,23 +533,25 @@ def run_ours(args):
             result["e2e"] = {"value": round(e2e, 2), "unit": "GB/s",
                              "h2d_bytes_per_step": (HQ * D + 2 * HKV * D) * 4,
                              "d2h_bytes_per_step": HQ * D * 4, "steps": ne,
-                             "path": "decode step over the sharded HBM-resident KV cache: q and the "
-                                     "new token's k/v from pinned host memory (the last rank "
-                                     "appends), partial + NCCL all-gather + merge, output read back"}
+                             "path": "decode step over the sharded HBM-resident KV cache: q from pinned "
+                                     "host memory on every rank, the new token's k/v appended by the "
+                                     "last rank, sa_attn_decode_sp (one launch per rank, exchange over "
+                                     "NVLink), output read back"}
+            if weak:
+                result["weak_scaling"] = weak
         # ---- CPU baseline: the reference's CPU path on a bounded sample (rank 0, N=1)
         if world == 1 and not args.no_cpu:
             try:
-                import numpy as np
                 qn, kn, vn = q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy()
                 T_s = 65536
-                t_s, reps = cpu_reference_time(qn, kn, vn, T_s, budget_s=args.cpu_budget)
+                t_s, reps, cores = cpu_reference_time(qn, kn, vn, T_s, budget_s=args.cpu_budget)
                 result["cpu_baseline"] = {
                     "value": round(algo_bytes(T_s) / t_s / 1e9, 3), "unit": "GB/s",
-                    "cores": os.cpu_count(), "kind": "reference",
+                    "cores": cores, "kind": "reference",
                     "sample": f"streaming_attention_omp per query head (16 heads) over the first "
-                              f"{T_s} of {T} KV rows, {reps} reps, median"}
+                              f"{T_s} of {T_GLOBAL} KV rows, {reps} reps, median, num_threads={cores}"}
             except Exception as e:  # the baseline is reported, never required
-                result["cpu_baseline"] = {"value": None, "unit": "GB/s", "cores": os.cpu_count(),
+                result["cpu_baseline"] = {"value": None, "unit": "GB/s", "cores": host_cores(),
                                           "kind": "reference", "sample": f"unavailable: {e}"}
         if world == 1 and not args.no_extra:
             pms, ptf = measure_prefill(ctx, dev, stream, 10, 3)
@@ -465,7 +563,8 @@ def run_ours(args):
             try:
                 q3, weights = measure_qwen3(ctx, dev, stream, 20, 3)
                 q3line = {"metric": "Qwen3-0.6B tok/s", "workload": Q3_WORKLOAD,
-                          **{k: round(v, 3) for k, v in q3.items()}}
+                          **{k_: round(v_, 4) for k_, v_ in q3.items()}}
+                q3line["roofline"] = qwen3_roofline(q3)
                 if not args.no_cpu:
                     try:
                         q3line["cpu_baseline"] = cpu_qwen3_baseline(weights)
@@ -476,9 +575,11 @@ def run_ours(args):
                 result["extra"]["qwen3_configs3_4"] = {"error": str(e)}
         print(json.dumps(result), flush=True)
 
+    if sp:
+        sp.close()
     ctx.close()
     if world > 1:
-        dist.barrier(device_ids=[local])
+        dist.barrier()
         dist.destroy_process_group()
     return 0
 
@@ -797,6 +898,45 @@ def measure_qwen3(ctx, dev, stream, steps, warmup, weights=None, long_prompt=Fal
     return out, weights
 
 
+def qwen3_bytes_flops(S: int = Q3_PROMPT):
+    """Algorithmic weight bytes of one Qwen3-0.6B pass (bf16: every layer
+    matrix and the tied embedding / lm_head once) and the FLOPs of an S-token
+    prefill (2 per weight per token + causal attention)."""
+    import streaming_attention_b200 as sa
+    c = sa.QWEN3_0_6B
+    H, D_, I, V = c["hidden"], c["head_dim"], c["inter"], c["vocab"]
+    QD, KD = c["hq"] * D_, c["hkv"] * D_
+    layer = QD * H + 2 * KD * H + H * QD + 3 * I * H
+    params = c["n_layers"] * layer + V * H
+    attn = c["n_layers"] * 4 * c["hq"] * D_ * S * (S + 1) / 2
+    return params * 2, 2.0 * S * params + attn
+
+
+def qwen3_roofline(res: dict) -> dict:
+    """Roofline of the Qwen3 measurements (HBM-bound: the weights are read once
+    per pass).  Decode adds the KV cache read of its mean context at bf16
+    width (the algorithmic minimum; the cache here is fp32, so the fraction is
+    conservative)."""
+    import streaming_attention_b200 as sa
+    c = sa.QWEN3_0_6B
+    peak, kind = load_peak()
+    wbytes, flops = qwen3_bytes_flops()
+    kv_row = c["n_layers"] * 2 * c["hkv"] * c["head_dim"] * 2          # bytes per cached token
+    out = {"bound": "hbm", "peak": peak, "unit": "GB/s", "peak_kind": f"{kind} hbm_gbs",
+           "weight_bytes": wbytes}
+    if "prefill_ms" in res:
+        t = res["prefill_ms"] / 1e3
+        out["prefill"] = {"bytes": wbytes, "flops": flops, "ms": round(res["prefill_ms"], 4),
+                          "achieved": round(wbytes / t / 1e9, 1), "frac": round(wbytes / t / 1e9 / peak, 4)}
+    for key, ctx0 in (("decode", Q3_PROMPT), ("decode_4096", 4096)):
+        ms = res.get(f"{key}_ms_per_token")
+        if ms:
+            b = wbytes + kv_row * (ctx0 + Q3_GEN / 2)
+            out[key] = {"bytes_per_token": int(b), "ms_per_token": round(ms, 4),
+                        "achieved": round(b / (ms / 1e3) / 1e9, 1), "frac": round(b / (ms / 1e3) / 1e9 / peak, 4)}
+    return out
+
+
 def cpu_qwen3_baseline(weights, budget_tokens=16):
     """The reference's AVX2 Qwen3 forward (qwen3_ops_avx.cpp:383) on the host:
     prefill of a bounded prompt, and a few cached decode steps."""
@@ -906,6 +1046,10 @@ def run_qwen3(args):
                 "h2d_bytes_per_step": Q3_PROMPT * 8, "d2h_bytes_per_step": Q3_PROMPT * 151936 * 4},
         "clocks": clk,
     }
+    rl = qwen3_roofline(res)
+    line["roofline"] = {"bound": "hbm", "achieved": rl["prefill"]["achieved"], "peak": rl["peak"], "unit": "GB/s",
+                        "frac": rl["prefill"]["frac"], "traffic": None,
+                        "per": "whole forward (weight bytes of one pass / prefill time)", "detail": rl}
     if not args.no_cpu and world == 1:
         try:
             line["cpu_baseline"] = cpu_qwen3_baseline(weights)

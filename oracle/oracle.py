@@ -54,13 +54,19 @@ def layer_floats(cfg: Qwen3Cfg) -> int:
 
 
 def bf16_round(x: np.ndarray) -> np.ndarray:
-    """Round fp32 to the nearest bf16 (ties to even); returns fp32 values."""
+    """Round fp32 to the nearest bf16 (ties to even); returns fp32 values.
+    32-bit arithmetic: u + 0x7FFF + lsb stays below 2^32 for every non-NaN
+    pattern; NaNs are made quiet and truncated."""
     x = _f32(x)
-    u = x.view(np.uint32).astype(np.uint64)
-    nan = (u & 0x7FFFFFFF) > 0x7F800000
-    r = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
-    r = np.where(nan, (u | 0x00400000) & 0xFFFF0000, r)
-    return r.astype(np.uint32).view(np.float32).reshape(x.shape)
+    u = x.view(np.uint32)
+    r = (u >> 16) & np.uint32(1)
+    r += np.uint32(0x7FFF)
+    r += u
+    r &= np.uint32(0xFFFF0000)
+    nan = (u & np.uint32(0x7FFFFFFF)) > np.uint32(0x7F800000)
+    if nan.any():
+        r[nan] = (u[nan] | np.uint32(0x00400000)) & np.uint32(0xFFFF0000)
+    return r.view(np.float32).reshape(x.shape)
 
 
 class Oracle:

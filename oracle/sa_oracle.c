@@ -244,19 +244,61 @@ ORC_EXPORT void orc_rms_norm(const float* x, const float* w, int rows, int n,
     }
 }
 
-/* y[s, o] = sum_i x[s, i] * W[o, i]: tensor_cpp/src/ops.cpp:315-369 */
-ORC_EXPORT void orc_linear(const float* x, const float* W, int rows, int in_f, int out_f,
-                           float* y) {
-    #pragma omp parallel for collapse(2) schedule(static)
-    for (int s = 0; s < rows; ++s) {
-        for (int o = 0; o < out_f; ++o) {
-            const float* xr = x + (size_t)s * in_f;
-            const float* wr = W + (size_t)o * in_f;
-            float acc = 0.0f;
-            for (int i = 0; i < in_f; ++i) acc += xr[i] * wr[i];
-            y[(size_t)s * out_f + o] = acc;
+/* y[s, o] = sum_i x[s, i] * W[o, i]: tensor_cpp/src/ops.cpp:315-369.       */
+/* Every output is one sum over i in increasing order, as the reference's   */
+/* loop forms it; the register tiles below only interleave independent      */
+/* sums (4 rows x ORC_OB outputs) so that they overlap in the FMA pipeline  */
+/* -- the bits of every output are those of the plain loop.                */
+#define ORC_OB 8
+#define ORC_MAX_D 256   /* head_dim bound of the Qwen3 forward */
+static void lin_tile(const float* x, const float* W, int in_f, int out_f, int s0, int ns,
+                     int o0, float* y) {
+    int no = out_f - o0 < ORC_OB ? out_f - o0 : ORC_OB;
+    if (no == ORC_OB && ns == 4) {
+        float acc[4][ORC_OB] = {{0}};
+        const float* x0 = x + (size_t)s0 * in_f;
+        const float* w0 = W + (size_t)o0 * in_f;
+        for (int i = 0; i < in_f; ++i) {
+            float xv[4];
+            for (int a = 0; a < 4; ++a) xv[a] = x0[(size_t)a * in_f + i];
+            for (int b = 0; b < ORC_OB; ++b) {
+                float w = w0[(size_t)b * in_f + i];
+                for (int a = 0; a < 4; ++a) acc[a][b] += xv[a] * w;
+            }
+        }
+        for (int a = 0; a < 4; ++a)
+            for (int b = 0; b < ORC_OB; ++b) y[(size_t)(s0 + a) * out_f + o0 + b] = acc[a][b];
+        return;
+    }
+    for (int a = 0; a < ns; ++a) {
+        const float* xr = x + (size_t)(s0 + a) * in_f;
+        if (no == ORC_OB) {
+            float acc[ORC_OB] = {0};
+            const float* w0 = W + (size_t)o0 * in_f;
+            for (int i = 0; i < in_f; ++i)
+                for (int b = 0; b < ORC_OB; ++b) acc[b] += xr[i] * w0[(size_t)b * in_f + i];
+            for (int b = 0; b < ORC_OB; ++b) y[(size_t)(s0 + a) * out_f + o0 + b] = acc[b];
+        } else {
+            for (int b = 0; b < no; ++b) {
+                const float* wr = W + (size_t)(o0 + b) * in_f;
+                float acc = 0.0f;
+                for (int i = 0; i < in_f; ++i) acc += xr[i] * wr[i];
+                y[(size_t)(s0 + a) * out_f + o0 + b] = acc;
+            }
         }
     }
+}
+
+ORC_EXPORT void orc_linear(const float* x, const float* W, int rows, int in_f, int out_f,
+                           float* y) {
+    int nrb = (rows + 3) / 4, nob = (out_f + ORC_OB - 1) / ORC_OB;
+    #pragma omp parallel for collapse(2) schedule(static)
+    for (int rb = 0; rb < nrb; ++rb)
+        for (int ob = 0; ob < nob; ++ob) {
+            int s0 = rb * 4;
+            int ns = rows - s0 < 4 ? rows - s0 : 4;
+            lin_tile(x, W, in_f, out_f, s0, ns, ob * ORC_OB, y);
+        }
 }
 
 /* inv_freq_i = 1/theta^(i/D); cos/sin[pos, i] = cos/sin(pos*inv_freq_i)     */
@@ -327,6 +369,7 @@ ORC_EXPORT int orc_qwen3_forward(const orc_qwen3_cfg* c, const float* embed,
                                  float* kc, float* vc, int max_seq, int pos0,
                                  int all_logits, float* logits) {
     const int H = c->hidden, D = c->head_dim, HQ = c->hq, HKV = c->hkv, I = c->inter;
+    if (D > ORC_MAX_D) return -4;
     const int QD = HQ * D, KD = HKV * D;
     const int total = pos0 + S;
     if (!kc && pos0 != 0) return -1;
@@ -410,22 +453,34 @@ ORC_EXPORT int orc_qwen3_forward(const orc_qwen3_cfg* c, const float* embed,
                 int kvh = h / rep;
                 int last = pos0 + s;
                 float mx = -INFINITY;
-                for (int j = 0; j < total; ++j) {
+                /* scores: one sum over e per key, 8 keys interleaved */
+                int j = 0;
+                for (; j + 8 <= total; j += 8) {
+                    float acc[8] = {0};
+                    const float* k0 = kh + (size_t)j * KD + kvh * D;
+                    for (int e = 0; e < D; ++e)
+                        for (int b = 0; b < 8; ++b) acc[b] += qi[e] * k0[(size_t)b * KD + e];
+                    for (int b = 0; b < 8; ++b) sc[j + b] = acc[b] * scale + (j + b <= last ? 0.0f : -INFINITY);
+                }
+                for (; j < total; ++j) {
                     const float* kr = kh + (size_t)j * KD + kvh * D;
                     float acc = 0.0f;
                     for (int e = 0; e < D; ++e) acc += qi[e] * kr[e];
                     sc[j] = acc * scale + (j <= last ? 0.0f : -INFINITY);
-                    mx = fmaxf(mx, sc[j]);
                 }
+                for (j = 0; j < total; ++j) mx = fmaxf(mx, sc[j]);
                 float sum = 0.0f;
-                for (int j = 0; j < total; ++j) { sc[j] = expf(sc[j] - mx); sum += sc[j]; }
-                for (int j = 0; j < total; ++j) sc[j] /= sum;
+                for (j = 0; j < total; ++j) { sc[j] = expf(sc[j] - mx); sum += sc[j]; }
+                for (j = 0; j < total; ++j) sc[j] /= sum;
                 float* oi = att + (size_t)s * QD + h * D;
-                for (int e = 0; e < D; ++e) {
-                    float acc = 0.0f;
-                    for (int j = 0; j < total; ++j) acc += sc[j] * vh[(size_t)j * KD + kvh * D + e];
-                    oi[e] = acc;
+                /* P.V: one sum over j per output column, the columns side by side */
+                float acc[ORC_MAX_D];
+                for (int e = 0; e < D; ++e) acc[e] = 0.0f;
+                for (j = 0; j < total; ++j) {
+                    const float* vr = vh + (size_t)j * KD + kvh * D;
+                    for (int e = 0; e < D; ++e) acc[e] += sc[j] * vr[e];
                 }
+                for (int e = 0; e < D; ++e) oi[e] = acc[e];
                 free(sc);
             }
         }

@@ -13,7 +13,8 @@ from conftest import ROOT
 
 PKG = os.path.join(ROOT, "streaming_attention_b200")
 BIN = os.path.join(PKG, "bin")
-REF = "/root/reference"
+# the reference tree: $SA_REFERENCE_DIR, else a checkout named `reference` beside this repository
+REF = os.environ.get("SA_REFERENCE_DIR", os.path.join(os.path.dirname(ROOT), "reference"))
 CXX = "/usr/bin/g++" if os.path.exists("/usr/bin/g++") else shutil.which("g++")
 DRIVERS = ["test_naive_cuda", "test_streaming_cuda", "test_streaming_cuda_multi", "test_mpi_cuda"]
 
