@@ -208,10 +208,14 @@ class Qwen3:
 
 
 def bf16_round(x: np.ndarray) -> np.ndarray:
-    """Round fp32 values to the nearest bf16 (ties to even), kept as fp32."""
+    """Round fp32 values to the nearest bf16 (ties to even), kept as fp32
+    (finite inputs; 32-bit arithmetic, u + 0x7FFF + lsb < 2^32 for them)."""
     x = np.ascontiguousarray(x, np.float32)
-    u = x.view(np.uint32).astype(np.uint64)
-    r = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
+    u = x.view(np.uint32)
+    r = (u >> 16) & np.uint32(1)
+    r += np.uint32(0x7FFF)
+    r += u
+    r &= np.uint32(0xFFFF0000)
     return r.view(np.float32).reshape(x.shape)
 
 

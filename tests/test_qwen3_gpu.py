@@ -258,32 +258,91 @@ def test_qwen3_errors(ctx):
     assert e.value.code == -7
 
 
-def test_qwen3_0_6b_full_size(ctx, oracle):
-    """BASELINE configs[3] / [4] shapes: the real Qwen3-0.6B architecture with
-    random-init weights, 128-token prompt: last-token logits vs the oracle and
-    greedy tokens identical to the oracle's cached decode."""
-    from streaming_attention_b200 import QWEN3_0_6B, Qwen3
+@pytest.fixture(scope="module")
+def q06():
+    """The real Qwen3-0.6B architecture with seeded random-init weights
+    (BASELINE configs[3] / [4]), generated once for the module."""
+    from streaming_attention_b200 import QWEN3_0_6B
     cfg = Qwen3Cfg(**{k: QWEN3_0_6B[k] for k in ("vocab", "hidden", "n_layers", "hq", "hkv", "head_dim",
                                                    "inter", "eps", "theta")})
-    w = make_qwen3_weights(cfg, 2026)
-    ids = I.rng(42).integers(0, cfg.vocab, 128)
-    m = Qwen3(QWEN3_0_6B, max_seq=160, ctx=ctx)
-    m.load(w)
-    got = m.forward(ids, logits="all")
-    max_seq = 160
+    return cfg, make_qwen3_weights(cfg, 2026)
+
+
+@pytest.fixture(scope="module")
+def q06_model(q06, ctx):
+    from streaming_attention_b200 import QWEN3_0_6B, Qwen3
+    m = Qwen3(QWEN3_0_6B, max_seq=Q06_MAX_SEQ, ctx=ctx)
+    m.load(q06[1])
+    yield m
+    m.close()
+
+
+Q06_MAX_SEQ = 4096 + 16
+
+
+def _oracle_greedy(oracle, cfg, w, prompt, n, max_seq):
+    """The oracle's cached greedy decode (qwen3_forward_with_cache STANDARD,
+    qwen3_ops.cpp:936-1014, then ops::argmax): the prompt, then n-1 one-token
+    steps.  Returns the n tokens, the top-1 minus top-2 logit gap at each
+    choice, and the prompt's last-token logits."""
     kc = np.zeros((cfg.n_layers, cfg.hkv, max_seq, cfg.head_dim), np.float32)
     vc = np.zeros_like(kc)
-    ref = oracle.qwen3_forward(cfg, w, ids, kc, vc, max_seq, 0, all_logits=False)
-    _close(got[-1], ref[0], "last-token logits")
-    n_new = 4
+    lg = oracle.qwen3_forward(cfg, w, prompt, kc, vc, max_seq, 0, all_logits=False)[0]
+    first = lg.copy()
+    toks, gaps, pos = [], [], len(prompt)
+    for i in range(n):
+        top2 = np.partition(lg, -2)[-2:]
+        gaps.append(float(top2[1] - top2[0]))
+        nxt = int(np.argmax(lg))
+        toks.append(nxt)
+        if i + 1 < n:
+            lg = oracle.qwen3_forward(cfg, w, np.array([nxt]), kc, vc, max_seq, pos, all_logits=False)[0]
+            pos += 1
+    return toks, gaps, first
+
+
+def _same_tokens(got, ref, gaps, what):
+    got = [int(t) for t in got]
+    if got != ref:
+        i = next(j for j in range(len(ref)) if got[j] != ref[j])
+        pytest.fail(f"{what}: greedy token {i} differs (GPU {got[i]}, oracle {ref[i]}); the oracle's "
+                    f"top-1 minus top-2 logit gap there is {gaps[i]:.3e}")
+
+
+def test_qwen3_0_6b_prefill_and_100_greedy_tokens(q06, q06_model, oracle):
+    """logits of all 128 prompt positions (qwen3_forward) within
+    the bar; configs[4] first run: the 100 greedy tokens after the 128-token
+    prompt identical to the oracle's cached decode."""
+    cfg, w = q06
+    m = q06_model
+    ids = I.rng(42).integers(0, cfg.vocab, 128)
+    m.reset()
+    got = m.forward(ids, logits="all")
+    ref = oracle.qwen3_forward(cfg, w, ids)
+    for r in range(0, 128, 16):
+        _close(got[r:r + 16], ref[r:r + 16], f"prefill logits rows {r}..{r + 15}")
+    toks = m.generate(ids, 100)
+    ref_toks, gaps, last = _oracle_greedy(oracle, cfg, w, ids, 100, 128 + 100)
+    _close(got[-1], last, "last-token logits (cached forward)")
+    _same_tokens(toks, ref_toks, gaps, "128-token prompt, 100 new tokens")
+
+
+def test_qwen3_0_6b_4096_token_prompt(q06, q06_model, oracle):
+    """configs[4] second run: a 4096-token prompt, then long-KV decode: the
+    prompt's last-token logits within the bar and the greedy tokens identical
+    to the oracle's (8 new tokens keep the oracle's CPU time bounded)."""
+    cfg, w = q06
+    m = q06_model
+    ids = I.rng(4096).integers(0, cfg.vocab, 4096)
+    n_new = 8
+    ref_toks, gaps, last = _oracle_greedy(oracle, cfg, w, ids, n_new, 4096 + n_new)
+    m.reset()
+    lg = m.forward(ids, use_cache=True, logits="last")
+    assert m.cache_len == 4096
+    _close(lg[0], last, "4096-token prompt, last-token logits")
+    m.reset()
     toks = m.generate(ids, n_new)
-    ref_toks, pos, nxt = [], len(ids), int(np.argmax(ref[0]))
-    for _ in range(n_new):
-        ref_toks.append(nxt)
-        lg = oracle.qwen3_forward(cfg, w, np.array([nxt]), kc, vc, max_seq, pos, all_logits=False)
-        pos += 1
-        nxt = int(np.argmax(lg[0]))
-    assert [int(t) for t in toks] == ref_toks
+    _same_tokens(toks, ref_toks, gaps, "4096-token prompt, 8 new tokens")
 
 
 def test_qwen3_graph_replay_and_cache_isolation(ctx):
