@@ -211,6 +211,32 @@ int sa_attn_prefill(sa_ctx* ctx, const void* q, const void* k, const void* v, in
                     long long o_tok_stride, unsigned flags);
 
 /*
+ * fp32 attention of Sq query rows on CUDA cores (fp32 throughout, like the
+ * reference's own operators):
+ *   q   [Sq, hq, d]       token-major, token stride q_tok_stride (elements)
+ *   k,v [hkv, Skv(+pad), d] head-major (one batch row of the reference's
+ *                         [B, H, S, D] tensors), head stride kv_head_stride
+ *   out [Sq, hq, d] fp32  token stride o_tok_stride
+ * causal = 1: query i sees keys 0 .. min(q_pos0 + i, Skv - 1) -- the causal
+ *   mask of create_causal_mask (qwen3_ops.cpp:240-259) for a query block at
+ *   offset q_pos0, and self_attention_streaming_blockwise
+ *   (tensor_cpp/src/ops.cpp:1383-1450) with q_pos0 = 0;
+ * causal = 0: every query sees all Skv keys -- ops::self_attention without a
+ *   mask (ops.cpp:514-641) and the decode of self_attention_streaming
+ *   (ops.cpp:964-1017, with the scale on the scores).
+ * Query head h reads KV head h / (hq / hkv) (repeat_kv, qwen3_ops.cpp:194-234,
+ * without the copy).  Scores are scaled by `scale` before the softmax.
+ * Requirements: d in {64, 128, 256}; hq/hkv in {1, 2, 4, 8} (also 16 for
+ * causal rows inside the sequence at d = 128); strides multiples of 4
+ * elements (kv_head_stride a multiple of d); device pointers 16-byte aligned
+ * unless SA_HOST_PTRS.
+ */
+int sa_attn_prompt_f32(sa_ctx* ctx, const float* q, const float* k, const float* v, int Sq, int Skv,
+                       int q_pos0, int causal, int d, int hq, int hkv, long long q_tok_stride,
+                       long long kv_head_stride, float scale, float* out, long long o_tok_stride,
+                       unsigned flags);
+
+/*
  * One decode step over a device-resident KV cache (batch 1):
  *   k_cache, v_cache [hkv, max_seq, d]  device memory, element type `dtype`
  *   k_new, v_new     [hkv, d]           the new token's key / value

@@ -14,7 +14,14 @@
 //      continued on the GPU (host KVCache adoption), sync_kv_to_host, two
 //      caches taking turns on the device cache, the qkv_projs and the split
 //      q/k/v_proj weight layouts, and the error behaviour (out-of-vocabulary
-//      id, full cache, a displaced GPU-only cache).
+//      id, full cache, a displaced GPU-only cache);
+//   C. tensor_cpp attention operators: ops::self_attention (no mask, the
+//      causal mask, an offset causal mask), self_attention_streaming_blockwise
+//      (Sq = Skv and Sq < Skv) and the decode attention (tensor_cpp/include/
+//      tensor_cpp/ops.h:133-279) vs ops::cuda::* (include/sa_ops_tensorcpp.hpp),
+//      and the head-wise / sequence strategies ops::mpi::cuda::* against the
+//      reference's unsplit ops::self_attention after repeat_kv (its MPI
+//      versions need an MPI install), at head_dim 128 and 64.
 // Bars: attention 1e-4 max-abs (fp32 path); Qwen3 logits 2e-3 of max |logit|
 // and identical greedy tokens.  Prints "CUDA METHOD CHECK OK" and exits 0 on
 // success.  Built by oracle/Makefile (target `check`) where the reference
@@ -23,15 +30,18 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <limits>
 #include <random>
 #include <stdexcept>
 #include <string>
 #include <vector>
 
 #include "attention.h"
+#include "tensor_cpp/ops.h"
 #include "tensor_cpp/qwen3_ops.h"
 
 #include "sa_attention_cuda.h"
+#include "sa_ops_tensorcpp.hpp"
 #include "sa_qwen3_tensorcpp.hpp"
 
 using namespace tensor_cpp;
@@ -259,11 +269,108 @@ void check_qwen3(bool split_qkv) {
     expect(full, "prompt longer than the cache raises std::runtime_error" + tag);
 }
 
+// ---------------------------------------------------------------- C
+Tensor uniform(const Shape& s, std::mt19937& g) {
+    std::uniform_real_distribution<float> u(-1.0f, 1.0f);
+    Tensor t(s);
+    for (size_t i = 0; i < t.size(); ++i) t.data()[i] = u(g);
+    return t;
+}
+
+bool close_attn(const Tensor& got, const Tensor& ref, const std::string& what) {
+    const double err = max_abs_diff(got.data(), ref.data(), ref.size(), nullptr);
+    const bool ok = got.shape() == ref.shape() && err <= 1e-4;
+    if (!ok) std::printf("     %s: max|err| %.3e\n", what.c_str(), err);
+    return ok;
+}
+
+// mask [Sq, Sk]: 0 where key j <= query i + off, -inf after
+Tensor offset_causal_mask(size_t Sq, size_t Sk, size_t off) {
+    Tensor m(Shape{Sq, Sk});
+    for (size_t i = 0; i < Sq; ++i)
+        for (size_t j = 0; j < Sk; ++j)
+            m.data()[i * Sk + j] = j <= i + off ? 0.0f : -std::numeric_limits<float>::infinity();
+    return m;
+}
+
+void check_ops(size_t D) {
+    const std::string tag = " [d=" + std::to_string(D) + "]";
+    std::mt19937 g(42 + D);
+    const float scale = 1.0f / std::sqrt((float)D);
+    const size_t B = 2, H = 8, S = 150;
+    const Tensor q = uniform(Shape{B, H, S, D}, g), k = uniform(Shape{B, H, S, D}, g), v = uniform(Shape{B, H, S, D}, g);
+    const Tensor causal = qwen3::create_causal_mask(S).view(Shape{1, 1, S, S});
+    expect(close_attn(ops::cuda::self_attention(q, k, v, &causal, scale), ops::self_attention(q, k, v, &causal, scale),
+                      "causal"),
+           "ops::cuda::self_attention, causal mask (create_causal_mask)" + tag);
+    expect(close_attn(ops::cuda::self_attention(q, k, v, nullptr, scale), ops::self_attention(q, k, v, nullptr, scale),
+                      "no mask"),
+           "ops::cuda::self_attention, no mask" + tag);
+    expect(close_attn(ops::cuda::self_attention_streaming_blockwise(q, k, v, scale, 32, 64),
+                      ops::self_attention_streaming_blockwise(q, k, v, scale, 32, 64), "blockwise"),
+           "ops::cuda::self_attention_streaming_blockwise, Sq = Skv" + tag);
+    {   // a query block after a cached prefix: offset causal mask, and the
+        // block-wise form (queries see keys 0..i)
+        const size_t Sq = 40, Sk = 170;
+        const Tensor qq = uniform(Shape{1, H, Sq, D}, g), kk = uniform(Shape{1, H, Sk, D}, g),
+                     vv = uniform(Shape{1, H, Sk, D}, g);
+        const Tensor m = offset_causal_mask(Sq, Sk, Sk - Sq);
+        expect(close_attn(ops::cuda::self_attention(qq, kk, vv, &m, scale), ops::self_attention(qq, kk, vv, &m, scale),
+                          "offset causal"),
+               "ops::cuda::self_attention, causal mask of a query block at offset Sk - Sq" + tag);
+        expect(close_attn(ops::cuda::self_attention_streaming_blockwise(qq, kk, vv, scale, 32, 64),
+                          ops::self_attention_streaming_blockwise(qq, kk, vv, scale, 32, 64), "blockwise Sq<Skv"),
+               "ops::cuda::self_attention_streaming_blockwise, Sq < Skv" + tag);
+        Tensor bad = offset_causal_mask(Sq, Sk, 3);
+        bad.data()[5] = 0.5f;
+        bool rejected = false;
+        try {
+            ops::cuda::self_attention(qq, kk, vv, &bad, scale);
+        } catch (const std::invalid_argument&) {
+            rejected = true;
+        }
+        expect(rejected, "a mask that is not causal raises std::invalid_argument" + tag);
+    }
+    {   // decode: one query over a long cache (the attention the Qwen3 decode needs)
+        const size_t T = 3001;
+        const Tensor qd = uniform(Shape{1, 16, 1, D}, g), kd = uniform(Shape{1, 16, T, D}, g),
+                     vd = uniform(Shape{1, 16, T, D}, g);
+        expect(close_attn(ops::cuda::self_attention_streaming(qd, kd, vd, scale, 64),
+                          ops::self_attention(qd, kd, vd, nullptr, scale), "decode"),
+               "ops::cuda::self_attention_streaming (decode, scale on the scores) = ops::self_attention" + tag);
+    }
+    {   // GQA strategies: 16 query heads, 8 KV heads, ground truth after repeat_kv
+        const size_t hq = 16, hkv = 8, Sg = 203;
+        const Tensor qg = uniform(Shape{1, hq, Sg, D}, g), kg = uniform(Shape{1, hkv, Sg, D}, g),
+                     vg = uniform(Shape{1, hkv, Sg, D}, g);
+        const Tensor kr = qwen3::repeat_kv(kg, (int)(hq / hkv)), vr = qwen3::repeat_kv(vg, (int)(hq / hkv));
+        const Tensor cm = qwen3::create_causal_mask(Sg).view(Shape{1, 1, Sg, Sg});
+        const Tensor ref_c = ops::self_attention(qg, kr, vr, &cm, scale);
+        const Tensor ref_n = ops::self_attention(qg, kr, vr, nullptr, scale);
+        expect(close_attn(ops::mpi::cuda::attention_headwise_standard(qg, kg, vg, &cm, scale, hq, hkv), ref_c, "hw std"),
+               "ops::mpi::cuda::attention_headwise_standard (causal mask, heads over the GPUs)" + tag);
+        expect(close_attn(ops::mpi::cuda::attention_headwise_standard(qg, kg, vg, nullptr, scale, hq, hkv), ref_n,
+                          "hw std nomask"),
+               "ops::mpi::cuda::attention_headwise_standard (no mask)" + tag);
+        expect(close_attn(ops::mpi::cuda::attention_headwise_online_softmax(qg, kg, vg, nullptr, scale, hq, hkv), ref_c,
+                          "hw online"),
+               "ops::mpi::cuda::attention_headwise_online_softmax (causal)" + tag);
+        expect(close_attn(ops::mpi::cuda::attention_sequence_online_softmax(qg, kg, vg, nullptr, scale, hq, hkv, Sg),
+                          ref_c, "sequence"),
+               "ops::mpi::cuda::attention_sequence_online_softmax (zig-zag chunks over the GPUs)" + tag);
+        expect(close_attn(ops::mpi::cuda::attention_sequence_online_softmax(qg, kg, vg, nullptr, scale, hq, hkv, Sg, 1),
+                          ref_c, "sequence 1 gpu"),
+               "ops::mpi::cuda::attention_sequence_online_softmax on one GPU" + tag);
+    }
+}
+
 }  // namespace
 
 int main() {
     try {
         check_attention();
+        check_ops(128);
+        check_ops(64);
         check_qwen3(false);
         check_qwen3(true);
     } catch (const std::exception& e) {

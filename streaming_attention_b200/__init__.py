@@ -22,6 +22,7 @@ from .attention import (  # noqa: F401
     attn_decode_step,
     attn_merge,
     attn_prefill,
+    attn_prompt_f32,
     naive_attention_cuda,
     streaming_attention_cuda,
     streaming_attention_mpi_cuda,
@@ -31,6 +32,6 @@ from .qwen3 import QWEN3_0_6B, Qwen3, Qwen3Config  # noqa: F401
 
 __all__ = [
     "Context", "SAError", "lib", "LIB_PATH", "SA_F32", "SA_BF16", "SA_HOST_PTRS",
-    "attn_decode", "attn_decode_partial", "attn_decode_step", "attn_merge", "attn_prefill", "streaming_attention_cuda",
+    "attn_decode", "attn_decode_partial", "attn_decode_step", "attn_merge", "attn_prefill", "attn_prompt_f32", "streaming_attention_cuda",
     "naive_attention_cuda", "streaming_attention_mpi_cuda", "Qwen3", "Qwen3Config", "QWEN3_0_6B",
 ]

@@ -69,6 +69,9 @@ SIGNATURES = {
                                    C.c_uint]),
     "sa_qwen3_generate": (C.c_int, [_vp, C.POINTER(C.c_int64), C.c_int, C.c_int,
                                     C.POINTER(C.c_int64), C.c_uint]),
+    "sa_attn_prompt_f32": (C.c_int, [_vp, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                     C.c_int, C.c_int, C.c_longlong, C.c_longlong, C.c_float, _vp,
+                                     C.c_longlong, C.c_uint]),
     "sa_sp_create": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]),
     "sa_sp_handle": (C.c_int, [_vp, _vp]),
     "sa_sp_connect": (C.c_int, [_vp, _vp]),

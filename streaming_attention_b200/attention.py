@@ -171,6 +171,28 @@ def attn_prefill(q, k, v, scale: float, q_pos0: int = 0, out_dtype: str = "float
     return out
 
 
+def attn_prompt_f32(q, k, v, scale: float, q_pos0: int = 0, causal: bool = True, ctx: Context | None = None,
+                    out=None):
+    """fp32 attention of several query rows (sa_attn_prompt_f32).
+
+    q [Sq, hq, d] token-major; k, v [hkv, Skv, d] head-major (one batch row
+    of the reference's [B, H, S, D] tensors); fp32, numpy (host) or CUDA
+    torch tensors.  causal: query i sees keys 0 .. min(q_pos0 + i, Skv - 1);
+    else every key.  Returns out [Sq, hq, d] fp32.
+    """
+    q, k, v = _prep(q), _prep(k), _prep(v)
+    Sq, hq, d = q.shape
+    hkv, Skv, _ = k.shape
+    ctx = _ctx_for(q, ctx)
+    flags = 0 if _is_torch(q) else SA_HOST_PTRS
+    if out is None:
+        out = _out_like(q, (Sq, hq, d))
+    _bind_stream(ctx, q)
+    check(lib().sa_attn_prompt_f32(ctx.h, _ptr(q), _ptr(k), _ptr(v), Sq, Skv, q_pos0, 1 if causal else 0, d, hq,
+                                   hkv, hq * d, Skv * d, scale, _ptr(out), hq * d, flags))
+    return out
+
+
 # ---- attention.h mirror ---------------------------------------------------
 
 def streaming_attention_cuda(Q, K, V, T: int, d: int, block_size: int, ctx: Context | None = None):

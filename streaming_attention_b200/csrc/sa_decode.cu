@@ -23,6 +23,7 @@
 //    head to finish (atomic arrival counter) merges all splits -- the
 //    associative merge of streaming_omp.cpp:27-48 -- so a call is one launch.
 #include <cuda_bf16.h>
+#include <algorithm>
 #include <cmath>
 
 #include "sa_decode_plan.h"
@@ -80,8 +81,10 @@ struct Args {
     float* out_l;               // optional [hq]
     int* status;
     // multi-query launches (gridDim.z > 1): query z reads q + z*q_stride,
-    // attends rows [0, T + z) and writes out + z*o_stride (n_splits == 1)
+    // attends rows [0, T + z*q_causal), at most rows_per_split, and writes
+    // out + z*o_stride (n_splits == 1)
     long long q_stride, o_stride;
+    int q_causal;
     // when set, the row count is read on the device: T = *len_dev + 1 (the
     // KV-cache length before the token being decoded, plus that token), so a
     // captured launch stays valid as the cache grows
@@ -253,7 +256,7 @@ __global__ void __launch_bounds__(THREADS, NST <= 3 ? 2 : 1) decode_kernel(const
         if (split >= nsplit) return;
     }
     const int t0 = split * rps;
-    const int nrows = max(0, min(T + qz - t0, rps));
+    const int nrows = max(0, min(T + qz * a.q_causal - t0, rps));
     const int nst = (nrows + SR - 1) / SR;
     const KT* kg = static_cast<const KT*>(a.k) + (size_t)kvh * a.kv_head_stride + (size_t)t0 * D;
     const KT* vg = static_cast<const KT*>(a.v) + (size_t)kvh * a.kv_head_stride + (size_t)t0 * D;
@@ -703,7 +706,7 @@ static int launch_decode(sa_ctx* ctx, int dtype, const void* q, const void* k, c
     a.counters = ctx->counters;
     a.out = out; a.out_m = out_m; a.out_l = out_l;
     a.status = ctx->status;
-    a.q_stride = 0; a.o_stride = 0;
+    a.q_stride = 0; a.o_stride = 0; a.q_causal = 1;
     a.len_dev = nullptr;
     a.sp = {};
     a.sp.world = 1;
@@ -852,7 +855,7 @@ int decode_dev_launch(cudaStream_t st, int* status, int num_sms, const float* q,
     a.counters = counters;
     a.out = out; a.out_m = nullptr; a.out_l = nullptr;
     a.status = status;
-    a.q_stride = 0; a.o_stride = 0;
+    a.q_stride = 0; a.o_stride = 0; a.q_causal = 1;
     a.len_dev = len_dev;
     a.sp = {};
     a.sp.world = 1;
@@ -969,7 +972,7 @@ SA_API int sa_attn_decode_noalloc(void* stream, int dtype, const void* q, const 
     a.counters = counters;
     a.out = out; a.out_m = nullptr; a.out_l = nullptr;
     a.status = status;
-    a.q_stride = 0; a.o_stride = 0;
+    a.q_stride = 0; a.o_stride = 0; a.q_causal = 1;
     a.len_dev = nullptr;
     a.sp = {};
     a.sp.world = 1;
@@ -1247,4 +1250,110 @@ SA_API int sa_attn_decode_sp(sa_sp* sp, int dtype, const void* q, const void* k,
     a.done = sp->ctl + 1;
     return decode_common("sa_attn_decode_sp", sp->ctx, dtype, q, k, v, kv_head_stride, T_local, d, hq, hkv,
                          block, scale, out, m_out, l_out, flags, &a);
+}
+
+// ===========================================================================
+// fp32 attention of several query rows: ops::self_attention with no mask or
+// the causal mask (tensor_cpp/src/ops.cpp:514-641, create_causal_mask
+// qwen3_ops.cpp:240-259) and self_attention_streaming_blockwise
+// (ops.cpp:1383-1450), fp32 like the reference.  Causal rows whose limit lies
+// inside the sequence run on the prompt-attention kernel (head_dim 128); the
+// other rows -- full visibility, rows whose limit is past the last key, other
+// head sizes -- on the decode kernel's multi-query launch (one CTA per query
+// and KV head).
+// ===========================================================================
+namespace sa {
+static int attn_prompt_dev(sa_ctx* ctx, const float* q, const float* k, const float* v, int Sq, int Skv, int q_pos0,
+                           int causal, int d, int hq, int hkv, long long qs, long long kvs, float scale, float* out,
+                           long long os) {
+    const int G = hq / hkv;
+    int i0 = 0;
+    if (causal && d == 128 && (G == 1 || G == 2 || G == 4 || G == 8 || G == 16)) {
+        const int n_causal = std::min(Sq, Skv - q_pos0);   // rows whose last key is inside the sequence
+        if (n_causal > 0) {
+            SA_RC_TRY(prompt_attn_launch(ctx->stream, ctx->status, q, qs, k, v, kvs,
+                                         (long long)(hkv - 1) * (kvs / d) + Skv, q_pos0 + 1, n_causal, d, hq, hkv,
+                                         scale, out, os, nullptr, nullptr));
+            i0 = n_causal;
+        }
+    }
+    if (i0 >= Sq) return SA_OK;
+    dec::KernelFn fn = dec::pick<float>(d, G);
+    SA_CHECK_ARG(fn != nullptr, "sa_attn_prompt_f32: hq/hkv = %d at d = %d takes only causal rows inside the "
+                 "sequence (d = 128)", G, d);
+    SA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::SMEM_BYTES));
+    for (int z0 = i0; z0 < Sq; z0 += 65535) {
+        const int nz = std::min(65535, Sq - z0);
+        dec::Args a;
+        a.q = q + (size_t)z0 * qs;
+        a.k = k;
+        a.v = v;
+        a.kv_head_stride = kvs;
+        a.T = causal ? q_pos0 + z0 + 1 : Skv;
+        a.hq = hq;
+        a.hkv = hkv;
+        a.rows_per_split = Skv;                    // one split: query z sees min(T + z*causal, Skv) rows
+        a.n_splits = 1;
+        a.qscale = scale * dec::LOG2E;
+        a.part_m = a.part_l = a.part_o = nullptr;  // one split: no partials
+        a.counters = ctx->counters;
+        a.out = out + (size_t)z0 * os;
+        a.out_m = a.out_l = nullptr;
+        a.status = ctx->status;
+        a.q_stride = qs;
+        a.o_stride = os;
+        a.q_causal = causal ? 1 : 0;
+        a.len_dev = nullptr;
+        a.sp = {};
+        a.sp.world = 1;
+        fn<<<dim3(1, hkv, nz), dec::THREADS, dec::SMEM_BYTES, ctx->stream>>>(a);
+        SA_CUDA_TRY(cudaGetLastError());
+    }
+    return SA_OK;
+}
+}  // namespace sa
+
+SA_API int sa_attn_prompt_f32(sa_ctx* ctx, const float* q, const float* k, const float* v, int Sq, int Skv,
+                              int q_pos0, int causal, int d, int hq, int hkv, long long q_tok_stride,
+                              long long kv_head_stride, float scale, float* out, long long o_tok_stride,
+                              unsigned flags) {
+    using namespace sa;
+    clear_error();
+    SA_CHECK_ARG(ctx && q && out && (Skv == 0 || (k && v)), "sa_attn_prompt_f32: null argument");
+    SA_CHECK_ARG(Sq >= 1 && Skv >= 1 && q_pos0 >= 0, "sa_attn_prompt_f32: Sq = %d, Skv = %d, q_pos0 = %d", Sq, Skv,
+                 q_pos0);
+    SA_CHECK_ARG(!causal || q_pos0 < Skv, "sa_attn_prompt_f32: q_pos0 = %d leaves query 0 without keys (Skv = %d)",
+                 q_pos0, Skv);
+    SA_CHECK_ARG(d == 64 || d == 128 || d == 256, "sa_attn_prompt_f32: d = %d (64, 128, 256)", d);
+    SA_CHECK_ARG(hkv >= 1 && hq >= hkv && hq % hkv == 0 && hkv <= 65535, "sa_attn_prompt_f32: hq = %d, hkv = %d", hq,
+                 hkv);
+    SA_CHECK_ARG(q_tok_stride >= (long long)hq * d && o_tok_stride >= (long long)hq * d &&
+                     kv_head_stride >= (long long)Skv * d,
+                 "sa_attn_prompt_f32: strides below the row sizes");
+    SA_CHECK_ARG(q_tok_stride % 4 == 0 && o_tok_stride % 4 == 0 && kv_head_stride % d == 0,
+                 "sa_attn_prompt_f32: strides must be multiples of 4 elements (kv: of d)");
+    DeviceGuard guard(ctx->device);
+    if (!(flags & SA_HOST_PTRS)) {
+        SA_CHECK_ARG((((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 15) == 0,
+                     "sa_attn_prompt_f32: pointers must be 16-byte aligned");
+        return attn_prompt_dev(ctx, q, k, v, Sq, Skv, q_pos0, causal, d, hq, hkv, q_tok_stride, kv_head_stride,
+                               scale, out, o_tok_stride);
+    }
+    // host buffers: dense device copies, then the output back with its stride
+    const size_t row = (size_t)hq * d * 4, kvrow = (size_t)Skv * d * 4;
+    const size_t qb = align_up((size_t)Sq * row, 256), kvb = align_up((size_t)hkv * kvrow, 256);
+    SA_RC_TRY(ensure_stage(ctx, 2 * qb + 2 * kvb));
+    char* base = static_cast<char*>(ctx->stage);
+    float* dq = reinterpret_cast<float*>(base);
+    float* dk = reinterpret_cast<float*>(base + qb);
+    float* dv = reinterpret_cast<float*>(base + qb + kvb);
+    float* dout = reinterpret_cast<float*>(base + qb + 2 * kvb);
+    cudaStream_t st = ctx->stream;
+    SA_CUDA_TRY(cudaMemcpy2DAsync(dq, row, q, (size_t)q_tok_stride * 4, row, Sq, cudaMemcpyHostToDevice, st));
+    SA_CUDA_TRY(cudaMemcpy2DAsync(dk, kvrow, k, (size_t)kv_head_stride * 4, kvrow, hkv, cudaMemcpyHostToDevice, st));
+    SA_CUDA_TRY(cudaMemcpy2DAsync(dv, kvrow, v, (size_t)kv_head_stride * 4, kvrow, hkv, cudaMemcpyHostToDevice, st));
+    SA_RC_TRY(attn_prompt_dev(ctx, dq, dk, dv, Sq, Skv, q_pos0, causal, d, hq, hkv, (long long)hq * d,
+                              (long long)Skv * d, scale, dout, (long long)hq * d));
+    SA_CUDA_TRY(cudaMemcpy2DAsync(out, (size_t)o_tok_stride * 4, dout, row, row, Sq, cudaMemcpyDeviceToHost, st));
+    return sync_and_check(ctx);
 }

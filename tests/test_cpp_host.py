@@ -66,3 +66,27 @@ def test_qwen3_adapter_compiles_against_reference_headers(tmp_path):
                         "-I", os.path.join(ROOT, "include"), '-include', "tensor_cpp/qwen3_loader.h", str(src)],
                        capture_output=True, text=True)
     assert r.returncode == 0, r.stderr[-2000:]
+
+
+@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "tensor_cpp", "include")),
+                    reason="reference headers not present")
+def test_ops_adapter_compiles_against_reference_headers(tmp_path):
+    """include/sa_ops_tensorcpp.hpp: the CUDA method of ops::self_attention,
+    self_attention_streaming[_blockwise] and the ops::mpi head-wise / sequence
+    operators, called with the reference's Tensor types."""
+    src = tmp_path / "use_ops.cpp"
+    src.write_text(
+        '#include "tensor_cpp/ops.h"\n#include "sa_ops_tensorcpp.hpp"\n'
+        "using namespace tensor_cpp;\n"
+        "Tensor f(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor* m) {\n"
+        "  Tensor a = ops::cuda::self_attention(q, k, v, m, 0.1f);\n"
+        "  Tensor b = ops::cuda::self_attention_streaming(q, k, v, 0.1f, 64);\n"
+        "  Tensor c = ops::cuda::self_attention_streaming_blockwise(q, k, v, 0.1f, 32, 64);\n"
+        "  Tensor d = ops::mpi::cuda::attention_headwise_standard(q, k, v, m, 0.1f, 16, 8);\n"
+        "  Tensor e = ops::mpi::cuda::attention_headwise_online_softmax(q, k, v, m, 0.1f, 16, 8, 2);\n"
+        "  return ops::mpi::cuda::attention_sequence_online_softmax(q, k, v, m, 0.1f, 16, 8, 128, 4);\n}\n")
+    r = subprocess.run([CXX, "-std=c++17", "-fsyntax-only", "-Wall", "-Wextra", "-I",
+                        os.path.join(REF, "tensor_cpp", "include"), "-I", os.path.join(ROOT, "include"), str(src)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert "sa_ops_tensorcpp.hpp" not in r.stderr, r.stderr[-2000:]    # no warnings from the header itself
