@@ -426,6 +426,41 @@ int sa_qwen3_load_safetensors_tp(sa_ctx* ctx, const char* path, int max_seq, flo
 int sa_qwen3_tp_handle(sa_qwen3* m, void* handle);
 int sa_qwen3_tp_connect(sa_qwen3* m, const void* handles);
 
+/*
+ * Sequence-parallel Qwen3 over `world` GPUs (1..8), one model per GPU -- the
+ * reference's SEQUENCE strategy (ParallelStrategy, qwen3_ops_mpi.h:30-50;
+ * qwen3_forward_mpi_omp, qwen3_ops_mpi.cpp:498-642), whose outputs are wrong
+ * there; here they equal the single-GPU forward's.
+ *
+ * Every rank holds the whole model and a whole KV cache.  A prompt of S >=
+ * 2 * world tokens is split over the ranks by tokens, rank r taking tokens
+ * [S*r/world, S*(r+1)/world): its projections and MLP run on its own tokens
+ * at their global RoPE positions; after each layer's K/V cache append the
+ * rank stores its new K/V rows into the same rows of every other rank's
+ * cache over NVLink (CUDA IPC mappings) and publishes a flag, and every rank
+ * waits for all ranks' rows before its causal attention; at the end the
+ * final residual rows are gathered the same way, so every rank computes the
+ * same logits / next token.  Shorter prompts and single-token decode steps
+ * run whole on every rank (the caches are identical), so generate() gives the
+ * same tokens on every rank without further exchanges.
+ *
+ * sa_qwen3_create_sp: as sa_qwen3_create for rank `rank` of `world`; weights
+ *   are set with the same full tensors on every rank.
+ * sa_qwen3_sp_handle: SA_QWEN3_SP_HANDLE_BYTES bytes naming this rank's row
+ *   buffer and K/V caches (CUDA IPC handles) and its GPU, for every rank.
+ * sa_qwen3_sp_connect: the world handles in rank order; maps the other ranks'
+ *   buffers.  Ranks on one GPU are rejected (SA_ERR_ARG).  Required before
+ *   forward / generate.
+ * Every rank then calls sa_qwen3_forward / sa_qwen3_generate with the same
+ * arguments in the same order; prompts of up to min(max_seq, 8192) tokens.
+ * A rank that stops taking part makes the others' waits give up after a few
+ * seconds (SA_ERR_TIMEOUT at the next synchronising call).
+ */
+#define SA_QWEN3_SP_HANDLE_BYTES 256
+int sa_qwen3_create_sp(sa_ctx* ctx, const sa_qwen3_config* cfg, int rank, int world, sa_qwen3** out);
+int sa_qwen3_sp_handle(sa_qwen3* m, void* handle);
+int sa_qwen3_sp_connect(sa_qwen3* m, const void* handles);
+
 #ifdef __cplusplus
 }
 #endif

@@ -57,6 +57,9 @@ SIGNATURES = {
                                                C.POINTER(_vp)]),
     "sa_qwen3_tp_handle": (C.c_int, [_vp, _vp]),
     "sa_qwen3_tp_connect": (C.c_int, [_vp, _vp]),
+    "sa_qwen3_create_sp": (C.c_int, [_vp, _vp, C.c_int, C.c_int, C.POINTER(_vp)]),
+    "sa_qwen3_sp_handle": (C.c_int, [_vp, _vp]),
+    "sa_qwen3_sp_connect": (C.c_int, [_vp, _vp]),
     "sa_qwen3_destroy": (C.c_int, [_vp]),
     "sa_qwen3_set_embed": (C.c_int, [_vp, _fp, _fp, _fp]),
     "sa_qwen3_set_layer": (C.c_int, [_vp, C.c_int] + [_fp] * 11),

@@ -107,6 +107,20 @@ struct sa_qwen3 {
     float* tp_x2 = nullptr;              // [hidden] decode-path residual, other half of the ping-pong
     float* x_last = nullptr;             // residual after the last run_layers (m->x or tp_x2)
     bool x_last_ll = false;              // its pending exchange came as words (single-token path)
+    // sequence-parallel rank (sa_qwen3_create_sp; the whole model on every
+    // rank): prompts are split over the ranks by tokens; this rank's buffer
+    // holds the flags [2][world] (256 bytes) and then the residual rows of a
+    // prompt [sp_rows][hidden]; the peers' buffers and K/V caches are mapped
+    int sp_rank = 0, sp_world = 1;
+    void* sp_buf = nullptr;
+    int sp_rows = 0;
+    void* sp_peer_buf[sa::TP_MAX] = {};
+    float* sp_peer_kc[sa::TP_MAX] = {};
+    float* sp_peer_vc[sa::TP_MAX] = {};
+    bool sp_connected = false;
+    unsigned* sp_seq = nullptr;          // [1] exchange instances completed
+    unsigned* sp_cnt = nullptr;          // [1] producer arrival counter
+    unsigned char uuid[16] = {};         // the GPU's UUID (ranks must be on different GPUs)
 };
 
 namespace sa {
@@ -154,6 +168,13 @@ static void free_model(sa_qwen3* m) {
     for (int r = 0; r < sa::TP_MAX; ++r)
         if (m->tp_peer[r] && r != m->tp_rank) cudaIpcCloseMemHandle(m->tp_peer[r]);
     cudaFree(m->tp_buf); cudaFree(m->tp_seq); cudaFree(m->tp_cnt); cudaFree(m->tp_part); cudaFree(m->tp_x2);
+    for (int r = 0; r < sa::TP_MAX; ++r) {
+        if (r == m->sp_rank) continue;
+        if (m->sp_peer_buf[r]) cudaIpcCloseMemHandle(m->sp_peer_buf[r]);
+        if (m->sp_peer_kc[r]) cudaIpcCloseMemHandle(m->sp_peer_kc[r]);
+        if (m->sp_peer_vc[r]) cudaIpcCloseMemHandle(m->sp_peer_vc[r]);
+    }
+    cudaFree(m->sp_buf); cudaFree(m->sp_seq); cudaFree(m->sp_cnt);
     if (m->dec_graph) cudaGraphExecDestroy(m->dec_graph);
     for (auto& kv : m->pf_graphs) cudaGraphExecDestroy(kv.second);
     if (m->ev_in) cudaEventDestroy(m->ev_in);
@@ -266,6 +287,23 @@ static TpArgs tp_args(sa_qwen3* m, int k) {
     return t;
 }
 
+// Exchange operands of instance k of the current sequence-parallel segment:
+// the flags of every rank's buffer, the sequence word and arrival counter.
+static TpArgs sp_args(sa_qwen3* m, int k) {
+    TpArgs t;
+    t.rank = m->sp_rank;
+    t.world = m->sp_world;
+    for (int r = 0; r < m->sp_world; ++r) t.flags[r] = static_cast<unsigned*>(m->sp_peer_buf[r]);
+    t.seq = m->sp_seq;
+    t.k = k;
+    t.cnt = m->sp_cnt;
+    t.status = m->ctx->status;
+    return t;
+}
+static float* sp_xrows(sa_qwen3* m, int r) {
+    return reinterpret_cast<float*>(static_cast<char*>(m->sp_peer_buf[r]) + 256);
+}
+
 // Head-parallel ranks run the same schedule on their share of the heads and
 // intermediate features; each layer exchanges two partial sums of the
 // residual update (o_proj, down_proj: instances 2l and 2l + 1 of the
@@ -273,7 +311,14 @@ static TpArgs tp_args(sa_qwen3* m, int k) {
 // the single-token path the residual alternates between m->x and m->tp_x2
 // (the consuming GEMV reads one and writes the other); m->x_last records
 // where it ends.  The prompt path updates m->x in place.
-static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr, int kv_row0 = -1) {
+//
+// Sequence-parallel ranks (sp) run the prompt path on their own tokens at
+// their global positions; after QK-norm, RoPE and the cache append of a
+// layer, the rank's new K/V rows go to the same rows of every other rank's
+// cache (instance l of the segment) and every rank waits for all ranks'
+// rows before the causal attention, which then sees the whole prefix.
+static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr, int kv_row0 = -1,
+                      bool sp = false) {
     if (kv_row0 < 0) kv_row0 = pos0;
     const sa_qwen3_config& c = m->c;
     cudaStream_t st = m->cur;
@@ -342,6 +387,22 @@ static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr
                        true, &sq));
             SA_RC(launch_qknorm_rope_append(st, sq > 1 ? m->gemm_ws : m->qkv, sq, M, m->hq, m->hkv, L.q_norm, L.k_norm,
                                             m->cos_t, m->sin_t, pos0, nullptr, shift, m->q, kc, vc, c.max_seq));
+            if (sp) {
+                SpCopy cp;
+                cp.nreg = 2;
+                cp.src[0] = kc + (size_t)kv_row0 * D;
+                cp.src[1] = vc + (size_t)kv_row0 * D;
+                for (int r = 0; r < m->sp_world; ++r) {
+                    if (r == m->sp_rank) continue;
+                    cp.dst[0][r] = m->sp_peer_kc[r] + l * layer_kv + (size_t)kv_row0 * D;
+                    cp.dst[1][r] = m->sp_peer_vc[r] + l * layer_kv + (size_t)kv_row0 * D;
+                }
+                cp.nblk = m->hkv;
+                cp.blk_floats = (long long)M * D;
+                cp.stride = (long long)c.max_seq * D;
+                SA_RC(launch_sp_rows_scatter(st, cp, sp_args(m, l), m->ctx->num_sms));
+                SA_RC(launch_sp_wait(st, sp_args(m, l)));
+            }
             SA_RC(prompt_attn_launch(st, m->ctx->status, m->q, m->QD, ka, va, (long long)c.max_seq * D,
                                      (long long)m->hkv * c.max_seq - shift, pos0 + 1, M, D, m->hq, m->hkv, scale,
                                      nullptr, m->QD, m->a_hi, m->a_lo));
@@ -383,7 +444,9 @@ static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr
 // add the last layer's exchanged down_proj sums (instance 2L - 1); with
 // `token` each rank takes the argmax over its vocabulary slice and the
 // ranks' maxima are exchanged (instance 2L), which also closes the segment.
-static int run_head(sa_qwen3* m, int r0, int n, int64_t* token = nullptr) {
+// `xsrc` (the single-GPU path only) reads the residual rows from there
+// instead of m->x: the rows a sequence-parallel prompt gathered.
+static int run_head(sa_qwen3* m, int r0, int n, int64_t* token = nullptr, const float* xsrc = nullptr) {
     const sa_qwen3_config& c = m->c;
     cudaStream_t st = m->cur;
     const size_t H = c.hidden;
@@ -413,15 +476,47 @@ static int run_head(sa_qwen3* m, int r0, int n, int64_t* token = nullptr) {
         }
         return SA_OK;
     }
+    const float* xs = xsrc ? xsrc : m->x;
     if (n == 1) {
-        SA_RC(launch_gemv2(st, QW_EPI_STORE, true, m->lm_head, c.vocab, c.hidden, m->x + (size_t)r0 * c.hidden,
+        SA_RC(launch_gemv2(st, QW_EPI_STORE, true, m->lm_head, c.vocab, c.hidden, xs + (size_t)r0 * c.hidden,
                            m->final_norm, c.eps, m->logits, token ? m->d_amax : nullptr));
         if (token) SA_RC(launch_amax_to_token(st, m->d_amax, token));
     } else {
-        SA_RC(launch_rmsnorm_hilo(st, m->x + (size_t)r0 * c.hidden, m->final_norm, n, c.hidden, c.eps, m->a_hi, m->a_lo));
+        SA_RC(launch_rmsnorm_hilo(st, const_cast<float*>(xs) + (size_t)r0 * c.hidden, m->final_norm, n, c.hidden, c.eps,
+                                  m->a_hi, m->a_lo));
         SA_RC(gemm(m, m->a_hi, m->a_lo, c.hidden, m->lm_head, n, c.vocab, c.hidden, QW_EPI_STORE, m->logits, c.vocab,
                    nullptr, nullptr, 0));
     }
+    return SA_OK;
+}
+
+// This rank's tokens [s0, s1) of an S-token sequence-parallel prompt.
+static void sp_share(const sa_qwen3* m, int S, int* s0, int* s1) {
+    *s0 = (int)((long long)S * m->sp_rank / m->sp_world);
+    *s1 = (int)((long long)S * (m->sp_rank + 1) / m->sp_world);
+}
+static bool sp_split(const sa_qwen3* m, int S) { return m->sp_world > 1 && S >= 2 * m->sp_world; }
+
+// A sequence-parallel prompt of S tokens at positions pos0.. and cache rows
+// kv_row0.. (m->ids holds this rank's tokens): this rank's layers with the
+// per-layer K/V exchanges (instances 0..L-1), then every rank's final
+// residual rows gathered in every rank's row buffer (instance L), which
+// *x_all points to; the segment's L + 1 instances are then counted.
+static int run_prompt_sp(sa_qwen3* m, int S, int pos0, int kv_row0, const float** x_all) {
+    const int L = m->c.n_layers, H = m->c.hidden;
+    int s0, s1;
+    sp_share(m, S, &s0, &s1);
+    SA_RC(run_layers(m, s1 - s0, pos0 + s0, nullptr, kv_row0 + s0, true));
+    SpCopy cp;
+    cp.nreg = 1;
+    cp.src[0] = m->x;
+    for (int r = 0; r < m->sp_world; ++r) cp.dst[0][r] = sp_xrows(m, r) + (size_t)s0 * H;
+    cp.nblk = 1;
+    cp.blk_floats = (long long)(s1 - s0) * H;
+    SA_RC(launch_sp_rows_scatter(m->cur, cp, sp_args(m, L), m->ctx->num_sms));
+    SA_RC(launch_sp_wait(m->cur, sp_args(m, L)));
+    SA_RC(launch_tp_seq_add(m->cur, m->sp_seq, L + 1));
+    *x_all = sp_xrows(m, m->sp_rank);
     return SA_OK;
 }
 
@@ -590,6 +685,124 @@ SA_API int sa_qwen3_tp_connect(sa_qwen3* m, const void* handles) {
         m->tp_peer[r] = p;
     }
     m->tp_connected = true;
+    return SA_OK;
+}
+
+namespace sa {
+namespace {
+constexpr uint32_t QSP_MAGIC = 0x50535133u;   // "3QSP"
+struct QspHandle {                            // the SA_QWEN3_SP_HANDLE_BYTES blob
+    cudaIpcMemHandle_t buf, kc, vc;
+    unsigned char uuid[16];
+    int32_t rank, world, max_seq, hidden, n_layers, hkv;
+    uint32_t magic;
+};
+static_assert(sizeof(QspHandle) <= SA_QWEN3_SP_HANDLE_BYTES, "handle size");
+}  // namespace
+}  // namespace sa
+
+SA_API int sa_qwen3_create_sp(sa_ctx* ctx, const sa_qwen3_config* cfg, int rank, int world, sa_qwen3** out) {
+    clear_error();
+    SA_CHECK_ARG(ctx && cfg && out, "sa_qwen3_create_sp: null argument");
+    SA_CHECK_ARG(world >= 1 && world <= TP_MAX && rank >= 0 && rank < world,
+                 "sa_qwen3_create_sp: rank %d of world %d (1..%d)", rank, world, TP_MAX);
+    SA_RC(qwen3_create_model(ctx, cfg, 0, 1, out));
+    sa_qwen3* m = *out;
+    m->sp_rank = rank;
+    m->sp_world = world;
+    if (world == 1) return SA_OK;
+    DeviceGuard guard(ctx->device);
+    cudaDeviceProp prop;
+    m->sp_rows = std::min(cfg->max_seq, 8192);
+    const size_t bytes = 256 + (size_t)m->sp_rows * cfg->hidden * sizeof(float);
+    int rc = SA_OK;
+    if (cudaGetDeviceProperties(&prop, ctx->device) != cudaSuccess) rc = set_error(SA_ERR_CUDA, "device properties");
+    if (!rc) rc = dmalloc(&m->sp_buf, bytes);
+    if (!rc) rc = dalloc(&m->sp_seq, 1);
+    if (!rc) rc = dalloc(&m->sp_cnt, 1);
+    if (!rc && (cudaMemset(m->sp_buf, 0, bytes) != cudaSuccess || cudaMemset(m->sp_seq, 0, 4) != cudaSuccess ||
+                cudaMemset(m->sp_cnt, 0, 4) != cudaSuccess))
+        rc = set_error(SA_ERR_CUDA, "memset");
+    if (rc) {
+        sa_qwen3_destroy(m);
+        *out = nullptr;
+        return rc;
+    }
+    std::memcpy(m->uuid, &prop.uuid, sizeof(m->uuid));
+    m->sp_peer_buf[rank] = m->sp_buf;
+    m->sp_peer_kc[rank] = m->kc;
+    m->sp_peer_vc[rank] = m->vc;
+    return SA_OK;
+}
+
+SA_API int sa_qwen3_sp_handle(sa_qwen3* m, void* handle) {
+    clear_error();
+    SA_CHECK_ARG(m && handle, "sa_qwen3_sp_handle: null argument");
+    SA_CHECK_ARG(m->sp_world > 1, "sa_qwen3_sp_handle: not a sequence-parallel model (world 1)");
+    DeviceGuard guard(m->device);
+    QspHandle h;
+    std::memset(&h, 0, sizeof(h));
+    SA_CUDA_TRY(cudaIpcGetMemHandle(&h.buf, m->sp_buf));
+    SA_CUDA_TRY(cudaIpcGetMemHandle(&h.kc, m->kc));
+    SA_CUDA_TRY(cudaIpcGetMemHandle(&h.vc, m->vc));
+    std::memcpy(h.uuid, m->uuid, sizeof(h.uuid));
+    h.rank = m->sp_rank;
+    h.world = m->sp_world;
+    h.max_seq = m->c.max_seq;
+    h.hidden = m->c.hidden;
+    h.n_layers = m->c.n_layers;
+    h.hkv = m->c.hkv;
+    h.magic = QSP_MAGIC;
+    std::memset(handle, 0, SA_QWEN3_SP_HANDLE_BYTES);
+    std::memcpy(handle, &h, sizeof(h));
+    return SA_OK;
+}
+
+SA_API int sa_qwen3_sp_connect(sa_qwen3* m, const void* handles) {
+    clear_error();
+    SA_CHECK_ARG(m && handles, "sa_qwen3_sp_connect: null argument");
+    SA_CHECK_ARG(m->sp_world > 1, "sa_qwen3_sp_connect: not a sequence-parallel model (world 1)");
+    SA_CHECK_ARG(!m->sp_connected, "sa_qwen3_sp_connect: already connected");
+    DeviceGuard guard(m->device);
+    const unsigned char* hb = static_cast<const unsigned char*>(handles);
+    auto fail = [&](int code, const char* fmt, int r, const char* what) {
+        for (int q = 0; q < TP_MAX; ++q) {
+            if (q == m->sp_rank) continue;
+            if (m->sp_peer_buf[q]) cudaIpcCloseMemHandle(m->sp_peer_buf[q]);
+            if (m->sp_peer_kc[q]) cudaIpcCloseMemHandle(m->sp_peer_kc[q]);
+            if (m->sp_peer_vc[q]) cudaIpcCloseMemHandle(m->sp_peer_vc[q]);
+            m->sp_peer_buf[q] = nullptr;
+            m->sp_peer_kc[q] = m->sp_peer_vc[q] = nullptr;
+        }
+        return set_error(code, fmt, r, what);
+    };
+    for (int r = 0; r < m->sp_world; ++r) {
+        QspHandle h;
+        std::memcpy(&h, hb + (size_t)r * SA_QWEN3_SP_HANDLE_BYTES, sizeof(h));
+        if (h.magic != QSP_MAGIC) return fail(SA_ERR_ARG, "sa_qwen3_sp_connect: handle %d %s", r, "is not a model handle");
+        if (h.rank != r || h.world != m->sp_world || h.max_seq != m->c.max_seq || h.hidden != m->c.hidden ||
+            h.n_layers != m->c.n_layers || h.hkv != m->c.hkv)
+            return fail(SA_ERR_ARG, "sa_qwen3_sp_connect: handle %d %s", r,
+                        "names another rank, world size or model shape");
+        if (r == m->sp_rank) continue;
+        if (std::memcmp(h.uuid, m->uuid, sizeof(h.uuid)) == 0)
+            return fail(SA_ERR_ARG, "sa_qwen3_sp_connect: handle %d %s", r,
+                        "is on this rank's GPU (the ranks wait for one another: one GPU per rank)");
+        void *pb = nullptr, *pk = nullptr, *pv = nullptr;
+        if (cudaIpcOpenMemHandle(&pb, h.buf, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess ||
+            cudaIpcOpenMemHandle(&pk, h.kc, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess ||
+            cudaIpcOpenMemHandle(&pv, h.vc, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            const cudaError_t e = cudaGetLastError();
+            if (pb) cudaIpcCloseMemHandle(pb);
+            if (pk) cudaIpcCloseMemHandle(pk);
+            return fail(SA_ERR_CUDA, "sa_qwen3_sp_connect: opening rank %d's buffers failed: %s", r,
+                        cudaGetErrorString(e));
+        }
+        m->sp_peer_buf[r] = pb;
+        m->sp_peer_kc[r] = static_cast<float*>(pk);
+        m->sp_peer_vc[r] = static_cast<float*>(pv);
+    }
+    m->sp_connected = true;
     return SA_OK;
 }
 
@@ -840,6 +1053,9 @@ SA_API int sa_qwen3_forward(sa_qwen3* m, const int64_t* ids, int S, int use_cach
     SA_CHECK_ARG(m->tp_world == 1 || m->tp_connected, "sa_qwen3_forward: head-parallel ranks not connected");
     SA_CHECK_ARG(m->tp_world == 1 || S <= m->tp_rows, "sa_qwen3_forward: S = %d > %d rows per head-parallel forward",
                  S, m->tp_rows);
+    SA_CHECK_ARG(m->sp_world == 1 || m->sp_connected, "sa_qwen3_forward: sequence-parallel ranks not connected");
+    SA_CHECK_ARG(!sp_split(m, S) || S <= m->sp_rows,
+                 "sa_qwen3_forward: S = %d > %d rows per sequence-parallel forward", S, m->sp_rows);
     DeviceGuard guard(m->ctx->device);
     m->cur = m->ctx->stream;
     const int pos0 = use_cache ? m->cache_len : 0;
@@ -856,9 +1072,18 @@ SA_API int sa_qwen3_forward(sa_qwen3* m, const int64_t* ids, int S, int use_cach
     const int r0 = logits_mode == 1 ? S - 1 : 0, n = logits_mode == 1 ? 1 : S;
     if (logits_mode != 2) SA_RC(ensure_logits(m, n));
     const cudaMemcpyKind in_kind = host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+    const bool sp = sp_split(m, S);
+    int s0 = 0, s1 = S;
+    if (sp) sp_share(m, S, &s0, &s1);
     int rc = on_own_stream(m, [&]() -> int {
-        SA_CUDA_TRY(cudaMemcpyAsync(m->ids, ids, (size_t)S * 8, in_kind, m->own));
+        SA_CUDA_TRY(cudaMemcpyAsync(m->ids, ids + s0, (size_t)(s1 - s0) * 8, in_kind, m->own));
         auto body = [&]() -> int {
+            if (sp) {
+                const float* xa = nullptr;
+                SA_RC(run_prompt_sp(m, S, pos0, kv_row0, &xa));
+                if (logits_mode != 2) SA_RC(run_head(m, r0, n, nullptr, xa));
+                return SA_OK;
+            }
             SA_RC(run_layers(m, S, pos0, nullptr, kv_row0));
             if (logits_mode != 2) SA_RC(run_head(m, r0, n));
             return tp_close_segment(m);
@@ -960,6 +1185,9 @@ SA_API int sa_qwen3_generate(sa_qwen3* m, const int64_t* prompt, int S, int n_ne
     SA_CHECK_ARG(m->tp_world == 1 || m->tp_connected, "sa_qwen3_generate: head-parallel ranks not connected");
     SA_CHECK_ARG(m->tp_world == 1 || S <= m->tp_rows, "sa_qwen3_generate: S = %d > %d prompt rows (head-parallel)",
                  S, m->tp_rows);
+    SA_CHECK_ARG(m->sp_world == 1 || m->sp_connected, "sa_qwen3_generate: sequence-parallel ranks not connected");
+    SA_CHECK_ARG(!sp_split(m, S) || S <= m->sp_rows, "sa_qwen3_generate: S = %d > %d prompt rows (sequence-parallel)",
+                 S, m->sp_rows);
     DeviceGuard guard(m->ctx->device);
     m->cur = m->ctx->stream;
     if (m->cache_len + S + n_new > m->c.max_seq + 1)
@@ -975,14 +1203,23 @@ SA_API int sa_qwen3_generate(sa_qwen3* m, const int64_t* prompt, int S, int n_ne
     const int pos0 = m->cache_len;
     int rc = on_own_stream(m, [&]() -> int {
         cudaStream_t st = m->own;
-        SA_CUDA_TRY(cudaMemcpyAsync(m->ids, prompt, (size_t)S * 8,
+        const bool sp = sp_split(m, S);
+        int s0 = 0, s1 = S;
+        if (sp) sp_share(m, S, &s0, &s1);
+        SA_CUDA_TRY(cudaMemcpyAsync(m->ids, prompt + s0, (size_t)(s1 - s0) * 8,
                                     host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, st));
-        SA_RC(run_layers(m, S, pos0));
+        // the prompt: split over sequence-parallel ranks (their gathered
+        // residual rows then feed the head on every rank), else whole
+        const float* xa = nullptr;
+        if (sp)
+            SA_RC(run_prompt_sp(m, S, pos0, pos0, &xa));
+        else
+            SA_RC(run_layers(m, S, pos0));
         if (n_new == 0) {
-            SA_RC(run_head(m, S - 1, 1));
-            return tp_close_segment(m);
+            SA_RC(run_head(m, S - 1, 1, nullptr, xa));
+            return sp ? SA_OK : tp_close_segment(m);
         }
-        SA_RC(run_head(m, S - 1, 1, m->ids));
+        SA_RC(run_head(m, S - 1, 1, m->ids, xa));
         const int state[2] = {pos0 + S, 0};
         SA_CUDA_TRY(cudaMemcpyAsync(m->d_state, state, sizeof(state), cudaMemcpyHostToDevice, st));
         SA_RC(launch_advance(st, m->d_state, m->ids, m->d_toks, m->toks_cap, 0, false));   // first new token

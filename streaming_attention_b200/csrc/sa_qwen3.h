@@ -122,6 +122,22 @@ int launch_rmsnorm_hilo_tp(cudaStream_t st, float* x, const float* w, int M, int
 // then *seq += seg (the segment's instances).
 int launch_tp_amax_token(cudaStream_t st, unsigned long long* amax, int64_t* tok, const TpArgs& tp, int seg);
 int launch_tp_seq_add(cudaStream_t st, unsigned* seq, int n);
+// Sequence-parallel prompt: up to two regions of nblk blocks of blk_floats
+// floats (stride floats apart) that this rank produced, copied to the same
+// offsets (plus slot * slot_floats) in every other rank's copy of the region,
+// then the instance published on every rank (the flags and sequence word of
+// a TpArgs); and the matching bounded wait for every rank's publication.
+struct SpCopy {
+    int nreg = 0;
+    const float* src[2] = {};
+    float* dst[2][TP_MAX] = {};
+    long long slot_floats = 0;
+    int nblk = 0;
+    long long blk_floats = 0;
+    long long stride = 0;
+};
+int launch_sp_rows_scatter(cudaStream_t st, const SpCopy& c, const TpArgs& tp, int grid);
+int launch_sp_wait(cudaStream_t st, const TpArgs& tp);
 // Model allocation for rank `rank` of `world` (sa_qwen3.cu).
 int qwen3_create_model(sa_ctx* ctx, const sa_qwen3_config* cfg, int rank, int world, sa_qwen3** out);
 int launch_amax_to_token(cudaStream_t st, unsigned long long* amax, int64_t* tok);

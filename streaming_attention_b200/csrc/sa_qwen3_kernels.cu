@@ -708,6 +708,46 @@ __global__ void tp_amax_token_kernel(unsigned long long* amax, int64_t* tok, con
     }
 }
 
+// ---- sequence-parallel prompt: row exchange --------------------------------
+// Blocks of rows this rank produced (one layer's K and V cache rows of its
+// tokens; the final residual rows) are copied to the same place in every
+// other rank's memory (CUDA IPC mappings), then the instance is published on
+// every rank as in tp_scatter_kernel.
+__global__ void sp_rows_scatter_kernel(const SpCopy c, const TpArgs tp) {
+    pdl_trigger();
+    pdl_wait();
+    int slot;
+    unsigned epoch;
+    tp_instance(tp, slot, epoch);
+    const long long per4 = c.blk_floats / 4;
+    const long long n4 = (long long)c.nreg * c.nblk * per4;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+        const int reg = (int)(i / ((long long)c.nblk * per4));
+        const long long rem = i - (long long)reg * c.nblk * per4;
+        const long long b = rem / per4, e = rem - b * per4;
+        const long long off = b * c.stride + e * 4;
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(c.src[reg] + off));
+        for (int r = 0; r < tp.world; ++r)
+            if (c.dst[reg][r])   // null: this rank's own copy, already in place
+                *reinterpret_cast<float4*>(c.dst[reg][r] + (long long)slot * c.slot_floats + off) = v;
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < 32) tp_arrive_publish(tp, slot, epoch, threadIdx.x);
+}
+
+// Wait (bounded) until every rank published this instance.
+__global__ void sp_wait_kernel(const TpArgs tp) {
+    pdl_trigger();
+    pdl_wait();
+    if ((int)threadIdx.x < tp.world) {
+        int slot;
+        unsigned epoch;
+        tp_instance(tp, slot, epoch);
+        tp_wait(tp, slot, epoch, threadIdx.x);
+    }
+}
+
 __global__ void tp_seq_add_kernel(unsigned* seq, int n) {
     pdl_trigger();
     pdl_wait();
@@ -879,6 +919,21 @@ int launch_rmsnorm_hilo_tp(cudaStream_t st, float* x, const float* w, int M, int
 int launch_tp_amax_token(cudaStream_t st, unsigned long long* amax, int64_t* tok, const TpArgs& tp, int seg) {
     SA_CHECK_ARG(tp.world > 1 && tp.seq && tp.status, "tp_amax_token: exchange operands missing");
     SA_CUDA_TRY(launch_pdl_k(3, qk::tp_amax_token_kernel, dim3(1), dim3(32), 0, st, amax, tok, tp, seg));
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
+int launch_sp_rows_scatter(cudaStream_t st, const SpCopy& c, const TpArgs& tp, int grid) {
+    SA_CHECK_ARG(tp.world > 1 && tp.seq && tp.cnt && c.nreg >= 1 && c.nreg <= 2 && c.blk_floats % 4 == 0 &&
+                     c.stride % 4 == 0 && c.slot_floats % 4 == 0,
+                 "sp_rows_scatter: regions %d, block %lld, stride %lld", c.nreg, c.blk_floats, c.stride);
+    if (c.nblk == 0 || c.blk_floats == 0) grid = 1;     // nothing to copy: publish only
+    qk::sp_rows_scatter_kernel<<<grid, 256, 0, st>>>(c, tp);
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
+int launch_sp_wait(cudaStream_t st, const TpArgs& tp) {
+    SA_CHECK_ARG(tp.world > 1 && tp.world <= 32 && tp.seq && tp.status, "sp_wait: world %d", tp.world);
+    qk::sp_wait_kernel<<<1, 32, 0, st>>>(tp);
     SA_CUDA_TRY(cudaGetLastError());
     return SA_OK;
 }

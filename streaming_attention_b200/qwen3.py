@@ -64,14 +64,17 @@ def inspect_safetensors(path: str) -> dict:
 
 
 SA_TP_HANDLE_BYTES = 64
+SA_QWEN3_SP_HANDLE_BYTES = 256
 
 
 class Qwen3:
-    """One Qwen3 model on one GPU, or (rank, world) of a head-parallel model
-    over `world` GPUs (sa_qwen3_create_tp): every rank is given the same full
-    weights and keeps its share; after ``connect`` every rank calls
-    ``forward`` / ``generate`` with the same arguments and gets the same
-    results."""
+    """One Qwen3 model on one GPU, or (rank, world) of a model over `world`
+    GPUs: ``strategy="head"`` is head-parallel (sa_qwen3_create_tp: every rank
+    keeps its share of the heads and MLP features), ``strategy="sequence"``
+    sequence-parallel (sa_qwen3_create_sp: every rank holds the whole model,
+    prompts are split over the ranks by tokens).  Every rank is given the
+    same full weights; after ``connect`` every rank calls ``forward`` /
+    ``generate`` with the same arguments and gets the same results."""
 
     @classmethod
     def from_safetensors(cls, path: str, max_seq: int = 4096, ctx: Context | None = None,
@@ -94,16 +97,21 @@ class Qwen3:
         self.max_seq = max_seq
         return self
 
-    def __init__(self, cfg: dict, max_seq: int = 4096, ctx: Context | None = None, rank: int = 0, world: int = 1):
+    def __init__(self, cfg: dict, max_seq: int = 4096, ctx: Context | None = None, rank: int = 0, world: int = 1,
+                 strategy: str = "head"):
+        if strategy not in ("head", "sequence"):
+            raise ValueError(f"strategy {strategy!r}: 'head' or 'sequence'")
         self.cfg = dict(cfg)
         self.ctx = ctx or default_context(0)
-        self.rank, self.world = rank, world
+        self.rank, self.world, self.strategy = rank, world, strategy
         c = Qwen3Config(vocab=cfg["vocab"], hidden=cfg["hidden"], n_layers=cfg["n_layers"],
                         hq=cfg["hq"], hkv=cfg["hkv"], head_dim=cfg["head_dim"], inter=cfg["inter"],
                         eps=cfg.get("eps", 1e-6), theta=cfg.get("theta", 1e6), max_seq=max_seq)
         h = C.c_void_p()
         if world == 1:
             check(lib().sa_qwen3_create(self.ctx.h, C.byref(c), C.byref(h)))
+        elif strategy == "sequence":
+            check(lib().sa_qwen3_create_sp(self.ctx.h, C.byref(c), rank, world, C.byref(h)))
         else:
             check(lib().sa_qwen3_create_tp(self.ctx.h, C.byref(c), rank, world, C.byref(h)))
         self.h = h
@@ -122,13 +130,30 @@ class Qwen3:
         blob = b"".join(handles)
         check(lib().sa_qwen3_tp_connect(self.h, C.create_string_buffer(blob, len(blob))))
 
+    # -- sequence-parallel ranks --------------------------------------------
+    def sp_handle(self) -> bytes:
+        """This rank's row-buffer and K/V-cache handles (sa_qwen3_sp_handle)."""
+        buf = C.create_string_buffer(SA_QWEN3_SP_HANDLE_BYTES)
+        check(lib().sa_qwen3_sp_handle(self.h, buf))
+        return buf.raw
+
+    def sp_connect(self, handles) -> None:
+        """Map the other ranks' buffers and caches: `handles` in rank order."""
+        assert len(handles) == self.world and all(len(x) == SA_QWEN3_SP_HANDLE_BYTES for x in handles)
+        blob = b"".join(handles)
+        check(lib().sa_qwen3_sp_connect(self.h, C.create_string_buffer(blob, len(blob))))
+
     def connect(self, group=None) -> None:
         """Exchange handles over a torch.distributed group (one rank per
         process, ranks in group order) and connect."""
         import torch.distributed as dist
+        mine = self.sp_handle() if getattr(self, "strategy", "head") == "sequence" else self.tp_handle()
         handles = [None] * self.world
-        dist.all_gather_object(handles, self.tp_handle(), group=group)
-        self.tp_connect(handles)
+        dist.all_gather_object(handles, mine, group=group)
+        if getattr(self, "strategy", "head") == "sequence":
+            self.sp_connect(handles)
+        else:
+            self.tp_connect(handles)
 
     def close(self):
         if getattr(self, "h", None):
