@@ -561,7 +561,7 @@ def run_ours(args):
                 "ms": round(pms, 4), "frac_of_bf16_peak": round(ptf / bpk, 4),
                 "peak": f"{bpk} ({bkind} bf16_tflops)", "workload": PF_WORKLOAD}}
             try:
-                q3, weights = measure_qwen3(ctx, dev, stream, 20, 3)
+                q3, weights = measure_qwen3(ctx, dev, stream, 20, 3, long_prompt=True)
                 q3line = {"metric": "Qwen3-0.6B tok/s", "workload": Q3_WORKLOAD,
                           **{k_: round(v_, 4) for k_, v_ in q3.items()}}
                 q3line["roofline"] = qwen3_roofline(q3)
@@ -806,7 +806,8 @@ Q3_WORKLOAD = ("configs[3]/[4] Qwen3-0.6B random-init (bf16-exact N(0,0.02) weig
                "decode of 100 greedy tokens after a 128-token prompt with the KV cache")
 
 
-def measure_qwen3(ctx, dev, stream, steps, warmup, weights=None, long_prompt=False, rank=0, world=1):
+def measure_qwen3(ctx, dev, stream, steps, warmup, weights=None, long_prompt=False, rank=0, world=1,
+                  strategy="head"):
     """Returns dict with prefill / decode tok/s (device-resident and e2e).
     With world > 1 every rank runs its head-parallel share (sa_qwen3_create_tp)
     of the same calls; each timed region starts after a barrier and its time
@@ -819,7 +820,7 @@ def measure_qwen3(ctx, dev, stream, steps, warmup, weights=None, long_prompt=Fal
     if weights is None:
         weights = sa.qwen3.random_weights(cfg, SEED)
     max_seq = 4096 + Q3_GEN + 8 if long_prompt else 512
-    m = sa.Qwen3(cfg, max_seq=max_seq, ctx=ctx, rank=rank, world=world)
+    m = sa.Qwen3(cfg, max_seq=max_seq, ctx=ctx, rank=rank, world=world, strategy=strategy)
     m.load(weights)
 
     def sync():
@@ -878,6 +879,25 @@ def measure_qwen3(ctx, dev, stream, steps, warmup, weights=None, long_prompt=Fal
         for _ in range(ne):
             pf_host()
         out["prefill_e2e_tok_s"] = Q3_PROMPT * ne / tmax(time.perf_counter() - t0)
+        if long_prompt:
+            # configs[4]'s second run: the 4096-token prompt (cache-free, last-token logits)
+            ids_l = torch.from_numpy(rng.integers(0, cfg["vocab"], 4096).astype("int64")).to(dev)
+            last_d = torch.empty(1, cfg["vocab"], device=dev)
+            def pf_long():
+                _capi.check(L.sa_qwen3_forward(m.h, C.cast(P(ids_l), C.POINTER(C.c_int64)), 4096, 0,
+                                               C.cast(P(last_d), C.POINTER(C.c_float)), 1, 0))
+            for _ in range(2):
+                pf_long()
+            stream.synchronize()
+            sync()
+            e0.record(stream)
+            for _ in range(3):
+                pf_long()
+            e1.record(stream)
+            e1.synchronize()
+            lms = tmax(e0.elapsed_time(e1) / 3)
+            out["prefill_4096_ms"] = lms
+            out["prefill_4096_tok_s"] = 4096 / (lms / 1e3)
         # ---- decode: generate(101) - generate(1) = 100 decode steps (same prefill)
         def gen(n, prompt):
             m.reset()
@@ -928,6 +948,14 @@ def qwen3_roofline(res: dict) -> dict:
         t = res["prefill_ms"] / 1e3
         out["prefill"] = {"bytes": wbytes, "flops": flops, "ms": round(res["prefill_ms"], 4),
                           "achieved": round(wbytes / t / 1e9, 1), "frac": round(wbytes / t / 1e9 / peak, 4)}
+    if "prefill_4096_ms" in res:
+        # 4096 tokens: compute-bound (2 FLOP per weight per token + causal attention)
+        f4 = qwen3_bytes_flops(4096)[1]
+        tpk, tkind = load_bf16_peak()
+        tf = f4 / (res["prefill_4096_ms"] / 1e3) / 1e12
+        out["prefill_4096"] = {"bound": "tensor", "flops": f4, "ms": round(res["prefill_4096_ms"], 3),
+                               "achieved_tflops": round(tf, 1), "peak_tflops": tpk,
+                               "frac": round(tf / tpk, 4), "peak_kind": f"{tkind} bf16_tflops (burst)"}
     for key, ctx0 in (("decode", Q3_PROMPT), ("decode_4096", 4096)):
         ms = res.get(f"{key}_ms_per_token")
         if ms:
@@ -1025,7 +1053,7 @@ def run_qwen3(args):
     clocks = ClockSampler(vis.split(",")[local].strip() if vis else str(local))
     clocks.start()
     res, weights = measure_qwen3(ctx, dev, stream, args.steps, args.warmup, long_prompt=args.long_prompt,
-                                 rank=rank, world=world)
+                                 rank=rank, world=world, strategy=args.strategy)
     clk = clocks.stop()
     if rank != 0:
         ctx.close()
@@ -1040,7 +1068,9 @@ def run_qwen3(args):
         "scaling": "weak" if world == 1 else "strong",
         "vs_baseline": None, "dtype": "bf16 weights, fp32 activations", "data": "synthetic",
         "config": {"workload": Q3_WORKLOAD,
-                   "parallelism": "single" if world == 1 else f"head-parallel over {world} GPUs"},
+                   "parallelism": "single" if world == 1 else
+                   (f"head-parallel over {world} GPUs" if args.strategy == "head" else
+                    f"sequence-parallel over {world} GPUs (prompt tokens split, decode replicated)")},
         "decode": {k: round(v, 3) for k, v in res.items() if k.startswith("decode")},
         "e2e": {"value": round(res["prefill_e2e_tok_s"], 1), "unit": "tok/s",
                 "h2d_bytes_per_step": Q3_PROMPT * 8, "d2h_bytes_per_step": Q3_PROMPT * 151936 * 4},
@@ -1080,6 +1110,8 @@ def main():
                          "prefill on tensor cores (TFLOP/s)")
     ap.add_argument("--profile", action="store_true",
                     help="only W warm-up + K device steps (a short launch sequence for ncu)")
+    ap.add_argument("--strategy", choices=["head", "sequence"], default="head",
+                    help="qwen3 workload on N > 1 GPUs: head-parallel or sequence-parallel")
     ap.add_argument("--cpu-budget", type=float, default=10.0,
                     help="seconds of CPU work for the cpu_baseline sample")
     args = ap.parse_args()
