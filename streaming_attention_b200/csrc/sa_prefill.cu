@@ -53,6 +53,7 @@
 #include <cmath>
 
 #include "sa_internal.h"
+#include "sa_qwen3.h"
 #include "sa_tc.cuh"
 
 namespace sa {
@@ -479,9 +480,9 @@ prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
 //   q   [Sq,  q_tok stride,  hq heads of 128]   bf16
 //   k,v [Skv, kv_tok stride, hkv heads of 128]  bf16
 //   out [Sq,  o_tok stride,  hq heads of 128]   fp32 or bf16
-static int launch_prefill(sa_ctx* ctx, const void* q, const void* k, const void* v, void* out, int out_dtype,
-                          int Sq, int Skv, int q_pos0, int hq, int hkv, long long q_tok, long long kv_tok,
-                          long long o_tok, float scale) {
+int prefill_launch(cudaStream_t st, int* status, const void* q, const void* k, const void* v, void* out,
+                   int out_dtype, int Sq, int Skv, int q_pos0, int hq, int hkv, long long q_tok, long long kv_tok,
+                   long long o_tok, float scale) {
     CUtensorMap mq, mk, mv;
     int rc = make_tmap_2d_bf16(&mq, q, (uint64_t)Sq, (uint64_t)hq * pf::D, (uint64_t)q_tok, pf::BM, 64);
     if (!rc) rc = make_tmap_2d_bf16(&mk, k, (uint64_t)Skv, (uint64_t)hkv * pf::D, (uint64_t)kv_tok, pf::BN, 64);
@@ -496,16 +497,23 @@ static int launch_prefill(sa_ctx* ctx, const void* q, const void* k, const void*
     a.sl2 = scale * pf::LOG2E;
     a.out = out; a.o_tok = o_tok; a.o_head = pf::D;
     a.out_bf16 = out_dtype == SA_BF16;
-    a.status = ctx->status;
+    a.status = status;
     // All exponentials on the SFU: with 128-key tiles the softmax is issue-bound,
     // and moving every 8th/4th/3rd exponential to exp2_poly measured 3%/5%/9%
     // slower on config 3 (S=8192, 16/8 heads).
     auto kern = pf::prefill_kernel<0>;
     SA_RC_TRY(set_smem_attr_once((const void*)kern, pf::SMEM_BYTES));
     const int grid = rows * a.units_per_row;
-    kern<<<grid, pf::THREADS, pf::SMEM_BYTES, ctx->stream>>>(mq, mk, mv, a);
+    kern<<<grid, pf::THREADS, pf::SMEM_BYTES, st>>>(mq, mk, mv, a);
     SA_CUDA_TRY(cudaGetLastError());
     return SA_OK;
+}
+
+static int launch_prefill(sa_ctx* ctx, const void* q, const void* k, const void* v, void* out, int out_dtype,
+                          int Sq, int Skv, int q_pos0, int hq, int hkv, long long q_tok, long long kv_tok,
+                          long long o_tok, float scale) {
+    return prefill_launch(ctx->stream, ctx->status, q, k, v, out, out_dtype, Sq, Skv, q_pos0, hq, hkv, q_tok,
+                          kv_tok, o_tok, scale);
 }
 
 }  // namespace sa

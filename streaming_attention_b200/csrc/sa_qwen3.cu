@@ -121,6 +121,12 @@ struct sa_qwen3 {
     unsigned* sp_seq = nullptr;          // [1] exchange instances completed
     unsigned* sp_cnt = nullptr;          // [1] producer arrival counter
     unsigned char uuid[16] = {};         // the GPU's UUID (ranks must be on different GPUs)
+    // long prompts' tensor-core attention: bf16 q [tc_cap, QD] and token-major
+    // K / V [max_seq, KD] operands (allocated on first use)
+    __nv_bfloat16* tc_q = nullptr;
+    __nv_bfloat16* tc_k = nullptr;
+    __nv_bfloat16* tc_v = nullptr;
+    int tc_cap = 0;
 };
 
 namespace sa {
@@ -175,6 +181,7 @@ static void free_model(sa_qwen3* m) {
         if (m->sp_peer_vc[r]) cudaIpcCloseMemHandle(m->sp_peer_vc[r]);
     }
     cudaFree(m->sp_buf); cudaFree(m->sp_seq); cudaFree(m->sp_cnt);
+    cudaFree(m->tc_q); cudaFree(m->tc_k); cudaFree(m->tc_v);
     if (m->dec_graph) cudaGraphExecDestroy(m->dec_graph);
     for (auto& kv : m->pf_graphs) cudaGraphExecDestroy(kv.second);
     if (m->ev_in) cudaEventDestroy(m->ev_in);
@@ -259,6 +266,36 @@ static int gemm(sa_qwen3* m, const __nv_bfloat16* hi, const __nv_bfloat16* lo, l
 }
 
 #define SA_RC(expr) do { int rc_ = (expr); if (rc_) return rc_; } while (0)
+
+// Prompts of at least this many tokens run their attention on the tcgen05
+// tensor cores (bf16 q / K / V, fp32 accumulation, sa_prefill.cu); shorter
+// ones on the fp32 CUDA-core prompt-attention kernel, whose cost grows with
+// the square of the prompt.  SA_QWEN3_TC_ATTN_MIN overrides the crossover.
+static int tc_attn_min_rows() {
+    static const int v = [] {
+        const char* e = std::getenv("SA_QWEN3_TC_ATTN_MIN");
+        return e ? std::atoi(e) : 1024;
+    }();
+    return v;
+}
+
+// The tensor-core attention's operand buffers for M query rows.
+static int ensure_tc(sa_qwen3* m, int M) {
+    if (m->tc_k && M <= m->tc_cap) return SA_OK;
+    SA_CUDA_TRY(cudaStreamSynchronize(m->cur));
+    SA_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    invalidate_graphs(m);
+    cudaFree(m->tc_q);
+    m->tc_q = nullptr;
+    m->tc_cap = 0;
+    if (!m->tc_k) {
+        SA_RC(dalloc(&m->tc_k, (size_t)m->c.max_seq * m->KD));
+        SA_RC(dalloc(&m->tc_v, (size_t)m->c.max_seq * m->KD));
+    }
+    SA_RC(dalloc(&m->tc_q, (size_t)M * m->QD));
+    m->tc_cap = M;
+    return SA_OK;
+}
 
 
 // Tokens ids (device) at positions pos0 .. pos0+M-1 through every layer.
@@ -403,9 +440,20 @@ static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr
                 SA_RC(launch_sp_rows_scatter(st, cp, sp_args(m, l), m->ctx->num_sms));
                 SA_RC(launch_sp_wait(st, sp_args(m, l)));
             }
-            SA_RC(prompt_attn_launch(st, m->ctx->status, m->q, m->QD, ka, va, (long long)c.max_seq * D,
-                                     (long long)m->hkv * c.max_seq - shift, pos0 + 1, M, D, m->hq, m->hkv, scale,
-                                     nullptr, m->QD, m->a_hi, m->a_lo));
+            if (M >= tc_attn_min_rows()) {
+                // rows [0, pos0 + M) of the attention view as bf16 operands, the
+                // causal prefill on the tensor cores, its output as hi/lo planes
+                const int T = pos0 + M;
+                SA_RC(launch_tc_pack(st, m->q, M, m->QD, ka, va, c.max_seq, m->hkv, T, m->tc_q, m->tc_k, m->tc_v,
+                                     m->ctx->num_sms));
+                SA_RC(prefill_launch(st, m->ctx->status, m->tc_q, m->tc_k, m->tc_v, m->attn, SA_F32, M, T, pos0,
+                                     m->hq, m->hkv, m->QD, m->KD, m->QD, scale));
+                SA_RC(launch_hilo_split(st, m->attn, (long long)M * m->QD, m->a_hi, m->a_lo, m->ctx->num_sms));
+            } else {
+                SA_RC(prompt_attn_launch(st, m->ctx->status, m->q, m->QD, ka, va, (long long)c.max_seq * D,
+                                         (long long)m->hkv * c.max_seq - shift, pos0 + 1, M, D, m->hq, m->hkv, scale,
+                                         nullptr, m->QD, m->a_hi, m->a_lo));
+            }
             if (tp) {
                 SA_RC(gemm(m, m->a_hi, m->a_lo, m->QD, L.wo, M, H, m->QD, QW_EPI_STORE, m->tp_part, H, nullptr, nullptr,
                            0));
@@ -1069,6 +1117,7 @@ SA_API int sa_qwen3_forward(sa_qwen3* m, const int64_t* ids, int S, int use_cach
             if (ids[s] < 0 || ids[s] >= m->c.vocab)
                 return set_error(SA_ERR_RANGE, "Embedding index out of range: ids[%d] = %lld", s, (long long)ids[s]);
     SA_RC(ensure_acts(m, S));
+    if (S >= tc_attn_min_rows()) SA_RC(ensure_tc(m, S));
     const int r0 = logits_mode == 1 ? S - 1 : 0, n = logits_mode == 1 ? 1 : S;
     if (logits_mode != 2) SA_RC(ensure_logits(m, n));
     const cudaMemcpyKind in_kind = host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
@@ -1199,6 +1248,7 @@ SA_API int sa_qwen3_generate(sa_qwen3* m, const int64_t* prompt, int S, int n_ne
             if (prompt[s] < 0 || prompt[s] >= m->c.vocab)
                 return set_error(SA_ERR_RANGE, "Embedding index out of range: prompt[%d]", s);
     SA_RC(ensure_acts(m, S));
+    if (S >= tc_attn_min_rows()) SA_RC(ensure_tc(m, S));
     SA_RC(ensure_logits(m, 1));
     const int pos0 = m->cache_len;
     int rc = on_own_stream(m, [&]() -> int {

@@ -137,6 +137,18 @@ struct SpCopy {
     long long stride = 0;
 };
 int launch_sp_rows_scatter(cudaStream_t st, const SpCopy& c, const TpArgs& tp, int grid);
+// Long prompts' attention on the tensor cores: q [M, QD] fp32 -> bf16 (same
+// layout), and rows [0, T) of the fp32 head-major K/V cache view (head h at
+// h * max_seq rows) -> bf16 token-major [T, hkv, 128] for K and V; then the
+// tcgen05 causal prefill (sa_prefill.cu); then its fp32 output split into
+// the o_proj GEMM's bf16 hi/lo planes.
+int launch_tc_pack(cudaStream_t st, const float* q, int M, int QD, const float* kc, const float* vc, int max_seq,
+                   int hkv, int T, __nv_bfloat16* qb, __nv_bfloat16* kb, __nv_bfloat16* vb, int num_sms);
+int launch_hilo_split(cudaStream_t st, const float* x, long long n, __nv_bfloat16* hi, __nv_bfloat16* lo,
+                      int num_sms);
+int prefill_launch(cudaStream_t st, int* status, const void* q, const void* k, const void* v, void* out,
+                   int out_dtype, int Sq, int Skv, int q_pos0, int hq, int hkv, long long q_tok, long long kv_tok,
+                   long long o_tok, float scale);
 int launch_sp_wait(cudaStream_t st, const TpArgs& tp);
 // Model allocation for rank `rank` of `world` (sa_qwen3.cu).
 int qwen3_create_model(sa_ctx* ctx, const sa_qwen3_config* cfg, int rank, int world, sa_qwen3** out);

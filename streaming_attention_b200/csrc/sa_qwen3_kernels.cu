@@ -736,6 +736,65 @@ __global__ void sp_rows_scatter_kernel(const SpCopy c, const TpArgs tp) {
     if (threadIdx.x < 32) tp_arrive_publish(tp, slot, epoch, threadIdx.x);
 }
 
+// ---- long prompts: operands of the tensor-core attention --------------------
+__device__ __forceinline__ uint4 pack8_bf16(float4 a, float4 b) {
+    uint4 r;
+    __nv_bfloat162 t;
+    t = __floats2bfloat162_rn(a.x, a.y); r.x = *reinterpret_cast<uint32_t*>(&t);
+    t = __floats2bfloat162_rn(a.z, a.w); r.y = *reinterpret_cast<uint32_t*>(&t);
+    t = __floats2bfloat162_rn(b.x, b.y); r.z = *reinterpret_cast<uint32_t*>(&t);
+    t = __floats2bfloat162_rn(b.z, b.w); r.w = *reinterpret_cast<uint32_t*>(&t);
+    return r;
+}
+
+// Groups of 8 values: [0, nq8) of q (same layout), then K and V rows t of
+// head h (source row h * max_seq + t, destination row t * hkv + h).
+__global__ void tc_pack_kernel(const float* __restrict__ q, long long nq8, const float* __restrict__ kc,
+                               const float* __restrict__ vc, int max_seq, int hkv, int T, __nv_bfloat16* qb,
+                               __nv_bfloat16* kb, __nv_bfloat16* vb) {
+    pdl_trigger();
+    pdl_wait();
+    const long long nkv8 = (long long)T * hkv * 16;
+    const long long n = nq8 + 2 * nkv8;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const float* src;
+        __nv_bfloat16* dst;
+        if (i < nq8) {
+            src = q + i * 8;
+            dst = qb + i * 8;
+        } else {
+            long long j = i - nq8;
+            const bool is_v = j >= nkv8;
+            if (is_v) j -= nkv8;
+            const long long c = j & 15, th = j >> 4;          // 16 groups of 8 per 128-wide row
+            const long long t = th / hkv, h = th - t * hkv;
+            src = (is_v ? vc : kc) + ((size_t)h * max_seq + t) * 128 + c * 8;
+            dst = (is_v ? vb : kb) + ((size_t)t * hkv + h) * 128 + c * 8;
+        }
+        const float4 a = __ldcg(reinterpret_cast<const float4*>(src));
+        const float4 b = __ldcg(reinterpret_cast<const float4*>(src) + 1);
+        *reinterpret_cast<uint4*>(dst) = pack8_bf16(a, b);
+    }
+}
+
+// x = hi + lo with hi = bf16(x), lo = bf16(x - hi), 8 values per step.
+__global__ void hilo_split_kernel(const float* __restrict__ x, long long n8, __nv_bfloat16* hi, __nv_bfloat16* lo) {
+    pdl_trigger();
+    pdl_wait();
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+        const float4 a = __ldcg(reinterpret_cast<const float4*>(x + i * 8));
+        const float4 b = __ldcg(reinterpret_cast<const float4*>(x + i * 8) + 1);
+        const uint4 h = pack8_bf16(a, b);
+        const __nv_bfloat162* hp = reinterpret_cast<const __nv_bfloat162*>(&h);
+        const float2 h0 = __bfloat1622float2(hp[0]), h1 = __bfloat1622float2(hp[1]);
+        const float2 h2 = __bfloat1622float2(hp[2]), h3 = __bfloat1622float2(hp[3]);
+        const float4 la = make_float4(a.x - h0.x, a.y - h0.y, a.z - h1.x, a.w - h1.y);
+        const float4 lb = make_float4(b.x - h2.x, b.y - h2.y, b.z - h3.x, b.w - h3.y);
+        *reinterpret_cast<uint4*>(hi + i * 8) = h;
+        *reinterpret_cast<uint4*>(lo + i * 8) = pack8_bf16(la, lb);
+    }
+}
+
 // Wait (bounded) until every rank published this instance.
 __global__ void sp_wait_kernel(const TpArgs tp) {
     pdl_trigger();
@@ -929,6 +988,19 @@ int launch_sp_rows_scatter(cudaStream_t st, const SpCopy& c, const TpArgs& tp, i
     if (c.nblk == 0 || c.blk_floats == 0) grid = 1;     // nothing to copy: publish only
     qk::sp_rows_scatter_kernel<<<grid, 256, 0, st>>>(c, tp);
     SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
+int launch_tc_pack(cudaStream_t st, const float* q, int M, int QD, const float* kc, const float* vc, int max_seq,
+                   int hkv, int T, __nv_bfloat16* qb, __nv_bfloat16* kb, __nv_bfloat16* vb, int num_sms) {
+    SA_CHECK_ARG(M >= 1 && QD % 8 == 0 && T >= 1 && T <= max_seq && hkv >= 1, "tc_pack: M=%d QD=%d T=%d", M, QD, T);
+    SA_CUDA_TRY(launch_pdl_k(4, qk::tc_pack_kernel, dim3(4 * num_sms), dim3(256), 0, st, q, (long long)M * QD / 8, kc,
+                             vc, max_seq, hkv, T, qb, kb, vb));
+    return SA_OK;
+}
+int launch_hilo_split(cudaStream_t st, const float* x, long long n, __nv_bfloat16* hi, __nv_bfloat16* lo,
+                      int num_sms) {
+    SA_CHECK_ARG(n % 8 == 0, "hilo_split: n=%lld", n);
+    SA_CUDA_TRY(launch_pdl_k(4, qk::hilo_split_kernel, dim3(4 * num_sms), dim3(256), 0, st, x, n / 8, hi, lo));
     return SA_OK;
 }
 int launch_sp_wait(cudaStream_t st, const TpArgs& tp) {
