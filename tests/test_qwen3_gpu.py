@@ -110,6 +110,40 @@ def test_qwen3_long_prompt(ctx, oracle):
     _close(m.forward(ids, logits="all"), oracle.qwen3_forward(cfg, w, ids, all_logits=True), "S=1000")
 
 
+@pytest.mark.parametrize("hq,hkv,S,cached", [(4, 2, 1100, 0), (8, 2, 1300, 200), (4, 4, 2048, 0)])
+def test_qwen3_prompt_tensor_core_attention(ctx, oracle, hq, hkv, S, cached):
+    """Prompts of >= 1024 tokens run their attention on the tcgen05 prefill
+    kernel (bf16 q / K / V, fp32 accumulation): logits of every position
+    within the bar, and greedy tokens after the prompt identical to the
+    oracle's; also a chunk of 1300 - 200 = 1100 tokens after a 200-token
+    cached prefix (the tensor-core attention over prefix + chunk)."""
+    from streaming_attention_b200 import Qwen3
+    cfg = Qwen3Cfg(vocab=700, hidden=256, n_layers=2, hq=hq, hkv=hkv, head_dim=128, inter=512,
+                   eps=1e-6, theta=1e6)
+    w = make_qwen3_weights(cfg, 61)
+    ids = I.rng(S).integers(0, cfg.vocab, S)
+    m = Qwen3(_cfgdict(cfg), max_seq=S + 16, ctx=ctx)
+    m.load(w)
+    ref = oracle.qwen3_forward(cfg, w, ids, all_logits=True)
+    if cached:
+        m.forward(ids[:cached], use_cache=True, logits="none")
+        got = m.forward(ids[cached:], use_cache=True, logits="all")
+        _close(got, ref[cached:], f"S={S} after {cached} cached rows")
+        return
+    _close(m.forward(ids, logits="all"), ref, f"S={S}")
+    toks = m.generate(ids, 6)
+    L, D = cfg.n_layers, cfg.head_dim
+    kc = np.zeros((L, hkv, S + 16, D), np.float32)
+    vc = np.zeros_like(kc)
+    lg = oracle.qwen3_forward(cfg, w, ids, kc, vc, S + 16, 0, all_logits=False)
+    want, pos = [int(np.argmax(lg[0]))], S
+    for _ in range(5):
+        lg = oracle.qwen3_forward(cfg, w, np.array(want[-1:]), kc, vc, S + 16, pos, all_logits=False)
+        pos += 1
+        want.append(int(np.argmax(lg[0])))
+    assert [int(t) for t in toks] == want
+
+
 def test_qwen3_long_prefix_continuation(ctx, oracle):
     """A 40-token prompt continued after 300 cached tokens: its attention runs
     over several 128-row rounds of the cache."""
