@@ -127,6 +127,10 @@ struct sa_qwen3 {
     __nv_bfloat16* tc_k = nullptr;
     __nv_bfloat16* tc_v = nullptr;
     int tc_cap = 0;
+    // single-token steps: a side branch that prefetches the next layer's
+    // weights into L2 while the current layer runs
+    cudaStream_t pf_side = nullptr;
+    cudaEvent_t ev_pf = nullptr, ev_pf_join = nullptr;
 };
 
 namespace sa {
@@ -187,6 +191,9 @@ static void free_model(sa_qwen3* m) {
     if (m->ev_in) cudaEventDestroy(m->ev_in);
     if (m->ev_out) cudaEventDestroy(m->ev_out);
     if (m->own) cudaStreamDestroy(m->own);
+    if (m->pf_side) cudaStreamDestroy(m->pf_side);
+    if (m->ev_pf) cudaEventDestroy(m->ev_pf);
+    if (m->ev_pf_join) cudaEventDestroy(m->ev_pf_join);
 }
 
 // Graphs hold buffer addresses; drop them whenever a buffer is reallocated.
@@ -279,6 +286,16 @@ static int tc_attn_min_rows() {
     return v;
 }
 
+// Single-token steps prefetch each next layer's weights into L2 from a side
+// branch (SA_QWEN3_L2_PREFETCH=0 turns it off).
+static bool l2_prefetch_on() {
+    static const bool v = [] {
+        const char* e = std::getenv("SA_QWEN3_L2_PREFETCH");
+        return !(e && e[0] == '0');
+    }();
+    return v;
+}
+
 // The tensor-core attention's operand buffers for M query rows.
 static int ensure_tc(sa_qwen3* m, int M) {
     if (m->tc_k && M <= m->tc_cap) return SA_OK;
@@ -366,9 +383,30 @@ static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr
     float* xc = m->x;          // single-token path: the residual the next consumer reads
     float* xo = m->tp_x2;
     SA_RC(launch_embedding(st, m->ids, M, m->embed, c.vocab, H, m->x, m->ctx->status));
+    // single-token steps: at the start of layer l a side branch (forked from
+    // the main stream, joined after the last layer) issues L2 prefetches of
+    // layer l + 1's weights (and layer 0's with layer 0), so the dependent
+    // chain of small GEMVs reads them from L2 while HBM streams ahead
+    const bool pf = M == 1 && l2_prefetch_on();
+    auto prefetch_layer = [&](int j) -> int {
+        const sa_qwen3::Layer& P = m->layers[j];
+        L2Prefetch p;
+        p.n = 4;
+        p.ptr[0] = P.wqkv; p.bytes[0] = (unsigned long long)m->NQKV * H * 2;
+        p.ptr[1] = P.wo;   p.bytes[1] = (unsigned long long)H * m->QD * 2;
+        p.ptr[2] = P.wgu;  p.bytes[2] = (unsigned long long)2 * I * H * 2;
+        p.ptr[3] = P.wd;   p.bytes[3] = (unsigned long long)H * I * 2;
+        return launch_l2_prefetch(m->pf_side, p);
+    };
     int resid = 0;   // partial planes of the last down_proj not yet added to x
     for (int l = 0; l < c.n_layers; ++l) {
         const sa_qwen3::Layer& L = m->layers[l];
+        if (pf) {
+            SA_CUDA_TRY(cudaEventRecord(m->ev_pf, st));
+            SA_CUDA_TRY(cudaStreamWaitEvent(m->pf_side, m->ev_pf, 0));
+            if (l == 0) SA_RC(prefetch_layer(0));
+            if (l + 1 < c.n_layers) SA_RC(prefetch_layer(l + 1));
+        }
         float* kc = m->kc + l * layer_kv;
         float* vc = m->vc + l * layer_kv;
         const int shift = kv_row0 - pos0;                     // cache row - RoPE position
@@ -481,6 +519,10 @@ static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr
         }
     }
     if (resid) SA_RC(launch_resid_add(st, m->x, m->gemm_ws, resid, M, H, m->ctx->num_sms));
+    if (pf) {
+        SA_CUDA_TRY(cudaEventRecord(m->ev_pf_join, m->pf_side));
+        SA_CUDA_TRY(cudaStreamWaitEvent(st, m->ev_pf_join, 0));
+    }
     m->x_last = M == 1 ? xc : m->x;
     m->x_last_ll = M == 1;
     return SA_OK;
@@ -638,8 +680,12 @@ int qwen3_create_model(sa_ctx* ctx, const sa_qwen3_config* cfg, int rank, int wo
     if (!rc && cudaStreamCreateWithFlags(&m->own, cudaStreamNonBlocking) != cudaSuccess)
         rc = set_error(SA_ERR_CUDA, "stream create");
     if (!rc && (cudaEventCreateWithFlags(&m->ev_in, cudaEventDisableTiming) != cudaSuccess ||
-                cudaEventCreateWithFlags(&m->ev_out, cudaEventDisableTiming) != cudaSuccess))
+                cudaEventCreateWithFlags(&m->ev_out, cudaEventDisableTiming) != cudaSuccess ||
+                cudaEventCreateWithFlags(&m->ev_pf, cudaEventDisableTiming) != cudaSuccess ||
+                cudaEventCreateWithFlags(&m->ev_pf_join, cudaEventDisableTiming) != cudaSuccess))
         rc = set_error(SA_ERR_CUDA, "event create");
+    if (!rc && cudaStreamCreateWithFlags(&m->pf_side, cudaStreamNonBlocking) != cudaSuccess)
+        rc = set_error(SA_ERR_CUDA, "stream create");
     m->toks_cap = c.max_seq + 1;
     if (!rc) rc = dalloc(&m->d_state, 2);
     if (!rc) rc = dalloc(&m->d_toks, (size_t)m->toks_cap);

@@ -150,6 +150,15 @@ int prefill_launch(cudaStream_t st, int* status, const void* q, const void* k, c
                    int out_dtype, int Sq, int Skv, int q_pos0, int hq, int hkv, long long q_tok, long long kv_tok,
                    long long o_tok, float scale);
 int launch_sp_wait(cudaStream_t st, const TpArgs& tp);
+// L2 prefetch of one decode layer's weights: `n` regions (pointer, bytes;
+// 16-byte aligned, multiples of 16), issued by the TMA engine; the kernel
+// does not wait for the data.
+struct L2Prefetch {
+    int n = 0;
+    const void* ptr[4] = {};
+    unsigned long long bytes[4] = {};
+};
+int launch_l2_prefetch(cudaStream_t st, const L2Prefetch& p);
 // Model allocation for rank `rank` of `world` (sa_qwen3.cu).
 int qwen3_create_model(sa_ctx* ctx, const sa_qwen3_config* cfg, int rank, int world, sa_qwen3** out);
 int launch_amax_to_token(cudaStream_t st, unsigned long long* amax, int64_t* tok);

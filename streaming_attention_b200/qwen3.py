@@ -130,6 +130,14 @@ class Qwen3:
         blob = b"".join(handles)
         check(lib().sa_qwen3_tp_connect(self.h, C.create_string_buffer(blob, len(blob))))
 
+    @property
+    def local_kv_heads(self) -> int:
+        """KV heads this rank's cache holds: its share under the head-parallel
+        strategy, all of them otherwise."""
+        if self.world > 1 and getattr(self, "strategy", "head") == "head":
+            return self.cfg["hkv"] // self.world
+        return self.cfg["hkv"]
+
     # -- sequence-parallel ranks --------------------------------------------
     def sp_handle(self) -> bytes:
         """This rank's row-buffer and K/V-cache handles (sa_qwen3_sp_handle)."""
@@ -199,7 +207,7 @@ class Qwen3:
         (rows past cache_len are zero), the layout of KVCache's layer tensors."""
         L = self.cache_len
         stride = L if seq_stride is None else seq_stride
-        shape = (self.cfg["hkv"] // self.world, stride, self.cfg["head_dim"])
+        shape = (self.local_kv_heads, stride, self.cfg["head_dim"])
         k, v = np.zeros(shape, np.float32), np.zeros(shape, np.float32)
         check(lib().sa_qwen3_read_kv(self.h, layer, k.ctypes.data, v.ctypes.data, stride))
         return k, v
@@ -208,7 +216,7 @@ class Qwen3:
         """Upload rows 0..len-1 of one layer's cache from float32 [hkv, len, head_dim]."""
         k = np.ascontiguousarray(k, np.float32)
         v = np.ascontiguousarray(v, np.float32)
-        assert k.shape == v.shape and k.shape[0] == self.cfg["hkv"] // self.world and k.shape[2] == self.cfg["head_dim"]
+        assert k.shape == v.shape and k.shape[0] == self.local_kv_heads and k.shape[2] == self.cfg["head_dim"]
         check(lib().sa_qwen3_write_kv(self.h, layer, k.ctypes.data, v.ctypes.data, k.shape[1], k.shape[1]))
 
     def set_cache_len(self, n: int):
