@@ -127,10 +127,6 @@ struct sa_qwen3 {
     __nv_bfloat16* tc_k = nullptr;
     __nv_bfloat16* tc_v = nullptr;
     int tc_cap = 0;
-    // single-token steps: a side branch that prefetches the next layer's
-    // weights into L2 while the current layer runs
-    cudaStream_t pf_side = nullptr;
-    cudaEvent_t ev_pf = nullptr, ev_pf_join = nullptr;
 };
 
 namespace sa {
@@ -191,9 +187,6 @@ static void free_model(sa_qwen3* m) {
     if (m->ev_in) cudaEventDestroy(m->ev_in);
     if (m->ev_out) cudaEventDestroy(m->ev_out);
     if (m->own) cudaStreamDestroy(m->own);
-    if (m->pf_side) cudaStreamDestroy(m->pf_side);
-    if (m->ev_pf) cudaEventDestroy(m->ev_pf);
-    if (m->ev_pf_join) cudaEventDestroy(m->ev_pf_join);
 }
 
 // Graphs hold buffer addresses; drop them whenever a buffer is reallocated.
@@ -281,13 +274,13 @@ static int gemm(sa_qwen3* m, const __nv_bfloat16* hi, const __nv_bfloat16* lo, l
 static int tc_attn_min_rows() {
     static const int v = [] {
         const char* e = std::getenv("SA_QWEN3_TC_ATTN_MIN");
-        return e ? std::atoi(e) : 1024;
+        return e ? std::atoi(e) : 256;
     }();
     return v;
 }
 
-// Single-token steps prefetch each next layer's weights into L2 from a side
-// branch (SA_QWEN3_L2_PREFETCH=0 turns it off).
+// Single-token steps prefetch weights into L2 from the decode attention
+// kernel (SA_QWEN3_L2_PREFETCH=0 turns it off).
 static bool l2_prefetch_on() {
     static const bool v = [] {
         const char* e = std::getenv("SA_QWEN3_L2_PREFETCH");
@@ -383,30 +376,9 @@ static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr
     float* xc = m->x;          // single-token path: the residual the next consumer reads
     float* xo = m->tp_x2;
     SA_RC(launch_embedding(st, m->ids, M, m->embed, c.vocab, H, m->x, m->ctx->status));
-    // single-token steps: at the start of layer l a side branch (forked from
-    // the main stream, joined after the last layer) issues L2 prefetches of
-    // layer l + 1's weights (and layer 0's with layer 0), so the dependent
-    // chain of small GEMVs reads them from L2 while HBM streams ahead
-    const bool pf = M == 1 && l2_prefetch_on();
-    auto prefetch_layer = [&](int j) -> int {
-        const sa_qwen3::Layer& P = m->layers[j];
-        L2Prefetch p;
-        p.n = 4;
-        p.ptr[0] = P.wqkv; p.bytes[0] = (unsigned long long)m->NQKV * H * 2;
-        p.ptr[1] = P.wo;   p.bytes[1] = (unsigned long long)H * m->QD * 2;
-        p.ptr[2] = P.wgu;  p.bytes[2] = (unsigned long long)2 * I * H * 2;
-        p.ptr[3] = P.wd;   p.bytes[3] = (unsigned long long)H * I * 2;
-        return launch_l2_prefetch(m->pf_side, p);
-    };
     int resid = 0;   // partial planes of the last down_proj not yet added to x
     for (int l = 0; l < c.n_layers; ++l) {
         const sa_qwen3::Layer& L = m->layers[l];
-        if (pf) {
-            SA_CUDA_TRY(cudaEventRecord(m->ev_pf, st));
-            SA_CUDA_TRY(cudaStreamWaitEvent(m->pf_side, m->ev_pf, 0));
-            if (l == 0) SA_RC(prefetch_layer(0));
-            if (l + 1 < c.n_layers) SA_RC(prefetch_layer(l + 1));
-        }
         float* kc = m->kc + l * layer_kv;
         float* vc = m->vc + l * layer_kv;
         const int shift = kv_row0 - pos0;                     // cache row - RoPE position
@@ -430,9 +402,28 @@ static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr
                 SA_RC(launch_gemv2(st, QW_EPI_QKV, true, L.wqkv, m->NQKV, H, xc, L.in_norm, c.eps, m->qkv, nullptr,
                                    &e));
             }
+            // the decode attention's CTAs also prefetch into L2 what the
+            // rest of the step reads next: this layer's o_proj, gate/up and
+            // down_proj and the next layer's QKV (the last layer: the first
+            // 16 MB of the lm_head), so that the dependent chain of small
+            // GEMVs reads from L2 while HBM streams ahead of it
+            L2Prefetch pf;
+            if (l2_prefetch_on()) {
+                pf.n = 4;
+                pf.ptr[0] = L.wo;  pf.bytes[0] = (unsigned long long)H * m->QD * 2;
+                pf.ptr[1] = L.wgu; pf.bytes[1] = (unsigned long long)2 * I * H * 2;
+                pf.ptr[2] = L.wd;  pf.bytes[2] = (unsigned long long)H * I * 2;
+                if (l + 1 < c.n_layers) {
+                    pf.ptr[3] = m->layers[l + 1].wqkv;
+                    pf.bytes[3] = (unsigned long long)m->NQKV * H * 2;
+                } else {
+                    pf.ptr[3] = m->lm_head;
+                    pf.bytes[3] = std::min<unsigned long long>(16ull << 20, (unsigned long long)c.vocab * H * 2);
+                }
+            }
             SA_RC(decode_dev_launch(st, m->ctx->status, m->ctx->num_sms, m->q, ka, va, (long long)c.max_seq * D,
                                     pos_dev, pos0 + 1, c.max_seq - shift, D, m->hq, m->hkv, scale, m->attn,
-                                    m->dec_scratch, m->dec_cnt));
+                                    m->dec_scratch, m->dec_cnt, pf.n ? &pf : nullptr));
             if (tp) {
                 SA_RC(launch_gemv2_tp(st, QW_EPI_XCHG, false, L.wo, H, m->QD, m->attn, nullptr, 0.f, nullptr, nullptr,
                                       nullptr, tp_args(m, 2 * l), false));
@@ -519,10 +510,6 @@ static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr
         }
     }
     if (resid) SA_RC(launch_resid_add(st, m->x, m->gemm_ws, resid, M, H, m->ctx->num_sms));
-    if (pf) {
-        SA_CUDA_TRY(cudaEventRecord(m->ev_pf_join, m->pf_side));
-        SA_CUDA_TRY(cudaStreamWaitEvent(st, m->ev_pf_join, 0));
-    }
     m->x_last = M == 1 ? xc : m->x;
     m->x_last_ll = M == 1;
     return SA_OK;
@@ -680,12 +667,8 @@ int qwen3_create_model(sa_ctx* ctx, const sa_qwen3_config* cfg, int rank, int wo
     if (!rc && cudaStreamCreateWithFlags(&m->own, cudaStreamNonBlocking) != cudaSuccess)
         rc = set_error(SA_ERR_CUDA, "stream create");
     if (!rc && (cudaEventCreateWithFlags(&m->ev_in, cudaEventDisableTiming) != cudaSuccess ||
-                cudaEventCreateWithFlags(&m->ev_out, cudaEventDisableTiming) != cudaSuccess ||
-                cudaEventCreateWithFlags(&m->ev_pf, cudaEventDisableTiming) != cudaSuccess ||
-                cudaEventCreateWithFlags(&m->ev_pf_join, cudaEventDisableTiming) != cudaSuccess))
+                cudaEventCreateWithFlags(&m->ev_out, cudaEventDisableTiming) != cudaSuccess))
         rc = set_error(SA_ERR_CUDA, "event create");
-    if (!rc && cudaStreamCreateWithFlags(&m->pf_side, cudaStreamNonBlocking) != cudaSuccess)
-        rc = set_error(SA_ERR_CUDA, "stream create");
     m->toks_cap = c.max_seq + 1;
     if (!rc) rc = dalloc(&m->d_state, 2);
     if (!rc) rc = dalloc(&m->d_toks, (size_t)m->toks_cap);

