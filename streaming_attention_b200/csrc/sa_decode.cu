@@ -90,7 +90,6 @@ struct Args {
     // captured launch stays valid as the cache grows
     const int* len_dev;
     SpArgs sp;                  // sp.world > 1: sequence-parallel exchange after the merge
-    L2Prefetch pf;              // regions the CTAs prefetch into L2 for the kernels after this one
 };
 
 // Unpack one 16-byte chunk into VEC floats.
@@ -143,24 +142,6 @@ __device__ __forceinline__ void combine_weights(float m, float m2, float& a, flo
     M = fmaxf(m, m2);
     a = (m == -INFINITY) ? 0.f : ex2(m - M);
     b = (m2 == -INFINITY) ? 0.f : ex2(m2 - M);
-}
-
-// Issue the L2 prefetches of `p` in 64 KB chunks, chunk c by global lane c
-// (mod nth) of the launch.
-__device__ __forceinline__ void l2_prefetch_share(const L2Prefetch& p, long long me, long long nth) {
-    constexpr unsigned long long CH = 65536;
-    long long base = 0;
-    for (int r = 0; r < p.n; ++r) {
-        const long long nch = (long long)((p.bytes[r] + CH - 1) / CH);
-        long long c = me - base;
-        if (c < 0) c += ((-c + nth - 1) / nth) * nth;
-        for (; c < nch; c += nth) {
-            const unsigned long long off = (unsigned long long)c * CH;
-            const unsigned long long len = p.bytes[r] - off < CH ? p.bytes[r] - off : CH;
-            bulk_prefetch_l2(static_cast<const char*>(p.ptr[r]) + off, (uint32_t)len);
-        }
-        base += nch;
-    }
 }
 
 // Shared-memory offsets of the final states [G][D+2] a sequence-parallel
@@ -262,9 +243,6 @@ __global__ void __launch_bounds__(THREADS, NST <= 3 ? 2 : 1) decode_kernel(const
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int kvh = blockIdx.y, split = blockIdx.x, qz = blockIdx.z;
-    if (a.pf.n && warp == NW)   // the producer warps of all CTAs share the prefetch chunks
-        l2_prefetch_share(a.pf, ((long long)(qz * gridDim.y + kvh) * gridDim.x + split) * 32 + lane,
-                          (long long)gridDim.x * gridDim.y * gridDim.z * 32);
     const int T = a.len_dev ? (*a.len_dev + 1) : a.T;
     // With the length read on the device the grid is planned for the cache's
     // capacity; the rows actually present are re-split here into about
@@ -861,7 +839,7 @@ size_t decode_dev_scratch_floats(int num_sms, int max_T, int d, int hq, int hkv,
 
 int decode_dev_launch(cudaStream_t st, int* status, int num_sms, const float* q, const float* k, const float* v,
                       long long kv_head_stride, const int* len_dev, int T_host, int max_T, int d, int hq, int hkv,
-                      float scale, float* out, float* scratch, unsigned* counters, const L2Prefetch* pf) {
+                      float scale, float* out, float* scratch, unsigned* counters) {
     int ns, rps;
     plan_splits(num_sms, max_T, hkv, dec::stage_rows(SA_F32, d), &ns, &rps);
     const size_t npart = (size_t)hq * ns;
@@ -881,7 +859,6 @@ int decode_dev_launch(cudaStream_t st, int* status, int num_sms, const float* q,
     a.len_dev = len_dev;
     a.sp = {};
     a.sp.world = 1;
-    if (pf) a.pf = *pf;
     dec::KernelFn fn = dec::pick_dev(d, hq / hkv);
     int smem = dec::smem_bytes<dec::DEV_STAGES>();
     if (!fn) {

@@ -92,12 +92,6 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
     return p;
 }
 
-// Bring `bytes` at `src` into L2 without waiting for it (the TMA engine's
-// bulk prefetch); both 16-byte aligned / a multiple of 16.
-__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-
 // Programmatic dependent launch: let the next kernel in the stream start its
 // launch now, and (in a kernel launched with programmatic serialization) wait
 // until the previous kernel has completed and its writes are visible.  Both

@@ -279,16 +279,6 @@ static int tc_attn_min_rows() {
     return v;
 }
 
-// Single-token steps prefetch weights into L2 from the decode attention
-// kernel (SA_QWEN3_L2_PREFETCH=0 turns it off).
-static bool l2_prefetch_on() {
-    static const bool v = [] {
-        const char* e = std::getenv("SA_QWEN3_L2_PREFETCH");
-        return !(e && e[0] == '0');
-    }();
-    return v;
-}
-
 // The tensor-core attention's operand buffers for M query rows.
 static int ensure_tc(sa_qwen3* m, int M) {
     if (m->tc_k && M <= m->tc_cap) return SA_OK;
@@ -402,28 +392,9 @@ static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr
                 SA_RC(launch_gemv2(st, QW_EPI_QKV, true, L.wqkv, m->NQKV, H, xc, L.in_norm, c.eps, m->qkv, nullptr,
                                    &e));
             }
-            // the decode attention's CTAs also prefetch into L2 what the
-            // rest of the step reads next: this layer's o_proj, gate/up and
-            // down_proj and the next layer's QKV (the last layer: the first
-            // 16 MB of the lm_head), so that the dependent chain of small
-            // GEMVs reads from L2 while HBM streams ahead of it
-            L2Prefetch pf;
-            if (l2_prefetch_on()) {
-                pf.n = 4;
-                pf.ptr[0] = L.wo;  pf.bytes[0] = (unsigned long long)H * m->QD * 2;
-                pf.ptr[1] = L.wgu; pf.bytes[1] = (unsigned long long)2 * I * H * 2;
-                pf.ptr[2] = L.wd;  pf.bytes[2] = (unsigned long long)H * I * 2;
-                if (l + 1 < c.n_layers) {
-                    pf.ptr[3] = m->layers[l + 1].wqkv;
-                    pf.bytes[3] = (unsigned long long)m->NQKV * H * 2;
-                } else {
-                    pf.ptr[3] = m->lm_head;
-                    pf.bytes[3] = std::min<unsigned long long>(16ull << 20, (unsigned long long)c.vocab * H * 2);
-                }
-            }
             SA_RC(decode_dev_launch(st, m->ctx->status, m->ctx->num_sms, m->q, ka, va, (long long)c.max_seq * D,
                                     pos_dev, pos0 + 1, c.max_seq - shift, D, m->hq, m->hkv, scale, m->attn,
-                                    m->dec_scratch, m->dec_cnt, pf.n ? &pf : nullptr));
+                                    m->dec_scratch, m->dec_cnt));
             if (tp) {
                 SA_RC(launch_gemv2_tp(st, QW_EPI_XCHG, false, L.wo, H, m->QD, m->attn, nullptr, 0.f, nullptr, nullptr,
                                       nullptr, tp_args(m, 2 * l), false));

@@ -71,17 +71,10 @@ int launch_qknorm_rope_append(cudaStream_t st, const float* qkv, int splits, int
                               int row_shift, float* q_out, float* kc, float* vc, int max_seq);
 int launch_advance(cudaStream_t st, int* state, const int64_t* tok, int64_t* toks, int cap, int inc_len,
                    bool after_kernel);
-// Up to four regions (pointer, bytes; 16-byte aligned, multiples of 16) that
-// a kernel asks the TMA engine to bring into L2 without waiting for them.
-struct L2Prefetch {
-    int n = 0;
-    const void* ptr[4] = {};
-    unsigned long long bytes[4] = {};
-};
 size_t decode_dev_scratch_floats(int num_sms, int max_T, int d, int hq, int hkv, int* n_splits);
 int decode_dev_launch(cudaStream_t st, int* status, int num_sms, const float* q, const float* k, const float* v,
                       long long kv_head_stride, const int* len_dev, int T_host, int max_T, int d, int hq, int hkv,
-                      float scale, float* out, float* scratch, unsigned* counters, const L2Prefetch* pf = nullptr);
+                      float scale, float* out, float* scratch, unsigned* counters);
 int launch_gemv2(cudaStream_t st, int mode, bool norm, const __nv_bfloat16* W, int N_out, int K, const float* x,
                  const float* nw, float eps, float* y, unsigned long long* amax, const QkvEpi* qkv = nullptr);
 
