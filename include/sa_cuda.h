@@ -458,6 +458,10 @@ int sa_qwen3_tp_connect(sa_qwen3* m, const void* handles);
  */
 #define SA_QWEN3_SP_HANDLE_BYTES 256
 int sa_qwen3_create_sp(sa_ctx* ctx, const sa_qwen3_config* cfg, int rank, int world, sa_qwen3** out);
+/* The same rank with its weights read from a safetensors checkpoint, as
+ * sa_qwen3_load_safetensors. */
+int sa_qwen3_load_safetensors_sp(sa_ctx* ctx, const char* path, int max_seq, float eps, float theta, int rank,
+                                 int world, sa_qwen3** out);
 int sa_qwen3_sp_handle(sa_qwen3* m, void* handle);
 int sa_qwen3_sp_connect(sa_qwen3* m, const void* handles);
 

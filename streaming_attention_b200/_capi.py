@@ -58,6 +58,8 @@ SIGNATURES = {
     "sa_qwen3_tp_handle": (C.c_int, [_vp, _vp]),
     "sa_qwen3_tp_connect": (C.c_int, [_vp, _vp]),
     "sa_qwen3_create_sp": (C.c_int, [_vp, _vp, C.c_int, C.c_int, C.POINTER(_vp)]),
+    "sa_qwen3_load_safetensors_sp": (C.c_int, [_vp, C.c_char_p, C.c_int, C.c_float, C.c_float, C.c_int, C.c_int,
+                                               C.POINTER(_vp)]),
     "sa_qwen3_sp_handle": (C.c_int, [_vp, _vp]),
     "sa_qwen3_sp_connect": (C.c_int, [_vp, _vp]),
     "sa_qwen3_destroy": (C.c_int, [_vp]),

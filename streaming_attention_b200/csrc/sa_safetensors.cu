@@ -388,9 +388,11 @@ SA_API int sa_qwen3_load_safetensors(sa_ctx* ctx, const char* path, int max_seq,
     return sa_qwen3_load_safetensors_tp(ctx, path, max_seq, eps, theta, 0, 1, out);
 }
 
-SA_API int sa_qwen3_load_safetensors_tp(sa_ctx* ctx, const char* path, int max_seq, float eps, float theta, int rank,
-                                        int world, sa_qwen3** out) {
-    using namespace sa;
+namespace sa {
+// Create the model (head-parallel share, or with `sequence` a whole model of
+// a sequence-parallel rank) and upload the checkpoint's tensors.
+static int load_checkpoint(sa_ctx* ctx, const char* path, int max_seq, float eps, float theta, int rank, int world,
+                           bool sequence, sa_qwen3** out) {
     clear_error();
     SA_CHECK_ARG(ctx && out, "sa_qwen3_load_safetensors: null argument");
     *out = nullptr;
@@ -402,7 +404,10 @@ SA_API int sa_qwen3_load_safetensors_tp(sa_ctx* ctx, const char* path, int max_s
     st::Sources s;
     SA_RC_TRY(st::collect(f, c, &s));   // every tensor checked before the model is allocated
     sa_qwen3* m = nullptr;
-    SA_RC_TRY(qwen3_create_model(ctx, &c, rank, world, &m));
+    if (sequence)
+        SA_RC_TRY(sa_qwen3_create_sp(ctx, &c, rank, world, &m));
+    else
+        SA_RC_TRY(qwen3_create_model(ctx, &c, rank, world, &m));
     int rc;
     {
         DeviceGuard guard(ctx->device);
@@ -419,4 +424,15 @@ SA_API int sa_qwen3_load_safetensors_tp(sa_ctx* ctx, const char* path, int max_s
     }
     *out = m;
     return SA_OK;
+}
+}  // namespace sa
+
+SA_API int sa_qwen3_load_safetensors_tp(sa_ctx* ctx, const char* path, int max_seq, float eps, float theta, int rank,
+                                        int world, sa_qwen3** out) {
+    return sa::load_checkpoint(ctx, path, max_seq, eps, theta, rank, world, false, out);
+}
+
+SA_API int sa_qwen3_load_safetensors_sp(sa_ctx* ctx, const char* path, int max_seq, float eps, float theta, int rank,
+                                        int world, sa_qwen3** out) {
+    return sa::load_checkpoint(ctx, path, max_seq, eps, theta, rank, world, true, out);
 }

@@ -16,7 +16,8 @@ BIN = os.path.join(PKG, "bin")
 # the reference tree: $SA_REFERENCE_DIR, else a checkout named `reference` beside this repository
 REF = os.environ.get("SA_REFERENCE_DIR", os.path.join(os.path.dirname(ROOT), "reference"))
 CXX = "/usr/bin/g++" if os.path.exists("/usr/bin/g++") else shutil.which("g++")
-DRIVERS = ["test_naive_cuda", "test_streaming_cuda", "test_streaming_cuda_multi", "test_mpi_cuda"]
+DRIVERS = ["test_naive_cuda", "test_streaming_cuda", "test_streaming_cuda_multi", "test_mpi_cuda",
+           "benchmark_qwen3_cuda"]
 
 
 def _declared_cpp():
@@ -90,3 +91,17 @@ def test_ops_adapter_compiles_against_reference_headers(tmp_path):
                        capture_output=True, text=True)
     assert r.returncode == 0, r.stderr[-2000:]
     assert "sa_ops_tensorcpp.hpp" not in r.stderr, r.stderr[-2000:]    # no warnings from the header itself
+
+
+def test_qwen3_driver_rejects_other_methods_and_bad_options():
+    """benchmark_qwen3_cuda takes the reference driver's options; it runs the
+    CUDA method only and refuses what that method does not do (no GPU needed:
+    the options are checked before any CUDA call)."""
+    exe = os.path.join(BIN, "benchmark_qwen3_cuda")
+    r = subprocess.run([exe, "--model", "x.safetensors", "--method", "avx2"], capture_output=True, text=True)
+    assert r.returncode == 2 and "--method cuda" in r.stderr
+    r = subprocess.run([exe, "--model", "x.safetensors", "--batch-size", "4"], capture_output=True, text=True)
+    assert r.returncode == 2 and "batch 1" in r.stderr
+    r = subprocess.run([exe, "--model", "x.safetensors", "--parallel-strategy", "pipeline"], capture_output=True,
+                       text=True)
+    assert r.returncode == 2 and "usage:" in r.stderr
