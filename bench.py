@@ -1041,11 +1041,13 @@ def run_qwen3(args):
         # generate of 4 tokens (prefill + 3 captured decode steps)
         import numpy as np
         cfg = sa.QWEN3_0_6B
-        m = sa.Qwen3(cfg, max_seq=512, ctx=ctx)
+        m = sa.Qwen3(cfg, max_seq=4096 + 64 if args.long_prompt else 512, ctx=ctx)
         m.load(sa.qwen3.random_weights(cfg, SEED))
         ids = np.random.default_rng(SEED).integers(0, cfg["vocab"], Q3_PROMPT)
         m.forward(ids, logits="all")
         m.generate(ids, 4)
+        if args.long_prompt:   # one 4096-token forward (tensor-core prompt attention)
+            m.forward(np.random.default_rng(SEED).integers(0, cfg["vocab"], 4096), logits="last")
         torch.cuda.synchronize(dev)
         print(json.dumps({"profile": True, "workload": "qwen3"}), flush=True)
         return 0
