@@ -48,6 +48,13 @@ extern "C" {
 
 /* ---- flags -------------------------------------------------------------- */
 #define SA_HOST_PTRS   1u    /* pointers are host memory; call is blocking */
+/* Decode attention (sa_attn_decode, _partial, _sp) with device pointers: K
+ * and V are not written by any kernel still running when the call is issued
+ * (e.g. a KV cache appended by earlier steps or by a memory copy).  The
+ * kernel is then launched as a programmatic dependent of the stream's
+ * previous kernel and streams its first K/V stages while that kernel
+ * finishes; q and every output are read / written only after it completed. */
+#define SA_KV_STATIC   2u
 
 typedef struct sa_ctx sa_ctx;
 

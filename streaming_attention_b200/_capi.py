@@ -22,6 +22,7 @@ SA_SP_HANDLE_BYTES = 128
 SA_F32 = 0
 SA_BF16 = 1
 SA_HOST_PTRS = 1
+SA_KV_STATIC = 2
 
 _vp = C.c_void_p
 _fp = C.POINTER(C.c_float)

@@ -17,7 +17,7 @@ import ctypes as C
 
 import numpy as np
 
-from ._capi import SA_BF16, SA_F32, SA_HOST_PTRS, Context, check, default_context, lib
+from ._capi import SA_BF16, SA_F32, SA_HOST_PTRS, SA_KV_STATIC, Context, check, default_context, lib
 
 
 def _is_torch(x) -> bool:
@@ -71,12 +71,15 @@ def _out_like(x, shape):
 
 
 def attn_decode(q, k, v, scale: float = 1.0, block: int = 64, ctx: Context | None = None,
-                out=None):
+                out=None, kv_static: bool = False):
     """GQA decode attention (sa_attn_decode).
 
     q [hq, d]; k, v [hkv, T, d] (same dtype: fp32, or bf16 torch tensors);
     returns out [hq, d] fp32.  ``scale`` multiplies the scores (1.0 reproduces
     the unscaled attention.h kernels; 1/sqrt(d) the Qwen3 attention).
+    ``kv_static`` (device tensors): K and V are not written by a kernel still
+    running, so the call may stream them while the previous kernel finishes
+    (SA_KV_STATIC).
     """
     q, k, v = _prep(q), _prep(k), _prep(v)
     hq, d = q.shape
@@ -84,7 +87,7 @@ def attn_decode(q, k, v, scale: float = 1.0, block: int = 64, ctx: Context | Non
     assert d2 == d and tuple(v.shape) == tuple(k.shape)
     ctx = _ctx_for(q, ctx)
     dt = _dtype_code(q)
-    flags = 0 if _is_torch(q) else SA_HOST_PTRS
+    flags = (SA_KV_STATIC if kv_static else 0) if _is_torch(q) else SA_HOST_PTRS
     if out is None:
         out = _out_like(q, (hq, d))
     _bind_stream(ctx, q)

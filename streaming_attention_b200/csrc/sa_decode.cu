@@ -85,6 +85,10 @@ struct Args {
     // out + z*o_stride (n_splits == 1)
     long long q_stride, o_stride;
     int q_causal;
+    // K and V are not written by the kernel before this one (SA_KV_STATIC):
+    // launched programmatically, the producer streams the first ring stages
+    // before griddepcontrol.wait; q and every global write come after it
+    int kv_early;
     // when set, the row count is read on the device: T = *len_dev + 1 (the
     // KV-cache length before the token being decoded, plus that token), so a
     // captured launch stays valid as the cache grows
@@ -231,8 +235,9 @@ __global__ void __launch_bounds__(THREADS, NST <= 3 ? 2 : 1) decode_kernel(const
     // were written before the step's first kernel, an ordinary (not
     // programmatic) launch, so they are complete and visible here; only the
     // newest row (appended by the QKV kernel this kernel follows) and q need
-    // the wait.  Otherwise every input may come from the previous kernel.
-    if (!a.len_dev) pdl_wait();
+    // the wait.  With kv_early the same holds for all of K and V.  Otherwise
+    // every input may come from the previous kernel.
+    if (!a.len_dev && !a.kv_early) pdl_wait();
     extern __shared__ __align__(128) unsigned char smem[];
     unsigned char* kbuf = smem;
     unsigned char* vbuf = smem + NST * SR * RB;
@@ -281,7 +286,11 @@ __global__ void __launch_bounds__(THREADS, NST <= 3 ? 2 : 1) decode_kernel(const
         // that fits the ring goes out before the wait for the previous
         // kernel, including the rows of the newest row's stage before it;
         // the newest row (appended by that kernel) follows the wait
-        const PreWait pw = pre_wait_plan(a.len_dev != nullptr, T, t0, nrows, SR, NST);
+        PreWait pw = pre_wait_plan(a.len_dev != nullptr, T, t0, nrows, SR, NST);
+        if (a.kv_early && !a.len_dev) {   // every row is in place: fill the ring before the wait
+            pw.pre = min(NST, pw.nst);
+            pw.post0 = pw.pre;
+        }
         const int pre = pw.pre, st_new = pw.st_new;
         const bool split_new = pw.split_new;
         const uint64_t pol = policy_evict_first();
@@ -303,7 +312,7 @@ __global__ void __launch_bounds__(THREADS, NST <= 3 ? 2 : 1) decode_kernel(const
             }
         }
         __syncwarp();
-        if (a.len_dev) pdl_wait();
+        if (a.len_dev || a.kv_early) pdl_wait();
         if (lane == 0) {
             int it = pre;
             if (split_new) {
@@ -325,7 +334,7 @@ __global__ void __launch_bounds__(THREADS, NST <= 3 ? 2 : 1) decode_kernel(const
         }
     } else {
         // ---------------- consumers (q comes from the previous kernel)
-        if (a.len_dev) pdl_wait();
+        if (a.len_dev || a.kv_early) pdl_wait();
         float qr[G][CPL];
 #pragma unroll
         for (int g = 0; g < G; ++g) {
@@ -684,7 +693,7 @@ static int check_decode_args(const char* fn, int dtype, const void* q, const voi
 // hq*n_splits*(d+2) floats for the plan the call computes.
 static int launch_decode(sa_ctx* ctx, int dtype, const void* q, const void* k, const void* v,
                          long long stride, int T, int d, int hq, int hkv, float scale, float* out,
-                         float* out_m, float* out_l, const dec::SpArgs* sp = nullptr) {
+                         float* out_m, float* out_l, const dec::SpArgs* sp = nullptr, bool kv_early = false) {
     SA_CHECK_ARG(T == 0 || (((uintptr_t)k | (uintptr_t)v) & 15) == 0, "decode: k/v not 16-byte aligned");
     SA_CHECK_ARG((((uintptr_t)q) & 15) == 0, "decode: q not 16-byte aligned");
     int ns, rps;
@@ -706,15 +715,20 @@ static int launch_decode(sa_ctx* ctx, int dtype, const void* q, const void* k, c
     a.counters = ctx->counters;
     a.out = out; a.out_m = out_m; a.out_l = out_l;
     a.status = ctx->status;
-    a.q_stride = 0; a.o_stride = 0; a.q_causal = 1;
+    a.q_stride = 0; a.o_stride = 0; a.q_causal = 1; a.kv_early = 0;
     a.len_dev = nullptr;
     a.sp = {};
     a.sp.world = 1;
     if (sp) a.sp = *sp;
+    a.kv_early = kv_early ? 1 : 0;
     dec::KernelFn fn = dtype == SA_F32 ? dec::pick<float>(d, hq / hkv) : dec::pick<__nv_bfloat16>(d, hq / hkv);
     SA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::SMEM_BYTES));
-    fn<<<dim3(ns, hkv), dec::THREADS, dec::SMEM_BYTES, ctx->stream>>>(a);
-    SA_CUDA_TRY(cudaGetLastError());
+    if (kv_early) {
+        SA_CUDA_TRY(launch_pdl(fn, dim3(ns, hkv), dim3(dec::THREADS), dec::SMEM_BYTES, ctx->stream, a));
+    } else {
+        fn<<<dim3(ns, hkv), dec::THREADS, dec::SMEM_BYTES, ctx->stream>>>(a);
+        SA_CUDA_TRY(cudaGetLastError());
+    }
     return SA_OK;
 }
 
@@ -729,7 +743,8 @@ static int decode_common(const char* fn_name, sa_ctx* ctx, int dtype, const void
     if (rc) return rc;
     DeviceGuard guard(ctx->device);
     if (!(flags & SA_HOST_PTRS))
-        return launch_decode(ctx, dtype, q, k, v, stride, T, d, hq, hkv, scale, out, m_out, l_out, sp);
+        return launch_decode(ctx, dtype, q, k, v, stride, T, d, hq, hkv, scale, out, m_out, l_out, sp,
+                             (flags & SA_KV_STATIC) != 0);
 
     // Host buffers: stage through device memory on the context's stream.
     const int elt = dtype == SA_F32 ? 4 : 2;
@@ -855,7 +870,7 @@ int decode_dev_launch(cudaStream_t st, int* status, int num_sms, const float* q,
     a.counters = counters;
     a.out = out; a.out_m = nullptr; a.out_l = nullptr;
     a.status = status;
-    a.q_stride = 0; a.o_stride = 0; a.q_causal = 1;
+    a.q_stride = 0; a.o_stride = 0; a.q_causal = 1; a.kv_early = 0;
     a.len_dev = len_dev;
     a.sp = {};
     a.sp.world = 1;
@@ -972,7 +987,7 @@ SA_API int sa_attn_decode_noalloc(void* stream, int dtype, const void* q, const 
     a.counters = counters;
     a.out = out; a.out_m = nullptr; a.out_l = nullptr;
     a.status = status;
-    a.q_stride = 0; a.o_stride = 0; a.q_causal = 1;
+    a.q_stride = 0; a.o_stride = 0; a.q_causal = 1; a.kv_early = 0;
     a.len_dev = nullptr;
     a.sp = {};
     a.sp.world = 1;
@@ -1303,6 +1318,7 @@ static int attn_prompt_dev(sa_ctx* ctx, const float* q, const float* k, const fl
         a.q_stride = qs;
         a.o_stride = os;
         a.q_causal = causal ? 1 : 0;
+        a.kv_early = 0;
         a.len_dev = nullptr;
         a.sp = {};
         a.sp.world = 1;

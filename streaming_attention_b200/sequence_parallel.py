@@ -207,12 +207,14 @@ class SpDecoder:
         arr = (C.c_void_p * len(decoders))(*[d.h.value for d in decoders])
         check(lib().sa_sp_connect_local(arr, len(decoders)))
 
-    def decode(self, q, k, v, scale: float = 1.0, block: int = 64, out=None, with_state: bool = False):
+    def decode(self, q, k, v, scale: float = 1.0, block: int = 64, out=None, with_state: bool = False,
+               kv_static: bool = False):
         """q [hq, d]; k, v [hkv, T_local, d] (CUDA tensors, fp32 or bf16) ->
-        out [hq, d] fp32 (and the merged m, l [hq] with ``with_state``)."""
+        out [hq, d] fp32 (and the merged m, l [hq] with ``with_state``).
+        ``kv_static``: SA_KV_STATIC (K/V not written by a running kernel)."""
         import ctypes as C
         import torch
-        from ._capi import SA_BF16, SA_F32, check, lib
+        from ._capi import SA_BF16, SA_F32, SA_KV_STATIC, check, lib
         q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
         hq, d = q.shape
         hkv, T, _ = k.shape
@@ -224,7 +226,7 @@ class SpDecoder:
         P = lambda t: C.c_void_p(t.data_ptr()) if t is not None else None
         self.ctx.set_stream(torch.cuda.current_stream(q.device).cuda_stream)
         check(lib().sa_attn_decode_sp(self.h, dt, P(q), P(k), P(v), T * d, T, d, hq, hkv, block, scale,
-                                      P(out), P(m), P(l), 0))
+                                      P(out), P(m), P(l), SA_KV_STATIC if kv_static else 0))
         return (out, m, l) if with_state else out
 
     def close(self) -> None:

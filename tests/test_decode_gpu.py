@@ -238,3 +238,35 @@ def test_decode_step_cache_full(ctx):
     with pytest.raises(SAError) as e:
         attn_decode_step(q, kn, kn, kc, kc.clone(), 8, 1.0, 64, ctx)
     assert e.value.code == -7 and "full" in str(e.value)
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_decode_kv_static_back_to_back(ctx, oracle, dtype):
+    """SA_KV_STATIC: each call launches as a programmatic dependent of the
+    kernel before it and streams K/V early; q is written by that kernel (a
+    copy) right before every call, and every output must still be the
+    oracle's for its own q -- the early start may not read q or reuse the
+    split scratch before the previous kernel (here also the previous decode
+    call) is done."""
+    import torch
+    from oracle.oracle import bf16_round
+    from streaming_attention_b200 import attn_decode
+    hq, hkv, T, d = 16, 8, 9001, 128
+    _, k, v = I.gqa(hq, hkv, T, d, 31)
+    qs = [I.gqa(hq, hkv, 1, d, 100 + i)[0] for i in range(6)]
+    if dtype == "bfloat16":
+        k, v, qs = bf16_round(k), bf16_round(v), [bf16_round(x) for x in qs]
+    tdt = getattr(torch, dtype)
+    kt, vt = torch.from_numpy(k).cuda().to(tdt), torch.from_numpy(v).cuda().to(tdt)
+    qsrc = [torch.from_numpy(x).cuda().to(tdt) for x in qs]
+    q = torch.empty_like(qsrc[0])
+    outs = [torch.empty(hq, d, device="cuda") for _ in qs]
+    torch.cuda.synchronize()
+    for i in range(len(qs)):
+        q.copy_(qsrc[i])                     # the kernel right before the call writes q
+        attn_decode(q, kt, vt, 1 / np.sqrt(d), 64, ctx, outs[i], kv_static=True)
+        attn_decode(q, kt, vt, 1 / np.sqrt(d), 64, ctx, kv_static=True)   # back to back, same scratch
+    torch.cuda.synchronize()
+    for i, x in enumerate(qs):
+        ref = oracle.gqa_decode(x, k, v, 64, 1 / np.sqrt(d))
+        assert np.abs(outs[i].cpu().numpy() - ref).max() < 1e-4

@@ -81,9 +81,16 @@ def _worker(rank, world, port, out_dir):
         a = sp.decode(qt, kt, vt, 1 / np.sqrt(d), 64)
         b = sp.decode(qt, kt, vt, 1 / np.sqrt(d), 64)
         o, m, l = sp.decode(qt, kt, vt, 1 / np.sqrt(d), 64, with_state=True)
+        # SA_KV_STATIC: launched as a programmatic dependent of the copy that
+        # writes q, then of the previous decode (same scratch, next exchange slot)
+        q2 = torch.empty_like(qt)
+        q2.copy_(qt)
+        e = sp.decode(q2, kt, vt, 1 / np.sqrt(d), 64, kv_static=True)
+        f = sp.decode(q2, kt, vt, 1 / np.sqrt(d), 64, kv_static=True)
         ctx.synchronize()
         np.savez(os.path.join(out_dir, f"r{rank}_c{ci}.npz"), a=a.cpu().numpy(), b=b.cpu().numpy(),
-                 o=o.cpu().numpy(), m=m.cpu().numpy(), l=l.cpu().numpy())
+                 o=o.cpu().numpy(), m=m.cpu().numpy(), l=l.cpu().numpy(), e=e.cpu().numpy(),
+                 f=f.cpu().numpy())
     dist.barrier()
     sp.close()
     ctx.close()
@@ -98,10 +105,11 @@ def _check(out_dir, world, oracle):
         first = None
         for r in range(world):
             z = np.load(os.path.join(out_dir, f"r{r}_c{ci}.npz"))
-            for key in ("a", "b", "o"):
+            for key in ("a", "b", "o", "e", "f"):
                 err = np.abs(z[key] - ref).max()
                 assert err < TOL, (ci, r, key, err)
-            assert np.array_equal(z["a"], z["b"]) and np.array_equal(z["a"], z["o"])
+            for key in ("b", "o", "e", "f"):
+                assert np.array_equal(z["a"], z[key]), key
             np.testing.assert_allclose(z["m"], m_ref, rtol=1e-5, atol=1e-5)
             np.testing.assert_allclose(z["l"], l_ref, rtol=1e-4)
             if first is None:
