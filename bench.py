@@ -1047,6 +1047,7 @@ def run_qwen3(args):
         m.forward(ids, logits="all")
         m.generate(ids, 4)
         if args.long_prompt:   # one 4096-token forward (tensor-core prompt attention)
+            m.reset()
             m.forward(np.random.default_rng(SEED).integers(0, cfg["vocab"], 4096), logits="last")
         torch.cuda.synchronize(dev)
         print(json.dumps({"profile": True, "workload": "qwen3"}), flush=True)

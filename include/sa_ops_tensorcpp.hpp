@@ -46,8 +46,9 @@
  *        statistics all-reduce mixes positions).  global_seq_len must equal S.
  *  - errors are exceptions: std::invalid_argument for shapes / masks the CUDA
  *    path does not take, std::runtime_error for CUDA failures.
- * Threading: one sa_ctx per GPU, created on first use and kept; calls are
- * serialised per GPU.
+ * Threading: one sa_ctx per GPU, created on first use and kept until
+ * ops::cuda::release() (or the end of the process); calls are serialised per
+ * GPU.
  */
 #ifndef SA_OPS_TENSORCPP_HPP
 #define SA_OPS_TENSORCPP_HPP
@@ -82,9 +83,6 @@ inline void throw_rc(int rc, const char* what) {
 struct Device {
     std::mutex mu;
     sa_ctx* ctx = nullptr;
-    ~Device() {
-        if (ctx) sa_ctx_destroy(ctx);
-    }
 };
 
 struct Devices {
@@ -92,9 +90,12 @@ struct Devices {
     std::map<int, std::unique_ptr<Device>> dev;
 };
 
+// Never destroyed: a context left at exit goes with the process, and no CUDA
+// call runs from a static destructor while the runtime shuts down.  release()
+// frees them earlier.
 inline Devices& devices() {
-    static Devices d;
-    return d;
+    static Devices* d = new Devices;
+    return *d;
 }
 
 // The GPU's context (created on first use) with its lock held by the caller.
@@ -200,6 +201,18 @@ inline Tensor attend(const Tensor& query, const Tensor& key, const Tensor& value
 }
 
 }  // namespace sa_ops_detail
+
+/* Destroy the per-GPU contexts (device memory and streams); the next call
+ * creates them again.  Not to be called while an operator runs. */
+inline void release() {
+    sa_ops_detail::Devices& ds = sa_ops_detail::devices();
+    std::lock_guard<std::mutex> lk(ds.mu);
+    for (auto& kv : ds.dev) {
+        std::lock_guard<std::mutex> dl(kv.second->mu);
+        if (kv.second->ctx) sa_ctx_destroy(kv.second->ctx);
+        kv.second->ctx = nullptr;
+    }
+}
 
 /* ops::self_attention (ops.h:133-139): softmax(scale q k^T + mask) v. */
 inline Tensor self_attention(const Tensor& query, const Tensor& key, const Tensor& value,

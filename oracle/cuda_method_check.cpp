@@ -367,6 +367,7 @@ void check_ops(size_t D) {
 }  // namespace
 
 int main() {
+    std::setvbuf(stdout, nullptr, _IONBF, 0);   // every line out before a possible abort
     try {
         check_attention();
         check_ops(128);
@@ -378,6 +379,7 @@ int main() {
         ++g_fail;
     }
     qwen3::cuda::release();
+    ops::cuda::release();
     attention_cuda_release();
     if (g_fail) {
         std::printf("CUDA METHOD CHECK FAILED (%d)\n", g_fail);

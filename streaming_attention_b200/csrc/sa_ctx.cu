@@ -5,19 +5,21 @@
 
 namespace sa {
 
-static thread_local std::string g_last_error;
+// A plain array, not a std::string: it has no destructor, so a call made
+// while the process exits (a static object's destructor destroying its
+// context after the thread's thread_local objects are gone) still writes
+// into live memory.
+static thread_local char g_last_error[1024];
 
 int set_error(int code, const char* fmt, ...) {
-    char buf[1024];
     va_list ap;
     va_start(ap, fmt);
-    vsnprintf(buf, sizeof(buf), fmt, ap);
+    vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
     va_end(ap);
-    g_last_error = buf;
     return code;
 }
 
-void clear_error() { g_last_error.clear(); }
+void clear_error() { g_last_error[0] = '\0'; }
 
 int ensure_ws(sa_ctx* ctx, size_t bytes) {
     if (bytes <= ctx->ws_bytes) return SA_OK;
@@ -69,7 +71,7 @@ int sync_and_check(sa_ctx* ctx) {
 
 }  // namespace sa
 
-SA_API const char* sa_last_error(void) { return sa::g_last_error.c_str(); }
+SA_API const char* sa_last_error(void) { return sa::g_last_error; }
 
 SA_API const char* sa_version(void) { return "sa_cuda 0.1 (sm_100a)"; }
 

@@ -263,6 +263,7 @@ int run_rank(const Config& c, int rank, int world, Shared* sh) {
 int main(int argc, char** argv) {
     Config c;
     if (!parse(argc, argv, c)) return usage(argv[0]);
+    std::fflush(stdout);   // nothing buffered is duplicated into the forked ranks
     if (c.method != "cuda") {
         std::fprintf(stderr, "this driver runs --method cuda (got %s)\n", c.method.c_str());
         return 2;
@@ -279,7 +280,12 @@ int main(int argc, char** argv) {
     std::vector<pid_t> kids;
     for (int r = 0; r < c.gpus; ++r) {
         const pid_t p = fork();
-        if (p == 0) _exit(run_rank(c, r, c.gpus, sh));
+        if (p == 0) {
+            const int code = run_rank(c, r, c.gpus, sh);
+            std::fflush(stdout);   // _exit does not flush stdio
+            std::fflush(stderr);
+            _exit(code);
+        }
         if (p < 0) {
             sh->failed.store(1);
             break;
