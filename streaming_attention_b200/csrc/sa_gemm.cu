@@ -29,6 +29,13 @@
 //   SWIGLU  W holds [gate(32) ; up(32)] row blocks; out[:, n0/2 + i] =
 //           silu(g_i) * u_i written as A_hi/A_lo of the next GEMM
 //           (qwen3_mlp, qwen3_ops.cpp:265-296)
+//   RESID_NORM  C += acc, then the next GEMM's A = hi/lo(g . C) and the
+//           tile's row sums of C^2 (that GEMM's RMSNorm, deferred: it scales
+//           its accumulator rows by 1 / rms, qwen3_ops.cpp:450-456,516-520)
+//   QKV_ROWS    QK-norm + RoPE of whole heads and the KV-cache append
+//           (qwen3_attention, qwen3_ops.cpp:341-401), fp32 and/or bf16
+// and, with a deferred RMSNorm on the A operand, every mode first scales its
+// accumulator rows by 1 / rms(x) (GemmEpi in sa_qwen3.h).
 //
 // Launched with programmatic stream serialization: the producer streams the
 // first stages' weight tiles before griddepcontrol.wait, every other access
@@ -41,6 +48,7 @@
 #include "sa_internal.h"
 #include "sa_tc.cuh"
 #include "sa_qwen3.h"
+#include "sa_qwen3_dev.cuh"
 
 namespace sa {
 namespace gm {
@@ -56,7 +64,8 @@ struct Cfg {
     static constexpr int TP = BN + 4;                        // padded epilogue tile row pitch (floats)
     static constexpr int T_BYTES = BM * TP * 4;
     static constexpr int PIPE = STAGES * STAGE_BYTES;
-    static_assert(T_BYTES <= PIPE && BN * BM * 4 <= PIPE, "epilogue staging must fit in the pipeline stages");
+    static constexpr int RS_OFF = T_BYTES;                   // [BM] row scales of a deferred RMSNorm
+    static_assert(T_BYTES + BM * 4 <= PIPE && BN * BM * 4 <= PIPE, "epilogue staging must fit in the pipeline stages");
     static constexpr int OFF_BAR = (PIPE + 1023) / 1024 * 1024;
     static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;  // + barriers + alignment slack
 };
@@ -69,6 +78,7 @@ struct Args {
     __nv_bfloat16* out_hi;    // SWIGLU: [M, ldo]
     __nv_bfloat16* out_lo;
     long long ldo;
+    GemmEpi e;                // deferred RMSNorm, RESID_NORM and QKV_ROWS operands
     int* status;
 };
 
@@ -104,6 +114,130 @@ __device__ __forceinline__ void store_hilo4(__nv_bfloat16* hi, __nv_bfloat16* lo
     ul.x = *reinterpret_cast<const uint32_t*>(&l01); ul.y = *reinterpret_cast<const uint32_t*>(&l23);
     *reinterpret_cast<uint2*>(hi) = uh;
     *reinterpret_cast<uint2*>(lo) = ul;
+}
+
+// QW_EPI_QKV_ROWS: warp `quad` of the four epilogue warps takes rows quad,
+// quad + 4, ...; for each row, the tile's BN / 128 heads (lane l: elements
+// 4l..4l+3 of a head), interleaved so their reductions overlap.
+template <int BN>
+__device__ __forceinline__ void qkv_rows_epilogue(const Args& a, const float* T, const float* rs, bool scaled,
+                                                  int m0, int n0, int quad, int lane) {
+    constexpr int HPT = BN / 128, TP = Cfg<BN>::TP, D = 128;
+    const GemmEpi& e = a.e;
+    const int nqk = e.hq + e.hkv;                  // heads [nqk, nqk + hkv) are V heads
+    const int h0 = n0 / D;
+    float4 nw[HPT];
+#pragma unroll
+    for (int hh = 0; hh < HPT; ++hh) {
+        const int h = h0 + hh;
+        const float* w = h < e.hq ? e.qn : e.kn;
+        nw[hh] = h < nqk ? __ldg(reinterpret_cast<const float4*>(w) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll 1
+    for (int rr = quad; rr < BM; rr += 4) {
+        const int m = m0 + rr;
+        const int pos = e.pos0 + m, row = pos + e.row_shift;
+        if (m >= a.M || row >= e.max_seq) break;   // rows only grow along the loop
+        const int i0 = (4 * lane) & (D / 2 - 1);
+        const float4 c4 = __ldg(reinterpret_cast<const float4*>(e.cos_t + (size_t)pos * (D / 2) + i0));
+        const float4 s4 = __ldg(reinterpret_cast<const float4*>(e.sin_t + (size_t)pos * (D / 2) + i0));
+        const float sc = scaled ? rs[rr] : 1.f;
+        float ev[HPT][4];
+#pragma unroll
+        for (int hh = 0; hh < HPT; ++hh) {
+            const float4 t4 = *reinterpret_cast<const float4*>(T + rr * TP + hh * D + 4 * lane);
+            ev[hh][0] = t4.x * sc; ev[hh][1] = t4.y * sc; ev[hh][2] = t4.z * sc; ev[hh][3] = t4.w * sc;
+        }
+        float ss[HPT];
+#pragma unroll
+        for (int hh = 0; hh < HPT; ++hh)
+            ss[hh] = ev[hh][0] * ev[hh][0] + ev[hh][1] * ev[hh][1] + ev[hh][2] * ev[hh][2] + ev[hh][3] * ev[hh][3];
+#pragma unroll
+        for (int o = 16; o; o >>= 1)
+#pragma unroll
+            for (int hh = 0; hh < HPT; ++hh) ss[hh] += __shfl_xor_sync(0xffffffffu, ss[hh], o);
+        const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+        const bool first = lane < 16;
+#pragma unroll
+        for (int hh = 0; hh < HPT; ++hh) {
+            const int h = h0 + hh;
+            if (h >= nqk) {                        // V head: the projection as it is
+                const int vh = h - nqk;
+                const float4 v4 = make_float4(ev[hh][0], ev[hh][1], ev[hh][2], ev[hh][3]);
+                if (e.vc) *reinterpret_cast<float4*>(e.vc + ((size_t)vh * e.max_seq + row) * D + 4 * lane) = v4;
+                if (e.v_bf)
+                    *reinterpret_cast<uint2*>(e.v_bf + ((size_t)pos * e.hkv + vh) * D + 4 * lane) = qd::bf16x4(v4);
+                continue;
+            }
+            // QK-norm (eps 1e-6 inside the sqrt) with the head's gain, then
+            // rotate-half RoPE: element i pairs with i + 64 (lane l ^ 16)
+            const float rms = sqrtf(ss[hh] / (float)D + 1e-6f);
+            const float g4[4] = {nw[hh].x, nw[hh].y, nw[hh].z, nw[hh].w};
+            float y[4], p[4], o[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) y[j] = (ev[hh][j] / rms) * g4[j];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) p[j] = __shfl_xor_sync(0xffffffffu, y[j], 16);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o[j] = first ? y[j] * cs[j] + (-p[j]) * sn[j] : y[j] * cs[j] + p[j] * sn[j];
+            const float4 r4 = make_float4(o[0], o[1], o[2], o[3]);
+            if (h < e.hq) {
+                const size_t off = ((size_t)m * e.hq + h) * D + 4 * lane;
+                if (e.q_out) *reinterpret_cast<float4*>(e.q_out + off) = r4;
+                if (e.q_bf) *reinterpret_cast<uint2*>(e.q_bf + off) = qd::bf16x4(r4);
+            } else {
+                const int kh = h - e.hq;
+                if (e.kc) *reinterpret_cast<float4*>(e.kc + ((size_t)kh * e.max_seq + row) * D + 4 * lane) = r4;
+                if (e.k_bf)
+                    *reinterpret_cast<uint2*>(e.k_bf + ((size_t)pos * e.hkv + kh) * D + 4 * lane) = qd::bf16x4(r4);
+            }
+        }
+    }
+}
+
+// QW_EPI_RESID_NORM: warp `quad` takes rows quad, quad + 4, ... four at a
+// time (their residual loads issued before any is used); lane l holds the
+// float4 columns 4l + 128 j of the tile.  Writes C, the next GEMM's A operand
+// hi/lo(g . C) and the row's sum of C^2 over the tile at rowsq_out[tile][m].
+template <int BN>
+__device__ __forceinline__ void resid_norm_epilogue(const Args& a, const float* T, int m0, int n0, int quad,
+                                                    int lane) {
+    constexpr int V4 = BN / 128, TP = Cfg<BN>::TP;
+    float4 gv[V4];
+#pragma unroll
+    for (int j = 0; j < V4; ++j) gv[j] = __ldg(reinterpret_cast<const float4*>(a.e.g + n0 + 128 * j) + lane);
+#pragma unroll 1
+    for (int r0 = quad; r0 < BM; r0 += 16) {
+        float4 old[4][V4];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const int m = m0 + r0 + 4 * b;
+#pragma unroll
+            for (int j = 0; j < V4; ++j)
+                old[b][j] = m < a.M ? __ldcg(reinterpret_cast<const float4*>(a.C + (size_t)m * a.ldc + n0 + 128 * j) +
+                                             lane)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const int rr = r0 + 4 * b, m = m0 + rr;
+            if (m >= a.M) break;
+            float ss = 0.f;
+#pragma unroll
+            for (int j = 0; j < V4; ++j) {
+                const float4 v = *reinterpret_cast<const float4*>(T + rr * TP + 128 * j + 4 * lane);
+                const float4 x = make_float4(old[b][j].x + v.x, old[b][j].y + v.y, old[b][j].z + v.z,
+                                             old[b][j].w + v.w);
+                *(reinterpret_cast<float4*>(a.C + (size_t)m * a.ldc + n0 + 128 * j) + lane) = x;
+                ss += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
+                const size_t o = (size_t)m * a.ldo + n0 + 128 * j + 4 * lane;
+                store_hilo4(a.out_hi + o, a.out_lo + o,
+                            make_float4(x.x * gv[j].x, x.y * gv[j].y, x.z * gv[j].z, x.w * gv[j].w));
+            }
+            ss = qd::warp_sum(ss);
+            if (lane == 0) a.e.rowsq_out[(size_t)blockIdx.x * a.M + m] = ss;
+        }
+    }
 }
 
 template <int BN>
@@ -207,6 +341,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ C
         const int et = tid - 64;                       // 0..127
         const int quad = warp & 3;
         const int row = quad * 32 + lane;
+        // a deferred RMSNorm's row scale (thread et: row et), while the
+        // mainloop runs; the partial sums come from the previous kernel
+        float my_sc = 1.f;
+        if (s == 1 && a.e.rowsq_in && m0 + et < a.M) {
+            float ss = 0.f;
+            for (int p = 0; p < a.e.rowsq_parts; ++p) ss += __ldcg(a.e.rowsq_in + (size_t)p * a.M + m0 + et);
+            my_sc = 1.f / sqrtf(ss / a.e.norm_k + a.e.eps);
+        }
         const bool ok = wait_ab(&B->done, 0, abort, a.status);
         tc::fence_after_sync();
         if (s > 1) {
@@ -242,6 +384,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ C
             }
         } else {
             float* T = reinterpret_cast<float*>(sm);   // [BM][TP] fp32
+            float* rs = reinterpret_cast<float*>(sm + C_::RS_OFF);
+            const bool scaled = a.e.rowsq_in != nullptr;
+            if (ok && scaled) rs[et] = my_sc;
             if (ok) {
                 uint32_t r[32];
 #pragma unroll 1
@@ -265,13 +410,22 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ C
                         const int rr = it / J4, j = (it % J4) * 4, m = m0 + rr;
                         if (m >= a.M) continue;
                         const int gc = (j / 32) * 64 + (j % 32);
-                        const float4 g = *reinterpret_cast<const float4*>(T + rr * TP + gc);
-                        const float4 u = *reinterpret_cast<const float4*>(T + rr * TP + gc + 32);
+                        float4 g = *reinterpret_cast<const float4*>(T + rr * TP + gc);
+                        float4 u = *reinterpret_cast<const float4*>(T + rr * TP + gc + 32);
+                        if (scaled) {
+                            const float sc = rs[rr];
+                            g = make_float4(g.x * sc, g.y * sc, g.z * sc, g.w * sc);
+                            u = make_float4(u.x * sc, u.y * sc, u.z * sc, u.w * sc);
+                        }
                         const float4 v = make_float4(silu(g.x) * u.x, silu(g.y) * u.y, silu(g.z) * u.z,
                                                      silu(g.w) * u.w);
                         const size_t o = (size_t)m * a.ldo + n0 / 2 + j;
                         store_hilo4(a.out_hi + o, a.out_lo + o, v);
                     }
+                } else if (BN >= 128 && a.mode == QW_EPI_QKV_ROWS) {   // whole heads: the host checks the width
+                    if constexpr (BN >= 128) qkv_rows_epilogue<BN>(a, T, rs, scaled, m0, n0, quad, lane);
+                } else if (BN >= 128 && a.mode == QW_EPI_RESID_NORM) {
+                    if constexpr (BN >= 128) resid_norm_epilogue<BN>(a, T, m0, n0, quad, lane);
                 } else {
                     // a warp covers one row's BN columns as float4; residual
                     // loads are issued four rows at a time before any store
@@ -292,7 +446,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ C
                         for (int b = 0; b < 4; ++b) {
                             const int it = it0 + b * 128, rr = it / C4, c = (it % C4) * 4, m = m0 + rr;
                             if (it >= BM * C4 || m >= a.M || c >= nv) continue;
-                            const float4 v = *reinterpret_cast<const float4*>(T + rr * TP + c);
+                            float4 v = *reinterpret_cast<const float4*>(T + rr * TP + c);
+                            if (scaled) {
+                                const float sc = rs[rr];
+                                v = make_float4(v.x * sc, v.y * sc, v.z * sc, v.w * sc);
+                            }
                             float* cp = a.C + (size_t)m * a.ldc + n0 + c;
                             if (vec && c + 4 <= nv) {
                                 float4 o = v;
@@ -383,7 +541,7 @@ GemmPlan gemm_plan(int device, int num_sms, int M, int N, int K, bool split_ok) 
 int gemm_launch(cudaStream_t st, int* status, const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo,
                 long long lda, const __nv_bfloat16* w, int M, int N, int K, int mode, float* C,
                 long long ldc, __nv_bfloat16* out_hi, __nv_bfloat16* out_lo, long long ldo, GemmPlan plan,
-                float* part, size_t part_floats) {
+                float* part, size_t part_floats, const GemmEpi* epi) {
     SA_CHECK_ARG(M > 0 && N > 0 && K > 0 && K % gm::BK == 0, "gemm: M=%d N=%d K=%d", M, N, K);
     SA_CHECK_ARG(plan.bn == 64 || plan.bn == 128 || plan.bn == 256, "gemm: tile width %d", plan.bn);
     SA_CHECK_ARG(plan.splits >= 1 && plan.splits <= gm::MAX_SPLIT && plan.splits <= K / gm::BK,
@@ -392,12 +550,28 @@ int gemm_launch(cudaStream_t st, int* status, const __nv_bfloat16* a_hi, const _
     if (split) {
         SA_CHECK_ARG(part && ((uintptr_t)part & 15) == 0 && (size_t)plan.splits * M * N <= part_floats && N % 4 == 0,
                      "gemm: partial planes too small (%d x %d x %d)", plan.splits, M, N);
+        SA_CHECK_ARG(!epi || (!epi->rowsq_in && mode != QW_EPI_RESID_NORM && mode != QW_EPI_QKV_ROWS),
+                     "gemm: fused epilogues need an unsplit plan");
     } else {
         SA_CHECK_ARG(mode != QW_EPI_SWIGLU || N % plan.bn == 0, "gemm: SwiGLU needs N %% %d == 0", plan.bn);
-        SA_CHECK_ARG(mode == QW_EPI_SWIGLU
-                         ? (ldo % 4 == 0 && ((uintptr_t)out_hi & 7) == 0 && ((uintptr_t)out_lo & 7) == 0)
-                         : (C && ((uintptr_t)C & 15) == 0),
+        SA_CHECK_ARG(mode == QW_EPI_QKV_ROWS ||
+                         (mode == QW_EPI_SWIGLU
+                              ? (ldo % 4 == 0 && ((uintptr_t)out_hi & 7) == 0 && ((uintptr_t)out_lo & 7) == 0)
+                              : (C && ((uintptr_t)C & 15) == 0)),
                      "gemm: output alignment");
+        if (mode == QW_EPI_RESID_NORM)
+            SA_CHECK_ARG(epi && epi->g && epi->rowsq_out && plan.bn % 128 == 0 && N % plan.bn == 0 && ldc % 4 == 0 &&
+                             ldo % 4 == 0 && ((uintptr_t)out_hi & 7) == 0 && ((uintptr_t)out_lo & 7) == 0 &&
+                             ((uintptr_t)epi->g & 15) == 0,
+                         "gemm: RESID_NORM operands (gain, row sums, tile width %d, N %d)", plan.bn, N);
+        if (mode == QW_EPI_QKV_ROWS)
+            SA_CHECK_ARG(epi && plan.bn % 128 == 0 && N % plan.bn == 0 && N == (epi->hq + 2 * epi->hkv) * 128 &&
+                             epi->qn && epi->kn && epi->cos_t && epi->sin_t && (epi->q_out || epi->q_bf) &&
+                             (epi->kc || epi->k_bf) && (epi->vc || epi->v_bf),
+                         "gemm: QKV_ROWS operands (tile width %d, N %d)", plan.bn, N);
+        if (epi && epi->rowsq_in)
+            SA_CHECK_ARG(epi->rowsq_parts >= 1 && epi->norm_k > 0.f && mode != QW_EPI_RESID_NORM,
+                         "gemm: deferred RMSNorm operands");
     }
     const int bn = plan.bn, s = plan.splits;
     const int nt = (N + bn - 1) / bn, mt = (M + gm::BM - 1) / gm::BM;
@@ -411,6 +585,7 @@ int gemm_launch(cudaStream_t st, int* status, const __nv_bfloat16* a_hi, const _
     gm::Args a;
     a.M = M; a.N = N; a.K = K; a.mode = mode;
     a.C = C; a.ldc = ldc; a.out_hi = out_hi; a.out_lo = out_lo; a.ldo = ldo;
+    a.e = epi ? *epi : GemmEpi{};
     a.status = status;
     const void* fn = bn == 64 ? (const void*)gm::gemm_kernel<64>
                    : bn == 128 ? (const void*)gm::gemm_kernel<128> : (const void*)gm::gemm_kernel<256>;

@@ -84,7 +84,8 @@ struct Args {
     int units_per_row;          // units per heavy-first row of the schedule
     float sl2;                  // scale * log2(e)
     void* out;
-    long long o_tok, o_head;    // element strides of out
+    void* out_lo;               // bf16 output only: the rounding remainder, out_lo = bf16(o - out)
+    long long o_tok, o_head;    // element strides of out (and out_lo)
     int out_bf16;
     int* status;
 };
@@ -442,16 +443,29 @@ prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                     tc::tmem_wait_ld();
                     if (!store) continue;
                     if (a.out_bf16) {
-                        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.out) + (size_t)qrow * a.o_tok +
-                                             (size_t)h * a.o_head + cb * 32;
+                        const size_t off = (size_t)qrow * a.o_tok + (size_t)h * a.o_head + cb * 32;
+                        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.out) + off;
+                        __nv_bfloat16* dlo = a.out_lo ? static_cast<__nv_bfloat16*>(a.out_lo) + off : nullptr;
 #pragma unroll
                         for (int c = 0; c < 32; c += 8) {
+                            float f[8];
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(o[c + j]) * inv;
                             uint4 v;
-                            v.x = pack_bf16(__uint_as_float(o[c]) * inv, __uint_as_float(o[c + 1]) * inv);
-                            v.y = pack_bf16(__uint_as_float(o[c + 2]) * inv, __uint_as_float(o[c + 3]) * inv);
-                            v.z = pack_bf16(__uint_as_float(o[c + 4]) * inv, __uint_as_float(o[c + 5]) * inv);
-                            v.w = pack_bf16(__uint_as_float(o[c + 6]) * inv, __uint_as_float(o[c + 7]) * inv);
+                            v.x = pack_bf16(f[0], f[1]);
+                            v.y = pack_bf16(f[2], f[3]);
+                            v.z = pack_bf16(f[4], f[5]);
+                            v.w = pack_bf16(f[6], f[7]);
                             *reinterpret_cast<uint4*>(dst + c) = v;
+                            if (dlo) {   // remainders after the bf16 rounding above
+                                const uint32_t hv[4] = {v.x, v.y, v.z, v.w};
+                                uint32_t lv[4];
+#pragma unroll
+                                for (int j = 0; j < 4; ++j)
+                                    lv[j] = pack_bf16(f[2 * j] - __uint_as_float(hv[j] << 16),
+                                                      f[2 * j + 1] - __uint_as_float(hv[j] & 0xffff0000u));
+                                *reinterpret_cast<uint4*>(dlo + c) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+                            }
                         }
                     } else {
                         float* dst = static_cast<float*>(a.out) + (size_t)qrow * a.o_tok + (size_t)h * a.o_head +
@@ -482,7 +496,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
 //   out [Sq,  o_tok stride,  hq heads of 128]   fp32 or bf16
 int prefill_launch(cudaStream_t st, int* status, const void* q, const void* k, const void* v, void* out,
                    int out_dtype, int Sq, int Skv, int q_pos0, int hq, int hkv, long long q_tok, long long kv_tok,
-                   long long o_tok, float scale) {
+                   long long o_tok, float scale, void* out_lo) {
     CUtensorMap mq, mk, mv;
     int rc = make_tmap_2d_bf16(&mq, q, (uint64_t)Sq, (uint64_t)hq * pf::D, (uint64_t)q_tok, pf::BM, 64);
     if (!rc) rc = make_tmap_2d_bf16(&mk, k, (uint64_t)Skv, (uint64_t)hkv * pf::D, (uint64_t)kv_tok, pf::BN, 64);
@@ -497,6 +511,7 @@ int prefill_launch(cudaStream_t st, int* status, const void* q, const void* k, c
     a.sl2 = scale * pf::LOG2E;
     a.out = out; a.o_tok = o_tok; a.o_head = pf::D;
     a.out_bf16 = out_dtype == SA_BF16;
+    a.out_lo = a.out_bf16 ? out_lo : nullptr;
     a.status = status;
     // All exponentials on the SFU: with 128-key tiles the softmax is issue-bound,
     // and moving every 8th/4th/3rd exponential to exp2_poly measured 3%/5%/9%

@@ -70,6 +70,7 @@ struct sa_qwen3 {
     int logits_rows = 0;
     int64_t* ids = nullptr;              // [M]
     float* gemm_ws = nullptr;            // split-K partial planes of the prompt GEMMs
+    float* rowsq = nullptr;              // [H / 128 + 1][M] row sums of x^2 per GEMM tile (deferred RMSNorm)
     size_t gemm_ws_floats = 0;
     // streams: `cur` is where launches go (the context's stream, or the
     // model's own capturable stream inside graph-using calls)
@@ -167,7 +168,7 @@ static void free_model(sa_qwen3* m) {
     }
     cudaFree(m->kc); cudaFree(m->vc); cudaFree(m->cos_t); cudaFree(m->sin_t);
     cudaFree(m->x); cudaFree(m->qkv); cudaFree(m->q); cudaFree(m->attn); cudaFree(m->act); cudaFree(m->xn);
-    cudaFree(m->a_hi); cudaFree(m->a_lo); cudaFree(m->b_hi); cudaFree(m->b_lo);
+    cudaFree(m->a_hi); cudaFree(m->a_lo); cudaFree(m->b_hi); cudaFree(m->b_lo); cudaFree(m->rowsq);
     cudaFree(m->logits); cudaFree(m->ids); cudaFree(m->gemm_ws);
     cudaFree(m->d_state); cudaFree(m->d_toks); cudaFree(m->dec_scratch); cudaFree(m->dec_cnt); cudaFree(m->d_amax);
     cudaFree(m->d_mlayers); cudaFree(m->mpart); cudaFree(m->mhead_cnt); cudaFree(m->mgbar);
@@ -207,7 +208,9 @@ static int ensure_acts(sa_qwen3* m, int M) {
     cudaFree(m->x); cudaFree(m->qkv); cudaFree(m->q); cudaFree(m->attn); cudaFree(m->act); cudaFree(m->xn);
     cudaFree(m->a_hi); cudaFree(m->a_lo); cudaFree(m->b_hi); cudaFree(m->b_lo); cudaFree(m->ids);
     cudaFree(m->tp_part);
+    cudaFree(m->rowsq);
     m->tp_part = nullptr;
+    m->rowsq = nullptr;
     const sa_qwen3_config& c = m->c;
     const size_t wmax = (size_t)std::max(std::max(m->QD, m->inter), c.hidden);
     int rc = SA_OK;
@@ -223,6 +226,7 @@ static int ensure_acts(sa_qwen3* m, int M) {
     if (!rc) rc = dalloc(&m->b_hi, (size_t)M * wmax);
     if (!rc) rc = dalloc(&m->b_lo, (size_t)M * wmax);
     if (!rc) rc = dalloc(&m->ids, (size_t)M);
+    if (!rc) rc = dalloc(&m->rowsq, (size_t)M * (c.hidden / 128 + 1));
     if (rc) { m->cap_m = 0; return rc; }
     m->cap_m = M;
     return SA_OK;
@@ -246,8 +250,11 @@ static int ensure_logits(sa_qwen3* m, int rows) {
 // count; otherwise `mode` is applied and *splits is 1.
 static int gemm(sa_qwen3* m, const __nv_bfloat16* hi, const __nv_bfloat16* lo, long long lda,
                 const __nv_bfloat16* w, int M, int N, int K, int mode, float* C, long long ldc,
-                __nv_bfloat16* ohi, __nv_bfloat16* olo, long long ldo, bool split_ok = false, int* splits = nullptr) {
-    const GemmPlan plan = gemm_plan(m->ctx->device, m->ctx->num_sms, M, N, K, split_ok && splits);
+                __nv_bfloat16* ohi, __nv_bfloat16* olo, long long ldo, bool split_ok = false, int* splits = nullptr,
+                const GemmEpi* epi = nullptr) {
+    // fused epilogues: the plan run_layers chose them by (it must be unsplit)
+    const GemmPlan plan = gemm_plan(m->ctx->device, m->ctx->num_sms, M, N, K, (split_ok && splits) || epi);
+    if (epi && plan.splits != 1) return set_error(SA_ERR_ARG, "gemm: fused epilogue on a split plan");
     const size_t need = plan.splits > 1 ? (size_t)plan.splits * M * N : 0;
     if (need > m->gemm_ws_floats) {
         // grow-only; graphs captured with the old buffer are dropped
@@ -262,7 +269,7 @@ static int gemm(sa_qwen3* m, const __nv_bfloat16* hi, const __nv_bfloat16* lo, l
     }
     if (splits) *splits = plan.splits;
     return gemm_launch(m->cur, m->ctx->status, hi, lo, lda, w, M, N, K, mode, C, ldc, ohi, olo, ldo, plan,
-                       m->gemm_ws, m->gemm_ws_floats);
+                       m->gemm_ws, m->gemm_ws_floats, epi);
 }
 
 #define SA_RC(expr) do { int rc_ = (expr); if (rc_) return rc_; } while (0)
@@ -367,6 +374,30 @@ static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr
     float* xo = m->tp_x2;
     SA_RC(launch_embedding(st, m->ids, M, m->embed, c.vocab, H, m->x, m->ctx->status));
     int resid = 0;   // partial planes of the last down_proj not yet added to x
+    // Prompt path, one GPU or sequence-parallel: unsplit GEMMs take the fused
+    // epilogues (GemmEpi).  QKV with QK-norm + RoPE + cache append
+    // (fuse_qkv); an unsplit o_proj / down_proj whose consumer is unsplit
+    // too writes the consumer's A operand with its RMSNorm deferred
+    // (defer_gu: o_proj -> gate/up, defer_qkv: down_proj -> the next QKV).
+    // The plans are those gemm() picks for these shapes.
+    bool fuse_qkv = false, defer_gu = false, defer_qkv = false;
+    int parts_o = 0, parts_d = 0;
+    if (M > 1 && !tp && D == 128) {
+        const int dev = m->ctx->device, sms = m->ctx->num_sms;
+        const GemmPlan pq = gemm_plan(dev, sms, M, m->NQKV, H, true), po = gemm_plan(dev, sms, M, H, m->QD, true);
+        const GemmPlan pg = gemm_plan(dev, sms, M, 2 * I, H, true), pd = gemm_plan(dev, sms, M, H, I, true);
+        fuse_qkv = pq.splits == 1 && pq.bn % 128 == 0 && m->NQKV % pq.bn == 0;
+        defer_gu = po.splits == 1 && po.bn % 128 == 0 && H % po.bn == 0 && pg.splits == 1;
+        defer_qkv = fuse_qkv && pd.splits == 1 && pd.bn % 128 == 0 && H % pd.bn == 0;
+        parts_o = H / po.bn;
+        parts_d = H / pd.bn;
+    }
+    const bool tc_attn = M > 1 && M >= tc_attn_min_rows();
+    const bool tc_direct = fuse_qkv && tc_attn && !sp;   // the QKV epilogue writes the bf16 operands
+    // bf16 hi/lo activation buffers: `qkv_in` holds the QKV GEMM's A operand
+    // (RMSNorm'd x, or hi/lo(g . x) after a deferred down_proj); the
+    // attention output goes to a; a GEMM never writes the buffer it reads.
+    __nv_bfloat16 *qkv_hi = m->a_hi, *qkv_lo = m->a_lo;
     for (int l = 0; l < c.n_layers; ++l) {
         const sa_qwen3::Layer& L = m->layers[l];
         float* kc = m->kc + l * layer_kv;
@@ -414,16 +445,42 @@ static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr
         } else {
             // split GEMMs leave partial planes (m->gemm_ws) that the next
             // kernel adds: `resid` counts the planes of a pending residual add
+            const bool deferred_in = defer_qkv && l > 0;   // qkv_in = hi/lo(in_norm . x), rows unscaled
             if (tp && l > 0)
                 SA_RC(launch_rmsnorm_hilo_tp(st, m->x, L.in_norm, M, H, c.eps, m->a_hi, m->a_lo, tp_args(m, 2 * l - 1)));
-            else
+            else if (!deferred_in)
                 SA_RC(launch_rmsnorm_hilo(st, m->x, L.in_norm, M, H, c.eps, m->a_hi, m->a_lo, m->gemm_ws, resid));
+            if (!deferred_in) {
+                qkv_hi = m->a_hi;
+                qkv_lo = m->a_lo;
+            }
             resid = 0;
-            int sq = 1;
-            SA_RC(gemm(m, m->a_hi, m->a_lo, H, L.wqkv, M, m->NQKV, H, QW_EPI_STORE, m->qkv, m->NQKV, nullptr, nullptr, 0,
-                       true, &sq));
-            SA_RC(launch_qknorm_rope_append(st, sq > 1 ? m->gemm_ws : m->qkv, sq, M, m->hq, m->hkv, L.q_norm, L.k_norm,
-                                            m->cos_t, m->sin_t, pos0, nullptr, shift, m->q, kc, vc, c.max_seq));
+            if (fuse_qkv) {
+                GemmEpi e;
+                if (deferred_in) {
+                    e.rowsq_in = m->rowsq;
+                    e.rowsq_parts = parts_d;
+                    e.norm_k = (float)H;
+                    e.eps = c.eps;
+                }
+                e.hq = m->hq; e.hkv = m->hkv; e.max_seq = c.max_seq; e.pos0 = pos0; e.row_shift = shift;
+                e.qn = L.q_norm; e.kn = L.k_norm; e.cos_t = m->cos_t; e.sin_t = m->sin_t;
+                e.kc = kc; e.vc = vc;
+                if (tc_direct) {
+                    e.q_bf = m->tc_q; e.k_bf = m->tc_k; e.v_bf = m->tc_v;
+                } else {
+                    e.q_out = m->q;
+                }
+                SA_RC(gemm(m, qkv_hi, qkv_lo, H, L.wqkv, M, m->NQKV, H, QW_EPI_QKV_ROWS, nullptr, 0, nullptr, nullptr,
+                           0, false, nullptr, &e));
+            } else {
+                int sq = 1;
+                SA_RC(gemm(m, qkv_hi, qkv_lo, H, L.wqkv, M, m->NQKV, H, QW_EPI_STORE, m->qkv, m->NQKV, nullptr, nullptr,
+                           0, true, &sq));
+                SA_RC(launch_qknorm_rope_append(st, sq > 1 ? m->gemm_ws : m->qkv, sq, M, m->hq, m->hkv, L.q_norm,
+                                                L.k_norm, m->cos_t, m->sin_t, pos0, nullptr, shift, m->q, kc, vc,
+                                                c.max_seq));
+            }
             if (sp) {
                 SpCopy cp;
                 cp.nreg = 2;
@@ -440,25 +497,39 @@ static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr
                 SA_RC(launch_sp_rows_scatter(st, cp, sp_args(m, l), m->ctx->num_sms));
                 SA_RC(launch_sp_wait(st, sp_args(m, l)));
             }
-            if (M >= tc_attn_min_rows()) {
-                // rows [0, pos0 + M) of the attention view as bf16 operands, the
-                // causal prefill on the tensor cores, its output as hi/lo planes
+            if (tc_attn) {
+                // rows [0, pos0 + M) of the attention view as bf16 operands
+                // (only the cached prefix when the QKV epilogue wrote the
+                // new rows), the causal prefill on the tensor cores with its
+                // output as the o_proj GEMM's hi/lo planes
                 const int T = pos0 + M;
-                SA_RC(launch_tc_pack(st, m->q, M, m->QD, ka, va, c.max_seq, m->hkv, T, m->tc_q, m->tc_k, m->tc_v,
-                                     m->ctx->num_sms));
-                SA_RC(prefill_launch(st, m->ctx->status, m->tc_q, m->tc_k, m->tc_v, m->attn, SA_F32, M, T, pos0,
-                                     m->hq, m->hkv, m->QD, m->KD, m->QD, scale));
-                SA_RC(launch_hilo_split(st, m->attn, (long long)M * m->QD, m->a_hi, m->a_lo, m->ctx->num_sms));
+                if (!tc_direct)
+                    SA_RC(launch_tc_pack(st, m->q, M, m->QD, ka, va, c.max_seq, m->hkv, T, m->tc_q, m->tc_k, m->tc_v,
+                                         m->ctx->num_sms));
+                else if (pos0 > 0)
+                    SA_RC(launch_tc_pack(st, nullptr, 0, m->QD, ka, va, c.max_seq, m->hkv, pos0, m->tc_q, m->tc_k,
+                                         m->tc_v, m->ctx->num_sms));
+                SA_RC(prefill_launch(st, m->ctx->status, m->tc_q, m->tc_k, m->tc_v, m->a_hi, SA_BF16, M, T, pos0,
+                                     m->hq, m->hkv, m->QD, m->KD, m->QD, scale, m->a_lo));
             } else {
                 SA_RC(prompt_attn_launch(st, m->ctx->status, m->q, m->QD, ka, va, (long long)c.max_seq * D,
                                          (long long)m->hkv * c.max_seq - shift, pos0 + 1, M, D, m->hq, m->hkv, scale,
                                          nullptr, m->QD, m->a_hi, m->a_lo));
             }
+            // gate/up reads gu_in and writes the SwiGLU output to gu_out
+            __nv_bfloat16 *gu_in_hi = m->a_hi, *gu_in_lo = m->a_lo, *gu_out_hi = m->b_hi, *gu_out_lo = m->b_lo;
             if (tp) {
                 SA_RC(gemm(m, m->a_hi, m->a_lo, m->QD, L.wo, M, H, m->QD, QW_EPI_STORE, m->tp_part, H, nullptr, nullptr,
                            0));
                 SA_RC(launch_tp_scatter(st, m->tp_part, M, H, tp_args(m, 2 * l), m->ctx->num_sms));
                 SA_RC(launch_rmsnorm_hilo_tp(st, m->x, L.post_norm, M, H, c.eps, m->a_hi, m->a_lo, tp_args(m, 2 * l)));
+            } else if (defer_gu) {
+                GemmEpi e;
+                e.g = L.post_norm;
+                e.rowsq_out = m->rowsq;
+                SA_RC(gemm(m, m->a_hi, m->a_lo, m->QD, L.wo, M, H, m->QD, QW_EPI_RESID_NORM, m->x, H, m->b_hi, m->b_lo,
+                           H, false, nullptr, &e));
+                gu_in_hi = m->b_hi; gu_in_lo = m->b_lo; gu_out_hi = m->a_hi; gu_out_lo = m->a_lo;
             } else {
                 int so = 1;
                 SA_RC(gemm(m, m->a_hi, m->a_lo, m->QD, L.wo, M, H, m->QD, QW_EPI_RESID, m->x, H, nullptr, nullptr, 0,
@@ -467,15 +538,36 @@ static int run_layers(sa_qwen3* m, int M, int pos0, const int* pos_dev = nullptr
                                           so > 1 ? so : 0));
             }
             int sg = 1;
-            SA_RC(gemm(m, m->a_hi, m->a_lo, H, L.wgu, M, 2 * I, H, QW_EPI_SWIGLU, nullptr, 0, m->b_hi, m->b_lo, I, true,
-                       &sg));
-            if (sg > 1) SA_RC(launch_swiglu_hilo(st, m->gemm_ws, sg, M, I, m->b_hi, m->b_lo, I, m->ctx->num_sms));
+            if (defer_gu) {
+                GemmEpi e;
+                e.rowsq_in = m->rowsq;
+                e.rowsq_parts = parts_o;
+                e.norm_k = (float)H;
+                e.eps = c.eps;
+                SA_RC(gemm(m, gu_in_hi, gu_in_lo, H, L.wgu, M, 2 * I, H, QW_EPI_SWIGLU, nullptr, 0, gu_out_hi, gu_out_lo,
+                           I, false, nullptr, &e));
+            } else {
+                SA_RC(gemm(m, gu_in_hi, gu_in_lo, H, L.wgu, M, 2 * I, H, QW_EPI_SWIGLU, nullptr, 0, gu_out_hi, gu_out_lo,
+                           I, true, &sg));
+            }
+            if (sg > 1) SA_RC(launch_swiglu_hilo(st, m->gemm_ws, sg, M, I, gu_out_hi, gu_out_lo, I, m->ctx->num_sms));
             if (tp) {
-                SA_RC(gemm(m, m->b_hi, m->b_lo, I, L.wd, M, H, I, QW_EPI_STORE, m->tp_part, H, nullptr, nullptr, 0));
+                SA_RC(gemm(m, gu_out_hi, gu_out_lo, I, L.wd, M, H, I, QW_EPI_STORE, m->tp_part, H, nullptr, nullptr, 0));
                 SA_RC(launch_tp_scatter(st, m->tp_part, M, H, tp_args(m, 2 * l + 1), m->ctx->num_sms));
+            } else if (defer_qkv && l + 1 < c.n_layers) {
+                // the next layer's QKV A operand, in whichever buffer this
+                // GEMM does not read
+                GemmEpi e;
+                e.g = m->layers[l + 1].in_norm;
+                e.rowsq_out = m->rowsq;
+                qkv_hi = gu_out_hi == m->a_hi ? m->b_hi : m->a_hi;
+                qkv_lo = gu_out_hi == m->a_hi ? m->b_lo : m->a_lo;
+                SA_RC(gemm(m, gu_out_hi, gu_out_lo, I, L.wd, M, H, I, QW_EPI_RESID_NORM, m->x, H, qkv_hi, qkv_lo, H,
+                           false, nullptr, &e));
             } else {
                 int sd = 1;
-                SA_RC(gemm(m, m->b_hi, m->b_lo, I, L.wd, M, H, I, QW_EPI_RESID, m->x, H, nullptr, nullptr, 0, true, &sd));
+                SA_RC(gemm(m, gu_out_hi, gu_out_lo, I, L.wd, M, H, I, QW_EPI_RESID, m->x, H, nullptr, nullptr, 0, true,
+                           &sd));
                 resid = sd > 1 ? sd : 0;
             }
         }

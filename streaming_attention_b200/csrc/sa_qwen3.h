@@ -11,6 +11,9 @@
 #define QW_EPI_SWIGLU 2   // y_i = silu(g_i) * u_i over [gate(32); up(32)] row blocks
 #define QW_EPI_QKV    3   // decode QKV projection + QK-norm + RoPE + KV-cache append (head_dim 128)
 #define QW_EPI_XCHG   4   // partial sums sent to every rank's receive block (head-parallel)
+#define QW_EPI_RESID_NORM 5   // prompt GEMM: C += acc, then the next GEMM's A operand hi/lo(g . C)
+                              // and per-tile row sums of C^2 (its RMSNorm, deferred)
+#define QW_EPI_QKV_ROWS   6   // prompt GEMM: QK-norm + RoPE + KV-cache append of whole heads
 
 namespace sa {
 
@@ -29,6 +32,32 @@ struct QkvEpi {
 struct GemmPlan {
     int bn, splits;
 };
+
+// Optional epilogue operands of an unsplit prompt GEMM (gemm_launch).
+//
+// Deferred RMSNorm: RMSNorm(x) W^T = diag(1 / rms(x)) (g . x) W^T, so the
+// producer of x (a QW_EPI_RESID_NORM GEMM) writes A = hi/lo(g . x) and, per
+// output tile p, rowsq[p * M + r] = sum of x[r, :]^2 over the tile's columns;
+// the consumer multiplies row r of its accumulator by
+// 1 / sqrt(sum_p rowsq[p * M + r] / norm_k + eps) (parts added in order)
+// before its own epilogue.  rowsq_in == nullptr: A is already normalised.
+//
+// QW_EPI_QKV_ROWS (tile width a multiple of 128, so tiles hold whole heads):
+// token m at RoPE position pos0 + m; Q heads -> QK-norm + RoPE -> q_out
+// (fp32 [M, hq, 128]) and/or q_bf (bf16, same layout); K heads -> QK-norm +
+// RoPE -> K cache row (pos0 + m + row_shift) of kc and/or bf16 row pos0 + m
+// of k_bf ([rows, hkv, 128]); V heads -> vc / v_bf likewise.
+struct GemmEpi {
+    const float* rowsq_in = nullptr;
+    int rowsq_parts = 0;
+    float norm_k = 0.f, eps = 0.f;
+    const float* g = nullptr;      // RESID_NORM: gain of the next GEMM's RMSNorm [N]
+    float* rowsq_out = nullptr;    // RESID_NORM: [N / bn][M]
+    int hq = 0, hkv = 0, max_seq = 0, pos0 = 0, row_shift = 0;
+    const float *qn = nullptr, *kn = nullptr, *cos_t = nullptr, *sin_t = nullptr;
+    float *q_out = nullptr, *kc = nullptr, *vc = nullptr;
+    __nv_bfloat16 *q_bf = nullptr, *k_bf = nullptr, *v_bf = nullptr;
+};
 // Occupancy queries of the GEMM variants, once per device; call before any
 // stream capture.
 void gemm_prepare(int device);
@@ -41,7 +70,7 @@ GemmPlan gemm_plan(int device, int num_sms, int M, int N, int K, bool split_ok);
 int gemm_launch(cudaStream_t st, int* status, const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo,
                 long long lda, const __nv_bfloat16* w, int M, int N, int K, int mode, float* C,
                 long long ldc, __nv_bfloat16* out_hi, __nv_bfloat16* out_lo, long long ldo, GemmPlan plan,
-                float* part, size_t part_floats);
+                float* part, size_t part_floats, const GemmEpi* epi = nullptr);
 
 
 // Causal attention of M prompt queries (q at q + m*q_stride, [hq, 128]) over
@@ -139,16 +168,17 @@ struct SpCopy {
 int launch_sp_rows_scatter(cudaStream_t st, const SpCopy& c, const TpArgs& tp, int grid);
 // Long prompts' attention on the tensor cores: q [M, QD] fp32 -> bf16 (same
 // layout), and rows [0, T) of the fp32 head-major K/V cache view (head h at
-// h * max_seq rows) -> bf16 token-major [T, hkv, 128] for K and V; then the
-// tcgen05 causal prefill (sa_prefill.cu); then its fp32 output split into
-// the o_proj GEMM's bf16 hi/lo planes.
+// h * max_seq rows) -> bf16 token-major [T, hkv, 128] for K and V (M = 0,
+// q = nullptr: K and V only, e.g. the cached prefix when the QKV GEMM's
+// epilogue wrote the new rows); then the tcgen05 causal prefill
+// (sa_prefill.cu), which writes the o_proj GEMM's bf16 hi/lo planes.
 int launch_tc_pack(cudaStream_t st, const float* q, int M, int QD, const float* kc, const float* vc, int max_seq,
                    int hkv, int T, __nv_bfloat16* qb, __nv_bfloat16* kb, __nv_bfloat16* vb, int num_sms);
-int launch_hilo_split(cudaStream_t st, const float* x, long long n, __nv_bfloat16* hi, __nv_bfloat16* lo,
-                      int num_sms);
+// out_lo != nullptr (with out_dtype SA_BF16): the output as two bf16 planes,
+// out = bf16(o) and out_lo = bf16(o - out), the next GEMM's A operand.
 int prefill_launch(cudaStream_t st, int* status, const void* q, const void* k, const void* v, void* out,
                    int out_dtype, int Sq, int Skv, int q_pos0, int hq, int hkv, long long q_tok, long long kv_tok,
-                   long long o_tok, float scale);
+                   long long o_tok, float scale, void* out_lo = nullptr);
 int launch_sp_wait(cudaStream_t st, const TpArgs& tp);
 
 // Model allocation for rank `rank` of `world` (sa_qwen3.cu).

@@ -12,6 +12,7 @@
 #include "sa_internal.h"
 #include "sa_ptx.cuh"
 #include "sa_qwen3.h"
+#include "sa_qwen3_dev.cuh"
 #include <algorithm>
 
 namespace sa {
@@ -19,11 +20,8 @@ namespace qk {
 
 constexpr int QK_MAX_PLANES = 8;   // split-K planes a consumer adds (the GEMM's largest split)
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
+using qd::warp_sum;
+using qd::head_norm_rope;
 
 // Block-wide sum for blockDim.x <= 1024; `red` holds 32 floats.
 __device__ __forceinline__ float block_sum(float v, float* red) {
@@ -193,33 +191,6 @@ __global__ void rope_table_kernel(int n_pos, int D, float theta, float* cos_t, f
 // times q_norm, then rotate-half RoPE at position pos0 + m
 // (qwen3_ops.cpp:110-188) -> q_out [M, hq, 128].  K heads: the same with
 // k_norm -> K cache row pos0 + m.  V heads: copied to the V cache.
-// RMS-normalise one 128-wide head held by a warp (lane l: elements 4l..4l+3)
-// with gain nw, then rotate-half RoPE with the position's cos/sin rows.
-__device__ __forceinline__ float4 head_norm_rope(const float (&e_in)[4], const float* nw, const float* cr,
-                                                 const float* sr, int lane) {
-    constexpr int D = 128;
-    float e[4] = {e_in[0], e_in[1], e_in[2], e_in[3]};
-    float ss = e[0] * e[0] + e[1] * e[1] + e[2] * e[2] + e[3] * e[3];
-    ss = warp_sum(ss);
-    const float rms = sqrtf(ss / (float)D + 1e-6f);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) e[j] = (e[j] / rms) * nw[4 * lane + j];
-    // rotate-half: element i pairs with i + 64 (lanes l and l ^ 16)
-    float p[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) p[j] = __shfl_xor_sync(0xffffffffu, e[j], 16);
-    const bool first = lane < 16;
-    float o[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int i = (4 * lane + j) & (D / 2 - 1);
-        const float c = cr[i], s = sr[i];
-        // first half: x1*c + (-x2)*s ; second half: x2*c + x1*s
-        o[j] = first ? e[j] * c + (-p[j]) * s : e[j] * c + p[j] * s;
-    }
-    return make_float4(o[0], o[1], o[2], o[3]);
-}
-
 // qkv holds `splits` planes of `plane` floats (split-K partial sums of the
 // QKV GEMM, added here in plane order) or the finished projection (splits 1).
 __global__ void qknorm_rope_append_kernel(const float* qkv, int splits, size_t plane, int M, int hq, int hkv,
@@ -777,24 +748,6 @@ __global__ void tc_pack_kernel(const float* __restrict__ q, long long nq8, const
     }
 }
 
-// x = hi + lo with hi = bf16(x), lo = bf16(x - hi), 8 values per step.
-__global__ void hilo_split_kernel(const float* __restrict__ x, long long n8, __nv_bfloat16* hi, __nv_bfloat16* lo) {
-    pdl_trigger();
-    pdl_wait();
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
-        const float4 a = __ldcg(reinterpret_cast<const float4*>(x + i * 8));
-        const float4 b = __ldcg(reinterpret_cast<const float4*>(x + i * 8) + 1);
-        const uint4 h = pack8_bf16(a, b);
-        const __nv_bfloat162* hp = reinterpret_cast<const __nv_bfloat162*>(&h);
-        const float2 h0 = __bfloat1622float2(hp[0]), h1 = __bfloat1622float2(hp[1]);
-        const float2 h2 = __bfloat1622float2(hp[2]), h3 = __bfloat1622float2(hp[3]);
-        const float4 la = make_float4(a.x - h0.x, a.y - h0.y, a.z - h1.x, a.w - h1.y);
-        const float4 lb = make_float4(b.x - h2.x, b.y - h2.y, b.z - h3.x, b.w - h3.y);
-        *reinterpret_cast<uint4*>(hi + i * 8) = h;
-        *reinterpret_cast<uint4*>(lo + i * 8) = pack8_bf16(la, lb);
-    }
-}
-
 // Wait (bounded) until every rank published this instance.
 __global__ void sp_wait_kernel(const TpArgs tp) {
     pdl_trigger();
@@ -992,15 +945,10 @@ int launch_sp_rows_scatter(cudaStream_t st, const SpCopy& c, const TpArgs& tp, i
 }
 int launch_tc_pack(cudaStream_t st, const float* q, int M, int QD, const float* kc, const float* vc, int max_seq,
                    int hkv, int T, __nv_bfloat16* qb, __nv_bfloat16* kb, __nv_bfloat16* vb, int num_sms) {
-    SA_CHECK_ARG(M >= 1 && QD % 8 == 0 && T >= 1 && T <= max_seq && hkv >= 1, "tc_pack: M=%d QD=%d T=%d", M, QD, T);
+    SA_CHECK_ARG(M >= 0 && (M == 0 || q) && QD % 8 == 0 && T >= 1 && T <= max_seq && hkv >= 1,
+                 "tc_pack: M=%d QD=%d T=%d", M, QD, T);
     SA_CUDA_TRY(launch_pdl_k(4, qk::tc_pack_kernel, dim3(4 * num_sms), dim3(256), 0, st, q, (long long)M * QD / 8, kc,
                              vc, max_seq, hkv, T, qb, kb, vb));
-    return SA_OK;
-}
-int launch_hilo_split(cudaStream_t st, const float* x, long long n, __nv_bfloat16* hi, __nv_bfloat16* lo,
-                      int num_sms) {
-    SA_CHECK_ARG(n % 8 == 0, "hilo_split: n=%lld", n);
-    SA_CUDA_TRY(launch_pdl_k(4, qk::hilo_split_kernel, dim3(4 * num_sms), dim3(256), 0, st, x, n / 8, hi, lo));
     return SA_OK;
 }
 int launch_sp_wait(cudaStream_t st, const TpArgs& tp) {

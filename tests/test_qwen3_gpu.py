@@ -147,6 +147,77 @@ def test_qwen3_prompt_tensor_core_attention(ctx, oracle, hq, hkv, S, cached):
     assert [int(t) for t in toks] == want
 
 
+# The 0.6B layer shapes (hidden 1024, 16 / 8 heads, intermediate 3072) at a
+# prompt long enough that all four projections run unsplit, so every fused
+# GEMM epilogue runs: QKV with QK-norm + RoPE + cache append, o_proj and
+# down_proj writing the next GEMM's operand with its RMSNorm deferred, gate/up
+# and QKV scaling their rows by 1 / rms.
+FUSED_CFG = dict(vocab=2000, hidden=1024, n_layers=2, hq=16, hkv=8, head_dim=128, inter=3072, eps=1e-6, theta=1e6)
+FUSED_S = 3500
+
+_FUSED_SCRIPT = """
+import sys, numpy as np
+sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[1] + "/tests")
+import _inputs as I
+from oracle.oracle import Qwen3Cfg, make_qwen3_weights
+from streaming_attention_b200 import Context, Qwen3
+cfg = dict(%s)
+w = make_qwen3_weights(Qwen3Cfg(**cfg), 71)
+ids = I.rng(%d).integers(0, cfg["vocab"], %d)
+ctx = Context(0)
+m = Qwen3(cfg, max_seq=%d + 16, ctx=ctx)
+m.load(w)
+np.save(sys.argv[2], m.forward(ids, logits="all"))
+m.close(); ctx.close()
+"""
+
+
+def _fused_ref(oracle):
+    cfg = Qwen3Cfg(**FUSED_CFG)
+    w = make_qwen3_weights(cfg, 71)
+    ids = I.rng(FUSED_S).integers(0, cfg.vocab, FUSED_S)
+    return cfg, w, ids
+
+
+def test_qwen3_fused_epilogues_fp32_attention(oracle, tmp_path):
+    """Fused prompt GEMM epilogues with the fp32 prompt attention (the
+    tensor-core crossover raised past the prompt, in a child process since
+    the crossover is read once per process): every position's logits within
+    the fp32 bar (2e-3 of max |logit|)."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    cfg_src = ", ".join(f"{k}={v!r}" for k, v in FUSED_CFG.items())
+    out = tmp_path / "logits.npy"
+    env = dict(os.environ, SA_QWEN3_TC_ATTN_MIN="1000000")
+    r = subprocess.run([sys.executable, "-c", _FUSED_SCRIPT % (cfg_src, FUSED_S, FUSED_S, FUSED_S), root, str(out)],
+                       env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    cfg, w, ids = _fused_ref(oracle)
+    ref = oracle.qwen3_forward(cfg, w, ids, all_logits=True)
+    got = np.load(out)
+    for r0 in range(0, FUSED_S, 500):
+        _close(got[r0:r0 + 500], ref[r0:r0 + 500], f"fused epilogues, fp32 attention, rows {r0}..")
+
+
+def test_qwen3_fused_epilogues_tensor_core_attention(ctx, oracle):
+    """The same prompt with its attention on the tensor cores (q / K / V
+    written in bf16 by the QKV epilogue, the output as the o_proj operand's
+    hi / lo planes): logits within the bf16 bar, then greedy tokens equal to
+    the oracle's."""
+    from streaming_attention_b200 import Qwen3
+    cfg, w, ids = _fused_ref(oracle)
+    S, n_new = FUSED_S, 4
+    m = Qwen3(FUSED_CFG, max_seq=S + 16, ctx=ctx)
+    m.load(w)
+    ref = oracle.qwen3_forward(cfg, w, ids, all_logits=True)
+    _close(m.forward(ids, logits="all"), ref, "fused epilogues, tensor-core attention", REL_BF16)
+    ref_toks, gaps, _ = _oracle_greedy(oracle, cfg, w, ids, n_new, S + 16)
+    _same_tokens(m.generate(ids, n_new), ref_toks, gaps, "fused epilogues, 4 new tokens")
+    m.close()
+
+
 def test_qwen3_long_prefix_continuation(ctx, oracle):
     """A 40-token prompt continued after 300 cached tokens: its attention runs
     over several 128-row rounds of the cache."""
