@@ -681,14 +681,16 @@ def run_prefill_reference(args):
 
 
 def run_prefill_sp(args):
-    """configs[2] on N GPUs: zig-zag sequence-parallel causal prefill (each rank
-    two query chunks, K/V all-gathered over NCCL, no output merge).  Total work is
-    fixed (strong scaling); time = max over ranks of CUDA-event time per step."""
+    """configs[2] on N GPUs: zig-zag sequence-parallel causal prefill through
+    sa_spp_prefill (each rank two query chunks; its K/V chunks stored into every
+    rank's buffer over NVLink; one tensor-core launch over key-block pieces and
+    their log-sum-exp merge).  Total work is fixed (strong scaling); time = max
+    over ranks of CUDA-event time per step."""
     import torch
     import torch.distributed as dist
     from datetime import timedelta
     import streaming_attention_b200 as sa
-    from streaming_attention_b200.sequence_parallel import sp_prefill, zigzag_shard
+    from streaming_attention_b200.sequence_parallel import SpPrefill, zigzag_shard
     world, rank, local = env_int("WORLD_SIZE", 1), env_int("RANK", 0), env_int("LOCAL_RANK", 0)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -700,16 +702,15 @@ def run_prefill_sp(args):
     ql, kl, vl = zigzag_shard(q, rank, world), zigzag_shard(k, rank, world), zigzag_shard(v, rank, world)
     del q, k, v
     ctx = sa.Context(local)
-    streams = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
+    sp = SpPrefill(ctx, rank, world, max_seq=PF_S, hkv=PF_HKV)
+    sp.connect_dist()
+    out = torch.empty(ql.shape, dtype=torch.bfloat16, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     main = torch.cuda.Stream(dev)
 
-    def pf(qc, kc, vc, s, q_pos0, out):
-        return sa.attn_prefill(qc, kc, vc, s, q_pos0, "bfloat16", ctx, out)
-
     with torch.cuda.stream(main):
         for _ in range(args.warmup):
-            sp_prefill(ql, kl, vl, SCALE, None, pf, streams, torch.bfloat16)
+            sp.prefill(ql, kl, vl, SCALE, out)
     torch.cuda.synchronize(dev)
     dist.barrier(device_ids=[local])
     tot = 0.0
@@ -719,7 +720,7 @@ def run_prefill_sp(args):
             flush.zero_()
             dist.barrier(device_ids=[local])
             e0.record(main)
-            sp_prefill(ql, kl, vl, SCALE, None, pf, streams, torch.bfloat16)
+            sp.prefill(ql, kl, vl, SCALE, out)
             e1.record(main)
         e1.synchronize()
         tot += e0.elapsed_time(e1)
@@ -734,13 +735,16 @@ def run_prefill_sp(args):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": PF_WORKLOAD, "parallelism": f"sp{world} zig-zag (2 chunks/rank, "
-                                                             "K/V all-gather over NCCL)",
+            "config": {"workload": PF_WORKLOAD, "parallelism": f"sp{world} zig-zag (2 chunks/rank, K/V "
+                                                             "stored to every rank over NVLink, key-block "
+                                                             "pieces merged by log-sum-exp)",
                        "l2": "256 MB buffer written between timed steps"},
             "roofline": {"bound": "tensor", "achieved": round(tf / world, 2), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(tf / world / peak, 4), "per": "GPU",
                          "peak_kind": f"{kind} bf16_tflops (burst)"},
-            "gpu_launches": 2 * args.steps}), flush=True)
+            "gpu_launches": 4 * args.steps}), flush=True)
+    ctx.synchronize()
+    sp.close()
     ctx.close()
     dist.barrier(device_ids=[local])
     dist.destroy_process_group()

@@ -217,6 +217,46 @@ int sa_attn_prefill(sa_ctx* ctx, const void* q, const void* k, const void* v, in
                     long long kv_tok_stride, float scale, void* out, int out_dtype,
                     long long o_tok_stride, unsigned flags);
 
+/* ======================================================================== */
+/* Sequence-parallel causal prefill (one rank per GPU)                       */
+/* ======================================================================== */
+
+/*
+ * The causal prefill of S tokens with the sequence split over `world` ranks
+ * (1..8), one GPU each, in the load-balanced zig-zag order: the sequence is
+ * cut into 2 x world chunks of C = S / (2 world) tokens and rank r holds
+ * chunks r and 2 world - 1 - r -- the sequence strategy of
+ * attention_sequence_online_softmax (tensor_cpp/include/tensor_cpp/ops_mpi.h:326,
+ * ops_mpi.cpp:1000-1212), computing the causal attention that strategy stands
+ * for (its statistics all-reduce mixes positions).
+ *
+ * sa_spp_create: this rank's object on the context's GPU for sequences of up
+ *   to max_seq tokens with hkv KV heads of d = 128 (two K/V buffers of
+ *   max_seq x hkv x 128 bf16 each, shared with the other ranks).
+ * sa_spp_handle / sa_spp_connect / sa_spp_connect_local / sa_spp_destroy:
+ *   as the sa_sp_* functions (SA_SPP_HANDLE_BYTES per handle; one GPU per
+ *   rank, checked).
+ * sa_spp_prefill: q_local [2C, hq, 128], k_local / v_local [2C, hkv, 128]
+ *   bf16, contiguous, device memory: this rank's two chunks, chunk r first.
+ *   Each rank writes its K/V chunks into every rank's buffer over NVLink,
+ *   waits (bounded) for the others', then computes its query rows' causal
+ *   attention over the whole prefix on the tensor cores, and writes
+ *   out_local [2C, hq, 128] in out_dtype (SA_BF16 or SA_F32).  S must be a
+ *   multiple of 2 x world.  Asynchronous on the context's stream; every rank
+ *   makes the same calls in the same order.  A rank that does not take part
+ *   makes the others' waits expire after a few seconds (NaN in out_local,
+ *   SA_ERR_TIMEOUT at their next synchronising call).
+ */
+#define SA_SPP_HANDLE_BYTES 128
+typedef struct sa_spp sa_spp;
+int sa_spp_create(sa_ctx* ctx, int rank, int world, int max_seq, int hkv, int d, sa_spp** out);
+int sa_spp_handle(sa_spp* sp, void* handle);
+int sa_spp_connect(sa_spp* sp, const void* handles);
+int sa_spp_connect_local(sa_spp* const* sps, int n);
+int sa_spp_destroy(sa_spp* sp);
+int sa_spp_prefill(sa_spp* sp, const void* q_local, const void* k_local, const void* v_local, int S, int hq,
+                   int hkv, int d, float scale, void* out_local, int out_dtype, unsigned flags);
+
 /*
  * fp32 attention of Sq query rows on CUDA cores (fp32 throughout, like the
  * reference's own operators):

@@ -18,6 +18,7 @@ SA_ERR_RANGE = -6
 SA_ERR_FULL = -7
 
 SA_SP_HANDLE_BYTES = 128
+SA_SPP_HANDLE_BYTES = 128
 
 SA_F32 = 0
 SA_BF16 = 1
@@ -83,6 +84,13 @@ SIGNATURES = {
     "sa_sp_connect": (C.c_int, [_vp, _vp]),
     "sa_sp_connect_local": (C.c_int, [C.POINTER(_vp), C.c_int]),
     "sa_sp_destroy": (C.c_int, [_vp]),
+    "sa_spp_create": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]),
+    "sa_spp_handle": (C.c_int, [_vp, _vp]),
+    "sa_spp_connect": (C.c_int, [_vp, _vp]),
+    "sa_spp_connect_local": (C.c_int, [C.POINTER(_vp), C.c_int]),
+    "sa_spp_destroy": (C.c_int, [_vp]),
+    "sa_spp_prefill": (C.c_int, [_vp, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, _vp,
+                                 C.c_int, C.c_uint]),
     "sa_attn_decode_sp": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, C.c_longlong, C.c_int, C.c_int,
                                     C.c_int, C.c_int, C.c_int, C.c_float, _vp, _vp, _vp, C.c_uint]),
     "sa_attn_decode_noalloc": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, C.c_longlong, C.c_int,

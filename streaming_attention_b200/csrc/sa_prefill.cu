@@ -77,16 +77,32 @@ __device__ __forceinline__ uint32_t col_o(int x) { return 256u + (uint32_t)x * 1
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float RESCALE_THRESHOLD = 8.0f;      // log2 units
 
-struct Args {
-    int Sq, Skv, q_pos0, hq, hkv, G;
+// One launch covers up to MAX_PIECES "pieces": a block of Sq query rows
+// (rows q_row0.. of the Q tensor) against a block of Skv keys (rows kv_row0..
+// of the K/V tensors), query i seeing key j of the block when j <= q_pos0 + i.
+// A sequence-parallel rank splits its long causal key ranges into pieces of
+// similar length (so no CTA carries a whole row's keys) and merges them by
+// their log-sum-exp; a plain prefill is one piece.
+constexpr int MAX_PIECES = 24;
+struct Piece {
+    int q_row0, kv_row0;
+    int Sq, Skv, q_pos0;
     int n_qtiles;
+    int cta0;                   // first CTA of the piece
+    void* out;                  // [Sq] rows at o_tok; bf16 or fp32 (Args::out_bf16)
+    float* lse;                 // [Sq][hq] log2-domain log-sum-exp of the scaled scores, or null
+};
+
+struct Args {
+    int hq, hkv, G;
     int pair_heads;             // 1: slots are heads (h, h+1) of one q tile; 0: q tiles (2p, 2p+1) of one head
     int units_per_row;          // units per heavy-first row of the schedule
     float sl2;                  // scale * log2(e)
-    void* out;
-    void* out_lo;               // bf16 output only: the rounding remainder, out_lo = bf16(o - out)
-    long long o_tok, o_head;    // element strides of out (and out_lo)
+    void* out_lo;               // bf16 output of a one-piece launch: the rounding remainder, bf16(o - out)
+    long long o_tok, o_head;    // element strides of the outputs (and out_lo)
     int out_bf16;
+    int n_pieces;
+    Piece pc[MAX_PIECES];
     int* status;
 };
 
@@ -191,7 +207,7 @@ __device__ __forceinline__ float emit_p(const float* sc, float sl2, float nm, ui
 template <int POLY>
 __global__ void __launch_bounds__(THREADS, 1)
 prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-               const __grid_constant__ CUtensorMap tv, const Args a) {
+               const __grid_constant__ CUtensorMap tv, const __grid_constant__ Args a) {
     extern __shared__ unsigned char smem_raw[];
     // 1024-byte alignment for the 128-byte-swizzled operand tiles
     const uint32_t raw = smem_u32(smem_raw);
@@ -200,14 +216,19 @@ prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     volatile int* abort = &B->abort;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // ---- this CTA's unit: heads, first query rows and KV extent of its two slots
-    const int rowi = (int)blockIdx.x / a.units_per_row;
-    const int u = (int)blockIdx.x % a.units_per_row;
+    // ---- this CTA's piece, then its unit: heads, first query rows and KV
+    // extent of its two slots
+    int pi = 0;
+    while (pi + 1 < a.n_pieces && (int)blockIdx.x >= a.pc[pi + 1].cta0) ++pi;
+    const Piece& P = a.pc[pi];
+    const int local = (int)blockIdx.x - P.cta0;
+    const int rowi = local / a.units_per_row;
+    const int u = local % a.units_per_row;
     int head[2], q0[2], nkv[2];
     bool on[2];
     int kvh;
     if (a.pair_heads) {
-        const int qt = a.n_qtiles - 1 - rowi;                       // heavy tiles first
+        const int qt = P.n_qtiles - 1 - rowi;                       // heavy tiles first
         const int upk = a.G / 2;
         kvh = u / upk;
         head[0] = kvh * a.G + 2 * (u % upk);
@@ -215,18 +236,18 @@ prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
         q0[0] = q0[1] = qt * BM;
         on[0] = on[1] = true;
     } else {
-        const int n_pairs = (a.n_qtiles + 1) / 2;
+        const int n_pairs = (P.n_qtiles + 1) / 2;
         const int qp = n_pairs - 1 - rowi;
         head[0] = head[1] = u;
         kvh = u / a.G;
         q0[0] = 2 * qp * BM;
         q0[1] = q0[0] + BM;
         on[0] = true;
-        on[1] = q0[1] < a.Sq;
+        on[1] = q0[1] < P.Sq;
     }
     for (int x = 0; x < 2; ++x) {
-        const int last_row = min(q0[x] + BM - 1, a.Sq - 1);
-        const int last_key = min(a.Skv - 1, a.q_pos0 + last_row);
+        const int last_row = min(q0[x] + BM - 1, P.Sq - 1);
+        const int last_key = min(P.Skv - 1, P.q_pos0 + last_row);
         nkv[x] = on[x] ? last_key / BN + 1 : 0;
     }
     const int n_kv = max(nkv[0], nkv[1]);
@@ -268,8 +289,8 @@ prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
             for (int x = 0; x < 2; ++x) {
                 if (!on[x]) continue;
                 for (int kb = 0; kb < 2; ++kb)
-                    tc::tma_load_2d(sm + OFF_Q + x * TILE_BYTES + kb * BOX_BYTES, &tq, head[x] * D + kb * 64, q0[x],
-                                    &B->q_full);
+                    tc::tma_load_2d(sm + OFF_Q + x * TILE_BYTES + kb * BOX_BYTES, &tq, head[x] * D + kb * 64,
+                                    P.q_row0 + q0[x], &B->q_full);
             }
             int k_issued = 0, v_issued = 0;
             for (int j = 0; j < n_kv; ++j) {
@@ -277,14 +298,14 @@ prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                 if (j >= KST && !wait_ab(&B->k_empty[ks], ((j / KST) & 1) ^ 1, abort, a.status)) break;
                 mbar_arrive_expect_tx(&B->k_full[ks], TILE_BYTES);
                 for (int kb = 0; kb < 2; ++kb)
-                    tc::tma_load_2d(sm + OFF_K + ks * TILE_BYTES + kb * BOX_BYTES, &tk, kvh * D + kb * 64, j * BN,
-                                    &B->k_full[ks]);
+                    tc::tma_load_2d(sm + OFF_K + ks * TILE_BYTES + kb * BOX_BYTES, &tk, kvh * D + kb * 64,
+                                    P.kv_row0 + j * BN, &B->k_full[ks]);
                 k_issued = j + 1;
                 if (j >= VST && !wait_ab(&B->v_empty[vs], ((j / VST) & 1) ^ 1, abort, a.status)) break;
                 mbar_arrive_expect_tx(&B->v_full[vs], TILE_BYTES);
                 for (int kb = 0; kb < 2; ++kb)
-                    tc::tma_load_2d(sm + OFF_V + vs * TILE_BYTES + kb * BOX_BYTES, &tv, kvh * D + kb * 64, j * BN,
-                                    &B->v_full[vs]);
+                    tc::tma_load_2d(sm + OFF_V + vs * TILE_BYTES + kb * BOX_BYTES, &tv, kvh * D + kb * 64,
+                                    P.kv_row0 + j * BN, &B->v_full[vs]);
                 v_issued = j + 1;
             }
             if (*abort) {
@@ -373,7 +394,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
             const int row = quad * 32 + lane;
             const uint32_t lane_addr = tbase + ((uint32_t)(quad * 32) << 16);
             const int qrow = my_q0 + row;
-            const int limit = a.q_pos0 + qrow;          // last visible key of this row
+            const int limit = P.q_pos0 + qrow;          // last visible key of this row
             const float sl2 = a.sl2;
             float m = -INFINITY, l = 0.f;               // m in scaled log2 units
             bool ok = true;
@@ -386,10 +407,10 @@ prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                 tc::tmem_wait_ld();
                 float* sc = reinterpret_cast<float*>(u32);
                 const int k0 = j * BN;
-                if (k0 + BN - 1 > a.q_pos0 + my_q0 || k0 + BN > a.Skv) {
+                if (k0 + BN - 1 > P.q_pos0 + my_q0 || k0 + BN > P.Skv) {
 #pragma unroll
                     for (int c = 0; c < BN; ++c)
-                        if (k0 + c > limit || k0 + c >= a.Skv) sc[c] = -INFINITY;
+                        if (k0 + c > limit || k0 + c >= P.Skv) sc[c] = -INFINITY;
                 }
                 const uint32_t p_addr = lane_addr + col_p(x);
                 float alpha = 1.f, sum;
@@ -435,7 +456,8 @@ prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
             if (ok && wait_ab(&B->o_full[x], 0, abort, a.status)) {
                 tc::fence_after_sync();
                 const float inv = l > 0.f ? 1.f / l : 0.f;
-                const bool store = qrow < a.Sq;
+                const bool store = qrow < P.Sq;
+                if (store && P.lse) P.lse[(size_t)qrow * a.hq + h] = l > 0.f ? m + log2f(l) : -INFINITY;
 #pragma unroll 1
                 for (int cb = 0; cb < D / 32; ++cb) {
                     uint32_t o[32];
@@ -444,7 +466,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                     if (!store) continue;
                     if (a.out_bf16) {
                         const size_t off = (size_t)qrow * a.o_tok + (size_t)h * a.o_head + cb * 32;
-                        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.out) + off;
+                        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(P.out) + off;
                         __nv_bfloat16* dlo = a.out_lo ? static_cast<__nv_bfloat16*>(a.out_lo) + off : nullptr;
 #pragma unroll
                         for (int c = 0; c < 32; c += 8) {
@@ -468,7 +490,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                             }
                         }
                     } else {
-                        float* dst = static_cast<float*>(a.out) + (size_t)qrow * a.o_tok + (size_t)h * a.o_head +
+                        float* dst = static_cast<float*>(P.out) + (size_t)qrow * a.o_tok + (size_t)h * a.o_head +
                                      cb * 32;
 #pragma unroll
                         for (int c = 0; c < 32; c += 4)
@@ -490,38 +512,71 @@ prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
 
 }  // namespace pf
 
-// Launch the causal prefill on device pointers.
+// Launch the prefill over a table of pieces (PrefillPiece in sa_qwen3.h):
+//   q    [q_rows,  q_tok stride,  hq heads of 128]   bf16
+//   k,v  [kv_rows, kv_tok stride, hkv heads of 128]  bf16
+// each piece's output [Sq rows, o_tok stride, hq heads of 128] in out_dtype.
+int prefill_pieces_launch(cudaStream_t st, int* status, const void* q, int q_rows, long long q_tok, const void* k,
+                          const void* v, int kv_rows, long long kv_tok, int hq, int hkv, float scale, int out_dtype,
+                          long long o_tok, const PrefillPiece* pieces, int n, void* out_lo) {
+    SA_CHECK_ARG(n >= 1 && n <= pf::MAX_PIECES && hkv >= 1 && hq % hkv == 0 && (n == 1 || !out_lo),
+                 "prefill: %d pieces, hq %d, hkv %d", n, hq, hkv);
+    CUtensorMap mq, mk, mv;
+    int rc = make_tmap_2d_bf16(&mq, q, (uint64_t)q_rows, (uint64_t)hq * pf::D, (uint64_t)q_tok, pf::BM, 64);
+    if (!rc) rc = make_tmap_2d_bf16(&mk, k, (uint64_t)kv_rows, (uint64_t)hkv * pf::D, (uint64_t)kv_tok, pf::BN, 64);
+    if (!rc) rc = make_tmap_2d_bf16(&mv, v, (uint64_t)kv_rows, (uint64_t)hkv * pf::D, (uint64_t)kv_tok, pf::BN, 64);
+    if (rc) return rc;
+    pf::Args a;
+    a.hq = hq; a.hkv = hkv; a.G = hq / hkv;
+    a.pair_heads = (a.G % 2 == 0) ? 1 : 0;
+    a.units_per_row = a.pair_heads ? hkv * (a.G / 2) : hq;
+    a.sl2 = scale * pf::LOG2E;
+    a.o_tok = o_tok; a.o_head = pf::D;
+    a.out_bf16 = out_dtype == SA_BF16;
+    a.out_lo = a.out_bf16 ? out_lo : nullptr;
+    a.status = status;
+    a.n_pieces = n;
+    int grid = 0;
+    for (int i = 0; i < n; ++i) {
+        const PrefillPiece& s = pieces[i];
+        SA_CHECK_ARG(s.Sq >= 1 && s.Skv >= 1 && s.q_pos0 >= 0 && s.q_row0 >= 0 && s.kv_row0 >= 0 &&
+                         s.q_row0 + s.Sq <= q_rows && s.kv_row0 + s.Skv <= kv_rows && s.out,
+                     "prefill: piece %d (q rows %d+%d of %d, keys %d+%d of %d)", i, s.q_row0, s.Sq, q_rows, s.kv_row0,
+                     s.Skv, kv_rows);
+        pf::Piece& P = a.pc[i];
+        P.q_row0 = s.q_row0; P.kv_row0 = s.kv_row0;
+        P.Sq = s.Sq; P.Skv = s.Skv; P.q_pos0 = s.q_pos0;
+        P.n_qtiles = (s.Sq + pf::BM - 1) / pf::BM;
+        P.cta0 = grid;
+        P.out = s.out;
+        P.lse = s.lse;
+        const int rows = a.pair_heads ? P.n_qtiles : (P.n_qtiles + 1) / 2;
+        grid += rows * a.units_per_row;
+    }
+    // All exponentials on the SFU: with 128-key tiles the softmax is issue-bound,
+    // and moving every 8th/4th/3rd exponential to exp2_poly measured 3%/5%/9%
+    // slower on config 3 (S=8192, 16/8 heads).
+    auto kern = pf::prefill_kernel<0>;
+    SA_RC_TRY(set_smem_attr_once((const void*)kern, pf::SMEM_BYTES));
+    kern<<<grid, pf::THREADS, pf::SMEM_BYTES, st>>>(mq, mk, mv, a);
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+}
+
+// Launch the causal prefill on device pointers (one piece).
 //   q   [Sq,  q_tok stride,  hq heads of 128]   bf16
 //   k,v [Skv, kv_tok stride, hkv heads of 128]  bf16
 //   out [Sq,  o_tok stride,  hq heads of 128]   fp32 or bf16
 int prefill_launch(cudaStream_t st, int* status, const void* q, const void* k, const void* v, void* out,
                    int out_dtype, int Sq, int Skv, int q_pos0, int hq, int hkv, long long q_tok, long long kv_tok,
                    long long o_tok, float scale, void* out_lo) {
-    CUtensorMap mq, mk, mv;
-    int rc = make_tmap_2d_bf16(&mq, q, (uint64_t)Sq, (uint64_t)hq * pf::D, (uint64_t)q_tok, pf::BM, 64);
-    if (!rc) rc = make_tmap_2d_bf16(&mk, k, (uint64_t)Skv, (uint64_t)hkv * pf::D, (uint64_t)kv_tok, pf::BN, 64);
-    if (!rc) rc = make_tmap_2d_bf16(&mv, v, (uint64_t)Skv, (uint64_t)hkv * pf::D, (uint64_t)kv_tok, pf::BN, 64);
-    if (rc) return rc;
-    pf::Args a;
-    a.Sq = Sq; a.Skv = Skv; a.q_pos0 = q_pos0; a.hq = hq; a.hkv = hkv; a.G = hq / hkv;
-    a.n_qtiles = (Sq + pf::BM - 1) / pf::BM;
-    a.pair_heads = (a.G % 2 == 0) ? 1 : 0;
-    a.units_per_row = a.pair_heads ? hkv * (a.G / 2) : hq;
-    const int rows = a.pair_heads ? a.n_qtiles : (a.n_qtiles + 1) / 2;
-    a.sl2 = scale * pf::LOG2E;
-    a.out = out; a.o_tok = o_tok; a.o_head = pf::D;
-    a.out_bf16 = out_dtype == SA_BF16;
-    a.out_lo = a.out_bf16 ? out_lo : nullptr;
-    a.status = status;
-    // All exponentials on the SFU: with 128-key tiles the softmax is issue-bound,
-    // and moving every 8th/4th/3rd exponential to exp2_poly measured 3%/5%/9%
-    // slower on config 3 (S=8192, 16/8 heads).
-    auto kern = pf::prefill_kernel<0>;
-    SA_RC_TRY(set_smem_attr_once((const void*)kern, pf::SMEM_BYTES));
-    const int grid = rows * a.units_per_row;
-    kern<<<grid, pf::THREADS, pf::SMEM_BYTES, st>>>(mq, mk, mv, a);
-    SA_CUDA_TRY(cudaGetLastError());
-    return SA_OK;
+    PrefillPiece p;
+    p.q_row0 = 0; p.kv_row0 = 0;
+    p.Sq = Sq; p.Skv = Skv; p.q_pos0 = q_pos0;
+    p.out = out;
+    p.lse = nullptr;
+    return prefill_pieces_launch(st, status, q, Sq, q_tok, k, v, Skv, kv_tok, hq, hkv, scale, out_dtype, o_tok, &p, 1,
+                                 out_lo);
 }
 
 static int launch_prefill(sa_ctx* ctx, const void* q, const void* k, const void* v, void* out, int out_dtype,

@@ -174,6 +174,20 @@ int launch_sp_rows_scatter(cudaStream_t st, const SpCopy& c, const TpArgs& tp, i
 // (sa_prefill.cu), which writes the o_proj GEMM's bf16 hi/lo planes.
 int launch_tc_pack(cudaStream_t st, const float* q, int M, int QD, const float* kc, const float* vc, int max_seq,
                    int hkv, int T, __nv_bfloat16* qb, __nv_bfloat16* kb, __nv_bfloat16* vb, int num_sms);
+// A block of query rows against a block of keys for prefill_pieces_launch
+// (sa_prefill.cu): queries q_row0 .. q_row0+Sq-1 of the Q tensor, keys
+// kv_row0 .. kv_row0+Skv-1 of the K/V tensors, query i seeing key j of the
+// block when j <= q_pos0 + i; output rows `out`, and with `lse` the rows'
+// log2-domain log-sum-exp of the scaled scores ([Sq][hq] floats), so that
+// pieces of one query block over disjoint key blocks can be merged.
+struct PrefillPiece {
+    int q_row0 = 0, kv_row0 = 0, Sq = 0, Skv = 0, q_pos0 = 0;
+    void* out = nullptr;
+    float* lse = nullptr;
+};
+int prefill_pieces_launch(cudaStream_t st, int* status, const void* q, int q_rows, long long q_tok, const void* k,
+                          const void* v, int kv_rows, long long kv_tok, int hq, int hkv, float scale, int out_dtype,
+                          long long o_tok, const PrefillPiece* pieces, int n, void* out_lo = nullptr);
 // out_lo != nullptr (with out_dtype SA_BF16): the output as two bf16 planes,
 // out = bf16(o) and out_lo = bf16(o - out), the next GEMM's A operand.
 int prefill_launch(cudaStream_t st, int* status, const void* q, const void* k, const void* v, void* out,

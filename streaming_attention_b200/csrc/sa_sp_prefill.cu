@@ -1,0 +1,461 @@
+// sa_sp_prefill.cu -- sequence-parallel causal prefill over the GPUs of one
+// node (configs[2]: S = 8192, 16 / 8 heads of 128, bf16), one rank per GPU.
+//
+// Replaces the reference's sequence-parallel attention
+// (attention_sequence_online_softmax, tensor_cpp/src/ops_mpi.cpp:1000-1212,
+// whose statistics all-reduce mixes positions) with the causal prefill the
+// strategy stands for: the sequence is cut into 2P chunks of C = S / 2P
+// tokens and rank r holds chunks r and 2P-1-r (zig-zag), which gives every
+// rank the same causal work.
+//
+// One call, all on the context's stream:
+//   1. spp_scatter_kernel: the rank's K and V chunks go straight into slot
+//      (instance & 1) of EVERY rank's K/V buffer (its own and the peers',
+//      mapped over CUDA IPC or peer access) at their sequence rows, with
+//      16-byte stores; after a system-scope fence and an arrival count, the
+//      last CTA stores the instance's epoch into flag [slot][rank] of every
+//      rank (release, system scope).
+//   2. spp_wait_kernel: one thread per rank waits (bounded by %globaltimer)
+//      until this rank's flag [slot][r] carries the epoch: all K/V rows of
+//      the sequence are then in the local buffer.
+//   3. prefill_pieces_launch: ONE launch of the tcgen05 prefill over a table
+//      of pieces.  Each chunk's key range [0, end of chunk) is cut into blocks
+//      of C keys: the blocks before the chunk are fully visible (no mask), the
+//      last one is the causal diagonal.  So every CTA streams at most C keys
+//      (the heavy chunk's CTAs would otherwise carry the whole prefix), and a
+//      rank's 2P + 1 pieces fill the SMs.  Pieces write fp32 partial outputs
+//      and their rows' log-sum-exp.
+//   4. spp_merge_kernel: out = sum_p 2^(lse_p - lse) O_p over the pieces of
+//      each chunk (lse = log2 sum_p 2^lse_p), in the caller's dtype; then the
+//      instance count advances.
+// Slots alternate between calls, so a rank writing call i+1's rows never
+// overwrites rows a slower peer still reads for call i: a rank can only
+// start call i+2 after every peer published call i+1, which each does only
+// after finishing call i.
+#include <cuda_bf16.h>
+#include <cstring>
+
+#include "sa_internal.h"
+#include "sa_ptx.cuh"
+#include "sa_qwen3.h"
+
+constexpr int SPP_MAX = 8;
+
+struct sa_spp {
+    sa_ctx* ctx = nullptr;
+    int device = 0, rank = 0, world = 1;
+    int max_seq = 0, hkv = 0;
+    size_t slot_bytes = 0;                     // one slot: K then V, [max_seq][hkv][128] bf16 each
+    size_t buf_bytes = 0;
+    unsigned char* buf = nullptr;              // own buffer: flags, then 2 slots
+    unsigned* ctl = nullptr;                   // [0] arrivals of the scatter's CTAs
+    unsigned inst = 0;                         // calls issued (slot = inst & 1, epoch = inst + 1)
+    unsigned char* peer[SPP_MAX] = {};
+    bool opened[SPP_MAX] = {};
+    bool connected = false;
+    unsigned char uuid[16] = {};
+    float* part = nullptr;                     // piece outputs and their lse
+    size_t part_floats = 0;
+};
+
+namespace sa {
+namespace spp {
+
+constexpr int D = 128;
+constexpr size_t FLAG_BYTES = 4096;            // [2 slots][SPP_MAX] u32 flags, then the K/V slots
+constexpr uint32_t MAGIC = 0x50505341u;        // "ASPP"
+
+struct Handle {                                // the SA_SPP_HANDLE_BYTES blob
+    cudaIpcMemHandle_t ipc;
+    unsigned char uuid[16];
+    int32_t rank, world, max_seq, hkv;
+    uint64_t buf_bytes;
+    uint32_t magic;
+};
+static_assert(sizeof(Handle) <= SA_SPP_HANDLE_BYTES, "handle size");
+
+struct ScatterArgs {
+    const uint4* k;                // this rank's [2C][hkv * 128] bf16 rows as 16-byte vectors
+    const uint4* v;
+    unsigned char* dst[SPP_MAX];   // every rank's buffer
+    int world, rank, C, row_vecs;  // row_vecs = hkv * 128 * 2 / 16
+    int chunk[2];                  // the sequence chunks of local rows [0, C) and [C, 2C)
+    size_t slot_bytes, tensor_bytes;
+    unsigned inst;
+    unsigned* cnt;
+};
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__global__ void spp_scatter_kernel(const ScatterArgs a) {
+    const unsigned inst = a.inst;
+    const int slot = (int)(inst & 1u);
+    const long long per_tensor = 2LL * a.C * a.row_vecs;          // vectors of one local tensor
+    const long long per_rank = 2 * per_tensor;
+    const long long n = per_rank * a.world;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int r = (int)(i / per_rank);
+        long long j = i - (long long)r * per_rank;
+        const int t = j >= per_tensor ? 1 : 0;                     // 0: K, 1: V
+        if (t) j -= per_tensor;
+        const long long row = j / a.row_vecs, c = j - row * a.row_vecs;
+        const int half = row >= a.C ? 1 : 0;
+        const long long seq_row = (long long)a.chunk[half] * a.C + (row - (long long)half * a.C);
+        const uint4 val = (t ? a.v : a.k)[j];
+        uint4* dst = reinterpret_cast<uint4*>(a.dst[r] + FLAG_BYTES + (size_t)slot * a.slot_bytes +
+                                              (size_t)t * a.tensor_bytes) +
+                     seq_row * a.row_vecs + c;
+        *dst = val;
+    }
+    // publish: every CTA's stores before its arrival; the last CTA to arrive
+    // stores the epoch into flag [slot][rank] of every rank
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned prev = atomicAdd(a.cnt, 1u);
+        if (prev == gridDim.x - 1) {
+            __threadfence_system();
+            *a.cnt = 0u;
+            for (int r = 0; r < a.world; ++r)
+                st_release_sys(reinterpret_cast<unsigned*>(a.dst[r]) + slot * SPP_MAX + a.rank, inst + 1u);
+        }
+    }
+}
+
+__global__ void spp_wait_kernel(const unsigned* flags, int world, unsigned inst, int* status) {
+    const int slot = (int)(inst & 1u);
+    const int r = threadIdx.x;
+    if (r >= world) return;
+    const unsigned* f = flags + slot * SPP_MAX + r;
+    if (ld_acquire_sys(f) == inst + 1u) return;
+    const unsigned long long t0 = globaltimer();
+    while (ld_acquire_sys(f) != inst + 1u) {
+        if (*reinterpret_cast<volatile int*>(status) != 0) return;   // another wait already gave up
+        if (globaltimer() - t0 > kWaitLimitNs) {
+            atomicExch(status, SA_STATUS_TIMEOUT);
+            return;
+        }
+    }
+}
+
+struct MergeArgs {
+    const float* part;             // piece p's output at part + p * piece_floats, [C][hq][128]
+    const float* lse;              // piece p's lse at lse + p * C * hq
+    long long piece_floats;
+    int C, hq;
+    int first[2], count[2];        // pieces of local chunk 0 / 1
+    void* out;                     // [2C][hq][128], bf16 or fp32
+    int out_bf16;
+    const int* status;
+};
+
+// One warp per (local row, head); lane l owns dims 4l..4l+3.  Rows whose
+// pieces were cut short by an expired wait come out NaN.
+__global__ void spp_merge_kernel(const MergeArgs a) {
+    const int lane = threadIdx.x & 31;
+    const long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+    const long long n = 2LL * a.C * a.hq;
+    if (w < n) {
+        const int row = (int)(w / a.hq), h = (int)(w - (long long)row * a.hq);
+        const int half = row >= a.C ? 1 : 0, lr = row - half * a.C;
+        const int p0 = a.first[half], np = a.count[half];
+        float mx = -INFINITY;
+        for (int p = 0; p < np; ++p) mx = fmaxf(mx, __ldg(a.lse + (size_t)(p0 + p) * a.C * a.hq + (size_t)lr * a.hq + h));
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        float den = 0.f;
+        for (int p = 0; p < np; ++p) {
+            const float wt = ex2(__ldg(a.lse + (size_t)(p0 + p) * a.C * a.hq + (size_t)lr * a.hq + h) - mx);
+            const float4 o = __ldg(reinterpret_cast<const float4*>(a.part + (size_t)(p0 + p) * a.piece_floats +
+                                                                   ((size_t)lr * a.hq + h) * D) + lane);
+            acc.x = fmaf(wt, o.x, acc.x);
+            acc.y = fmaf(wt, o.y, acc.y);
+            acc.z = fmaf(wt, o.z, acc.z);
+            acc.w = fmaf(wt, o.w, acc.w);
+            den += wt;
+        }
+        const bool failed = *reinterpret_cast<const volatile int*>(a.status) != 0;
+        const float inv = failed ? __int_as_float(0x7fffffff) : 1.f / den;
+        acc = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        const size_t off = ((size_t)row * a.hq + h) * D + 4 * lane;
+        if (a.out_bf16) {
+            const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+            uint2 u;
+            u.x = *reinterpret_cast<const uint32_t*>(&lo);
+            u.y = *reinterpret_cast<const uint32_t*>(&hi);
+            *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.out) + off) = u;
+        } else {
+            *reinterpret_cast<float4*>(static_cast<float*>(a.out) + off) = acc;
+        }
+    }
+}
+
+void close_peers(sa_spp* sp) {
+    for (int r = 0; r < SPP_MAX; ++r) {
+        if (sp->opened[r] && sp->peer[r]) cudaIpcCloseMemHandle(sp->peer[r]);
+        sp->opened[r] = false;
+        sp->peer[r] = nullptr;
+    }
+    sp->connected = false;
+}
+
+}  // namespace spp
+}  // namespace sa
+
+SA_API int sa_spp_create(sa_ctx* ctx, int rank, int world, int max_seq, int hkv, int d, sa_spp** out) {
+    using namespace sa;
+    clear_error();
+    SA_CHECK_ARG(ctx && out, "sa_spp_create: null argument");
+    *out = nullptr;
+    SA_CHECK_ARG(world >= 1 && world <= SPP_MAX, "sa_spp_create: world = %d (1..%d)", world, SPP_MAX);
+    SA_CHECK_ARG(rank >= 0 && rank < world, "sa_spp_create: rank %d of %d", rank, world);
+    SA_CHECK_ARG(d == spp::D, "sa_spp_create: d = %d (the tensor-core prefill is built for d = 128)", d);
+    SA_CHECK_ARG(hkv >= 1 && hkv <= 64 && max_seq >= 2 * world && max_seq <= (1 << 22),
+                 "sa_spp_create: hkv = %d, max_seq = %d", hkv, max_seq);
+    DeviceGuard guard(ctx->device);
+    sa_spp* sp = new sa_spp();
+    sp->ctx = ctx;
+    sp->device = ctx->device;
+    sp->rank = rank;
+    sp->world = world;
+    sp->max_seq = max_seq;
+    sp->hkv = hkv;
+    const size_t tensor_bytes = (size_t)max_seq * hkv * spp::D * 2;
+    sp->slot_bytes = 2 * tensor_bytes;
+    sp->buf_bytes = spp::FLAG_BYTES + 2 * sp->slot_bytes;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, ctx->device) != cudaSuccess ||
+        cudaMalloc(&sp->buf, sp->buf_bytes) != cudaSuccess ||
+        cudaMalloc(&sp->ctl, sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(sp->buf, 0, spp::FLAG_BYTES) != cudaSuccess ||
+        cudaMemset(sp->ctl, 0, sizeof(unsigned)) != cudaSuccess) {
+        const cudaError_t e = cudaGetLastError();
+        cudaFree(sp->buf);
+        cudaFree(sp->ctl);
+        delete sp;
+        return set_error(SA_ERR_OOM, "sa_spp_create: %s", cudaGetErrorString(e));
+    }
+    std::memcpy(sp->uuid, &prop.uuid, sizeof(sp->uuid));
+    sp->peer[rank] = sp->buf;
+    sp->connected = world == 1;
+    *out = sp;
+    return SA_OK;
+}
+
+SA_API int sa_spp_handle(sa_spp* sp, void* handle) {
+    using namespace sa;
+    clear_error();
+    SA_CHECK_ARG(sp && handle, "sa_spp_handle: null argument");
+    DeviceGuard guard(sp->device);
+    spp::Handle h;
+    std::memset(&h, 0, sizeof(h));
+    SA_CUDA_TRY(cudaIpcGetMemHandle(&h.ipc, sp->buf));
+    std::memcpy(h.uuid, sp->uuid, sizeof(h.uuid));
+    h.rank = sp->rank;
+    h.world = sp->world;
+    h.max_seq = sp->max_seq;
+    h.hkv = sp->hkv;
+    h.buf_bytes = sp->buf_bytes;
+    h.magic = spp::MAGIC;
+    std::memset(handle, 0, SA_SPP_HANDLE_BYTES);
+    std::memcpy(handle, &h, sizeof(h));
+    return SA_OK;
+}
+
+SA_API int sa_spp_connect(sa_spp* sp, const void* handles) {
+    using namespace sa;
+    clear_error();
+    SA_CHECK_ARG(sp && handles, "sa_spp_connect: null argument");
+    if (sp->world == 1) return SA_OK;
+    SA_CHECK_ARG(!sp->connected, "sa_spp_connect: already connected");
+    DeviceGuard guard(sp->device);
+    const unsigned char* hb = static_cast<const unsigned char*>(handles);
+    for (int r = 0; r < sp->world; ++r) {
+        spp::Handle h;
+        std::memcpy(&h, hb + (size_t)r * SA_SPP_HANDLE_BYTES, sizeof(h));
+        const char* bad = nullptr;
+        if (h.magic != spp::MAGIC) bad = "is not an sa_spp handle";
+        else if (h.rank != r || h.world != sp->world) bad = "names another rank or world size";
+        else if (h.max_seq != sp->max_seq || h.hkv != sp->hkv || h.buf_bytes != sp->buf_bytes)
+            bad = "was created with other max_seq / hkv";
+        else if (r != sp->rank && std::memcmp(h.uuid, sp->uuid, sizeof(h.uuid)) == 0)
+            bad = "is on this rank's GPU (the ranks wait for one another: one GPU per rank)";
+        if (bad) {
+            spp::close_peers(sp);
+            sp->peer[sp->rank] = sp->buf;
+            return set_error(SA_ERR_ARG, "sa_spp_connect: handle %d %s", r, bad);
+        }
+        if (r == sp->rank) continue;
+        void* p = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&p, h.ipc, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            spp::close_peers(sp);
+            sp->peer[sp->rank] = sp->buf;
+            return set_error(SA_ERR_CUDA, "sa_spp_connect: opening rank %d's buffer failed: %s", r,
+                             cudaGetErrorString(e));
+        }
+        sp->peer[r] = static_cast<unsigned char*>(p);
+        sp->opened[r] = true;
+    }
+    sp->peer[sp->rank] = sp->buf;
+    sp->connected = true;
+    return SA_OK;
+}
+
+SA_API int sa_spp_connect_local(sa_spp* const* sps, int n) {
+    using namespace sa;
+    clear_error();
+    SA_CHECK_ARG(sps && n >= 1 && n <= SPP_MAX, "sa_spp_connect_local: n = %d", n);
+    for (int i = 0; i < n; ++i) {
+        SA_CHECK_ARG(sps[i] && sps[i]->rank == i && sps[i]->world == n,
+                     "sa_spp_connect_local: entry %d is not rank %d of %d", i, i, n);
+        SA_CHECK_ARG(!sps[i]->connected || n == 1, "sa_spp_connect_local: rank %d already connected", i);
+        SA_CHECK_ARG(sps[i]->buf_bytes == sps[0]->buf_bytes,
+                     "sa_spp_connect_local: rank %d was created with other max_seq / hkv", i);
+        for (int j = 0; j < i; ++j)
+            SA_CHECK_ARG(sps[j]->device != sps[i]->device,
+                         "sa_spp_connect_local: ranks %d and %d share GPU %d (one GPU per rank)", j, i,
+                         sps[i]->device);
+    }
+    for (int i = 0; i < n; ++i) {
+        DeviceGuard guard(sps[i]->device);
+        for (int j = 0; j < n; ++j) {
+            if (j == i) continue;
+            int can = 0;
+            SA_CUDA_TRY(cudaDeviceCanAccessPeer(&can, sps[i]->device, sps[j]->device));
+            SA_CHECK_ARG(can, "sa_spp_connect_local: GPU %d cannot access GPU %d", sps[i]->device,
+                         sps[j]->device);
+            const cudaError_t e = cudaDeviceEnablePeerAccess(sps[j]->device, 0);
+            if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled)
+                return set_error(SA_ERR_CUDA, "sa_spp_connect_local: peer access %d -> %d: %s", sps[i]->device,
+                                 sps[j]->device, cudaGetErrorString(e));
+            cudaGetLastError();
+        }
+    }
+    for (int i = 0; i < n; ++i) {
+        for (int j = 0; j < n; ++j) sps[i]->peer[j] = sps[j]->buf;
+        sps[i]->connected = true;
+    }
+    return SA_OK;
+}
+
+SA_API int sa_spp_destroy(sa_spp* sp) {
+    using namespace sa;
+    clear_error();
+    if (!sp) return SA_OK;
+    DeviceGuard guard(sp->device);
+    cudaDeviceSynchronize();
+    spp::close_peers(sp);
+    cudaFree(sp->buf);
+    cudaFree(sp->ctl);
+    cudaFree(sp->part);
+    delete sp;
+    return SA_OK;
+}
+
+SA_API int sa_spp_prefill(sa_spp* sp, const void* q_local, const void* k_local, const void* v_local, int S, int hq,
+                          int hkv, int d, float scale, void* out_local, int out_dtype, unsigned flags) {
+    using namespace sa;
+    clear_error();
+    SA_CHECK_ARG(sp != nullptr, "sa_spp_prefill: sp is NULL");
+    SA_CHECK_ARG(sp->connected, "sa_spp_prefill: rank %d of %d is not connected (sa_spp_connect)", sp->rank,
+                 sp->world);
+    SA_CHECK_ARG(q_local && k_local && v_local && out_local, "sa_spp_prefill: null pointer");
+    SA_CHECK_ARG(!(flags & SA_HOST_PTRS), "sa_spp_prefill: host pointers are not supported (pass device memory)");
+    SA_CHECK_ARG(d == spp::D && hkv == sp->hkv && hq >= hkv && hq % hkv == 0 && hq <= 256,
+                 "sa_spp_prefill: d = %d, hq = %d, hkv = %d (created for hkv = %d, d = 128)", d, hq, hkv, sp->hkv);
+    const int P = sp->world;
+    SA_CHECK_ARG(S >= 2 * P && S % (2 * P) == 0 && S <= sp->max_seq,
+                 "sa_spp_prefill: S = %d must be a multiple of 2 x %d ranks, at most max_seq = %d", S, P, sp->max_seq);
+    SA_CHECK_ARG(out_dtype == SA_F32 || out_dtype == SA_BF16, "sa_spp_prefill: out_dtype %d", out_dtype);
+    SA_CHECK_ARG(((((uintptr_t)q_local) | ((uintptr_t)k_local) | ((uintptr_t)v_local) | ((uintptr_t)out_local)) & 15) == 0,
+                 "sa_spp_prefill: pointers must be 16-byte aligned");
+    DeviceGuard guard(sp->device);
+    cudaStream_t st = sp->ctx->stream;
+    const int C = S / (2 * P);
+    const int chunk[2] = {sp->rank, 2 * P - 1 - sp->rank};
+
+    // the pieces: per chunk, blocks of C keys before it (unmasked), then its diagonal block
+    PrefillPiece pcs[2 * SPP_MAX + 2];
+    int first[2], count[2], n = 0;
+    for (int half = 0; half < 2; ++half) {
+        first[half] = n;
+        const int start = chunk[half] * C;
+        for (int kv0 = 0; kv0 <= start; kv0 += C) {
+            PrefillPiece& p = pcs[n++];
+            p.q_row0 = half * C;
+            p.kv_row0 = kv0;
+            p.Sq = C;
+            p.Skv = C;
+            p.q_pos0 = start - kv0;           // C or more: every key visible; 0 on the diagonal
+        }
+        count[half] = n - first[half];
+    }
+    const long long piece_floats = (long long)C * hq * spp::D;
+    const size_t need = (size_t)n * (piece_floats + (size_t)C * hq) + 64;
+    if (need > sp->part_floats) {
+        SA_CUDA_TRY(cudaStreamSynchronize(st));
+        cudaFree(sp->part);
+        sp->part = nullptr;
+        sp->part_floats = 0;
+        if (cudaMalloc(&sp->part, need * sizeof(float)) != cudaSuccess) {
+            cudaGetLastError();
+            return set_error(SA_ERR_OOM, "sa_spp_prefill: %zu bytes of piece outputs", need * sizeof(float));
+        }
+        sp->part_floats = need;
+    }
+    float* lse = sp->part + (size_t)n * piece_floats;
+    for (int i = 0; i < n; ++i) {
+        pcs[i].out = sp->part + (size_t)i * piece_floats;
+        pcs[i].lse = lse + (size_t)i * C * hq;
+    }
+
+    spp::ScatterArgs sa_{};
+    sa_.k = static_cast<const uint4*>(k_local);
+    sa_.v = static_cast<const uint4*>(v_local);
+    for (int r = 0; r < P; ++r) sa_.dst[r] = sp->peer[r];
+    sa_.world = P;
+    sa_.rank = sp->rank;
+    sa_.C = C;
+    sa_.row_vecs = hkv * spp::D * 2 / 16;
+    sa_.chunk[0] = chunk[0];
+    sa_.chunk[1] = chunk[1];
+    sa_.slot_bytes = sp->slot_bytes;
+    sa_.tensor_bytes = sp->slot_bytes / 2;
+    sa_.inst = sp->inst;
+    sa_.cnt = sp->ctl;
+    spp::spp_scatter_kernel<<<2 * sp->ctx->num_sms, 512, 0, st>>>(sa_);
+    SA_CUDA_TRY(cudaGetLastError());
+    spp::spp_wait_kernel<<<1, 32, 0, st>>>(reinterpret_cast<const unsigned*>(sp->buf), P, sp->inst,
+                                           sp->ctx->status);
+    SA_CUDA_TRY(cudaGetLastError());
+    const unsigned char* kv = sp->buf + spp::FLAG_BYTES + (size_t)(sp->inst & 1u) * sp->slot_bytes;
+    const long long tok = (long long)hkv * spp::D;
+    SA_RC_TRY(prefill_pieces_launch(st, sp->ctx->status, q_local, 2 * C, (long long)hq * spp::D, kv,
+                                    kv + sp->slot_bytes / 2, S, tok, hq, hkv, scale, SA_F32, (long long)hq * spp::D,
+                                    pcs, n));
+    spp::MergeArgs ma{};
+    ma.part = sp->part;
+    ma.lse = lse;
+    ma.piece_floats = piece_floats;
+    ma.C = C;
+    ma.hq = hq;
+    ma.first[0] = first[0]; ma.first[1] = first[1];
+    ma.count[0] = count[0]; ma.count[1] = count[1];
+    ma.out = out_local;
+    ma.out_bf16 = out_dtype == SA_BF16;
+    ma.status = sp->ctx->status;
+    const long long warps = 2LL * C * hq;
+    spp::spp_merge_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(ma);
+    SA_CUDA_TRY(cudaGetLastError());
+    ++sp->inst;   // the next call uses the other slot
+    return SA_OK;
+}

@@ -240,3 +240,81 @@ class SpDecoder:
             self.close()
         except Exception:
             pass
+
+
+class SpPrefill:
+    """This rank's share of the sequence-parallel causal prefill (sa_spp_*).
+
+    The sequence of S tokens is cut into 2P zig-zag chunks (``zigzag_shard``):
+    rank r holds chunks r and 2P-1-r.  Every rank creates one with the same
+    ``world``, exchanges handles (``connect_dist``, ``connect`` or
+    ``connect_local`` for the GPUs of one process), then calls ``prefill``
+    with its own chunks; the K/V chunks cross NVLink by direct stores into
+    every rank's buffer and each rank gets the causal attention of its own
+    query rows over the whole prefix.  Ranks must be on distinct GPUs.
+    """
+
+    def __init__(self, ctx, rank: int, world: int, max_seq: int, hkv: int, d: int = 128):
+        import ctypes as C
+        from ._capi import check, lib
+        self.ctx, self.rank, self.world = ctx, rank, world
+        h = C.c_void_p()
+        check(lib().sa_spp_create(ctx.h, rank, world, max_seq, hkv, d, C.byref(h)))
+        self.h = h
+
+    def handle(self) -> bytes:
+        import ctypes as C
+        from ._capi import SA_SPP_HANDLE_BYTES, check, lib
+        buf = C.create_string_buffer(SA_SPP_HANDLE_BYTES)
+        check(lib().sa_spp_handle(self.h, buf))
+        return buf.raw
+
+    def connect(self, handles) -> None:
+        import ctypes as C
+        from ._capi import check, lib
+        blob = b"".join(handles)
+        check(lib().sa_spp_connect(self.h, C.create_string_buffer(blob, len(blob))))
+
+    def connect_dist(self, group=None) -> None:
+        import torch.distributed as dist
+        hs = [None] * self.world
+        dist.all_gather_object(hs, self.handle(), group=group)
+        self.connect(hs)
+
+    @staticmethod
+    def connect_local(prefills) -> None:
+        import ctypes as C
+        from ._capi import check, lib
+        arr = (C.c_void_p * len(prefills))(*[p.h.value for p in prefills])
+        check(lib().sa_spp_connect_local(arr, len(prefills)))
+
+    def prefill(self, q_local, k_local, v_local, scale: float, out=None, out_dtype=None):
+        """q_local [2C, hq, 128], k_local / v_local [2C, hkv, 128] bf16 CUDA
+        tensors (this rank's chunks r and 2P-1-r, in that order) ->
+        out [2C, hq, 128] (bf16 unless ``out_dtype`` is torch.float32)."""
+        import ctypes as C
+        import torch
+        from ._capi import SA_BF16, SA_F32, check, lib
+        q_local, k_local, v_local = q_local.contiguous(), k_local.contiguous(), v_local.contiguous()
+        C2, hq, d = q_local.shape
+        hkv = k_local.shape[1]
+        if out is None:
+            out = torch.empty(C2, hq, d, dtype=out_dtype or torch.bfloat16, device=q_local.device)
+        dt = SA_F32 if out.dtype == torch.float32 else SA_BF16
+        P = lambda t: C.c_void_p(t.data_ptr())
+        self.ctx.set_stream(torch.cuda.current_stream(q_local.device).cuda_stream)
+        check(lib().sa_spp_prefill(self.h, P(q_local), P(k_local), P(v_local), C2 * self.world, hq, hkv, d,
+                                   scale, P(out), dt, 0))
+        return out
+
+    def close(self) -> None:
+        from ._capi import lib
+        if getattr(self, "h", None):
+            lib().sa_spp_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
