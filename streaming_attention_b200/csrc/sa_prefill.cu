@@ -220,7 +220,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     // extent of its two slots
     int pi = 0;
     while (pi + 1 < a.n_pieces && (int)blockIdx.x >= a.pc[pi + 1].cta0) ++pi;
-    const Piece& P = a.pc[pi];
+    const Piece P = a.pc[pi];      // in registers: the softmax loop reads its bounds every tile
     const int local = (int)blockIdx.x - P.cta0;
     const int rowi = local / a.units_per_row;
     const int u = local % a.units_per_row;
