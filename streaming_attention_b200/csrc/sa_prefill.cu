@@ -83,7 +83,7 @@ constexpr float RESCALE_THRESHOLD = 8.0f;      // log2 units
 // A sequence-parallel rank splits its long causal key ranges into pieces of
 // similar length (so no CTA carries a whole row's keys) and merges them by
 // their log-sum-exp; a plain prefill is one piece.
-constexpr int MAX_PIECES = 24;
+constexpr int MAX_PIECES = kPrefillMaxPieces;
 struct Piece {
     int q_row0, kv_row0;
     int Sq, Skv, q_pos0;

@@ -180,6 +180,7 @@ int launch_tc_pack(cudaStream_t st, const float* q, int M, int QD, const float* 
 // block when j <= q_pos0 + i; output rows `out`, and with `lse` the rows'
 // log2-domain log-sum-exp of the scaled scores ([Sq][hq] floats), so that
 // pieces of one query block over disjoint key blocks can be merged.
+constexpr int kPrefillMaxPieces = 32;   // pieces of one prefill_pieces_launch
 struct PrefillPiece {
     int q_row0 = 0, kv_row0 = 0, Sq = 0, Skv = 0, q_pos0 = 0;
     void* out = nullptr;

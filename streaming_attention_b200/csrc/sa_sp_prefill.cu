@@ -20,11 +20,11 @@
 //      the sequence are then in the local buffer.
 //   3. prefill_pieces_launch: ONE launch of the tcgen05 prefill over a table
 //      of pieces.  Each chunk's key range [0, end of chunk) is cut into blocks
-//      of C keys: the blocks before the chunk are fully visible (no mask), the
-//      last one is the causal diagonal.  So every CTA streams at most C keys
-//      (the heavy chunk's CTAs would otherwise carry the whole prefix), and a
-//      rank's 2P + 1 pieces fill the SMs.  Pieces write fp32 partial outputs
-//      and their rows' log-sum-exp.
+//      of max(C, 1024) keys: the blocks before the chunk are fully visible (no
+//      mask), the last one is the causal diagonal of C keys.  So no CTA
+//      streams more than a block (the heavy chunk's CTAs would otherwise
+//      carry the whole prefix), and a rank's pieces fill the SMs.  Pieces
+//      write bf16 partial outputs and their rows' log-sum-exp.
 //   4. spp_merge_kernel: out = sum_p 2^(lse_p - lse) O_p over the pieces of
 //      each chunk (lse = log2 sum_p 2^lse_p), in the caller's dtype; then the
 //      instance count advances.
@@ -62,6 +62,7 @@ namespace sa {
 namespace spp {
 
 constexpr int D = 128;
+constexpr int MIN_PIECE_KEYS = 1024;           // shorter key blocks cost more in per-CTA set-up than they balance
 constexpr size_t FLAG_BYTES = 4096;            // [2 slots][SPP_MAX] u32 flags, then the K/V slots
 constexpr uint32_t MAGIC = 0x50505341u;        // "ASPP"
 
@@ -94,26 +95,29 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     return v;
 }
 
+// Thread i handles 16-byte vector i of the rank's K and of its V (32-bit
+// indexing: 2C * row_vecs < 2^31), loads both once and stores them to every
+// rank's buffer, so each pass keeps 2 x world stores in flight per thread.
 __global__ void spp_scatter_kernel(const ScatterArgs a) {
     const unsigned inst = a.inst;
     const int slot = (int)(inst & 1u);
-    const long long per_tensor = 2LL * a.C * a.row_vecs;          // vectors of one local tensor
-    const long long per_rank = 2 * per_tensor;
-    const long long n = per_rank * a.world;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
-         i += (long long)gridDim.x * blockDim.x) {
-        const int r = (int)(i / per_rank);
-        long long j = i - (long long)r * per_rank;
-        const int t = j >= per_tensor ? 1 : 0;                     // 0: K, 1: V
-        if (t) j -= per_tensor;
-        const long long row = j / a.row_vecs, c = j - row * a.row_vecs;
-        const int half = row >= a.C ? 1 : 0;
-        const long long seq_row = (long long)a.chunk[half] * a.C + (row - (long long)half * a.C);
-        const uint4 val = (t ? a.v : a.k)[j];
-        uint4* dst = reinterpret_cast<uint4*>(a.dst[r] + FLAG_BYTES + (size_t)slot * a.slot_bytes +
-                                              (size_t)t * a.tensor_bytes) +
-                     seq_row * a.row_vecs + c;
-        *dst = val;
+    const unsigned n = 2u * (unsigned)a.C * (unsigned)a.row_vecs;
+    unsigned char* base[SPP_MAX];
+#pragma unroll
+    for (int r = 0; r < SPP_MAX; ++r)
+        base[r] = r < a.world ? a.dst[r] + FLAG_BYTES + (size_t)slot * a.slot_bytes : nullptr;
+    for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const unsigned row = i / (unsigned)a.row_vecs, c = i - row * (unsigned)a.row_vecs;
+        const int half = row >= (unsigned)a.C ? 1 : 0;
+        const size_t seq_row = (size_t)(half ? a.chunk[1] : a.chunk[0]) * a.C + (row - (unsigned)half * a.C);
+        const uint4 kv = __ldg(a.k + i), vv = __ldg(a.v + i);
+        const size_t off = (seq_row * a.row_vecs + c) * 16;
+#pragma unroll
+        for (int r = 0; r < SPP_MAX; ++r) {
+            if (r >= a.world) break;
+            *reinterpret_cast<uint4*>(base[r] + off) = kv;
+            *reinterpret_cast<uint4*>(base[r] + a.tensor_bytes + off) = vv;
+        }
     }
     // publish: every CTA's stores before its arrival; the last CTA to arrive
     // stores the epoch into flag [slot][rank] of every rank
@@ -146,10 +150,12 @@ __global__ void spp_wait_kernel(const unsigned* flags, int world, unsigned inst,
     }
 }
 
+constexpr int MAX_CHUNK_PIECES = 16;          // pieces of one chunk (the call checks)
+
 struct MergeArgs {
-    const float* part;             // piece p's output at part + p * piece_floats, [C][hq][128]
+    const __nv_bfloat16* part;     // piece p's output at part + p * piece_elems, [C][hq][128] bf16
     const float* lse;              // piece p's lse at lse + p * C * hq
-    long long piece_floats;
+    long long piece_elems;
     int C, hq;
     int first[2], count[2];        // pieces of local chunk 0 / 1
     void* out;                     // [2C][hq][128], bf16 or fp32
@@ -157,43 +163,55 @@ struct MergeArgs {
     const int* status;
 };
 
-// One warp per (local row, head); lane l owns dims 4l..4l+3.  Rows whose
-// pieces were cut short by an expired wait come out NaN.
+// One warp per (local row, head); lane l owns dims 4l..4l+3.  All pieces'
+// lse values, then all their output vectors, are loaded before any is used.
+// Rows whose pieces were cut short by an expired wait come out NaN.
 __global__ void spp_merge_kernel(const MergeArgs a) {
     const int lane = threadIdx.x & 31;
     const long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
     const long long n = 2LL * a.C * a.hq;
-    if (w < n) {
-        const int row = (int)(w / a.hq), h = (int)(w - (long long)row * a.hq);
-        const int half = row >= a.C ? 1 : 0, lr = row - half * a.C;
-        const int p0 = a.first[half], np = a.count[half];
-        float mx = -INFINITY;
-        for (int p = 0; p < np; ++p) mx = fmaxf(mx, __ldg(a.lse + (size_t)(p0 + p) * a.C * a.hq + (size_t)lr * a.hq + h));
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        float den = 0.f;
-        for (int p = 0; p < np; ++p) {
-            const float wt = ex2(__ldg(a.lse + (size_t)(p0 + p) * a.C * a.hq + (size_t)lr * a.hq + h) - mx);
-            const float4 o = __ldg(reinterpret_cast<const float4*>(a.part + (size_t)(p0 + p) * a.piece_floats +
-                                                                   ((size_t)lr * a.hq + h) * D) + lane);
-            acc.x = fmaf(wt, o.x, acc.x);
-            acc.y = fmaf(wt, o.y, acc.y);
-            acc.z = fmaf(wt, o.z, acc.z);
-            acc.w = fmaf(wt, o.w, acc.w);
-            den += wt;
+    if (w >= n) return;
+    const int row = (int)(w / a.hq), h = (int)(w - (long long)row * a.hq);
+    const int half = row >= a.C ? 1 : 0, lr = row - half * a.C;
+    const int p0 = half ? a.first[1] : a.first[0], np = half ? a.count[1] : a.count[0];
+    const size_t lse_off = (size_t)lr * a.hq + h, o_off = lse_off * D + 4 * lane;
+    float ls[MAX_CHUNK_PIECES];
+    uint2 ov[MAX_CHUNK_PIECES];
+#pragma unroll
+    for (int p = 0; p < MAX_CHUNK_PIECES; ++p) {
+        ls[p] = -INFINITY;
+        ov[p] = make_uint2(0u, 0u);
+        if (p < np) {
+            ls[p] = __ldg(a.lse + (size_t)(p0 + p) * a.C * a.hq + lse_off);
+            ov[p] = __ldg(reinterpret_cast<const uint2*>(a.part + (size_t)(p0 + p) * a.piece_elems + o_off));
         }
-        const bool failed = *reinterpret_cast<const volatile int*>(a.status) != 0;
-        const float inv = failed ? __int_as_float(0x7fffffff) : 1.f / den;
-        acc = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-        const size_t off = ((size_t)row * a.hq + h) * D + 4 * lane;
-        if (a.out_bf16) {
-            const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
-            uint2 u;
-            u.x = *reinterpret_cast<const uint32_t*>(&lo);
-            u.y = *reinterpret_cast<const uint32_t*>(&hi);
-            *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.out) + off) = u;
-        } else {
-            *reinterpret_cast<float4*>(static_cast<float*>(a.out) + off) = acc;
-        }
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int p = 0; p < MAX_CHUNK_PIECES; ++p) mx = fmaxf(mx, ls[p]);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float den = 0.f;
+#pragma unroll
+    for (int p = 0; p < MAX_CHUNK_PIECES; ++p) {
+        const float wt = p < np ? ex2(ls[p] - mx) : 0.f;   // absent pieces: zero weight, zero vector
+        acc.x = fmaf(wt, __uint_as_float(ov[p].x << 16), acc.x);
+        acc.y = fmaf(wt, __uint_as_float(ov[p].x & 0xffff0000u), acc.y);
+        acc.z = fmaf(wt, __uint_as_float(ov[p].y << 16), acc.z);
+        acc.w = fmaf(wt, __uint_as_float(ov[p].y & 0xffff0000u), acc.w);
+        den += wt;
+    }
+    const bool failed = *reinterpret_cast<const volatile int*>(a.status) != 0;
+    const float inv = failed ? __int_as_float(0x7fffffff) : 1.f / den;
+    acc = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    const size_t off = ((size_t)row * a.hq + h) * D + 4 * lane;
+    if (a.out_bf16) {
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+        uint2 u;
+        u.x = *reinterpret_cast<const uint32_t*>(&lo);
+        u.y = *reinterpret_cast<const uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.out) + off) = u;
+    } else {
+        *reinterpret_cast<float4*>(static_cast<float*>(a.out) + off) = acc;
     }
 }
 
@@ -383,24 +401,38 @@ SA_API int sa_spp_prefill(sa_spp* sp, const void* q_local, const void* k_local, 
     const int C = S / (2 * P);
     const int chunk[2] = {sp->rank, 2 * P - 1 - sp->rank};
 
-    // the pieces: per chunk, blocks of C keys before it (unmasked), then its diagonal block
-    PrefillPiece pcs[2 * SPP_MAX + 2];
+    // the pieces: per chunk, blocks of L = max(C, 1024) keys before it
+    // (unmasked; the last one shorter), then its diagonal block of C keys
+    int L = C > spp::MIN_PIECE_KEYS ? C : spp::MIN_PIECE_KEYS;
+    const int most = (2 * P - 1) * C;                     // keys before the last chunk
+    const int cap = (most + spp::MAX_CHUNK_PIECES - 2) / (spp::MAX_CHUNK_PIECES - 1);
+    if (L < cap) L = cap;                                 // at most MAX_CHUNK_PIECES - 1 blocks per chunk
+    PrefillPiece pcs[2 * spp::MAX_CHUNK_PIECES];
     int first[2], count[2], n = 0;
     for (int half = 0; half < 2; ++half) {
         first[half] = n;
         const int start = chunk[half] * C;
-        for (int kv0 = 0; kv0 <= start; kv0 += C) {
+        for (int kv0 = 0; kv0 < start; kv0 += L) {
+            SA_CHECK_ARG(n - first[half] < spp::MAX_CHUNK_PIECES - 1, "sa_spp_prefill: too many key blocks");
             PrefillPiece& p = pcs[n++];
             p.q_row0 = half * C;
             p.kv_row0 = kv0;
             p.Sq = C;
-            p.Skv = C;
-            p.q_pos0 = start - kv0;           // C or more: every key visible; 0 on the diagonal
+            p.Skv = kv0 + L < start ? L : start - kv0;
+            p.q_pos0 = start - kv0;           // past the block's last key: every key visible
         }
+        PrefillPiece& d = pcs[n++];            // the diagonal
+        d.q_row0 = half * C;
+        d.kv_row0 = start;
+        d.Sq = C;
+        d.Skv = C;
+        d.q_pos0 = 0;
         count[half] = n - first[half];
     }
-    const long long piece_floats = (long long)C * hq * spp::D;
-    const size_t need = (size_t)n * (piece_floats + (size_t)C * hq) + 64;
+    SA_CHECK_ARG(n <= kPrefillMaxPieces, "sa_spp_prefill: %d pieces", n);
+    const long long piece_elems = (long long)C * hq * spp::D;
+    // bf16 piece outputs (half floats each) and fp32 lse, in floats
+    const size_t need = (size_t)n * (piece_elems / 2 + (size_t)C * hq) + 64;
     if (need > sp->part_floats) {
         SA_CUDA_TRY(cudaStreamSynchronize(st));
         cudaFree(sp->part);
@@ -412,9 +444,10 @@ SA_API int sa_spp_prefill(sa_spp* sp, const void* q_local, const void* k_local, 
         }
         sp->part_floats = need;
     }
-    float* lse = sp->part + (size_t)n * piece_floats;
+    __nv_bfloat16* parts = reinterpret_cast<__nv_bfloat16*>(sp->part);
+    float* lse = sp->part + (size_t)n * piece_elems / 2;
     for (int i = 0; i < n; ++i) {
-        pcs[i].out = sp->part + (size_t)i * piece_floats;
+        pcs[i].out = parts + (size_t)i * piece_elems;
         pcs[i].lse = lse + (size_t)i * C * hq;
     }
 
@@ -440,12 +473,12 @@ SA_API int sa_spp_prefill(sa_spp* sp, const void* q_local, const void* k_local, 
     const unsigned char* kv = sp->buf + spp::FLAG_BYTES + (size_t)(sp->inst & 1u) * sp->slot_bytes;
     const long long tok = (long long)hkv * spp::D;
     SA_RC_TRY(prefill_pieces_launch(st, sp->ctx->status, q_local, 2 * C, (long long)hq * spp::D, kv,
-                                    kv + sp->slot_bytes / 2, S, tok, hq, hkv, scale, SA_F32, (long long)hq * spp::D,
+                                    kv + sp->slot_bytes / 2, S, tok, hq, hkv, scale, SA_BF16, (long long)hq * spp::D,
                                     pcs, n));
     spp::MergeArgs ma{};
-    ma.part = sp->part;
+    ma.part = parts;
     ma.lse = lse;
-    ma.piece_floats = piece_floats;
+    ma.piece_elems = piece_elems;
     ma.C = C;
     ma.hq = hq;
     ma.first[0] = first[0]; ma.first[1] = first[1];
