@@ -231,7 +231,7 @@ int sa_attn_prefill(sa_ctx* ctx, const void* q, const void* k, const void* v, in
  * for (its statistics all-reduce mixes positions).
  *
  * sa_spp_create: this rank's object on the context's GPU for sequences of up
- *   to max_seq tokens with hkv KV heads of d = 128 (two K/V buffers of
+ *   to max_seq tokens with hkv <= 8 KV heads of d = 128 (two K/V buffers of
  *   max_seq x hkv x 128 bf16 each, shared with the other ranks).
  * sa_spp_handle / sa_spp_connect / sa_spp_connect_local / sa_spp_destroy:
  *   as the sa_sp_* functions (SA_SPP_HANDLE_BYTES per handle; one GPU per

@@ -95,28 +95,45 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     return v;
 }
 
-// Thread i handles 16-byte vector i of the rank's K and of its V (32-bit
-// indexing: 2C * row_vecs < 2^31), loads both once and stores them to every
-// rank's buffer, so each pass keeps 2 x world stores in flight per thread.
+// One warp per local row (hkv * 128 bf16 of K and of V): lane l loads
+// vectors l, l + 32, ... of both rows (all loads in flight before any store),
+// then stores them to the row's sequence position in every rank's buffer.
+constexpr int SC_VPL = 4;                      // vectors per lane per tensor (row_vecs <= 128: hkv <= 8)
 __global__ void spp_scatter_kernel(const ScatterArgs a) {
     const unsigned inst = a.inst;
     const int slot = (int)(inst & 1u);
-    const unsigned n = 2u * (unsigned)a.C * (unsigned)a.row_vecs;
+    const int lane = threadIdx.x & 31;
+    const int warps = (gridDim.x * blockDim.x) >> 5;
     unsigned char* base[SPP_MAX];
 #pragma unroll
     for (int r = 0; r < SPP_MAX; ++r)
         base[r] = r < a.world ? a.dst[r] + FLAG_BYTES + (size_t)slot * a.slot_bytes : nullptr;
-    for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-        const unsigned row = i / (unsigned)a.row_vecs, c = i - row * (unsigned)a.row_vecs;
-        const int half = row >= (unsigned)a.C ? 1 : 0;
-        const size_t seq_row = (size_t)(half ? a.chunk[1] : a.chunk[0]) * a.C + (row - (unsigned)half * a.C);
-        const uint4 kv = __ldg(a.k + i), vv = __ldg(a.v + i);
-        const size_t off = (seq_row * a.row_vecs + c) * 16;
+    for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < 2 * a.C; row += warps) {
+        const int half = row >= a.C ? 1 : 0;
+        const size_t seq_row = (size_t)(half ? a.chunk[1] : a.chunk[0]) * a.C + (row - half * a.C);
+        const uint4* ks = a.k + (size_t)row * a.row_vecs;
+        const uint4* vs = a.v + (size_t)row * a.row_vecs;
+        uint4 kv[SC_VPL], vv[SC_VPL];
+#pragma unroll
+        for (int j = 0; j < SC_VPL; ++j) {
+            const int c = lane + 32 * j;
+            if (c < a.row_vecs) {
+                kv[j] = __ldg(ks + c);
+                vv[j] = __ldg(vs + c);
+            }
+        }
+        const size_t off = seq_row * a.row_vecs * 16;
 #pragma unroll
         for (int r = 0; r < SPP_MAX; ++r) {
             if (r >= a.world) break;
-            *reinterpret_cast<uint4*>(base[r] + off) = kv;
-            *reinterpret_cast<uint4*>(base[r] + a.tensor_bytes + off) = vv;
+#pragma unroll
+            for (int j = 0; j < SC_VPL; ++j) {
+                const int c = lane + 32 * j;
+                if (c < a.row_vecs) {
+                    reinterpret_cast<uint4*>(base[r] + off)[c] = kv[j];
+                    reinterpret_cast<uint4*>(base[r] + a.tensor_bytes + off)[c] = vv[j];
+                }
+            }
         }
     }
     // publish: every CTA's stores before its arrival; the last CTA to arrive
@@ -167,6 +184,11 @@ struct MergeArgs {
 // lse values, then all their output vectors, are loaded before any is used.
 // Rows whose pieces were cut short by an expired wait come out NaN.
 __global__ void spp_merge_kernel(const MergeArgs a) {
+    // the status word once per block (a read per warp would queue tens of
+    // thousands of requests on one L2 line)
+    __shared__ int s_failed;
+    if (threadIdx.x == 0) s_failed = *reinterpret_cast<const volatile int*>(a.status) != 0;
+    __syncthreads();
     const int lane = threadIdx.x & 31;
     const long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
     const long long n = 2LL * a.C * a.hq;
@@ -200,8 +222,7 @@ __global__ void spp_merge_kernel(const MergeArgs a) {
         acc.w = fmaf(wt, __uint_as_float(ov[p].y & 0xffff0000u), acc.w);
         den += wt;
     }
-    const bool failed = *reinterpret_cast<const volatile int*>(a.status) != 0;
-    const float inv = failed ? __int_as_float(0x7fffffff) : 1.f / den;
+    const float inv = s_failed ? __int_as_float(0x7fffffff) : 1.f / den;
     acc = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
     const size_t off = ((size_t)row * a.hq + h) * D + 4 * lane;
     if (a.out_bf16) {
@@ -235,7 +256,7 @@ SA_API int sa_spp_create(sa_ctx* ctx, int rank, int world, int max_seq, int hkv,
     SA_CHECK_ARG(world >= 1 && world <= SPP_MAX, "sa_spp_create: world = %d (1..%d)", world, SPP_MAX);
     SA_CHECK_ARG(rank >= 0 && rank < world, "sa_spp_create: rank %d of %d", rank, world);
     SA_CHECK_ARG(d == spp::D, "sa_spp_create: d = %d (the tensor-core prefill is built for d = 128)", d);
-    SA_CHECK_ARG(hkv >= 1 && hkv <= 64 && max_seq >= 2 * world && max_seq <= (1 << 22),
+    SA_CHECK_ARG(hkv >= 1 && hkv <= 8 && max_seq >= 2 * world && max_seq <= (1 << 22),
                  "sa_spp_create: hkv = %d, max_seq = %d", hkv, max_seq);
     DeviceGuard guard(ctx->device);
     sa_spp* sp = new sa_spp();
@@ -388,7 +409,7 @@ SA_API int sa_spp_prefill(sa_spp* sp, const void* q_local, const void* k_local, 
                  sp->world);
     SA_CHECK_ARG(q_local && k_local && v_local && out_local, "sa_spp_prefill: null pointer");
     SA_CHECK_ARG(!(flags & SA_HOST_PTRS), "sa_spp_prefill: host pointers are not supported (pass device memory)");
-    SA_CHECK_ARG(d == spp::D && hkv == sp->hkv && hq >= hkv && hq % hkv == 0 && hq <= 256,
+    SA_CHECK_ARG(d == spp::D && hkv == sp->hkv && hkv <= 8 && hq >= hkv && hq % hkv == 0 && hq <= 256,
                  "sa_spp_prefill: d = %d, hq = %d, hkv = %d (created for hkv = %d, d = 128)", d, hq, hkv, sp->hkv);
     const int P = sp->world;
     SA_CHECK_ARG(S >= 2 * P && S % (2 * P) == 0 && S <= sp->max_seq,
@@ -487,7 +508,7 @@ SA_API int sa_spp_prefill(sa_spp* sp, const void* q_local, const void* k_local, 
     ma.out_bf16 = out_dtype == SA_BF16;
     ma.status = sp->ctx->status;
     const long long warps = 2LL * C * hq;
-    spp::spp_merge_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(ma);
+    spp::spp_merge_kernel<<<(unsigned)((warps * 32 + 1023) / 1024), 1024, 0, st>>>(ma);
     SA_CUDA_TRY(cudaGetLastError());
     ++sp->inst;   // the next call uses the other slot
     return SA_OK;

@@ -7,8 +7,9 @@ The target is the oracle's causal prefill (oracle/sa_oracle.c, the
 reference's block-wise online softmax, ops.cpp:1027-1112) on the same
 bf16-valued inputs, within the bf16 tensor-core bar (2e-2 of max |out|);
 the pieces' merge is also checked against the single-launch prefill of the
-whole sequence (same kernel, different key blocking) at 2e-3.  World 1 runs
-on one GPU (the piece table and the merge); 2 and 4 ranks need that many."""
+whole sequence (same kernel, different key blocking, bf16 piece outputs) at
+5e-3.  World 1 runs on one GPU (the piece table and the merge); 2 and 4
+ranks need that many."""
 import os
 
 import numpy as np
@@ -63,7 +64,8 @@ def test_spp_one_gpu(ctx, oracle, S, hq, hkv):
     ref = _ref(oracle, q, k, v)
     scale = np.abs(ref).max()
     assert np.abs(got - ref).max() <= BAR * scale
-    assert np.abs(got - full.cpu().numpy()).max() <= 2e-3 * scale
+    # the pieces' outputs are bf16: one bf16 rounding (2^-8 relative) apart
+    assert np.abs(got - full.cpu().numpy()).max() <= 5e-3 * scale
     # bf16 output: the fp32 result rounded
     ob = sp.prefill(ql, kl, vl, 1 / np.sqrt(128))
     ctx.synchronize()
