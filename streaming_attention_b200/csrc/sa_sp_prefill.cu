@@ -99,7 +99,7 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
 // vectors l, l + 32, ... of both rows (all loads in flight before any store),
 // then stores them to the row's sequence position in every rank's buffer.
 constexpr int SC_VPL = 4;                      // vectors per lane per tensor (row_vecs <= 128: hkv <= 8)
-__global__ void spp_scatter_kernel(const ScatterArgs a) {
+__global__ void __launch_bounds__(512) spp_scatter_kernel(const ScatterArgs a) {
     const unsigned inst = a.inst;
     const int slot = (int)(inst & 1u);
     const int lane = threadIdx.x & 31;
@@ -136,11 +136,13 @@ __global__ void spp_scatter_kernel(const ScatterArgs a) {
             }
         }
     }
-    // publish: every CTA's stores before its arrival; the last CTA to arrive
-    // stores the epoch into flag [slot][rank] of every rank
-    __threadfence_system();
+    // publish: the CTA barrier orders every thread's stores before thread 0's
+    // system-scope fence (fences are cumulative), which orders them before
+    // the CTA's arrival; the last CTA to arrive stores the epoch into flag
+    // [slot][rank] of every rank
     __syncthreads();
     if (threadIdx.x == 0) {
+        __threadfence_system();
         const unsigned prev = atomicAdd(a.cnt, 1u);
         if (prev == gridDim.x - 1) {
             __threadfence_system();
@@ -183,7 +185,7 @@ struct MergeArgs {
 // One warp per (local row, head); lane l owns dims 4l..4l+3.  All pieces'
 // lse values, then all their output vectors, are loaded before any is used.
 // Rows whose pieces were cut short by an expired wait come out NaN.
-__global__ void spp_merge_kernel(const MergeArgs a) {
+__global__ void __launch_bounds__(512) spp_merge_kernel(const MergeArgs a) {
     // the status word once per block (a read per warp would queue tens of
     // thousands of requests on one L2 line)
     __shared__ int s_failed;
@@ -508,7 +510,7 @@ SA_API int sa_spp_prefill(sa_spp* sp, const void* q_local, const void* k_local, 
     ma.out_bf16 = out_dtype == SA_BF16;
     ma.status = sp->ctx->status;
     const long long warps = 2LL * C * hq;
-    spp::spp_merge_kernel<<<(unsigned)((warps * 32 + 1023) / 1024), 1024, 0, st>>>(ma);
+    spp::spp_merge_kernel<<<(unsigned)((warps * 32 + 511) / 512), 512, 0, st>>>(ma);
     SA_CUDA_TRY(cudaGetLastError());
     ++sp->inst;   // the next call uses the other slot
     return SA_OK;
