@@ -99,7 +99,7 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
 // vectors l, l + 32, ... of both rows (all loads in flight before any store),
 // then stores them to the row's sequence position in every rank's buffer.
 constexpr int SC_VPL = 4;                      // vectors per lane per tensor (row_vecs <= 128: hkv <= 8)
-__global__ void __launch_bounds__(512) spp_scatter_kernel(const ScatterArgs a) {
+__global__ void __launch_bounds__(512, 2) spp_scatter_kernel(const ScatterArgs a) {
     const unsigned inst = a.inst;
     const int slot = (int)(inst & 1u);
     const int lane = threadIdx.x & 31;
@@ -182,59 +182,75 @@ struct MergeArgs {
     const int* status;
 };
 
-// One warp per (local row, head); lane l owns dims 4l..4l+3.  All pieces'
-// lse values, then all their output vectors, are loaded before any is used.
-// Rows whose pieces were cut short by an expired wait come out NaN.
+// Sixteen threads per (local row, head): thread j owns dims 8j..8j+7 (one
+// 16-byte load per piece).  Pieces are taken four at a time, their loads
+// issued together, and folded in with a running maximum, so a thread holds
+// few registers and many (row, head) pairs are in flight per SM.  Rows whose
+// pieces were cut short by an expired wait come out NaN.
+constexpr int MG = 4;                          // pieces per load group
 __global__ void __launch_bounds__(512) spp_merge_kernel(const MergeArgs a) {
     // the status word once per block (a read per warp would queue tens of
     // thousands of requests on one L2 line)
     __shared__ int s_failed;
     if (threadIdx.x == 0) s_failed = *reinterpret_cast<const volatile int*>(a.status) != 0;
     __syncthreads();
-    const int lane = threadIdx.x & 31;
-    const long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+    const int j = threadIdx.x & 15;
+    const long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 4;
     const long long n = 2LL * a.C * a.hq;
     if (w >= n) return;
     const int row = (int)(w / a.hq), h = (int)(w - (long long)row * a.hq);
     const int half = row >= a.C ? 1 : 0, lr = row - half * a.C;
     const int p0 = half ? a.first[1] : a.first[0], np = half ? a.count[1] : a.count[0];
-    const size_t lse_off = (size_t)lr * a.hq + h, o_off = lse_off * D + 4 * lane;
-    float ls[MAX_CHUNK_PIECES];
-    uint2 ov[MAX_CHUNK_PIECES];
+    const size_t lse_off = (size_t)lr * a.hq + h, o_off = lse_off * D + 8 * j;
+    const size_t lse_stride = (size_t)a.C * a.hq;
+    float mx = -INFINITY, den = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int g = 0; g < np; g += MG) {
+        float ls[MG];
+        uint4 ov[MG];
 #pragma unroll
-    for (int p = 0; p < MAX_CHUNK_PIECES; ++p) {
-        ls[p] = -INFINITY;
-        ov[p] = make_uint2(0u, 0u);
-        if (p < np) {
-            ls[p] = __ldg(a.lse + (size_t)(p0 + p) * a.C * a.hq + lse_off);
-            ov[p] = __ldg(reinterpret_cast<const uint2*>(a.part + (size_t)(p0 + p) * a.piece_elems + o_off));
+        for (int i = 0; i < MG; ++i) {
+            ls[i] = -INFINITY;
+            ov[i] = make_uint4(0u, 0u, 0u, 0u);
+            if (g + i < np) {
+                ls[i] = __ldg(a.lse + (size_t)(p0 + g + i) * lse_stride + lse_off);
+                ov[i] = __ldg(reinterpret_cast<const uint4*>(a.part + (size_t)(p0 + g + i) * a.piece_elems + o_off));
+            }
         }
-    }
-    float mx = -INFINITY;
+        float gm = mx;
 #pragma unroll
-    for (int p = 0; p < MAX_CHUNK_PIECES; ++p) mx = fmaxf(mx, ls[p]);
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    float den = 0.f;
+        for (int i = 0; i < MG; ++i) gm = fmaxf(gm, ls[i]);
+        const float r = ex2(mx - gm);              // rescale what is folded in so far (0 at the start)
+        den *= r;
 #pragma unroll
-    for (int p = 0; p < MAX_CHUNK_PIECES; ++p) {
-        const float wt = p < np ? ex2(ls[p] - mx) : 0.f;   // absent pieces: zero weight, zero vector
-        acc.x = fmaf(wt, __uint_as_float(ov[p].x << 16), acc.x);
-        acc.y = fmaf(wt, __uint_as_float(ov[p].x & 0xffff0000u), acc.y);
-        acc.z = fmaf(wt, __uint_as_float(ov[p].y << 16), acc.z);
-        acc.w = fmaf(wt, __uint_as_float(ov[p].y & 0xffff0000u), acc.w);
-        den += wt;
+        for (int e = 0; e < 8; ++e) acc[e] *= r;
+#pragma unroll
+        for (int i = 0; i < MG; ++i) {
+            const float wt = ex2(ls[i] - gm);      // absent pieces: 2^-inf = 0
+            const uint32_t u[4] = {ov[i].x, ov[i].y, ov[i].z, ov[i].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                acc[2 * e] = fmaf(wt, __uint_as_float(u[e] << 16), acc[2 * e]);
+                acc[2 * e + 1] = fmaf(wt, __uint_as_float(u[e] & 0xffff0000u), acc[2 * e + 1]);
+            }
+            den += wt;
+        }
+        mx = gm;
     }
     const float inv = s_failed ? __int_as_float(0x7fffffff) : 1.f / den;
-    acc = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-    const size_t off = ((size_t)row * a.hq + h) * D + 4 * lane;
+    const size_t off = ((size_t)row * a.hq + h) * D + 8 * j;
     if (a.out_bf16) {
-        const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
-        uint2 u;
-        u.x = *reinterpret_cast<const uint32_t*>(&lo);
-        u.y = *reinterpret_cast<const uint32_t*>(&hi);
-        *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.out) + off) = u;
+        uint4 u;
+        uint32_t* up = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const __nv_bfloat162 b2 = __floats2bfloat162_rn(acc[2 * e] * inv, acc[2 * e + 1] * inv);
+            up[e] = *reinterpret_cast<const uint32_t*>(&b2);
+        }
+        *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + off) = u;
     } else {
-        *reinterpret_cast<float4*>(static_cast<float*>(a.out) + off) = acc;
+        float4* o = reinterpret_cast<float4*>(static_cast<float*>(a.out) + off);
+        o[0] = make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
+        o[1] = make_float4(acc[4] * inv, acc[5] * inv, acc[6] * inv, acc[7] * inv);
     }
 }
 
@@ -509,8 +525,8 @@ SA_API int sa_spp_prefill(sa_spp* sp, const void* q_local, const void* k_local, 
     ma.out = out_local;
     ma.out_bf16 = out_dtype == SA_BF16;
     ma.status = sp->ctx->status;
-    const long long warps = 2LL * C * hq;
-    spp::spp_merge_kernel<<<(unsigned)((warps * 32 + 511) / 512), 512, 0, st>>>(ma);
+    const long long threads = 16LL * 2 * C * hq;
+    spp::spp_merge_kernel<<<(unsigned)((threads + 511) / 512), 512, 0, st>>>(ma);
     SA_CUDA_TRY(cudaGetLastError());
     ++sp->inst;   // the next call uses the other slot
     return SA_OK;
