@@ -117,15 +117,19 @@ __device__ __forceinline__ void store_hilo4(__nv_bfloat16* hi, __nv_bfloat16* lo
 }
 
 // QW_EPI_QKV_ROWS: warp `quad` of the four epilogue warps takes rows quad,
-// quad + 4, ...; for each row, the tile's BN / 128 heads (lane l: elements
-// 4l..4l+3 of a head), interleaved so their reductions overlap.
+// quad + 4, ... four at a time: the four rows' RoPE cos/sin and tile values
+// are loaded before any is used (one load latency per four rows), then each
+// row's BN / 128 heads (lane l: elements 4l..4l+3 of a head) are normalised,
+// rotated and stored, their reductions interleaved.
 template <int BN>
 __device__ __forceinline__ void qkv_rows_epilogue(const Args& a, const float* T, const float* rs, bool scaled,
                                                   int m0, int n0, int quad, int lane) {
-    constexpr int HPT = BN / 128, TP = Cfg<BN>::TP, D = 128;
+    constexpr int HPT = BN / 128, TP = Cfg<BN>::TP, D = 128, RB = 4;
     const GemmEpi& e = a.e;
     const int nqk = e.hq + e.hkv;                  // heads [nqk, nqk + hkv) are V heads
     const int h0 = n0 / D;
+    const int i0 = (4 * lane) & (D / 2 - 1);
+    const bool first = lane < 16;
     float4 nw[HPT];
 #pragma unroll
     for (int hh = 0; hh < HPT; ++hh) {
@@ -134,62 +138,71 @@ __device__ __forceinline__ void qkv_rows_epilogue(const Args& a, const float* T,
         nw[hh] = h < nqk ? __ldg(reinterpret_cast<const float4*>(w) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll 1
-    for (int rr = quad; rr < BM; rr += 4) {
-        const int m = m0 + rr;
-        const int pos = e.pos0 + m, row = pos + e.row_shift;
-        if (m >= a.M || row >= e.max_seq) break;   // rows only grow along the loop
-        const int i0 = (4 * lane) & (D / 2 - 1);
-        const float4 c4 = __ldg(reinterpret_cast<const float4*>(e.cos_t + (size_t)pos * (D / 2) + i0));
-        const float4 s4 = __ldg(reinterpret_cast<const float4*>(e.sin_t + (size_t)pos * (D / 2) + i0));
-        const float sc = scaled ? rs[rr] : 1.f;
-        float ev[HPT][4];
+    for (int r0 = quad; r0 < BM; r0 += 4 * RB) {
+        float4 c4[RB], s4[RB];
+        float ev[RB][HPT][4];
 #pragma unroll
-        for (int hh = 0; hh < HPT; ++hh) {
-            const float4 t4 = *reinterpret_cast<const float4*>(T + rr * TP + hh * D + 4 * lane);
-            ev[hh][0] = t4.x * sc; ev[hh][1] = t4.y * sc; ev[hh][2] = t4.z * sc; ev[hh][3] = t4.w * sc;
-        }
-        float ss[HPT];
+        for (int b = 0; b < RB; ++b) {
+            const int rr = r0 + 4 * b, m = m0 + rr;
+            const int pos = e.pos0 + (m < a.M ? m : m0);
+            c4[b] = __ldg(reinterpret_cast<const float4*>(e.cos_t + (size_t)pos * (D / 2) + i0));
+            s4[b] = __ldg(reinterpret_cast<const float4*>(e.sin_t + (size_t)pos * (D / 2) + i0));
+            const float sc = scaled ? rs[rr] : 1.f;
 #pragma unroll
-        for (int hh = 0; hh < HPT; ++hh)
-            ss[hh] = ev[hh][0] * ev[hh][0] + ev[hh][1] * ev[hh][1] + ev[hh][2] * ev[hh][2] + ev[hh][3] * ev[hh][3];
-#pragma unroll
-        for (int o = 16; o; o >>= 1)
-#pragma unroll
-            for (int hh = 0; hh < HPT; ++hh) ss[hh] += __shfl_xor_sync(0xffffffffu, ss[hh], o);
-        const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
-        const bool first = lane < 16;
-#pragma unroll
-        for (int hh = 0; hh < HPT; ++hh) {
-            const int h = h0 + hh;
-            if (h >= nqk) {                        // V head: the projection as it is
-                const int vh = h - nqk;
-                const float4 v4 = make_float4(ev[hh][0], ev[hh][1], ev[hh][2], ev[hh][3]);
-                if (e.vc) *reinterpret_cast<float4*>(e.vc + ((size_t)vh * e.max_seq + row) * D + 4 * lane) = v4;
-                if (e.v_bf)
-                    *reinterpret_cast<uint2*>(e.v_bf + ((size_t)pos * e.hkv + vh) * D + 4 * lane) = qd::bf16x4(v4);
-                continue;
+            for (int hh = 0; hh < HPT; ++hh) {
+                const float4 t4 = *reinterpret_cast<const float4*>(T + rr * TP + hh * D + 4 * lane);
+                ev[b][hh][0] = t4.x * sc; ev[b][hh][1] = t4.y * sc; ev[b][hh][2] = t4.z * sc; ev[b][hh][3] = t4.w * sc;
             }
-            // QK-norm (eps 1e-6 inside the sqrt) with the head's gain, then
-            // rotate-half RoPE: element i pairs with i + 64 (lane l ^ 16)
-            const float rms = sqrtf(ss[hh] / (float)D + 1e-6f);
-            const float g4[4] = {nw[hh].x, nw[hh].y, nw[hh].z, nw[hh].w};
-            float y[4], p[4], o[4];
+        }
 #pragma unroll
-            for (int j = 0; j < 4; ++j) y[j] = (ev[hh][j] / rms) * g4[j];
+        for (int b = 0; b < RB; ++b) {
+            const int rr = r0 + 4 * b, m = m0 + rr;
+            const int pos = e.pos0 + m, row = pos + e.row_shift;
+            if (m >= a.M || row >= e.max_seq) break;   // rows only grow along the loop (warp-uniform)
+            float ss[HPT];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) p[j] = __shfl_xor_sync(0xffffffffu, y[j], 16);
+            for (int hh = 0; hh < HPT; ++hh)
+                ss[hh] = ev[b][hh][0] * ev[b][hh][0] + ev[b][hh][1] * ev[b][hh][1] + ev[b][hh][2] * ev[b][hh][2] +
+                         ev[b][hh][3] * ev[b][hh][3];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) o[j] = first ? y[j] * cs[j] + (-p[j]) * sn[j] : y[j] * cs[j] + p[j] * sn[j];
-            const float4 r4 = make_float4(o[0], o[1], o[2], o[3]);
-            if (h < e.hq) {
-                const size_t off = ((size_t)m * e.hq + h) * D + 4 * lane;
-                if (e.q_out) *reinterpret_cast<float4*>(e.q_out + off) = r4;
-                if (e.q_bf) *reinterpret_cast<uint2*>(e.q_bf + off) = qd::bf16x4(r4);
-            } else {
-                const int kh = h - e.hq;
-                if (e.kc) *reinterpret_cast<float4*>(e.kc + ((size_t)kh * e.max_seq + row) * D + 4 * lane) = r4;
-                if (e.k_bf)
-                    *reinterpret_cast<uint2*>(e.k_bf + ((size_t)pos * e.hkv + kh) * D + 4 * lane) = qd::bf16x4(r4);
+            for (int o = 16; o; o >>= 1)
+#pragma unroll
+                for (int hh = 0; hh < HPT; ++hh) ss[hh] += __shfl_xor_sync(0xffffffffu, ss[hh], o);
+            const float cs[4] = {c4[b].x, c4[b].y, c4[b].z, c4[b].w}, sn[4] = {s4[b].x, s4[b].y, s4[b].z, s4[b].w};
+#pragma unroll
+            for (int hh = 0; hh < HPT; ++hh) {
+                const int h = h0 + hh;
+                if (h >= nqk) {                    // V head: the projection as it is
+                    const int vh = h - nqk;
+                    const float4 v4 = make_float4(ev[b][hh][0], ev[b][hh][1], ev[b][hh][2], ev[b][hh][3]);
+                    if (e.vc) *reinterpret_cast<float4*>(e.vc + ((size_t)vh * e.max_seq + row) * D + 4 * lane) = v4;
+                    if (e.v_bf)
+                        *reinterpret_cast<uint2*>(e.v_bf + ((size_t)pos * e.hkv + vh) * D + 4 * lane) = qd::bf16x4(v4);
+                    continue;
+                }
+                // QK-norm (eps 1e-6 inside the sqrt) with the head's gain, then
+                // rotate-half RoPE: element i pairs with i + 64 (lane l ^ 16)
+                const float rms = sqrtf(ss[hh] / (float)D + 1e-6f);
+                const float g4[4] = {nw[hh].x, nw[hh].y, nw[hh].z, nw[hh].w};
+                float y[4], p[4], o[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) y[j] = (ev[b][hh][j] / rms) * g4[j];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) p[j] = __shfl_xor_sync(0xffffffffu, y[j], 16);
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    o[j] = first ? y[j] * cs[j] + (-p[j]) * sn[j] : y[j] * cs[j] + p[j] * sn[j];
+                const float4 r4 = make_float4(o[0], o[1], o[2], o[3]);
+                if (h < e.hq) {
+                    const size_t off = ((size_t)m * e.hq + h) * D + 4 * lane;
+                    if (e.q_out) *reinterpret_cast<float4*>(e.q_out + off) = r4;
+                    if (e.q_bf) *reinterpret_cast<uint2*>(e.q_bf + off) = qd::bf16x4(r4);
+                } else {
+                    const int kh = h - e.hq;
+                    if (e.kc) *reinterpret_cast<float4*>(e.kc + ((size_t)kh * e.max_seq + row) * D + 4 * lane) = r4;
+                    if (e.k_bf)
+                        *reinterpret_cast<uint2*>(e.k_bf + ((size_t)pos * e.hkv + kh) * D + 4 * lane) = qd::bf16x4(r4);
+                }
             }
         }
     }
