@@ -26,8 +26,9 @@
 //      carry the whole prefix), and a rank's pieces fill the SMs.  Pieces
 //      write bf16 partial outputs and their rows' log-sum-exp.
 //   4. spp_merge_kernel: out = sum_p 2^(lse_p - lse) O_p over the pieces of
-//      each chunk (lse = log2 sum_p 2^lse_p), in the caller's dtype; then the
-//      instance count advances.
+//      each chunk (lse = log2 sum_p 2^lse_p), in the caller's dtype.
+// The host counts the calls (the instance: slot = instance & 1, epoch =
+// instance + 1); an instance is spent as soon as its exchange is issued.
 // Slots alternate between calls, so a rank writing call i+1's rows never
 // overwrites rows a slower peer still reads for call i: a rank can only
 // start call i+2 after every peer published call i+1, which each does only
@@ -508,8 +509,11 @@ SA_API int sa_spp_prefill(sa_spp* sp, const void* q_local, const void* k_local, 
     SA_CUDA_TRY(cudaGetLastError());
     spp::spp_wait_kernel<<<1, 32, 0, st>>>(reinterpret_cast<const unsigned*>(sp->buf), P, sp->inst,
                                            sp->ctx->status);
+    // the instance is spent once its exchange is issued, whatever follows, so
+    // the ranks' slots and epochs stay in step
+    const unsigned inst = sp->inst++;
     SA_CUDA_TRY(cudaGetLastError());
-    const unsigned char* kv = sp->buf + spp::FLAG_BYTES + (size_t)(sp->inst & 1u) * sp->slot_bytes;
+    const unsigned char* kv = sp->buf + spp::FLAG_BYTES + (size_t)(inst & 1u) * sp->slot_bytes;
     const long long tok = (long long)hkv * spp::D;
     SA_RC_TRY(prefill_pieces_launch(st, sp->ctx->status, q_local, 2 * C, (long long)hq * spp::D, kv,
                                     kv + sp->slot_bytes / 2, S, tok, hq, hkv, scale, SA_BF16, (long long)hq * spp::D,
@@ -528,6 +532,5 @@ SA_API int sa_spp_prefill(sa_spp* sp, const void* q_local, const void* k_local, 
     const long long threads = 16LL * 2 * C * hq;
     spp::spp_merge_kernel<<<(unsigned)((threads + 511) / 512), 512, 0, st>>>(ma);
     SA_CUDA_TRY(cudaGetLastError());
-    ++sp->inst;   // the next call uses the other slot
     return SA_OK;
 }
