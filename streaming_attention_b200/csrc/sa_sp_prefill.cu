@@ -39,6 +39,7 @@
 #include "sa_internal.h"
 #include "sa_ptx.cuh"
 #include "sa_qwen3.h"
+#include "sa_spp_plan.h"
 
 constexpr int SPP_MAX = 8;
 
@@ -441,33 +442,20 @@ SA_API int sa_spp_prefill(sa_spp* sp, const void* q_local, const void* k_local, 
     const int C = S / (2 * P);
     const int chunk[2] = {sp->rank, 2 * P - 1 - sp->rank};
 
-    // the pieces: per chunk, blocks of L = max(C, 1024) keys before it
-    // (unmasked; the last one shorter), then its diagonal block of C keys
-    int L = C > spp::MIN_PIECE_KEYS ? C : spp::MIN_PIECE_KEYS;
-    const int most = (2 * P - 1) * C;                     // keys before the last chunk
-    const int cap = (most + spp::MAX_CHUNK_PIECES - 2) / (spp::MAX_CHUNK_PIECES - 1);
-    if (L < cap) L = cap;                                 // at most MAX_CHUNK_PIECES - 1 blocks per chunk
-    PrefillPiece pcs[2 * spp::MAX_CHUNK_PIECES];
-    int first[2], count[2], n = 0;
-    for (int half = 0; half < 2; ++half) {
-        first[half] = n;
-        const int start = chunk[half] * C;
-        for (int kv0 = 0; kv0 < start; kv0 += L) {
-            SA_CHECK_ARG(n - first[half] < spp::MAX_CHUNK_PIECES - 1, "sa_spp_prefill: too many key blocks");
-            PrefillPiece& p = pcs[n++];
-            p.q_row0 = half * C;
-            p.kv_row0 = kv0;
-            p.Sq = C;
-            p.Skv = kv0 + L < start ? L : start - kv0;
-            p.q_pos0 = start - kv0;           // past the block's last key: every key visible
-        }
-        PrefillPiece& d = pcs[n++];            // the diagonal
-        d.q_row0 = half * C;
-        d.kv_row0 = start;
-        d.Sq = C;
-        d.Skv = C;
-        d.q_pos0 = 0;
-        count[half] = n - first[half];
+    // the pieces (sa_spp_plan.h): per chunk, unmasked key blocks before it,
+    // then its diagonal block
+    spp::PieceSpec spec[kPrefillMaxPieces];
+    PrefillPiece pcs[kPrefillMaxPieces];
+    int first[2], count[2];
+    const int n = spp::plan_pieces(sp->rank, P, C, spp::MIN_PIECE_KEYS, spp::MAX_CHUNK_PIECES, spec,
+                                   kPrefillMaxPieces, first, count);
+    SA_CHECK_ARG(n >= 1, "sa_spp_prefill: S = %d over %d ranks needs too many key blocks", S, P);
+    for (int i = 0; i < n; ++i) {
+        pcs[i].q_row0 = spec[i].q_row0;
+        pcs[i].kv_row0 = spec[i].kv_row0;
+        pcs[i].Sq = C;
+        pcs[i].Skv = spec[i].Skv;
+        pcs[i].q_pos0 = spec[i].q_pos0;
     }
     SA_CHECK_ARG(n <= kPrefillMaxPieces, "sa_spp_prefill: %d pieces", n);
     const long long piece_elems = (long long)C * hq * spp::D;
