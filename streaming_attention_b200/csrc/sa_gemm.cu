@@ -56,14 +56,9 @@ namespace gm {
 constexpr int BM = 128, BK = 64, THREADS = 192, MAX_SPLIT = 8;
 constexpr int A_BYTES = BM * BK * 2;          // 16 KB (one of hi / lo)
 
-// Ring depth of the one-CTA-per-SM variants; the 2-stage BN = 128 variant
-// (about 100 KB of shared memory) runs two CTAs per SM, so one CTA's
-// epilogue overlaps the other's main loop.
-constexpr int default_stages(int bn) { return bn == 256 ? 3 : 4; }
-
-template <int BN, int ST = default_stages(BN)>
+template <int BN>
 struct Cfg {
-    static constexpr int STAGES = ST;
+    static constexpr int STAGES = BN == 256 ? 3 : 4;
     static constexpr int W_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = 2 * A_BYTES + W_BYTES;
     static constexpr int TP = BN + 4;                        // padded epilogue tile row pitch (floats)
@@ -129,7 +124,7 @@ __device__ __forceinline__ void store_hilo4(__nv_bfloat16* hi, __nv_bfloat16* lo
 template <int BN>
 __device__ __forceinline__ void qkv_rows_epilogue(const Args& a, const float* T, const float* rs, bool scaled,
                                                   int m0, int n0, int quad, int lane) {
-    constexpr int HPT = BN / 128, TP = BN + 4, D = 128, RB = 4;
+    constexpr int HPT = BN / 128, TP = Cfg<BN>::TP, D = 128, RB = 4;
     const GemmEpi& e = a.e;
     const int nqk = e.hq + e.hkv;                  // heads [nqk, nqk + hkv) are V heads
     const int h0 = n0 / D;
@@ -220,7 +215,7 @@ __device__ __forceinline__ void qkv_rows_epilogue(const Args& a, const float* T,
 template <int BN>
 __device__ __forceinline__ void resid_norm_epilogue(const Args& a, const float* T, int m0, int n0, int quad,
                                                     int lane) {
-    constexpr int V4 = BN / 128, TP = BN + 4;
+    constexpr int V4 = BN / 128, TP = Cfg<BN>::TP;
     float4 gv[V4];
 #pragma unroll
     for (int j = 0; j < V4; ++j) gv[j] = __ldg(reinterpret_cast<const float4*>(a.e.g + n0 + 128 * j) + lane);
@@ -258,11 +253,11 @@ __device__ __forceinline__ void resid_norm_epilogue(const Args& a, const float* 
     }
 }
 
-template <int BN, int ST>
-__global__ void __launch_bounds__(THREADS, ST == 2 ? 2 : 1)
+template <int BN>
+__global__ void __launch_bounds__(THREADS, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
             const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tpart, const Args a) {
-    using C_ = Cfg<BN, ST>;
+    using C_ = Cfg<BN>;
     constexpr int STAGES = C_::STAGES, STAGE_BYTES = C_::STAGE_BYTES, TP = C_::TP;
     extern __shared__ unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -493,7 +488,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ C
 }
 
 // CTAs of the BN variant that fit on one SM, cached per device.
-template <int BN, int ST = default_stages(BN)>
+template <int BN>
 int ctas_per_sm(int device) {
     static std::mutex mu;
     static std::map<int, int> cache;
@@ -501,8 +496,8 @@ int ctas_per_sm(int device) {
     auto it = cache.find(device);
     if (it != cache.end()) return it->second;
     int n = 0;
-    if (set_smem_attr_once((const void*)gemm_kernel<BN, ST>, Cfg<BN, ST>::SMEM_BYTES) != SA_OK ||
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemm_kernel<BN, ST>, THREADS, Cfg<BN, ST>::SMEM_BYTES) !=
+    if (set_smem_attr_once((const void*)gemm_kernel<BN>, Cfg<BN>::SMEM_BYTES) != SA_OK ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemm_kernel<BN>, THREADS, Cfg<BN>::SMEM_BYTES) !=
             cudaSuccess) {
         cudaGetLastError();
         clear_error();
@@ -512,16 +507,14 @@ int ctas_per_sm(int device) {
     return n;
 }
 
-int ctas_per_sm_bn(int bn, int stages, int device) {
-    if (bn == 128 && stages == 2) return ctas_per_sm<128, 2>(device);
+int ctas_per_sm_bn(int bn, int device) {
     return bn == 64 ? ctas_per_sm<64>(device) : bn == 128 ? ctas_per_sm<128>(device) : ctas_per_sm<256>(device);
 }
 
 }  // namespace gm
 
 void gemm_prepare(int device) {
-    for (int bn : {64, 128, 256}) gm::ctas_per_sm_bn(bn, 0, device);
-    gm::ctas_per_sm_bn(128, 2, device);
+    for (int bn : {64, 128, 256}) gm::ctas_per_sm_bn(bn, device);
 }
 
 // Tile width and split count for one GEMM.  Cost per wave of resident CTAs =
@@ -534,7 +527,7 @@ GemmPlan gemm_plan(int device, int num_sms, int M, int N, int K, bool split_ok) 
     double best_cost = 1e30;
     const int mt = (M + gm::BM - 1) / gm::BM, kb = K / gm::BK;
     for (int bn : {64, 128, 256}) {
-        const int per_sm = gm::ctas_per_sm_bn(bn, 0, device);
+        const int per_sm = gm::ctas_per_sm_bn(bn, device);
         if (per_sm <= 0) continue;
         const int nt = (N + bn - 1) / bn;
         for (int s = 1; s <= (split_ok ? gm::MAX_SPLIT : 1) && s <= kb; ++s) {
@@ -550,20 +543,6 @@ GemmPlan gemm_plan(int device, int num_sms, int M, int N, int K, bool split_ok) 
                 best = GemmPlan{bn, s};
             }
         }
-    }
-    // long unsplit GEMMs: the two-CTA-per-SM variant when its waves cost no
-    // more (one CTA's epilogue then runs under the other's main loop);
-    // SA_GEMM_TWO_CTA=0 keeps one CTA per SM
-    static const bool two_cta = [] {
-        const char* e = std::getenv("SA_GEMM_TWO_CTA");
-        return !(e && e[0] == '0');
-    }();
-    const int per2 = gm::ctas_per_sm_bn(128, 2, device);
-    if (two_cta && best.splits == 1 && M >= 512 && N % 128 == 0 && per2 >= 2) {
-        const long long ctas = (long long)((N + 127) / 128) * mt;
-        const long long waves = (ctas + (long long)num_sms * per2 - 1) / ((long long)num_sms * per2);
-        const double cost = (double)waves * (kb * gm::BK * (gm::BM * 4.0 + 128 * 2.0) + 65536.0);
-        if (cost <= best_cost) best = GemmPlan{128, 1, 2};
     }
     return best;
 }
@@ -621,14 +600,9 @@ int gemm_launch(cudaStream_t st, int* status, const __nv_bfloat16* a_hi, const _
     a.C = C; a.ldc = ldc; a.out_hi = out_hi; a.out_lo = out_lo; a.ldo = ldo;
     a.e = epi ? *epi : GemmEpi{};
     a.status = status;
-    const bool two = plan.stages == 2;
-    SA_CHECK_ARG(!two || (bn == 128 && s == 1), "gemm: the two-CTA variant is unsplit with tile width 128");
-    const void* fn = two ? (const void*)gm::gemm_kernel<128, 2>
-                   : bn == 64 ? (const void*)gm::gemm_kernel<64, gm::default_stages(64)>
-                   : bn == 128 ? (const void*)gm::gemm_kernel<128, gm::default_stages(128)>
-                               : (const void*)gm::gemm_kernel<256, gm::default_stages(256)>;
-    const int smem = two ? gm::Cfg<128, 2>::SMEM_BYTES
-                   : bn == 64 ? gm::Cfg<64>::SMEM_BYTES
+    const void* fn = bn == 64 ? (const void*)gm::gemm_kernel<64>
+                   : bn == 128 ? (const void*)gm::gemm_kernel<128> : (const void*)gm::gemm_kernel<256>;
+    const int smem = bn == 64 ? gm::Cfg<64>::SMEM_BYTES
                    : bn == 128 ? gm::Cfg<128>::SMEM_BYTES : gm::Cfg<256>::SMEM_BYTES;
     SA_RC_TRY(set_smem_attr_once(fn, smem));
     cudaLaunchConfig_t cfg = {};

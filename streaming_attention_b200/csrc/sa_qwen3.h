@@ -31,7 +31,6 @@ struct QkvEpi {
 // cluster that split K.
 struct GemmPlan {
     int bn, splits;
-    int stages = 0;   // 0: the tile width's one-CTA-per-SM ring; 2: BN 128, two CTAs per SM (unsplit only)
 };
 
 // Optional epilogue operands of an unsplit prompt GEMM (gemm_launch).
