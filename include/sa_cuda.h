@@ -245,7 +245,10 @@ int sa_attn_prefill(sa_ctx* ctx, const void* q, const void* k, const void* v, in
  *   multiple of 2 x world.  Asynchronous on the context's stream; every rank
  *   makes the same calls in the same order.  A rank that does not take part
  *   makes the others' waits expire after a few seconds (NaN in out_local,
- *   SA_ERR_TIMEOUT at their next synchronising call).
+ *   SA_ERR_TIMEOUT at their next synchronising call).  The object's buffers
+ *   for the partial outputs grow on the first call with a larger S x hq
+ *   (a device allocation after a stream synchronisation); later calls of the
+ *   same shape allocate nothing.
  */
 #define SA_SPP_HANDLE_BYTES 128
 typedef struct sa_spp sa_spp;

@@ -295,9 +295,17 @@ class SpPrefill:
         import ctypes as C
         import torch
         from ._capi import SA_BF16, SA_F32, check, lib
+        for name, t in (("q_local", q_local), ("k_local", k_local), ("v_local", v_local)):
+            if t.dtype != torch.bfloat16 or not t.is_cuda or t.dim() != 3:
+                raise TypeError(f"SpPrefill.prefill: {name} must be a 3-D bfloat16 CUDA tensor")
         q_local, k_local, v_local = q_local.contiguous(), k_local.contiguous(), v_local.contiguous()
         C2, hq, d = q_local.shape
         hkv = k_local.shape[1]
+        if k_local.shape != (C2, hkv, d) or v_local.shape != k_local.shape:
+            raise ValueError(f"SpPrefill.prefill: k_local / v_local must be [{C2}, hkv, {d}] like q_local's rows")
+        if out is not None and (tuple(out.shape) != (C2, hq, d) or not out.is_contiguous() or
+                                out.dtype not in (torch.bfloat16, torch.float32)):
+            raise ValueError(f"SpPrefill.prefill: out must be a contiguous [{C2}, {hq}, {d}] bf16 or fp32 tensor")
         if out is None:
             out = torch.empty(C2, hq, d, dtype=out_dtype or torch.bfloat16, device=q_local.device)
         dt = SA_F32 if out.dtype == torch.float32 else SA_BF16
