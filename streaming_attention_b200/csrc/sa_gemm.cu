@@ -124,7 +124,7 @@ __device__ __forceinline__ void store_hilo4(__nv_bfloat16* hi, __nv_bfloat16* lo
 template <int BN>
 __device__ __forceinline__ void qkv_rows_epilogue(const Args& a, const float* T, const float* rs, bool scaled,
                                                   int m0, int n0, int quad, int lane) {
-    constexpr int HPT = BN / 128, TP = Cfg<BN>::TP, D = 128, RB = 8;
+    constexpr int HPT = BN / 128, TP = Cfg<BN>::TP, D = 128, RB = 4;
     const GemmEpi& e = a.e;
     const int nqk = e.hq + e.hkv;                  // heads [nqk, nqk + hkv) are V heads
     const int h0 = n0 / D;
